@@ -1,0 +1,171 @@
+"""Kernel microbenchmarks: ``python -m representax_b200.bench_kernels``.
+
+Times each hot kernel with CUDA events on the launching stream after warm-up,
+flushing L2 between iterations with a 256 MB write, and prints one JSON line
+per case with the achieved rate and its fraction of the measured device peaks
+(``MEASURED_PEAKS.json`` when present; else 6.65 TB/s and 1.59 PFLOP/s).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+
+import torch
+
+
+def _peaks():
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "MEASURED_PEAKS.json")
+    try:
+        with open(path) as handle:
+            data = json.load(handle)
+        return float(data["hbm_gbs"]) * 1e9, float(data["bf16_tflops"]) * 1e12, "measured"
+    except (OSError, KeyError, ValueError):
+        return 6.65e12, 1.59e15, "fallback"
+
+
+class Timer:
+    def __init__(self, warmup=3, iters=10):
+        self.warmup = warmup
+        self.iters = iters
+        self.flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
+
+    def __call__(self, fn):
+        for _ in range(self.warmup):
+            fn()
+        torch.cuda.synchronize()
+        times = []
+        for _ in range(self.iters):
+            self.flush.fill_(1.0)
+            start = torch.cuda.Event(enable_timing=True)
+            end = torch.cuda.Event(enable_timing=True)
+            start.record()
+            fn()
+            end.record()
+            torch.cuda.synchronize()
+            times.append(start.elapsed_time(end) / 1e3)
+        times.sort()
+        return times[len(times) // 2]
+
+
+def bench_gemm(timer, hbm, flops_peak, tag, report):
+    from representax_b200.ops import gemm as G
+
+    shapes = [
+        ("qkv_fwd", 18432, 2304, 768),
+        ("ffn1_fwd", 18432, 3072, 768),
+        ("ffn2_fwd", 18432, 768, 3072),
+        ("square_8k", 8192, 8192, 8192),
+    ]
+    for name, m, n, k in shapes:
+        a = torch.randn(m, k, device="cuda").to(torch.bfloat16)
+        b = torch.randn(n, k, device="cuda").to(torch.bfloat16)
+        c = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+        t = timer(lambda: G.gemm(a, b, c))
+        t_ref = timer(lambda: torch.matmul(a, b.T))
+        fl = 2.0 * m * n * k
+        report({"kernel": "gemm_tcgen05_fwd", "case": name, "M": m, "N": n, "K": k, "ms": t * 1e3,
+                "tflops": fl / t / 1e12, f"frac_of_{tag}_bf16": fl / t / flops_peak,
+                "cublas_ms": t_ref * 1e3})
+    for name, t_, n, k in [("qkv", 18432, 2304, 768), ("ffn2", 18432, 768, 3072)]:
+        dy = torch.randn(t_, n, device="cuda").to(torch.bfloat16)
+        w = torch.randn(n, k, device="cuda").to(torch.bfloat16)
+        x = torch.randn(t_, k, device="cuda").to(torch.bfloat16)
+        dx = torch.empty(t_, k, dtype=torch.bfloat16, device="cuda")
+        gw = torch.zeros(n, k, device="cuda")
+        fl = 2.0 * t_ * n * k
+        t = timer(lambda: G.linear_dgrad(dy, w, out=dx))
+        report({"kernel": "gemm_tcgen05_dgrad", "case": name, "ms": t * 1e3, "tflops": fl / t / 1e12,
+                f"frac_of_{tag}_bf16": fl / t / flops_peak, "cublas_ms": timer(lambda: dy @ w) * 1e3})
+        t = timer(lambda: G.linear_wgrad(dy, x, gw))
+        report({"kernel": "gemm_tcgen05_wgrad", "case": name, "ms": t * 1e3, "tflops": fl / t / 1e12,
+                f"frac_of_{tag}_bf16": fl / t / flops_peak, "cublas_ms": timer(lambda: dy.T @ x) * 1e3})
+
+
+def bench_attention(timer, hbm, flops_peak, tag, report):
+    from representax_b200.ops._ext import ext
+
+    C = ext()
+    torch.manual_seed(0)
+    batch, heads = 128, 12
+    lens = torch.randint(32, 257, (batch,))
+    total = int(lens.sum())
+    cu = torch.zeros(batch + 1, dtype=torch.int32)
+    cu[1:] = lens.cumsum(0)
+    cu = cu.cuda()
+    qkv = torch.randn(total, 3 * 768, device="cuda").to(torch.bfloat16)
+    q, k, v = qkv[:, :768], qkv[:, 768:1536], qkv[:, 1536:]
+    o = torch.empty(total, 768, dtype=torch.bfloat16, device="cuda")
+    lse = torch.empty(heads, total, device="cuda")
+    fl = float(sum(4 * n * n * 64 * heads for n in lens.tolist()))
+    t = timer(lambda: C.attention_forward(q, k, v, o, lse, cu, 256, heads, heads, 0.125, False, -1))
+    report({"kernel": "attention_fwd", "case": "bert_b128_len32-256", "ms": t * 1e3,
+            "tflops": fl / t / 1e12, f"frac_of_{tag}_bf16": fl / t / flops_peak})
+    do = torch.randn(total, 768, device="cuda").to(torch.bfloat16)
+    dqkv = torch.empty_like(qkv)
+    acc = torch.empty(total, 768, device="cuda")
+    dvec = torch.empty(heads, total, device="cuda")
+    t = timer(lambda: C.attention_backward(do, q, k, v, o, lse, dqkv[:, :768], dqkv[:, 768:1536],
+                                           dqkv[:, 1536:], acc, dvec, cu, 256, heads, heads, 0.125,
+                                           False, -1))
+    report({"kernel": "attention_bwd", "case": "bert_b128_len32-256", "ms": t * 1e3,
+            "tflops": 2.5 * fl / t / 1e12, f"frac_of_{tag}_bf16": 2.5 * fl / t / flops_peak})
+
+
+def bench_norm(timer, hbm, flops_peak, tag, report):
+    from representax_b200.ops._ext import ext
+
+    C = ext()
+    rows, h = 18432 * 4, 768
+    x = torch.randn(rows, h, device="cuda").to(torch.bfloat16)
+    g = torch.ones(h, device="cuda", dtype=torch.bfloat16)
+    b = torch.zeros(h, device="cuda", dtype=torch.bfloat16)
+    y = torch.empty_like(x)
+    mean = torch.empty(rows, device="cuda")
+    rstd = torch.empty(rows, device="cuda")
+    t = timer(lambda: C.norm_forward(x, g, b, y, mean, rstd, 1e-12, False))
+    by = 2 * rows * h * 2
+    report({"kernel": "layernorm_fwd", "rows": rows, "H": h, "ms": t * 1e3, "gbs": by / t / 1e9,
+            f"frac_of_{tag}_hbm": by / t / hbm})
+    dx = torch.empty_like(x)
+    dg = torch.zeros(h, device="cuda")
+    db = torch.zeros(h, device="cuda")
+    t = timer(lambda: C.norm_backward(y, x, mean, rstd, g, dx, dg, db, None, False))
+    by = 3 * rows * h * 2
+    report({"kernel": "layernorm_bwd", "rows": rows, "H": h, "ms": t * 1e3, "gbs": by / t / 1e9,
+            f"frac_of_{tag}_hbm": by / t / hbm})
+
+
+def main(argv=None):
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--only", default="gemm,attention,norm")
+    parser.add_argument("--out", default=None)
+    args = parser.parse_args(argv)
+    hbm, flops_peak, tag = _peaks()
+    timer = Timer()
+    rows = []
+
+    def report(row):
+        rows.append(row)
+        print(json.dumps(row), flush=True)
+
+    selected = args.only.split(",")
+    if "gemm" in selected:
+        bench_gemm(timer, hbm, flops_peak, tag, report)
+    if "attention" in selected:
+        bench_attention(timer, hbm, flops_peak, tag, report)
+    if "norm" in selected:
+        bench_norm(timer, hbm, flops_peak, tag, report)
+    from representax_b200.ops._ext import check_status
+
+    torch.cuda.synchronize()
+    check_status(torch.device("cuda", 0))
+    if args.out:
+        with open(args.out, "w") as handle:
+            for row in rows:
+                handle.write(json.dumps(row) + "\n")
+
+
+if __name__ == "__main__":
+    main()

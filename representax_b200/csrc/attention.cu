@@ -1,0 +1,633 @@
+// Variable-length (packed, padding-free) multi-head attention for sm_100a,
+// head dimension 64, bf16 operands, fp32 softmax and accumulation.
+//
+// Sequences are packed back to back ([T, heads * 64] rows addressed through
+// cu_seqlens), so no FLOP is spent on padding tokens. Supported masks: key
+// validity (sequence end), causal, and a symmetric sliding window
+// |i - j| <= window (ModernBERT local layers). Grouped-query attention maps
+// query head h to key/value head h / heads_per_kv.
+//
+// Forward: one CTA = 4 warps = 64 queries of one (sequence, head); key/value
+// tiles of 64 stream through double-buffered cp.async shared memory; online
+// softmax in base 2; the log-sum-exp is saved for the backward pass.
+// Backward: one CTA = 64 keys of one (sequence, head); loops over query tiles,
+// accumulates dK and dV in registers, and adds dQ partials with fp32 vector
+// atomics into a [T, heads * 64] accumulator.
+// Warp-level math uses mma.sync m16n8k16 with ldmatrix fragment loads.
+//
+// Reference parity: `dot_product_attention` with padding / window / causal
+// masks (src/representax/models/components.py:187-235), sliding windows
+// (src/representax/models/modernvbert/model.py:217-230) and GQA
+// (src/representax/models/qwen3_vl/text.py:188-199).
+#include "common.h"
+#include "sm100.cuh"
+
+namespace rx {
+namespace attn {
+
+constexpr int D = 64;
+constexpr int BM = 64;
+constexpr int BN = 64;
+constexpr int kThreads = 128;
+constexpr int kChunks = D / 8;  // 16-byte chunks per row
+
+struct Params {
+  const __nv_bfloat16* q;
+  const __nv_bfloat16* k;
+  const __nv_bfloat16* v;
+  int64_t ldq, ldk, ldv;  // row strides in elements
+  __nv_bfloat16* o;
+  int64_t ldo;
+  float* lse;  // [heads, T] base-2 log-sum-exp of the scaled scores
+  const int* cu_seqlens;
+  int batch, heads, heads_per_kv, total_tokens;
+  float scale_log2;  // softmax_scale * log2(e)
+  float scale;
+  int causal;
+  int window;  // -1: no window
+  // backward
+  const __nv_bfloat16* dO;
+  int64_t ld_do;
+  const float* dvec;  // [heads, T] rowsum(dO * O)
+  float* dq_acc;      // [T, heads * D] fp32, pre-zeroed
+  __nv_bfloat16* dk;
+  __nv_bfloat16* dv;
+  int64_t ld_dk, ld_dv;
+};
+
+__device__ __forceinline__ uint32_t swz(int row, int chunk) {
+  return static_cast<uint32_t>((row * kChunks + (chunk ^ (row & 7))) * 16);
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
+  const int bytes = valid ? 16 : 0;
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                        uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                          uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+      "{%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Load a [64 rows][64] bf16 tile (rows row0.. of a packed matrix) into
+// swizzled shared memory; rows at or beyond `rows_valid` are zero-filled.
+__device__ __forceinline__ void load_tile(uint32_t smem, const __nv_bfloat16* base, int64_t ld,
+                                          int row0, int rows_valid) {
+#pragma unroll
+  for (int i = 0; i < (64 * kChunks) / kThreads; ++i) {
+    const int idx = threadIdx.x + i * kThreads;
+    const int r = idx / kChunks;
+    const int c = idx % kChunks;
+    const bool valid = (row0 + r) < rows_valid;
+    const __nv_bfloat16* src = base + static_cast<int64_t>(valid ? row0 + r : 0) * ld + c * 8;
+    cp_async16(smem + swz(r, c), src, valid);
+  }
+}
+
+// Is key j visible from query i (both sequence-relative)?
+__device__ __forceinline__ bool visible(const Params& p, int i, int j, int len) {
+  if (j >= len) return false;
+  if (p.causal && j > i) return false;
+  if (p.window >= 0 && (j - i > p.window || i - j > p.window)) return false;
+  return true;
+}
+
+__device__ __forceinline__ void key_range(const Params& p, int q_lo, int q_hi, int len, int& k_lo,
+                                          int& k_hi) {
+  k_lo = 0;
+  k_hi = len;
+  if (p.causal) k_hi = min(k_hi, q_hi);
+  if (p.window >= 0) {
+    k_lo = max(0, q_lo - p.window);
+    k_hi = min(k_hi, q_hi - 1 + p.window + 1);
+  }
+}
+
+// ===================================================================== forward
+__global__ void __launch_bounds__(kThreads) attn_fwd_kernel(const Params p) {
+  const int qb = blockIdx.x;
+  const int h = blockIdx.y;
+  const int b = blockIdx.z;
+  const int start = p.cu_seqlens[b];
+  const int len = p.cu_seqlens[b + 1] - start;
+  if (qb * BM >= len) return;
+  const int kvh = h / p.heads_per_kv;
+
+  __shared__ __align__(128) uint8_t smem[3 * 64 * D * 2 + 2 * 64 * D * 2];
+  const uint32_t sQ = smem_u32(smem);
+  const uint32_t sK[2] = {sQ + 64 * D * 2, sQ + 2 * 64 * D * 2};
+  const uint32_t sV[2] = {sQ + 3 * 64 * D * 2, sQ + 4 * 64 * D * 2};
+
+  const __nv_bfloat16* qbase = p.q + static_cast<int64_t>(start) * p.ldq + h * D;
+  const __nv_bfloat16* kbase = p.k + static_cast<int64_t>(start) * p.ldk + kvh * D;
+  const __nv_bfloat16* vbase = p.v + static_cast<int64_t>(start) * p.ldv + kvh * D;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int q_lo = qb * BM;
+  const int q_hi = min(len, q_lo + BM);
+  int k_lo, k_hi;
+  key_range(p, q_lo, q_hi, len, k_lo, k_hi);
+  const int kb_first = k_lo / BN;
+  const int kb_last = (k_hi + BN - 1) / BN;  // exclusive
+
+  load_tile(sQ, qbase, p.ldq, q_lo, len);
+  if (kb_first < kb_last) {
+    load_tile(sK[0], kbase, p.ldk, kb_first * BN, len);
+    load_tile(sV[0], vbase, p.ldv, kb_first * BN, len);
+  }
+  cp_async_commit();
+
+  // Row state for rows (warp*16 + g) and (+8).
+  float m_r[2] = {-INFINITY, -INFINITY};
+  float l_r[2] = {0.f, 0.f};
+  float o_acc[D / 8][4];
+#pragma unroll
+  for (int i = 0; i < D / 8; ++i) o_acc[i][0] = o_acc[i][1] = o_acc[i][2] = o_acc[i][3] = 0.f;
+  uint32_t qf[D / 16][4];
+  const int qi0 = q_lo + warp * 16 + g;  // sequence-relative query rows qi0, qi0 + 8
+
+  for (int kb = kb_first; kb < kb_last; ++kb) {
+    const int buf = (kb - kb_first) & 1;
+    if (kb + 1 < kb_last) {
+      load_tile(sK[buf ^ 1], kbase, p.ldk, (kb + 1) * BN, len);
+      load_tile(sV[buf ^ 1], vbase, p.ldv, (kb + 1) * BN, len);
+    }
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    if (kb == kb_first) {
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk) {
+        const int r = warp * 16 + (lane & 15);
+        const int c = kk * 2 + (lane >> 4);
+        ldsm_x4(sQ + swz(r, c), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
+      }
+    }
+    // S = Q K^T for 16 rows x 64 keys.
+    float s[BN / 8][4];
+#pragma unroll
+    for (int nb = 0; nb < BN / 8; ++nb) {
+      s[nb][0] = s[nb][1] = s[nb][2] = s[nb][3] = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < D / 16; kk += 2) {
+        uint32_t b0, b1, b2, b3;
+        const int r = nb * 8 + (lane & 7);
+        const int c = kk * 2 + (lane >> 3);
+        ldsm_x4(sK[buf] + swz(r, c), b0, b1, b2, b3);
+        mma16816(s[nb], qf[kk], b0, b1);
+        mma16816(s[nb], qf[kk + 1], b2, b3);
+      }
+    }
+    // Mask, online softmax.
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int nb = 0; nb < BN / 8; ++nb) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int j = kb * BN + nb * 8 + 2 * t + (e & 1);
+        const int i = qi0 + (e >> 1) * 8;
+        float x = s[nb][e] * p.scale_log2;
+        if (!visible(p, i, j, len)) x = -INFINITY;
+        s[nb][e] = x;
+        mx[e >> 1] = fmaxf(mx[e >> 1], x);
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+    }
+    float alpha[2], m_use[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const float m_new = fmaxf(m_r[r], mx[r]);
+      m_use[r] = (m_new == -INFINITY) ? 0.f : m_new;
+      alpha[r] = (m_r[r] == -INFINITY) ? 0.f : exp2f(m_r[r] - m_use[r]);
+      m_r[r] = m_new;
+    }
+    float rs[2] = {0.f, 0.f};
+#pragma unroll
+    for (int nb = 0; nb < BN / 8; ++nb) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float pv = exp2f(s[nb][e] - m_use[e >> 1]);
+        s[nb][e] = pv;
+        rs[e >> 1] += pv;
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 1);
+      rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 2);
+      l_r[r] = l_r[r] * alpha[r] + rs[r];
+    }
+#pragma unroll
+    for (int nb = 0; nb < D / 8; ++nb) {
+      o_acc[nb][0] *= alpha[0];
+      o_acc[nb][1] *= alpha[0];
+      o_acc[nb][2] *= alpha[1];
+      o_acc[nb][3] *= alpha[1];
+    }
+    // O += P V.
+#pragma unroll
+    for (int kk = 0; kk < BN / 16; ++kk) {
+      uint32_t a[4];
+      a[0] = pack_bf16(s[2 * kk][0], s[2 * kk][1]);
+      a[1] = pack_bf16(s[2 * kk][2], s[2 * kk][3]);
+      a[2] = pack_bf16(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+      a[3] = pack_bf16(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+      for (int nb = 0; nb < D / 8; nb += 2) {
+        uint32_t b0, b1, b2, b3;
+        const int r = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int c = nb + (lane >> 4);
+        ldsm_x4_t(sV[buf] + swz(r, c), b0, b1, b2, b3);
+        mma16816(o_acc[nb], a, b0, b1);
+        mma16816(o_acc[nb + 1], a, b2, b3);
+      }
+    }
+    __syncthreads();
+  }
+  cp_async_wait<0>();
+
+  // Normalise and store.
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int i = qi0 + r * 8;
+    if (i >= len) continue;
+    const float inv = l_r[r] > 0.f ? 1.f / l_r[r] : 0.f;
+    __nv_bfloat16* orow = p.o + static_cast<int64_t>(start + i) * p.ldo + h * D;
+#pragma unroll
+    for (int nb = 0; nb < D / 8; ++nb) {
+      *reinterpret_cast<uint32_t*>(orow + nb * 8 + 2 * t) =
+          pack_bf16(o_acc[nb][2 * r] * inv, o_acc[nb][2 * r + 1] * inv);
+    }
+    if (t == 0) {
+      p.lse[static_cast<int64_t>(h) * p.total_tokens + start + i] =
+          l_r[r] > 0.f ? m_r[r] + log2f(l_r[r]) : INFINITY;
+    }
+  }
+}
+
+// ============================================================ backward prep
+// dvec[h, t] = sum_d dO[t, h, d] * O[t, h, d]  (one warp per (t, h)).
+__global__ void attn_dvec_kernel(const __nv_bfloat16* __restrict__ o, int64_t ldo,
+                                 const __nv_bfloat16* __restrict__ dO, int64_t ld_do,
+                                 float* __restrict__ dvec, int total, int heads) {
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (gw >= total * heads) return;
+  const int tok = gw / heads, h = gw % heads;
+  const __nv_bfloat162 a = reinterpret_cast<const __nv_bfloat162*>(o + tok * ldo + h * D)[lane];
+  const __nv_bfloat162 d = reinterpret_cast<const __nv_bfloat162*>(dO + tok * ld_do + h * D)[lane];
+  float2 fa = __bfloat1622float2(a), fd = __bfloat1622float2(d);
+  float s = fa.x * fd.x + fa.y * fd.y;
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  if (lane == 0) dvec[static_cast<int64_t>(h) * total + tok] = s;
+}
+
+// dq[t, h*D + d] = bf16(dq_acc[t, h*D + d])
+__global__ void attn_dq_convert_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ dq,
+                                       int64_t ld_dq, int total, int width) {
+  const int64_t idx = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
+  if (idx >= static_cast<int64_t>(total) * width) return;
+  const int64_t tok = idx / width, col = idx % width;
+  const float4 v = *reinterpret_cast<const float4*>(acc + idx);
+  uint2 w;
+  w.x = pack_bf16(v.x, v.y);
+  w.y = pack_bf16(v.z, v.w);
+  *reinterpret_cast<uint2*>(dq + tok * ld_dq + col) = w;
+}
+
+// ==================================================================== backward
+__global__ void __launch_bounds__(kThreads) attn_bwd_kernel(const Params p) {
+  const int kbk = blockIdx.x;
+  const int h = blockIdx.y;
+  const int b = blockIdx.z;
+  const int start = p.cu_seqlens[b];
+  const int len = p.cu_seqlens[b + 1] - start;
+  if (kbk * BN >= len) return;
+  const int kvh = h / p.heads_per_kv;
+
+  // K, V, Q, dO tiles + dS^T tile (bf16) + lse/dvec for 64 queries.
+  __shared__ __align__(128) uint8_t smem[5 * 64 * D * 2];
+  __shared__ float s_lse[64];
+  __shared__ float s_dv[64];
+  const uint32_t sK = smem_u32(smem);
+  const uint32_t sV = sK + 64 * D * 2;
+  const uint32_t sQ = sK + 2 * 64 * D * 2;
+  const uint32_t sdO = sK + 3 * 64 * D * 2;
+  const uint32_t sdS = sK + 4 * 64 * D * 2;  // [64 keys][64 queries] bf16, swizzled
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int k_lo = kbk * BN;
+  const int k_hi = min(len, k_lo + BN);
+
+  // Query range that can see this key block.
+  int q_lo = 0, q_hi = len;
+  if (p.causal) q_lo = k_lo;
+  if (p.window >= 0) {
+    q_lo = max(q_lo, k_lo - p.window);
+    q_hi = min(q_hi, k_hi - 1 + p.window + 1);
+  }
+  const int qb_first = q_lo / BM;
+  const int qb_last = (q_hi + BM - 1) / BM;
+
+  const __nv_bfloat16* kbase = p.k + static_cast<int64_t>(start) * p.ldk + kvh * D;
+  const __nv_bfloat16* vbase = p.v + static_cast<int64_t>(start) * p.ldv + kvh * D;
+  const __nv_bfloat16* qbase = p.q + static_cast<int64_t>(start) * p.ldq + h * D;
+  const __nv_bfloat16* dobase = p.dO + static_cast<int64_t>(start) * p.ld_do + h * D;
+
+  load_tile(sK, kbase, p.ldk, k_lo, len);
+  load_tile(sV, vbase, p.ldv, k_lo, len);
+  cp_async_commit();
+  cp_async_wait<0>();
+  __syncthreads();
+
+  uint32_t kf[D / 16][4], vf[D / 16][4];
+#pragma unroll
+  for (int kk = 0; kk < D / 16; ++kk) {
+    const int r = warp * 16 + (lane & 15);
+    const int c = kk * 2 + (lane >> 4);
+    ldsm_x4(sK + swz(r, c), kf[kk][0], kf[kk][1], kf[kk][2], kf[kk][3]);
+    ldsm_x4(sV + swz(r, c), vf[kk][0], vf[kk][1], vf[kk][2], vf[kk][3]);
+  }
+  float dk_acc[D / 8][4], dv_acc[D / 8][4];
+#pragma unroll
+  for (int i = 0; i < D / 8; ++i)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) dk_acc[i][e] = dv_acc[i][e] = 0.f;
+
+  const int kj0 = k_lo + warp * 16 + g;  // this thread's key rows kj0, kj0 + 8
+
+  for (int qb = qb_first; qb < qb_last; ++qb) {
+    const int q0 = qb * BM;
+    load_tile(sQ, qbase, p.ldq, q0, len);
+    load_tile(sdO, dobase, p.ld_do, q0, len);
+    cp_async_commit();
+    if (threadIdx.x < 64) {
+      const int i = q0 + threadIdx.x;
+      s_lse[threadIdx.x] = i < len ? p.lse[static_cast<int64_t>(h) * p.total_tokens + start + i] : INFINITY;
+      s_dv[threadIdx.x] = i < len ? p.dvec[static_cast<int64_t>(h) * p.total_tokens + start + i] : 0.f;
+    }
+    cp_async_wait<0>();
+    __syncthreads();
+
+    // S^T = K Q^T (16 keys x 64 queries per warp) and dP^T = V dO^T.
+    float st[BM / 8][4], dpt[BM / 8][4];
+#pragma unroll
+    for (int nb = 0; nb < BM / 8; ++nb) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) st[nb][e] = dpt[nb][e] = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < D / 16; kk += 2) {
+        uint32_t b0, b1, b2, b3;
+        const int r = nb * 8 + (lane & 7);
+        const int c = kk * 2 + (lane >> 3);
+        ldsm_x4(sQ + swz(r, c), b0, b1, b2, b3);
+        mma16816(st[nb], kf[kk], b0, b1);
+        mma16816(st[nb], kf[kk + 1], b2, b3);
+        ldsm_x4(sdO + swz(r, c), b0, b1, b2, b3);
+        mma16816(dpt[nb], vf[kk], b0, b1);
+        mma16816(dpt[nb], vf[kk + 1], b2, b3);
+      }
+    }
+    // P^T and dS^T.
+#pragma unroll
+    for (int nb = 0; nb < BM / 8; ++nb) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int qi = nb * 8 + 2 * t + (e & 1);
+        const int j = kj0 + (e >> 1) * 8;
+        const int i = q0 + qi;
+        float pv = 0.f;
+        if (i < len && visible(p, i, j, len)) pv = exp2f(st[nb][e] * p.scale_log2 - s_lse[qi]);
+        st[nb][e] = pv;
+        dpt[nb][e] = pv * (dpt[nb][e] - s_dv[qi]);
+      }
+    }
+    // dV += P^T dO ; dK += dS^T Q  (k = queries).
+#pragma unroll
+    for (int kk = 0; kk < BM / 16; ++kk) {
+      uint32_t ap[4], ad[4];
+      ap[0] = pack_bf16(st[2 * kk][0], st[2 * kk][1]);
+      ap[1] = pack_bf16(st[2 * kk][2], st[2 * kk][3]);
+      ap[2] = pack_bf16(st[2 * kk + 1][0], st[2 * kk + 1][1]);
+      ap[3] = pack_bf16(st[2 * kk + 1][2], st[2 * kk + 1][3]);
+      ad[0] = pack_bf16(dpt[2 * kk][0], dpt[2 * kk][1]);
+      ad[1] = pack_bf16(dpt[2 * kk][2], dpt[2 * kk][3]);
+      ad[2] = pack_bf16(dpt[2 * kk + 1][0], dpt[2 * kk + 1][1]);
+      ad[3] = pack_bf16(dpt[2 * kk + 1][2], dpt[2 * kk + 1][3]);
+#pragma unroll
+      for (int nb = 0; nb < D / 8; nb += 2) {
+        uint32_t b0, b1, b2, b3;
+        const int r = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int c = nb + (lane >> 4);
+        ldsm_x4_t(sdO + swz(r, c), b0, b1, b2, b3);
+        mma16816(dv_acc[nb], ap, b0, b1);
+        mma16816(dv_acc[nb + 1], ap, b2, b3);
+        ldsm_x4_t(sQ + swz(r, c), b0, b1, b2, b3);
+        mma16816(dk_acc[nb], ad, b0, b1);
+        mma16816(dk_acc[nb + 1], ad, b2, b3);
+      }
+      // Stash dS^T (rows = this warp's keys) for the dQ product.
+      const int key_r = warp * 16 + g;
+      const int qcol = kk * 16 + 2 * t;  // element column within the 64-query row
+      uint8_t* base = smem + 4 * 64 * D * 2;
+      *reinterpret_cast<uint32_t*>(base + swz(key_r, qcol >> 3) + (qcol & 7) * 2) = ad[0];
+      *reinterpret_cast<uint32_t*>(base + swz(key_r + 8, qcol >> 3) + (qcol & 7) * 2) = ad[1];
+      *reinterpret_cast<uint32_t*>(base + swz(key_r, (qcol + 8) >> 3) + (qcol & 7) * 2) = ad[2];
+      *reinterpret_cast<uint32_t*>(base + swz(key_r + 8, (qcol + 8) >> 3) + (qcol & 7) * 2) = ad[3];
+    }
+    __syncthreads();
+    // dQ[64 q x D] += dS K : warp w handles queries w*16..w*16+15, k = keys.
+    {
+      float dq[D / 8][4];
+#pragma unroll
+      for (int i = 0; i < D / 8; ++i) dq[i][0] = dq[i][1] = dq[i][2] = dq[i][3] = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < BN / 16; ++kk) {
+        uint32_t a[4];
+        {
+          const int mi = lane >> 3;
+          const int r = kk * 16 + (lane & 7) + (mi >> 1) * 8;  // key row in dS^T
+          const int c = warp * 2 + (mi & 1);                     // query chunk
+          ldsm_x4_t(sdS + swz(r, c), a[0], a[1], a[2], a[3]);
+        }
+#pragma unroll
+        for (int nb = 0; nb < D / 8; nb += 2) {
+          uint32_t b0, b1, b2, b3;
+          const int r = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+          const int c = nb + (lane >> 4);
+          ldsm_x4_t(sK + swz(r, c), b0, b1, b2, b3);
+          mma16816(dq[nb], a, b0, b1);
+          mma16816(dq[nb + 1], a, b2, b3);
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const int i = q0 + warp * 16 + g + r * 8;
+        if (i < len) {
+          float* row = p.dq_acc + static_cast<int64_t>(start + i) * (p.heads * D) + h * D;
+#pragma unroll
+          for (int nb = 0; nb < D / 8; ++nb) {
+            atomicAdd(reinterpret_cast<float2*>(row + nb * 8 + 2 * t),
+                      make_float2(dq[nb][2 * r] * p.scale, dq[nb][2 * r + 1] * p.scale));
+          }
+        }
+      }
+    }
+    __syncthreads();
+  }
+
+  // Store dK (scaled) and dV for this warp's 16 keys.
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int j = kj0 + r * 8;
+    if (j >= len) continue;
+    __nv_bfloat16* dkrow = p.dk + static_cast<int64_t>(start + j) * p.ld_dk + h * D;
+    __nv_bfloat16* dvrow = p.dv + static_cast<int64_t>(start + j) * p.ld_dv + h * D;
+#pragma unroll
+    for (int nb = 0; nb < D / 8; ++nb) {
+      *reinterpret_cast<uint32_t*>(dkrow + nb * 8 + 2 * t) =
+          pack_bf16(dk_acc[nb][2 * r] * p.scale, dk_acc[nb][2 * r + 1] * p.scale);
+      *reinterpret_cast<uint32_t*>(dvrow + nb * 8 + 2 * t) =
+          pack_bf16(dv_acc[nb][2 * r], dv_acc[nb][2 * r + 1]);
+    }
+  }
+}
+
+}  // namespace attn
+
+namespace {
+void fill_common(attn::Params& p, const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                 const at::Tensor& cu_seqlens, int64_t heads, int64_t kv_heads, double scale,
+                 bool causal, int64_t window) {
+  check_bf16(q, "q");
+  check_bf16(k, "k");
+  check_bf16(v, "v");
+  RX_CHECK(cu_seqlens.scalar_type() == at::kInt && cu_seqlens.is_cuda(), "cu_seqlens must be CUDA int32");
+  RX_CHECK(q.dim() == 2 && k.dim() == 2 && v.dim() == 2, "q/k/v must be [T, heads*64] views");
+  RX_CHECK(q.stride(1) == 1 && k.stride(1) == 1 && v.stride(1) == 1, "unit inner stride required");
+  RX_CHECK(q.size(1) == heads * attn::D && k.size(1) == kv_heads * attn::D && v.size(1) == kv_heads * attn::D,
+           "head_dim must be 64");
+  RX_CHECK(heads % kv_heads == 0, "heads must be a multiple of kv_heads");
+  for (const at::Tensor* t : {&q, &k, &v})
+    RX_CHECK(t->stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(t->data_ptr()) % 16 == 0,
+             "q/k/v rows must be 16-byte aligned");
+  p.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  p.k = reinterpret_cast<const __nv_bfloat16*>(k.data_ptr());
+  p.v = reinterpret_cast<const __nv_bfloat16*>(v.data_ptr());
+  p.ldq = q.stride(0);
+  p.ldk = k.stride(0);
+  p.ldv = v.stride(0);
+  p.cu_seqlens = cu_seqlens.data_ptr<int>();
+  p.batch = static_cast<int>(cu_seqlens.numel() - 1);
+  p.heads = static_cast<int>(heads);
+  p.heads_per_kv = static_cast<int>(heads / kv_heads);
+  p.total_tokens = static_cast<int>(q.size(0));
+  p.scale = static_cast<float>(scale);
+  p.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
+  p.causal = causal ? 1 : 0;
+  p.window = static_cast<int>(window);
+}
+}  // namespace
+
+void attention_forward(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o,
+                       at::Tensor& lse, const at::Tensor& cu_seqlens, int64_t max_len,
+                       int64_t heads, int64_t kv_heads, double scale, bool causal, int64_t window) {
+  attn::Params p{};
+  fill_common(p, q, k, v, cu_seqlens, heads, kv_heads, scale, causal, window);
+  check_bf16(o, "o");
+  check_f32(lse, "lse");
+  RX_CHECK(o.stride(1) == 1 && o.stride(0) % 2 == 0, "bad o layout");
+  RX_CHECK(lse.numel() >= heads * q.size(0), "lse too small");
+  p.o = reinterpret_cast<__nv_bfloat16*>(o.data_ptr());
+  p.ldo = o.stride(0);
+  p.lse = lse.data_ptr<float>();
+  if (p.batch == 0 || max_len == 0) return;
+  c10::cuda::CUDAGuard guard(q.get_device());
+  dim3 grid((max_len + attn::BM - 1) / attn::BM, heads, p.batch);
+  attn::attn_fwd_kernel<<<grid, attn::kThreads, 0, at::cuda::getCurrentCUDAStream().stream()>>>(p);
+  RX_CUDA_CHECK(cudaGetLastError());
+}
+
+void attention_backward(const at::Tensor& dO, const at::Tensor& q, const at::Tensor& k,
+                        const at::Tensor& v, const at::Tensor& o, const at::Tensor& lse,
+                        at::Tensor& dq, at::Tensor& dk, at::Tensor& dv, at::Tensor& dq_acc,
+                        at::Tensor& dvec, const at::Tensor& cu_seqlens, int64_t max_len,
+                        int64_t heads, int64_t kv_heads, double scale, bool causal,
+                        int64_t window) {
+  attn::Params p{};
+  fill_common(p, q, k, v, cu_seqlens, heads, kv_heads, scale, causal, window);
+  RX_CHECK(kv_heads == heads, "GQA backward is not supported yet");
+  check_bf16(dO, "dO");
+  check_f32(dq_acc, "dq_acc");
+  check_f32(dvec, "dvec");
+  RX_CHECK(dq_acc.is_contiguous() && dq_acc.numel() == q.size(0) * heads * attn::D, "bad dq_acc");
+  p.dO = reinterpret_cast<const __nv_bfloat16*>(dO.data_ptr());
+  p.ld_do = dO.stride(0);
+  p.lse = lse.data_ptr<float>();
+  p.dvec = dvec.data_ptr<float>();
+  p.dq_acc = dq_acc.data_ptr<float>();
+  p.dk = reinterpret_cast<__nv_bfloat16*>(dk.data_ptr());
+  p.dv = reinterpret_cast<__nv_bfloat16*>(dv.data_ptr());
+  p.ld_dk = dk.stride(0);
+  p.ld_dv = dv.stride(0);
+  const int total = p.total_tokens;
+  if (p.batch == 0 || max_len == 0 || total == 0) return;
+  c10::cuda::CUDAGuard guard(q.get_device());
+  auto st = at::cuda::getCurrentCUDAStream().stream();
+  RX_CUDA_CHECK(cudaMemsetAsync(dq_acc.data_ptr(), 0, dq_acc.numel() * sizeof(float), st));
+  {
+    const int64_t warps = static_cast<int64_t>(total) * heads;
+    const int threads = 256;
+    attn::attn_dvec_kernel<<<(warps * 32 + threads - 1) / threads, threads, 0, st>>>(
+        reinterpret_cast<const __nv_bfloat16*>(o.data_ptr()), o.stride(0), p.dO, p.ld_do,
+        dvec.data_ptr<float>(), total, static_cast<int>(heads));
+    RX_CUDA_CHECK(cudaGetLastError());
+  }
+  dim3 grid((max_len + attn::BN - 1) / attn::BN, heads, p.batch);
+  attn::attn_bwd_kernel<<<grid, attn::kThreads, 0, st>>>(p);
+  RX_CUDA_CHECK(cudaGetLastError());
+  {
+    const int width = static_cast<int>(heads * attn::D);
+    const int64_t n4 = static_cast<int64_t>(total) * width / 4;
+    attn::attn_dq_convert_kernel<<<(n4 + 255) / 256, 256, 0, st>>>(
+        p.dq_acc, reinterpret_cast<__nv_bfloat16*>(dq.data_ptr()), dq.stride(0), total, width);
+    RX_CUDA_CHECK(cudaGetLastError());
+  }
+}
+
+}  // namespace rx

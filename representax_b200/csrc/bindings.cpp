@@ -1,0 +1,77 @@
+// Python bindings of the sm_100a extension `representax_b200._C`.
+#include <torch/extension.h>
+
+namespace rx {
+void gemm_tcgen05(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_mn, bool b_mn,
+                  int64_t epi, int64_t out_mode, double alpha,
+                  const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& aux_in,
+                  const c10::optional<at::Tensor>& aux_out,
+                  const c10::optional<at::Tensor>& residual, const at::Tensor& status,
+                  int64_t split_k);
+void norm_forward(const at::Tensor& x, const at::Tensor& gamma, const c10::optional<at::Tensor>& beta,
+                  at::Tensor& y, const c10::optional<at::Tensor>& mean, at::Tensor& rstd,
+                  double eps, bool rms);
+void norm_backward(const at::Tensor& dy, const at::Tensor& x, const c10::optional<at::Tensor>& mean,
+                   const at::Tensor& rstd, const at::Tensor& gamma, at::Tensor& dx,
+                   const c10::optional<at::Tensor>& dgamma, const c10::optional<at::Tensor>& dbeta,
+                   const c10::optional<at::Tensor>& dbias_prev, bool rms);
+void embed_ln_forward(const at::Tensor& ids, const at::Tensor& pos_ids,
+                      const c10::optional<at::Tensor>& type_ids, const at::Tensor& word,
+                      const at::Tensor& pos, const at::Tensor& type, const at::Tensor& gamma,
+                      const at::Tensor& beta, at::Tensor& y, at::Tensor& mean, at::Tensor& rstd,
+                      double eps);
+void embed_ln_backward(const at::Tensor& dy, const at::Tensor& ids, const at::Tensor& pos_ids,
+                       const c10::optional<at::Tensor>& type_ids, const at::Tensor& word,
+                       const at::Tensor& pos, const at::Tensor& type, const at::Tensor& gamma,
+                       const at::Tensor& mean, const at::Tensor& rstd, at::Tensor& word_grad,
+                       at::Tensor& pos_grad, at::Tensor& type_grad, at::Tensor& dgamma,
+                       at::Tensor& dbeta, int64_t pad_id);
+void attention_forward(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o,
+                       at::Tensor& lse, const at::Tensor& cu_seqlens, int64_t max_len,
+                       int64_t heads, int64_t kv_heads, double scale, bool causal, int64_t window);
+void attention_backward(const at::Tensor& dO, const at::Tensor& q, const at::Tensor& k,
+                        const at::Tensor& v, const at::Tensor& o, const at::Tensor& lse,
+                        at::Tensor& dq, at::Tensor& dk, at::Tensor& dv, at::Tensor& dq_acc,
+                        at::Tensor& dvec, const at::Tensor& cu_seqlens, int64_t max_len,
+                        int64_t heads, int64_t kv_heads, double scale, bool causal,
+                        int64_t window);
+void pool_forward(const at::Tensor& h, const at::Tensor& cu_seqlens, at::Tensor& out,
+                  at::Tensor& norm, int64_t mode, bool normalize);
+void pool_backward(const at::Tensor& dout, const at::Tensor& out, const at::Tensor& norm,
+                   const at::Tensor& cu_seqlens, at::Tensor& dh, int64_t mode, bool normalize);
+void colsum_accumulate(const at::Tensor& x, at::Tensor& out);
+void sgemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, at::Tensor& C,
+           double alpha, bool accumulate);
+void mnr_rows(const at::Tensor& logits, const at::Tensor& positive_weight,
+              const at::Tensor& row_valid, const at::Tensor& col_valid, at::Tensor& grad,
+              at::Tensor& row_loss, at::Tensor& row_active, double scale,
+              const at::Tensor& coef);
+void adamw_step(const at::Tensor& param, const at::Tensor& grad, at::Tensor& exp_avg,
+                at::Tensor& exp_avg_sq, const c10::optional<at::Tensor>& compute_copy,
+                const at::Tensor& scalars, double lr, double beta1, double beta2, double eps,
+                double weight_decay);
+void grad_norm_sq(const at::Tensor& grad, at::Tensor& out);
+void finalize_clip(const at::Tensor& norm_sq, at::Tensor& scalars, const at::Tensor& loss,
+                   double max_norm, int64_t step_offset);
+void cast_bf16(const at::Tensor& src, at::Tensor& dst);
+}  // namespace rx
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "representax_b200 sm_100a kernels";
+  m.def("gemm", &rx::gemm_tcgen05, "tcgen05 GEMM with fused epilogue");
+  m.def("norm_forward", &rx::norm_forward);
+  m.def("norm_backward", &rx::norm_backward);
+  m.def("embed_ln_forward", &rx::embed_ln_forward);
+  m.def("embed_ln_backward", &rx::embed_ln_backward);
+  m.def("attention_forward", &rx::attention_forward);
+  m.def("attention_backward", &rx::attention_backward);
+  m.def("pool_forward", &rx::pool_forward);
+  m.def("pool_backward", &rx::pool_backward);
+  m.def("colsum_accumulate", &rx::colsum_accumulate);
+  m.def("sgemm", &rx::sgemm);
+  m.def("mnr_rows", &rx::mnr_rows);
+  m.def("adamw_step", &rx::adamw_step);
+  m.def("grad_norm_sq", &rx::grad_norm_sq);
+  m.def("finalize_clip", &rx::finalize_clip);
+  m.def("cast_bf16", &rx::cast_bf16);
+}

@@ -1,0 +1,116 @@
+// Host entry of the tcgen05 GEMM: argument checks, tile/split planning,
+// TMA tensor maps, variant dispatch. The kernel itself is in gemm_kernel.cuh.
+#include "gemm_kernel.cuh"
+
+#include <algorithm>
+
+namespace rx {
+// C = epilogue(alpha * A . B^T). Shapes: A is [M, K] (a_mn false) or [K, M]
+// (a_mn true); B is [N, K] (b_mn false) or [K, N] (b_mn true); C is [M, N].
+// `split_k` > 1 is allowed only with the atomic fp32 output mode; 0 picks a
+// split automatically when the output has too few tiles to fill the GPU.
+void gemm_tcgen05(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_mn, bool b_mn,
+                  int64_t epi, int64_t out_mode, double alpha,
+                  const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& aux_in,
+                  const c10::optional<at::Tensor>& aux_out,
+                  const c10::optional<at::Tensor>& residual, const at::Tensor& status,
+                  int64_t split_k) {
+  using namespace gemm;
+  check_bf16(A, "A");
+  check_bf16(B, "B");
+  RX_CHECK(A.dim() == 2 && B.dim() == 2 && C.dim() == 2, "gemm operands must be matrices");
+  RX_CHECK(A.stride(1) == 1 && B.stride(1) == 1 && C.stride(1) == 1,
+           "gemm operands must have unit inner stride");
+  const int64_t M = C.size(0), N = C.size(1);
+  const int64_t K = a_mn ? A.size(0) : A.size(1);
+  RX_CHECK((a_mn ? A.size(1) : A.size(0)) == M, "A does not match C rows");
+  RX_CHECK((b_mn ? B.size(1) : B.size(0)) == N, "B does not match C columns");
+  RX_CHECK((b_mn ? B.size(0) : B.size(1)) == K, "A and B reduction sizes differ");
+  RX_CHECK(M > 0 && N > 0 && K > 0, "empty gemm");
+  RX_CHECK(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), "gemm too large");
+  if (out_mode == OUT_BF16) {
+    check_bf16(C, "C");
+    RX_CHECK(C.stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(C.data_ptr()) % 16 == 0,
+             "bf16 C must be 16-byte aligned with ldc % 8 == 0");
+  } else {
+    check_f32(C, "C");
+    RX_CHECK(C.stride(0) % 4 == 0 && reinterpret_cast<uintptr_t>(C.data_ptr()) % 16 == 0,
+             "fp32 C must be 16-byte aligned with ldc % 4 == 0");
+  }
+  Params p{};
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.C = C.data_ptr();
+  p.ldc = C.stride(0);
+  p.alpha = static_cast<float>(alpha);
+  p.status = status_ptr(status);
+  p.timeout_ns = kWaitBudgetNs;
+  auto vec_ok = [](const at::Tensor& t) {
+    return t.stride(1) == 1 && (t.dim() == 1 || t.stride(0) % 8 == 0) &&
+           reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0;
+  };
+  if (epi & EPI_BIAS) {
+    RX_CHECK(bias.has_value(), "bias epilogue needs a bias");
+    check_bf16(*bias, "bias");
+    RX_CHECK(bias->numel() == N && bias->is_contiguous() &&
+                 reinterpret_cast<uintptr_t>(bias->data_ptr()) % 16 == 0,
+             "bias must be a contiguous aligned [N] vector");
+    p.bias = reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr());
+  }
+  if (epi & EPI_DGELU) {
+    RX_CHECK(aux_in.has_value(), "GELU-backward epilogue needs the pre-activation");
+    check_bf16(*aux_in, "aux_in");
+    RX_CHECK(aux_in->size(0) == M && aux_in->size(1) == N && vec_ok(*aux_in), "bad aux_in");
+    p.aux_in = reinterpret_cast<const __nv_bfloat16*>(aux_in->data_ptr());
+    p.ld_aux_in = aux_in->stride(0);
+  }
+  if (epi & EPI_GELU) {
+    RX_CHECK(aux_out.has_value(), "GELU epilogue needs a pre-activation output");
+    check_bf16(*aux_out, "aux_out");
+    RX_CHECK(aux_out->size(0) == M && aux_out->size(1) == N && vec_ok(*aux_out), "bad aux_out");
+    p.aux_out = reinterpret_cast<__nv_bfloat16*>(aux_out->data_ptr());
+    p.ld_aux_out = aux_out->stride(0);
+  }
+  if (epi & EPI_RESID) {
+    RX_CHECK(residual.has_value(), "residual epilogue needs a residual");
+    check_bf16(*residual, "residual");
+    RX_CHECK(residual->size(0) == M && residual->size(1) == N && vec_ok(*residual),
+             "bad residual");
+    p.residual = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());
+    p.ld_res = residual->stride(0);
+  }
+  constexpr int BN = 256;
+  p.m_tiles = static_cast<int>((M + BM - 1) / BM);
+  p.n_tiles = static_cast<int>((N + BN - 1) / BN);
+  p.kb_total = static_cast<int>((K + BK - 1) / BK);
+  const int device = C.get_device();
+  const int sms = num_sms(device);
+  int splits = 1;
+  const int tiles = p.m_tiles * p.n_tiles;
+  if (split_k == 0 && out_mode == OUT_F32_ATOMIC && tiles < sms) {
+    splits = std::max(1, std::min(p.kb_total / 4, (sms + tiles - 1) / tiles));
+  } else if (split_k > 1) {
+    RX_CHECK(out_mode == OUT_F32_ATOMIC, "split-K needs the atomic fp32 output mode");
+    splits = static_cast<int>(std::min<int64_t>(split_k, p.kb_total));
+  }
+  p.kb_per_split = (p.kb_total + splits - 1) / splits;
+  p.splits = (p.kb_total + p.kb_per_split - 1) / p.kb_per_split;
+  p.num_units = tiles * p.splits;
+  LaunchFn fn = nullptr;
+  if (!a_mn && !b_mn) fn = pick_forward(static_cast<int>(epi), static_cast<int>(out_mode));
+  else if (!a_mn && b_mn) fn = pick_dgrad(static_cast<int>(epi), static_cast<int>(out_mode));
+  else if (a_mn && b_mn) fn = pick_wgrad(static_cast<int>(epi), static_cast<int>(out_mode));
+  RX_CHECK(fn != nullptr, "unsupported gemm variant a_mn=", a_mn, " b_mn=", b_mn, " epi=", epi,
+           " out=", out_mode);
+  // A: K-major boxes [128 rows x 64 k]; MN-major boxes [64 k rows x 64 m].
+  CUtensorMap ta = a_mn ? make_tmap_2d_bf16(A.data_ptr(), K, M, A.stride(0), 64, 64)
+                        : make_tmap_2d_bf16(A.data_ptr(), M, K, A.stride(0), 64, BM);
+  CUtensorMap tb = b_mn ? make_tmap_2d_bf16(B.data_ptr(), K, N, B.stride(0), 64, 64)
+                        : make_tmap_2d_bf16(B.data_ptr(), N, K, B.stride(0), 64, BN);
+  const int grid = std::min(p.num_units, sms);
+  c10::cuda::CUDAGuard guard(device);
+  fn(ta, tb, p, grid, at::cuda::getCurrentCUDAStream(device).stream(), device);
+}
+
+}  // namespace rx

@@ -1,0 +1,414 @@
+// Persistent tcgen05 GEMM for sm_100a with fused epilogues.
+//
+//   C[M, N] = epilogue(alpha * sum_k A(m, k) * B(n, k))
+//
+// A is K-major (stored [M, K]) or MN-major (stored [K, M]); B is K-major
+// (stored [N, K]) or MN-major (stored [K, N]). The three combinations cover a
+// linear layer's forward (K/K), input gradient (K/MN) and weight gradient
+// (MN/MN) without materialising any transpose.
+//
+// Structure (one CTA per SM, persistent over output tiles):
+//   warp 0      TMA producer: 128x64 A tile + BNx64 B tile per stage, 128-byte
+//               swizzle, 4-stage ring guarded by full/empty mbarriers.
+//   warp 1      owns TMEM (2 x BN fp32 columns = a double-buffered 128xBN
+//               accumulator) and one thread issues tcgen05.mma (M=128, K=16)
+//               and tcgen05.commit.
+//   warps 2-5   epilogue: tcgen05.ld of their 32-lane TMEM quadrant (one
+//               output row per thread), fused bias / GELU / GELU-backward /
+//               residual, bf16 or fp32 stores, fp32 accumulate or split-K
+//               atomic reduction.
+// The double-buffered accumulator lets the epilogue of tile i overlap the
+// main loop of tile i+1.
+//
+// Linear-layer role parity: the reference's `Linear.__call__`
+// (src/representax/models/components.py:81-94) and its XLA-generated
+// backward; this kernel replaces both.
+#pragma once
+#include "common.h"
+#include "sm100.cuh"
+
+namespace rx {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int kThreads = 192;
+
+enum Epi : int { EPI_BIAS = 1, EPI_GELU = 2, EPI_DGELU = 4, EPI_RESID = 8 };
+enum Out : int { OUT_BF16 = 0, OUT_F32 = 1, OUT_F32_ACC = 2, OUT_F32_ATOMIC = 3 };
+
+struct Params {
+  int M, N, K;
+  int m_tiles, n_tiles, splits, kb_total, kb_per_split, num_units;
+  void* C;
+  int64_t ldc;
+  const __nv_bfloat16* bias;
+  const __nv_bfloat16* aux_in;
+  int64_t ld_aux_in;
+  __nv_bfloat16* aux_out;
+  int64_t ld_aux_out;
+  const __nv_bfloat16* residual;
+  int64_t ld_res;
+  float alpha;
+  int* status;
+  uint64_t timeout_ns;
+};
+
+__device__ __forceinline__ float gelu_erf(float x) {
+  return 0.5f * x * (1.0f + erff(x * 0.70710678118654752440f));
+}
+
+__device__ __forceinline__ float gelu_erf_grad(float x) {
+  const float cdf = 0.5f * (1.0f + erff(x * 0.70710678118654752440f));
+  const float pdf = 0.39894228040143267794f * __expf(-0.5f * x * x);
+  return cdf + x * pdf;
+}
+
+__device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* src, float (&v)[32]) {
+  const uint4* s = reinterpret_cast<const uint4*>(src);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint4 w = s[q];
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float2 f = __bfloat1622float2(h[j]);
+      v[q * 8 + 2 * j] = f.x;
+      v[q * 8 + 2 * j + 1] = f.y;
+    }
+  }
+}
+
+__device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float (&v)[32]) {
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint4 w;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&w);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) h[j] = __floats2bfloat162_rn(v[q * 8 + 2 * j], v[q * 8 + 2 * j + 1]);
+    d[q] = w;
+  }
+}
+
+// Epilogue for one row segment of 32 columns [n_base, n_base + 32).
+template <int EPI, int OUT>
+__device__ __forceinline__ void epilogue_row32(const Params& p, int m, int n_base,
+                                               const uint32_t (&r)[32]) {
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * p.alpha;
+  const bool full = (n_base + 32 <= p.N);
+  if (full) {
+    if constexpr ((EPI & EPI_BIAS) != 0) {
+      float b[32];
+      load_bf16x32(p.bias + n_base, b);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] += b[i];
+    }
+    if constexpr ((EPI & EPI_DGELU) != 0) {
+      float z[32];
+      load_bf16x32(p.aux_in + static_cast<int64_t>(m) * p.ld_aux_in + n_base, z);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] *= gelu_erf_grad(z[i]);
+    }
+    if constexpr ((EPI & EPI_GELU) != 0) {
+      store_bf16x32(p.aux_out + static_cast<int64_t>(m) * p.ld_aux_out + n_base, v);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
+    }
+    if constexpr ((EPI & EPI_RESID) != 0) {
+      float res[32];
+      load_bf16x32(p.residual + static_cast<int64_t>(m) * p.ld_res + n_base, res);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] += res[i];
+    }
+    if constexpr (OUT == OUT_BF16) {
+      store_bf16x32(reinterpret_cast<__nv_bfloat16*>(p.C) + static_cast<int64_t>(m) * p.ldc + n_base,
+                    v);
+    } else {
+      float* c = reinterpret_cast<float*>(p.C) + static_cast<int64_t>(m) * p.ldc + n_base;
+      float4* c4 = reinterpret_cast<float4*>(c);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        float4 w = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        if constexpr (OUT == OUT_F32) {
+          c4[q] = w;
+        } else if constexpr (OUT == OUT_F32_ACC) {
+          float4 o = c4[q];
+          c4[q] = make_float4(o.x + w.x, o.y + w.y, o.z + w.z, o.w + w.w);
+        } else {
+          atomicAdd(c4 + q, w);
+        }
+      }
+    }
+    return;
+  }
+  // Ragged right edge: scalar, bounds-checked, statically indexed so the
+  // values stay in registers.
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const int n = n_base + i;
+    if (n < p.N) {
+      float x = v[i];
+      if constexpr ((EPI & EPI_BIAS) != 0) x += __bfloat162float(p.bias[n]);
+      if constexpr ((EPI & EPI_DGELU) != 0)
+        x *= gelu_erf_grad(__bfloat162float(p.aux_in[static_cast<int64_t>(m) * p.ld_aux_in + n]));
+      if constexpr ((EPI & EPI_GELU) != 0) {
+        p.aux_out[static_cast<int64_t>(m) * p.ld_aux_out + n] = __float2bfloat16_rn(x);
+        x = gelu_erf(x);
+      }
+      if constexpr ((EPI & EPI_RESID) != 0)
+        x += __bfloat162float(p.residual[static_cast<int64_t>(m) * p.ld_res + n]);
+      const int64_t off = static_cast<int64_t>(m) * p.ldc + n;
+      if constexpr (OUT == OUT_BF16) {
+        reinterpret_cast<__nv_bfloat16*>(p.C)[off] = __float2bfloat16_rn(x);
+      } else if constexpr (OUT == OUT_F32) {
+        reinterpret_cast<float*>(p.C)[off] = x;
+      } else if constexpr (OUT == OUT_F32_ACC) {
+        reinterpret_cast<float*>(p.C)[off] += x;
+      } else {
+        atomicAdd(reinterpret_cast<float*>(p.C) + off, x);
+      }
+    }
+  }
+}
+
+// Work unit u -> (row tile origin, column tile index, k-block range). Column
+// tiles vary fastest so consecutive CTAs share an A row block in L2.
+__device__ __forceinline__ void decode_unit(const Params& p, int u, int& m0, int& n_tile, int& kb0,
+                                            int& kb1) {
+  n_tile = u % p.n_tiles;
+  const int t = u / p.n_tiles;
+  const int m_t = t % p.m_tiles;
+  const int split = t / p.m_tiles;
+  m0 = m_t * BM;
+  kb0 = split * p.kb_per_split;
+  kb1 = min(p.kb_total, kb0 + p.kb_per_split);
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, int OUT>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const Params p) {
+  constexpr int A_BYTES = BM * BK * 2;
+  constexpr int B_BYTES = BN * BK * 2;
+  constexpr uint32_t TMEM_COLS = 2 * BN;
+  static_assert(TMEM_COLS <= 512, "accumulator does not fit in TMEM");
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = base;
+  uint8_t* sB = base + STAGES * A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 128);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_map(&tmA);
+    tma_prefetch_map(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0, issued_parity = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; ok && u < p.num_units; u += gridDim.x) {
+        int m0, n_t, kb0, kb1;
+        decode_unit(p, u, m0, n_t, kb0, kb1);
+        const int n0 = n_t * BN;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (*abort_flag) { ok = false; break; }
+          if (!mbar_wait(&empty[stage], phase ^ 1, p.timeout_ns)) {
+            report_status(p.status, kStatusTimeoutProducer);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], A_BYTES + B_BYTES);
+          uint8_t* a_dst = sA + stage * A_BYTES;
+          uint8_t* b_dst = sB + stage * B_BYTES;
+          const int k0 = kb * BK;
+          if constexpr (A_MN) {
+            tma_load_2d(a_dst, &tmA, &full[stage], m0, k0);
+            tma_load_2d(a_dst + 8192, &tmA, &full[stage], m0 + 64, k0);
+          } else {
+            tma_load_2d(a_dst, &tmA, &full[stage], k0, m0);
+          }
+          if constexpr (B_MN) {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_2d(b_dst + j * 8192, &tmB, &full[stage], n0 + 64 * j, k0);
+          } else {
+            tma_load_2d(b_dst, &tmB, &full[stage], k0, n0);
+          }
+          issued_mask |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // Never leave the CTA with a TMA write still landing in its shared memory.
+      for (int s = 0; s < STAGES; ++s) {
+        if ((issued_mask >> s) & 1u) {
+          if (!mbar_wait(&full[s], (issued_parity >> s) & 1u, p.timeout_ns))
+            report_status(p.status, kStatusTimeoutDrain);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t IDESC = idesc_bf16_f32(BM, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      bool issued_any = false;
+      for (int u = blockIdx.x; ok && u < p.num_units; u += gridDim.x, ++local) {
+        int m0, n_t, kb0, kb1;
+        decode_unit(p, u, m0, n_t, kb0, kb1);
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (*abort_flag || !mbar_wait(&tempty[acc], acc_phase ^ 1, p.timeout_ns)) {
+          report_status(p.status, kStatusTimeoutMma);
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (*abort_flag || !mbar_wait(&full[stage], phase, p.timeout_ns)) {
+            report_status(p.status, kStatusTimeoutMma);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + stage * A_BYTES);
+          const uint32_t b_addr = smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t ad = A_MN ? smem_desc_sw128(a_addr + kk * 2048, 8192, 1024)
+                                     : smem_desc_sw128(a_addr + kk * 32, 16, 1024);
+            const uint64_t bd = B_MN ? smem_desc_sw128(b_addr + kk * 2048, 8192, 1024)
+                                     : smem_desc_sw128(b_addr + kk * 32, 16, 1024);
+            umma_f16_ss(d_tmem, ad, bd, IDESC, (kb > kb0 || kk > 0) ? 1u : 0u);
+          }
+          issued_any = true;
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+      }
+      // Every MMA must have retired before TMEM is released.
+      if (issued_any) {
+        umma_commit(drain);
+        if (!mbar_wait(drain, 0, p.timeout_ns)) report_status(p.status, kStatusTimeoutDrain);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quad = warp & 3;  // TMEM lanes this warp may access: [32*quad, 32*quad+32)
+    const int row_local = quad * 32 + lane;
+    int local = 0;
+    for (int u = blockIdx.x; u < p.num_units; u += gridDim.x, ++local) {
+      int m0, n_t, kb0, kb1;
+      decode_unit(p, u, m0, n_t, kb0, kb1);
+      const int n0 = n_t * BN;
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      bool ok = (*abort_flag == 0) && mbar_wait(&tfull[acc], acc_phase, p.timeout_ns);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) {
+        if (lane == 0) report_status(p.status, kStatusTimeoutEpilogue);
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const int m = m0 + row_local;
+      const uint32_t t_row =
+          tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(t_row + c * 32, r);
+        tmem_ld_wait();
+        const int n_base = n0 + c * 32;
+        if (m < p.M && n_base < p.N) epilogue_row32<EPI, OUT>(p, m, n_base, r);
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, TMEM_COLS);
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, int OUT>
+void launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int grid,
+            cudaStream_t stream, int device) {
+  auto kern = gemm_kernel<BN, STAGES, A_MN, B_MN, EPI, OUT>;
+  constexpr size_t smem = 1024 + STAGES * (BM * BK * 2 + BN * BK * 2) + 256;
+  static bool configured[64] = {false};
+  if (device < 0 || device >= 64 || !configured[device]) {
+    RX_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem)));
+    if (device >= 0 && device < 64) configured[device] = true;
+  }
+  kern<<<grid, kThreads, smem, stream>>>(ta, tb, p);
+  RX_CUDA_CHECK(cudaGetLastError());
+}
+
+using LaunchFn = void (*)(const CUtensorMap&, const CUtensorMap&, const Params&, int, cudaStream_t,
+                          int);
+
+// Variant tables, one translation unit each so they compile in parallel.
+LaunchFn pick_forward(int epi, int out);
+LaunchFn pick_dgrad(int epi, int out);
+LaunchFn pick_wgrad(int epi, int out);
+
+}  // namespace gemm
+}  // namespace rx

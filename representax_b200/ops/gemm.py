@@ -1,0 +1,100 @@
+"""Python entry points of the tcgen05 GEMM (``csrc/gemm*.cu``).
+
+All shapes follow the storage of the operands: a linear layer's forward is
+``A=x [T, K]`` (K-major) times ``B=W [N, K]`` (K-major); its input gradient is
+``dy [T, N]`` times ``W`` read MN-major; its weight gradient reads both ``dy``
+and ``x`` MN-major, so no transpose is ever materialised.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from ._ext import ext, status
+
+EPI_NONE = 0
+EPI_BIAS = 1
+EPI_GELU = 2
+EPI_DGELU = 4
+EPI_RESID = 8
+
+OUT_BF16 = 0
+OUT_F32 = 1
+OUT_F32_ACC = 2
+OUT_F32_ATOMIC = 3
+
+
+def gemm(
+    a: torch.Tensor,
+    b: torch.Tensor,
+    out: torch.Tensor,
+    *,
+    a_mn: bool = False,
+    b_mn: bool = False,
+    epi: int = EPI_NONE,
+    out_mode: int = OUT_BF16,
+    alpha: float = 1.0,
+    bias: torch.Tensor | None = None,
+    aux_in: torch.Tensor | None = None,
+    aux_out: torch.Tensor | None = None,
+    residual: torch.Tensor | None = None,
+    split_k: int = 0,
+) -> torch.Tensor:
+    ext().gemm(
+        a, b, out, a_mn, b_mn, epi, out_mode, alpha, bias, aux_in, aux_out, residual,
+        status(out.device), split_k,
+    )
+    return out
+
+
+def linear_forward(
+    x: torch.Tensor,
+    weight: torch.Tensor,
+    bias: torch.Tensor | None = None,
+    *,
+    gelu_preact: torch.Tensor | None = None,
+    residual: torch.Tensor | None = None,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """``y = x W^T (+ b) (-> gelu, storing the pre-activation) (+ residual)``."""
+
+    rows, n = x.shape[0], weight.shape[0]
+    if out is None:
+        out = torch.empty((rows, n), dtype=torch.bfloat16, device=x.device)
+    epi = EPI_NONE
+    if bias is not None:
+        epi |= EPI_BIAS
+    if gelu_preact is not None:
+        epi |= EPI_GELU
+    if residual is not None:
+        epi |= EPI_RESID
+    return gemm(x, weight, out, epi=epi, bias=bias, aux_out=gelu_preact, residual=residual)
+
+
+def linear_dgrad(
+    dy: torch.Tensor,
+    weight: torch.Tensor,
+    *,
+    gelu_preact: torch.Tensor | None = None,
+    residual: torch.Tensor | None = None,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """``dx = dy W`` (times gelu'(preact) of the layer below) (+ residual)."""
+
+    rows, k = dy.shape[0], weight.shape[1]
+    if out is None:
+        out = torch.empty((rows, k), dtype=torch.bfloat16, device=dy.device)
+    epi = EPI_NONE
+    if gelu_preact is not None:
+        epi |= EPI_DGELU
+    if residual is not None:
+        epi |= EPI_RESID
+    return gemm(
+        dy, weight, out, b_mn=True, epi=epi, aux_in=gelu_preact, residual=residual
+    )
+
+
+def linear_wgrad(dy: torch.Tensor, x: torch.Tensor, grad: torch.Tensor) -> torch.Tensor:
+    """``grad += dy^T x`` into an fp32 accumulator (split-K with atomics)."""
+
+    return gemm(dy, x, grad, a_mn=True, b_mn=True, out_mode=OUT_F32_ATOMIC)

@@ -1,0 +1,373 @@
+"""Numerics of every sm_100a kernel against plain fp32 PyTorch references."""
+
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def C():
+    from representax_b200.ops._ext import ext
+
+    return ext()
+
+
+def _dev():
+    return torch.device("cuda", 0)
+
+
+def _rand(*shape, dtype=torch.bfloat16, scale=1.0, gen=None):
+    return (torch.randn(*shape, generator=gen, device=_dev()) * scale).to(dtype)
+
+
+def _close(actual, expected, rtol, atol, what=""):
+    actual = actual.float()
+    expected = expected.float()
+    err = (actual - expected).abs()
+    tol = atol + rtol * expected.abs()
+    bad = (err > tol).sum().item()
+    assert bad == 0, f"{what}: {bad} elements off; max err {err.max().item():.3e}"
+
+
+GEMM_SHAPES = [(128, 256, 64), (300, 520, 200), (2048, 768, 768), (1000, 2304, 768), (4096, 3072, 768)]
+
+
+@pytest.mark.parametrize("m,n,k", GEMM_SHAPES)
+def test_gemm_forward_plain(m, n, k):
+    from representax_b200.ops import gemm as G
+    from representax_b200.ops._ext import check_status
+
+    torch.manual_seed(0)
+    a = _rand(m, k)
+    b = _rand(n, k)
+    out = torch.empty(m, n, dtype=torch.bfloat16, device=_dev())
+    G.gemm(a, b, out)
+    torch.cuda.synchronize()
+    check_status(_dev())
+    ref = a.float() @ b.float().T
+    _close(out, ref, rtol=1e-2, atol=1e-2 * math.sqrt(k), what="gemm")
+
+
+@pytest.mark.parametrize("m,n,k", [(333, 600, 256), (2048, 3072, 768)])
+def test_gemm_forward_epilogues(m, n, k):
+    from representax_b200.ops import gemm as G
+
+    torch.manual_seed(1)
+    x = _rand(m, k, scale=0.5)
+    w = _rand(n, k, scale=0.05)
+    bias = _rand(n, scale=0.1)
+    pre = torch.empty(m, n, dtype=torch.bfloat16, device=_dev())
+    y = G.linear_forward(x, w, bias, gelu_preact=pre)
+    ref_pre = x.float() @ w.float().T + bias.float()
+    _close(pre, ref_pre, rtol=1e-2, atol=2e-2, what="preact")
+    _close(y, torch.nn.functional.gelu(ref_pre), rtol=1e-2, atol=2e-2, what="gelu")
+    res = _rand(m, n)
+    y2 = G.linear_forward(x, w, bias, residual=res)
+    _close(y2, ref_pre + res.float(), rtol=1e-2, atol=3e-2, what="bias+residual")
+    y3 = torch.empty(m, n, dtype=torch.float32, device=_dev())
+    G.gemm(x, w, y3, epi=G.EPI_BIAS, out_mode=G.OUT_F32, bias=bias)
+    _close(y3, ref_pre, rtol=1e-3, atol=1e-3, what="f32 out")
+
+
+@pytest.mark.parametrize("m,n,k", [(300, 520, 200), (2048, 768, 3072)])
+def test_gemm_dgrad(m, n, k):
+    # dx[m, k] = dy[m, n] @ W[n, k]
+    from representax_b200.ops import gemm as G
+
+    torch.manual_seed(2)
+    dy = _rand(m, n)
+    w = _rand(n, k, scale=0.05)
+    dx = G.linear_dgrad(dy, w)
+    ref = dy.float() @ w.float()
+    _close(dx, ref, rtol=1e-2, atol=2e-2, what="dgrad")
+    pre = _rand(m, k)
+    dz = G.linear_dgrad(dy, w, gelu_preact=pre)
+    z = pre.float().requires_grad_(True)
+    torch.nn.functional.gelu(z).backward(ref)
+    _close(dz, z.grad, rtol=2e-2, atol=3e-2, what="dgrad*gelu'")
+    res = _rand(m, k)
+    dr = G.linear_dgrad(dy, w, residual=res)
+    _close(dr, ref + res.float(), rtol=1e-2, atol=3e-2, what="dgrad+res")
+
+
+@pytest.mark.parametrize("t,n,k", [(300, 520, 200), (4096, 768, 768), (9000, 3072, 768)])
+def test_gemm_wgrad_accumulates(t, n, k):
+    from representax_b200.ops import gemm as G
+
+    torch.manual_seed(3)
+    dy = _rand(t, n, scale=0.1)
+    x = _rand(t, k, scale=0.1)
+    grad = torch.full((n, k), 0.5, dtype=torch.float32, device=_dev())
+    G.linear_wgrad(dy, x, grad)
+    G.linear_wgrad(dy, x, grad)
+    ref = 0.5 + 2 * (dy.float().T @ x.float())
+    _close(grad, ref, rtol=1e-3, atol=1e-3, what="wgrad")
+
+
+@pytest.mark.parametrize("rows,h", [(1, 384), (777, 768), (64, 1024)])
+def test_layernorm_fwd_bwd(C, rows, h):
+    torch.manual_seed(4)
+    x = _rand(rows, h, scale=2.0)
+    g = _rand(h, scale=0.5) + 1
+    b = _rand(h, scale=0.1)
+    y = torch.empty_like(x)
+    mean = torch.empty(rows, device=_dev())
+    rstd = torch.empty(rows, device=_dev())
+    C.norm_forward(x, g.to(torch.bfloat16), b, y, mean, rstd, 1e-12, False)
+    xf = x.float().requires_grad_(True)
+    gf = g.float().requires_grad_(True)
+    bf = b.float().requires_grad_(True)
+    ref = torch.nn.functional.layer_norm(xf, (h,), gf, bf, 1e-12)
+    _close(y, ref, rtol=1e-2, atol=2e-2, what="ln fwd")
+    dy = _rand(rows, h)
+    ref.backward(dy.float())
+    dx = torch.empty_like(x)
+    dg = torch.zeros(h, device=_dev())
+    db = torch.zeros(h, device=_dev())
+    dprev = torch.zeros(h, device=_dev())
+    C.norm_backward(dy, x, mean, rstd, g, dx, dg, db, dprev, False)
+    _close(dx, xf.grad, rtol=2e-2, atol=3e-2, what="ln dx")
+    _close(dg, gf.grad, rtol=1e-3, atol=1e-2, what="ln dgamma")
+    _close(db, bf.grad, rtol=1e-3, atol=1e-2, what="ln dbeta")
+    _close(dprev, xf.grad.sum(0), rtol=2e-2, atol=5e-2, what="ln dbias_prev")
+
+
+def test_rmsnorm_fwd_bwd(C):
+    torch.manual_seed(5)
+    rows, h = 500, 768
+    x = _rand(rows, h)
+    g = _rand(h, scale=0.2) + 1
+    y = torch.empty_like(x)
+    rstd = torch.empty(rows, device=_dev())
+    C.norm_forward(x, g, None, y, None, rstd, 1e-6, True)
+    xf = x.float().requires_grad_(True)
+    gf = g.float().requires_grad_(True)
+    ref = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6) * gf
+    _close(y, ref, rtol=1e-2, atol=2e-2, what="rms fwd")
+    dy = _rand(rows, h)
+    ref.backward(dy.float())
+    dx = torch.empty_like(x)
+    dg = torch.zeros(h, device=_dev())
+    C.norm_backward(dy, x, None, rstd, g, dx, dg, None, None, True)
+    _close(dx, xf.grad, rtol=2e-2, atol=3e-2, what="rms dx")
+    _close(dg, gf.grad, rtol=1e-3, atol=1e-2, what="rms dgamma")
+
+
+def test_embedding_ln(C):
+    torch.manual_seed(6)
+    vocab, npos, h, rows = 1000, 512, 384, 3000
+    word = _rand(vocab, h, scale=0.1)
+    pos = _rand(npos, h, scale=0.1)
+    typ = _rand(2, h, scale=0.1)
+    g = _rand(h, scale=0.1) + 1
+    b = _rand(h, scale=0.1)
+    ids = torch.randint(0, vocab, (rows,), device=_dev(), dtype=torch.int32)
+    ids[::7] = 0
+    pids = torch.randint(0, npos, (rows,), device=_dev(), dtype=torch.int32)
+    y = torch.empty(rows, h, dtype=torch.bfloat16, device=_dev())
+    mean = torch.empty(rows, device=_dev())
+    rstd = torch.empty(rows, device=_dev())
+    C.embed_ln_forward(ids, pids, None, word, pos, typ, g, b, y, mean, rstd, 1e-12)
+    wf = word.float().requires_grad_(True)
+    pf = pos.float().requires_grad_(True)
+    tf = typ.float().requires_grad_(True)
+    gf = g.float().requires_grad_(True)
+    bf = b.float().requires_grad_(True)
+    s = wf[ids.long()] + pf[pids.long()] + tf[0]
+    ref = torch.nn.functional.layer_norm(s, (h,), gf, bf, 1e-12)
+    _close(y, ref, rtol=1e-2, atol=2e-2, what="embed fwd")
+    dy = _rand(rows, h)
+    ref.backward(dy.float())
+    wg = torch.zeros(vocab, h, device=_dev())
+    pg = torch.zeros(npos, h, device=_dev())
+    tg = torch.zeros(2, h, device=_dev())
+    dg = torch.zeros(h, device=_dev())
+    db = torch.zeros(h, device=_dev())
+    C.embed_ln_backward(dy, ids, pids, None, word, pos, typ, g, mean, rstd, wg, pg, tg, dg, db, 0)
+    expected_wg = wf.grad.clone()
+    expected_wg[0] = 0  # padding row receives no gradient
+    _close(wg, expected_wg, rtol=2e-2, atol=5e-2, what="word grad")
+    _close(pg, pf.grad, rtol=2e-2, atol=5e-2, what="pos grad")
+    _close(tg, tf.grad, rtol=2e-2, atol=2e-1, what="type grad")
+    _close(dg, gf.grad, rtol=1e-3, atol=5e-2, what="dgamma")
+
+
+def _attn_ref(q, k, v, lens, heads, kv_heads, scale, causal, window):
+    outs = []
+    start = 0
+    d = 64
+    for n in lens:
+        qs = q[start:start + n].float().view(n, heads, d).transpose(0, 1)
+        ks = k[start:start + n].float().view(n, kv_heads, d).transpose(0, 1)
+        vs = v[start:start + n].float().view(n, kv_heads, d).transpose(0, 1)
+        rep = heads // kv_heads
+        ks = ks.repeat_interleave(rep, 0)
+        vs = vs.repeat_interleave(rep, 0)
+        s = (qs @ ks.transpose(1, 2)) * scale
+        i = torch.arange(n, device=q.device)[:, None]
+        j = torch.arange(n, device=q.device)[None, :]
+        mask = torch.ones(n, n, dtype=torch.bool, device=q.device)
+        if causal:
+            mask &= j <= i
+        if window >= 0:
+            mask &= (j - i).abs() <= window
+        s = s.masked_fill(~mask, float("-inf"))
+        o = torch.softmax(s, -1) @ vs
+        outs.append(o.transpose(0, 1).reshape(n, heads * d))
+        start += n
+    return torch.cat(outs)
+
+
+@pytest.mark.parametrize(
+    "lens,heads,kv_heads,causal,window",
+    [([1, 17, 64, 65, 200, 256], 12, 12, False, -1), ([300, 129], 4, 4, False, 64), ([100, 257], 4, 2, True, -1)],
+)
+def test_attention_fwd_bwd(C, lens, heads, kv_heads, causal, window):
+    torch.manual_seed(7)
+    total = sum(lens)
+    hd = heads * 64
+    kvd = kv_heads * 64
+    qkv = _rand(total, hd + 2 * kvd)
+    q, k, v = qkv[:, :hd], qkv[:, hd:hd + kvd], qkv[:, hd + kvd:]
+    cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), dtype=torch.int32, device=_dev())
+    scale = 1 / 8
+    o = torch.empty(total, hd, dtype=torch.bfloat16, device=_dev())
+    lse = torch.empty(heads, total, device=_dev())
+    C.attention_forward(q, k, v, o, lse, cu, max(lens), heads, kv_heads, scale, causal, window)
+    qf = q.float().requires_grad_(True)
+    kf = k.float().requires_grad_(True)
+    vf = v.float().requires_grad_(True)
+    ref = _attn_ref(qf, kf, vf, lens, heads, kv_heads, scale, causal, window)
+    _close(o, ref, rtol=2e-2, atol=2e-2, what="attn fwd")
+    if kv_heads != heads:
+        return
+    do = _rand(total, hd)
+    ref.backward(do.float())
+    dqkv = torch.empty_like(qkv)
+    dq, dk, dv = dqkv[:, :hd], dqkv[:, hd:hd + kvd], dqkv[:, hd + kvd:]
+    dq_acc = torch.empty(total, hd, device=_dev())
+    dvec = torch.empty(heads, total, device=_dev())
+    C.attention_backward(do, q, k, v, o, lse, dq, dk, dv, dq_acc, dvec, cu, max(lens), heads,
+                         kv_heads, scale, causal, window)
+    _close(dq, qf.grad, rtol=3e-2, atol=3e-2, what="dq")
+    _close(dk, kf.grad, rtol=3e-2, atol=3e-2, what="dk")
+    _close(dv, vf.grad, rtol=3e-2, atol=3e-2, what="dv")
+
+
+@pytest.mark.parametrize("mode", [0, 1, 2])
+def test_pool(C, mode):
+    torch.manual_seed(8)
+    lens = [3, 1, 50, 128]
+    h = 768
+    total = sum(lens)
+    x = _rand(total, h)
+    cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), dtype=torch.int32, device=_dev())
+    out = torch.empty(len(lens), h, device=_dev())
+    norm = torch.empty(len(lens), device=_dev())
+    C.pool_forward(x, cu, out, norm, mode, True)
+    xf = x.float().requires_grad_(True)
+    pooled = []
+    s = 0
+    for n in lens:
+        seg = xf[s:s + n]
+        pooled.append(seg.mean(0) if mode == 0 else seg[0] if mode == 1 else seg[-1])
+        s += n
+    ref = torch.nn.functional.normalize(torch.stack(pooled), dim=-1, eps=1e-12)
+    _close(out, ref, rtol=1e-3, atol=1e-4, what="pool fwd")
+    g = torch.randn_like(out)
+    ref.backward(g)
+    dh = torch.empty_like(x)
+    C.pool_backward(g, out, norm, cu, dh, mode, True)
+    _close(dh, xf.grad, rtol=2e-2, atol=1e-3, what="pool bwd")
+
+
+def test_colsum_and_cast(C):
+    x = _rand(1000, 768)
+    out = torch.ones(768, device=_dev())
+    C.colsum_accumulate(x, out)
+    _close(out, 1 + x.float().sum(0), rtol=1e-4, atol=1e-3, what="colsum")
+    src = torch.randn(1001, device=_dev())
+    dst = torch.empty(1001, dtype=torch.bfloat16, device=_dev())
+    C.cast_bf16(src, dst)
+    assert torch.equal(dst, src.to(torch.bfloat16))
+
+
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, False), (True, True)])
+def test_sgemm(C, a_mn, b_mn):
+    torch.manual_seed(9)
+    m, n, k = 300, 257, 129
+    a = torch.randn(k, m, device=_dev()) if a_mn else torch.randn(m, k, device=_dev())
+    b = torch.randn(k, n, device=_dev()) if b_mn else torch.randn(n, k, device=_dev())
+    c = torch.ones(m, n, device=_dev())
+    C.sgemm(a, a_mn, b, b_mn, c, 0.5, True)
+    am = a.T if a_mn else a
+    bm = b if b_mn else b.T
+    ref = 1 + 0.5 * (am.double() @ bm.double())
+    _close(c, ref, rtol=1e-5, atol=1e-4, what="sgemm")
+
+
+def test_mnr_rows(C):
+    torch.manual_seed(10)
+    r, c = 37, 50
+    cos = torch.rand(r, c, device=_dev()) * 2 - 1
+    w = (torch.rand(r, c, device=_dev()) < 0.1).float() * torch.rand(r, c, device=_dev()) * 2
+    rv = torch.rand(r, device=_dev()) < 0.9
+    cv = torch.rand(c, device=_dev()) < 0.9
+    scale = 20.0
+    n_active = ((w * cv[None].float() * rv[:, None].float()).sum(1) > 0).sum().clamp(min=1)
+    coef = (1.0 / n_active.float()).reshape(1)
+    grad = torch.empty(r, c, device=_dev())
+    row_loss = torch.empty(r, device=_dev())
+    row_active = torch.empty(r, device=_dev())
+    C.mnr_rows(cos, w, rv, cv, grad, row_loss, row_active, scale, coef)
+    x = cos.double().requires_grad_(True)
+    raw = scale * x
+    logits = raw.masked_fill(~cv[None], float("-inf"))
+    lse = torch.logsumexp(logits, 1)
+    act = w.double() * rv[:, None].double() * cv[None].double()
+    rw = act.sum(1)
+    rl = (act * (lse[:, None] - raw)).nan_to_num(0).sum(1) / rw.clamp(min=1)
+    active = rv & (rw > 0)
+    loss = (rl * active).sum() / active.sum().clamp(min=1)
+    loss.backward()
+    _close(row_loss * row_active, (rl * active).float(), rtol=1e-4, atol=1e-4, what="row loss")
+    _close(grad, x.grad.float(), rtol=1e-4, atol=1e-6, what="mnr grad")
+
+
+def test_adamw_clip_gate(C):
+    torch.manual_seed(11)
+    n = 10_001
+    p = torch.randn(n, device=_dev())
+    g = torch.randn(n, device=_dev()) * 3
+    m = torch.zeros(n, device=_dev())
+    v = torch.zeros(n, device=_dev())
+    copy = torch.empty(n, dtype=torch.bfloat16, device=_dev())
+    scalars = torch.zeros(8, device=_dev())
+    nsq = torch.zeros(1, dtype=torch.float64, device=_dev())
+    loss = torch.tensor([1.0], device=_dev())
+    pr, mr, vr = p.clone(), m.clone(), v.clone()
+    lr, b1, b2, eps, wd, max_norm = 1e-3, 0.9, 0.999, 1e-8, 0.01, 1.0
+    for step in range(1, 4):
+        C.grad_norm_sq(g, nsq)
+        C.finalize_clip(nsq, scalars, loss, max_norm, 1)
+        C.adamw_step(p, g, m, v, copy, scalars, lr, b1, b2, eps, wd)
+        norm = g.double().norm()
+        coef = min(1.0, max_norm / (norm.item() + 1e-6))
+        gc = g * coef
+        mr = b1 * mr + (1 - b1) * gc
+        vr = b2 * vr + (1 - b2) * gc * gc
+        upd = (mr / (1 - b1**step)) / ((vr / (1 - b2**step)).sqrt() + eps) + wd * pr
+        pr = pr - lr * upd
+    _close(p, pr, rtol=1e-5, atol=1e-6, what="adamw")
+    assert torch.equal(copy, p.to(torch.bfloat16))
+    assert scalars[2].item() == 3.0
+    # A non-finite loss skips the update and keeps the step count.
+    before = p.clone()
+    C.grad_norm_sq(g, nsq)
+    C.finalize_clip(nsq, scalars, torch.tensor([float("nan")], device=_dev()), max_norm, 1)
+    C.adamw_step(p, g, m, v, copy, scalars, lr, b1, b2, eps, wd)
+    assert torch.equal(p, before)
+    assert scalars[2].item() == 3.0 and scalars[4].item() == 1.0
