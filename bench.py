@@ -1,0 +1,270 @@
+"""Flagship benchmark: BERT-base cached-MNR (GradCache) training on 1..8 B200.
+
+    python bench.py --gpus N --steps K --warmup W [--impl ours|reference]
+
+Configuration: BERT-base (12 layers, hidden 768,
+12 heads, FFN 3072, vocab 30522, mean pooling), bf16 compute with fp32
+master weights and AdamW, cached MNR (scale 20) with global batch 4096
+(anchor, positive) pairs, mini-batch 128, length 256, token ids uniform in
+[1000, 30522) with [CLS]/[SEP], valid lengths uniform in [32, 256]. Data
+parallel over N GPUs with cross-rank in-batch negatives (a 4096 x 4096
+similarity per step). The global batch is fixed as N grows (strong scaling).
+
+Timing: W untimed warm-up steps, then exactly K steps bracketed by a barrier
+and torch.cuda.synchronize() on both sides, timed with CUDA events on the
+launching stream; the maximum over ranks is reported. Each step's working set
+(weights, optimizer state, activations: several GB) exceeds the 126 MB L2, so
+no explicit flush is inserted. A second timed phase ("e2e") runs the same
+steps through the public API with every step's inputs copied host->device
+from pinned memory and the loss read back to the host.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+import torch
+
+METRIC = "train pairs/sec (box, device-timed, max over ranks) at 1/2/4/8 B200 vs ref JAX/NCCL"
+MODEL = "bert-base (12L, H768, 12 heads, FFN 3072, vocab 30522, mean pooling)"
+GLOBAL_BATCH = 4096
+MINI_BATCH = 128
+SEQ = 256
+MIN_LEN = 32
+VOCAB = 30522
+
+
+def _args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--global-batch", type=int, default=GLOBAL_BATCH)
+    p.add_argument("--no-e2e", action="store_true")
+    return p.parse_args()
+
+
+def _reference_arm(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    reason = ("the reference (JAX/Equinox/Optax/Grain/Orbax) cannot be installed offline: its build "
+              "backend hatchling and its runtime dependencies jax, equinox, optax, grain and "
+              "orbax-checkpoint are absent from the wheelhouse")
+    if rank == 0:
+        print(json.dumps({"impl": "reference", "unavailable": reason}), flush=True)
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int) -> None:
+        self.device_index = device_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.handle = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device_index}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.handle, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.handle.close()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as f:
+            for line in f:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    mx = float(parts[2])
+                except ValueError:
+                    continue
+                for name, flag in zip(names, parts[5:9]):
+                    if flag.lower() == "active":
+                        reasons.add(name)
+        os.unlink(self.path)
+        loaded = [x for x in sm if mx and x > 0.3 * mx] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def main() -> None:
+    args = _args()
+    if args.impl == "reference":
+        _reference_arm(args)
+        return
+
+    from representax_b200.data.synthetic import retrieval_pairs
+    from representax_b200.models.bert import BertConfig, BertEncoder
+    from representax_b200.ops._ext import check_status, launch_counter
+    from representax_b200.parallel.dist import barrier, init_from_env
+    from representax_b200.precision import BF16_MIXED_POLICY
+    from representax_b200.tasks._batch import to_device
+    from representax_b200.tasks.retrieval import MNRTask
+    from representax_b200.train.execution import GradCache
+    from representax_b200.train.optimizer import AdamW
+    from representax_b200.train.step import TrainStep, init_train_state
+
+    ctx = init_from_env(timeout_s=600.0)
+    world = ctx.world_size
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    device = torch.device("cuda", ctx.local_rank)
+    torch.cuda.set_device(device)
+    if args.global_batch % world:
+        raise SystemExit("global batch must divide evenly over ranks")
+    local = args.global_batch // world
+
+    config = BertConfig.base(hidden_dropout_probability=0.0, attention_dropout_probability=0.0)
+    model = BertEncoder(config, seed=0, compute_dtype=torch.bfloat16)
+    state = init_train_state(model, device=device, precision=BF16_MIXED_POLICY)
+    step = TrainStep(state, MNRTask(scale=20.0), optimizer=AdamW(learning_rate=2e-5, weight_decay=0.01),
+                     precision=BF16_MIXED_POLICY, execution=GradCache(query_chunk_size=MINI_BATCH),
+                     max_gradient_norm=1.0, dist=ctx, stochastic=False)
+
+    # Host batches (pinned), distinct per step and per rank; same shapes every step.
+    rng = np.random.default_rng(1234 + ctx.rank)
+    n_host = 4
+    host = []
+    for _ in range(n_host):
+        b = retrieval_pairs(rng, local, SEQ, vocab=VOCAB, low=1000, min_len=MIN_LEN, max_len=SEQ)
+        b = b.map_tensors(lambda t: t.pin_memory())
+        host.append(b)
+
+    def h2d(b):
+        return to_device(b, device)
+
+    def packed_bytes(b):
+        return b.query.packed.nbytes() + b.document.packed.nbytes() + sum(
+            t.nbytes for t in (b.query.attention_mask, b.query.input_ids, b.document.attention_mask,
+                               b.document.input_ids, b.positive_mask, b.query_valid, b.document_valid))
+
+    resident = [h2d(b) for b in host]
+    torch.cuda.synchronize()
+
+    it = 0
+    for _ in range(args.warmup):
+        step(resident[it % n_host], it)
+        it += 1
+    torch.cuda.synchronize()
+    check_status(device)
+
+    counter = launch_counter()
+    sampler = ClockSampler(ctx.local_rank)
+    barrier(ctx)
+    torch.cuda.synchronize()
+    sampler.start()
+    counter.launches = 0
+    counter.counting = True
+    start_ev = torch.cuda.Event(enable_timing=True)
+    end_ev = torch.cuda.Event(enable_timing=True)
+    start_ev.record()
+    for k in range(args.steps):
+        metrics = step(resident[it % n_host], it)
+        it += 1
+    end_ev.record()
+    torch.cuda.synchronize()
+    counter.counting = False
+    barrier(ctx)
+    clocks = sampler.stop()
+    launches = counter.launches
+    check_status(device)
+    elapsed = start_ev.elapsed_time(end_ev) / 1e3
+    t = torch.tensor([elapsed], device=device)
+    if ctx.enabled:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    elapsed = float(t)
+    final_loss = float(metrics.loss)
+
+    e2e = None
+    if not args.no_e2e:
+        barrier(ctx)
+        torch.cuda.synchronize()
+        s2 = torch.cuda.Event(enable_timing=True)
+        e2 = torch.cuda.Event(enable_timing=True)
+        s2.record()
+        for k in range(args.steps):
+            batch = h2d(host[it % n_host])
+            m = step(batch, it)
+            loss_host = float(m.loss)  # device -> host read of the step's loss
+            it += 1
+        e2.record()
+        torch.cuda.synchronize()
+        barrier(ctx)
+        te = torch.tensor([s2.elapsed_time(e2) / 1e3], device=device)
+        if ctx.enabled:
+            torch.distributed.all_reduce(te, op=torch.distributed.ReduceOp.MAX)
+        e2e_elapsed = float(te)
+        e2e = {"value": args.global_batch * args.steps / e2e_elapsed, "unit": "pairs/s",
+               "h2d_bytes_per_step": int(packed_bytes(host[0])), "d2h_bytes_per_step": 4,
+               "ms_per_step": 1e3 * e2e_elapsed / args.steps, "last_loss": loss_host}
+
+    if ctx.rank == 0:
+        value = args.global_batch * args.steps / elapsed
+        out = {
+            "metric": METRIC,
+            "value": value,
+            "unit": "pairs/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": 1e3 * elapsed / args.steps,
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (uniform token ids, uniform valid lengths); random-init weights",
+            "config": {
+                "model": MODEL,
+                "global_batch": args.global_batch,
+                "mini_batch": MINI_BATCH,
+                "seq_len": SEQ,
+                "valid_len": [MIN_LEN, SEQ],
+                "parallelism": f"dp{world}" + ("" if world == 1 else " with cross-rank negatives"),
+                "loss": "cached MNR (GradCache), scale 20, global negatives",
+                "optimizer": "AdamW lr 2e-5 wd 0.01, clip 1.0, fp32 master, bf16 compute",
+                "dropout": 0.0,
+                "padding": "packed (padding tokens are not computed)",
+                "l2": "per-step working set > 126 MB L2; no explicit flush",
+            },
+            "clocks": clocks,
+            "e2e": e2e,
+            "gpu_launches": launches,
+            "final_loss": final_loss,
+            "impl": "ours",
+        }
+        print(json.dumps(out), flush=True)
+    if ctx.enabled:
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -28,8 +28,34 @@ class KernelTimeoutError(RuntimeError):
     """A bounded device-side wait ran out; the kernel unwound and reported it."""
 
 
+# Kernels launched per binding call (used to count our own launches).
+KERNELS_PER_CALL = {"attention_backward": 3, "grad_norm_sq": 1}
+
+
+class _CountingModule:
+    """Proxy that counts kernel launches made through the extension."""
+
+    def __init__(self, module) -> None:
+        self._module = module
+        self.launches = 0
+        self.counting = False
+
+    def __getattr__(self, name):
+        fn = getattr(self._module, name)
+        if not callable(fn):
+            return fn
+        weight = KERNELS_PER_CALL.get(name, 1)
+
+        def wrapped(*args, **kwargs):
+            if self.counting:
+                self.launches += weight
+            return fn(*args, **kwargs)
+
+        return wrapped
+
+
 def ext():
-    """Return the compiled extension module, importing it once."""
+    """Return the compiled extension module (behind a launch counter)."""
 
     global _module
     if _module is None:
@@ -42,8 +68,14 @@ def ext():
                         "representax_b200 CUDA extension is not built; run "
                         "`python setup.py build_ext --inplace` (sm_100a)"
                     ) from error
-                _module = _C
+                _module = _CountingModule(_C)
     return _module
+
+
+def launch_counter():
+    """The counting proxy: set ``.counting`` and read ``.launches``."""
+
+    return ext()
 
 
 def available() -> bool:

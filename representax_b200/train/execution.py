@@ -1,0 +1,184 @@
+"""Loss executions: how a task's loss and its parameter gradients are computed.
+
+Parity: ``Direct`` (src/representax/train/execution.py:15-58), ``GradCache``
+(src/representax/train/grad_cache.py:110-315) and ``MegaBatchMining``
+(src/representax/train/mega_batch.py). An execution's ``run`` leaves the
+gradient of the (global) loss in the model's gradient accumulators and
+returns the detached loss output.
+
+GradCache runs in three stages: every chunk of queries and documents is
+encoded without autograd state; the objective and its gradient with respect
+to the representations are computed once over the whole batch (with
+cross-rank negatives when distributed); then each chunk is re-encoded with
+autograd and back-propagated with its slice of the representation gradient.
+Replay draws the same random streams as the first pass, so the update equals
+the direct one.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Any
+
+import torch
+
+from representax_b200.core import LossOutput, Route, encode, evaluate_loss
+from representax_b200.parallel.dist import LOCAL, DistContext, gather_rows
+from representax_b200.tasks._batch import leading_rows, slice_rows
+
+from .rng import StreamFactory
+
+
+def _detach(out: LossOutput) -> LossOutput:
+    return LossOutput(loss=out.loss.detach(), metrics={k: v.detach() for k, v in out.metrics.items()})
+
+
+def _global_batch(batch, queries, documents, ctx: DistContext):
+    """Gather representations and the positive relation across ranks.
+
+    A rank-local batch whose mask spans only its own documents is placed at
+    its rank's column block; a process-local batch already spans all ranks'
+    documents (rank-major). Every rank then evaluates the same global
+    objective.
+    """
+
+    from representax_b200.tasks.retrieval.batch import RetrievalBatch
+
+    if not ctx.enabled:
+        return queries, documents, batch
+    local_d = documents.shape[0]
+    global_d = local_d * ctx.world_size
+    mask = batch.positive_mask
+    weights = batch.weights()
+    if mask.shape[1] == local_d:
+        wide = torch.zeros(mask.shape[0], global_d, dtype=weights.dtype, device=weights.device)
+        wide[:, ctx.rank * local_d:(ctx.rank + 1) * local_d] = weights
+        weights = wide
+    elif mask.shape[1] != global_d:
+        raise ValueError("positive_mask columns must cover the local or the global documents")
+    q_all = gather_rows(queries, ctx)
+    d_all = gather_rows(documents, ctx)
+    w_all = gather_rows(weights.contiguous(), ctx)
+    qv = gather_rows(batch.query_valid.to(torch.uint8), ctx).bool()
+    dv = gather_rows(batch.document_valid.to(torch.uint8), ctx).bool()
+    global_batch = RetrievalBatch(query=q_all, document=d_all, positive_mask=w_all > 0,
+                                  positive_weights=w_all, query_valid=qv, document_valid=dv)
+    return q_all, d_all, global_batch
+
+
+@dataclass(frozen=True)
+class Direct:
+    """Plain full-batch differentiation."""
+
+    def validate(self, task: Any) -> None:
+        return None
+
+    def run(self, task, model, batch, *, streams: StreamFactory, ctx: DistContext = LOCAL) -> LossOutput:
+        base = getattr(task, "task", task)
+        if ctx.enabled and hasattr(base, "loss_from_representations") and hasattr(batch, "positive_mask"):
+            gen = streams("direct")
+            queries, documents = base.representations(model, batch, generator=gen, encode_fn=encode)
+            q_all, d_all, gbatch = _global_batch(batch, queries, documents, ctx)
+            out = task.loss_from_representations((q_all, d_all), gbatch)
+        else:
+            out = evaluate_loss(task, model, batch, generator=streams("direct"))
+        out.loss.backward()
+        return _detach(out)
+
+
+def _encode_chunks(model, payload, route: Route, chunk: int, streams: StreamFactory, role: str):
+    rows = leading_rows(payload)
+    outs = []
+    with torch.no_grad():
+        for i, start in enumerate(range(0, rows, chunk)):
+            part = slice_rows(payload, start, min(rows, start + chunk))
+            outs.append(encode(model, part, route=route, generator=streams(role, i)))
+    return torch.cat(outs), rows
+
+
+def _replay_chunks(model, payload, route: Route, chunk: int, grads: torch.Tensor, streams: StreamFactory,
+                   role: str) -> None:
+    rows = leading_rows(payload)
+    for i, start in enumerate(range(0, rows, chunk)):
+        stop = min(rows, start + chunk)
+        part = slice_rows(payload, start, stop)
+        with torch.enable_grad():
+            reps = encode(model, part, route=route, generator=streams(role, i))
+            reps.backward(grads[start:stop])
+
+
+@dataclass(frozen=True)
+class GradCache:
+    """Exact cached differentiation bounded by chunk size."""
+
+    query_chunk_size: int
+    document_chunk_size: int | None = None
+    loss_row_chunk_size: int | None = None
+
+    def __post_init__(self) -> None:
+        if self.query_chunk_size <= 0:
+            raise ValueError("query_chunk_size must be positive")
+        if self.document_chunk_size is not None and self.document_chunk_size <= 0:
+            raise ValueError("document_chunk_size must be positive when set")
+        if self.loss_row_chunk_size is not None and self.loss_row_chunk_size <= 0:
+            raise ValueError("loss_row_chunk_size must be positive when set")
+
+    @property
+    def resolved_document_chunk_size(self) -> int:
+        return self.document_chunk_size or self.query_chunk_size
+
+    @property
+    def resolved_loss_row_chunk_size(self) -> int:
+        return self.loss_row_chunk_size or self.query_chunk_size
+
+    def validate(self, task: Any) -> None:
+        from representax_b200.tasks.guided import GISTTask
+        from representax_b200.tasks.modifiers import MatryoshkaTask
+        from representax_b200.tasks.retrieval import MNRTask
+
+        base = task.task if isinstance(task, MatryoshkaTask) else task
+        if not isinstance(base, (MNRTask, GISTTask)):
+            raise TypeError("GradCache requires MNRTask, GISTTask, or their Matryoshka modifier")
+
+    def run(self, task, model, batch, *, streams: StreamFactory, ctx: DistContext = LOCAL) -> LossOutput:
+        from representax_b200.tasks.guided import GISTBatch, GISTTask
+        from representax_b200.tasks.modifiers import MatryoshkaTask
+
+        base = task.task if isinstance(task, MatryoshkaTask) else task
+        if isinstance(base, GISTTask) and isinstance(batch, GISTBatch):
+            return self._run_gist(task, base, model, batch, streams=streams, ctx=ctx)
+        qc, dc = self.query_chunk_size, self.resolved_document_chunk_size
+        queries, _ = _encode_chunks(model, batch.query, Route.QUERY, qc, streams, "query")
+        documents, _ = _encode_chunks(model, batch.document, Route.DOCUMENT, dc, streams, "document")
+        queries.requires_grad_(True)
+        documents.requires_grad_(True)
+        q_all, d_all, gbatch = _global_batch(batch, queries, documents, ctx)
+        with torch.enable_grad():
+            out = task.loss_from_representations((q_all, d_all), gbatch,
+                                                 row_chunk_size=self.resolved_loss_row_chunk_size)
+            out.loss.backward()
+        _replay_chunks(model, batch.query, Route.QUERY, qc, queries.grad, streams, "query")
+        _replay_chunks(model, batch.document, Route.DOCUMENT, dc, documents.grad, streams, "document")
+        return _detach(out)
+
+    def _run_gist(self, task, base, model, batch, *, streams, ctx):
+        if ctx.enabled:
+            raise NotImplementedError("distributed cached GIST is not implemented yet")
+        roles = base.cached_roles(batch)
+        reps = {}
+        for name, (payload, route) in roles.items():
+            chunk = self.query_chunk_size if route == Route.QUERY else self.resolved_document_chunk_size
+            value, _ = _encode_chunks(model, payload, route, chunk, streams, name)
+            reps[name] = value.requires_grad_(True)
+        with torch.enable_grad():
+            out = task.loss_from_representations(base.assemble(reps), batch,
+                                                 row_chunk_size=self.resolved_loss_row_chunk_size)
+            out.loss.backward()
+        for name, (payload, route) in roles.items():
+            chunk = self.query_chunk_size if route == Route.QUERY else self.resolved_document_chunk_size
+            if reps[name].grad is not None:
+                _replay_chunks(model, payload, route, chunk, reps[name].grad, streams, name)
+        return _detach(out)
+
+
+__all__ = ["Direct", "GradCache"]

@@ -1,0 +1,119 @@
+"""Flat parameter store: every trainable parameter is a view into one buffer.
+
+One contiguous fp32 buffer each holds the master parameters, their gradient
+accumulator and the two AdamW moments; a bf16 buffer holds the compute copy.
+The optimizer step, gradient-norm, finite check, clipping and compute-copy
+refresh then run as a handful of kernels over the whole model, and gradient
+collectives operate on one (bucketable) buffer.
+
+Every parameter starts at a 64-element boundary so views stay 256-byte
+aligned for TMA and vector loads. Frozen parameters (``requires_grad=False``)
+are stored separately and receive no gradient or moment storage.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+from torch import nn
+
+ALIGN = 64
+
+
+@dataclass
+class Slot:
+    name: str
+    offset: int
+    numel: int
+    shape: tuple[int, ...]
+
+
+def _align(n: int) -> int:
+    return (n + ALIGN - 1) // ALIGN * ALIGN
+
+
+class FlatParameterStore:
+    def __init__(self, model: nn.Module, *, device: torch.device, compute_dtype: torch.dtype = torch.float32,
+                 optimizer_state: bool = True) -> None:
+        self.device = torch.device(device)
+        self.compute_dtype = compute_dtype
+        self.slots: list[Slot] = []
+        params = [(n, p) for n, p in model.named_parameters() if p.requires_grad]
+        offset = 0
+        for name, p in params:
+            self.slots.append(Slot(name, offset, p.numel(), tuple(p.shape)))
+            offset = _align(offset + p.numel())
+        self.numel = max(offset, ALIGN)
+        self.master = torch.zeros(self.numel, dtype=torch.float32, device=self.device)
+        self.grad = torch.zeros(self.numel, dtype=torch.float32, device=self.device)
+        self.exp_avg = torch.zeros(self.numel, dtype=torch.float32, device=self.device) if optimizer_state else None
+        self.exp_avg_sq = torch.zeros(self.numel, dtype=torch.float32, device=self.device) if optimizer_state else None
+        self.mixed = compute_dtype != torch.float32
+        self.compute = torch.zeros(self.numel, dtype=compute_dtype, device=self.device) if self.mixed else None
+        self.params: dict[str, nn.Parameter] = {}
+        modules = dict(model.named_modules())
+        for slot, (name, p) in zip(self.slots, params):
+            view = self.master[slot.offset:slot.offset + slot.numel].view(slot.shape)
+            view.copy_(p.detach().to(self.device, torch.float32))
+            new = nn.Parameter(view, requires_grad=True)
+            new.main_grad = self.grad[slot.offset:slot.offset + slot.numel].view(slot.shape)
+            if self.mixed:
+                new.compute = self.compute[slot.offset:slot.offset + slot.numel].view(slot.shape)
+            owner_name, _, attr = name.rpartition(".")
+            owner = modules[owner_name] if owner_name else model
+            setattr(owner, attr, new)
+            self.params[name] = new
+        # Frozen parameters and buffers just move to the device.
+        for name, p in model.named_parameters():
+            if not p.requires_grad and p.device != self.device:
+                owner_name, _, attr = name.rpartition(".")
+                owner = modules[owner_name] if owner_name else model
+                setattr(owner, attr, nn.Parameter(p.detach().to(self.device), requires_grad=False))
+        for name, b in list(model.named_buffers()):
+            owner_name, _, attr = name.rpartition(".")
+            owner = modules[owner_name] if owner_name else model
+            owner._buffers[attr] = b.to(self.device)
+        self.refresh_compute()
+
+    # ------------------------------------------------------------------
+    def refresh_compute(self) -> None:
+        if not self.mixed:
+            return
+        if self.device.type == "cuda":
+            from representax_b200.ops._ext import ext
+
+            ext().cast_bf16(self.master, self.compute)
+        else:
+            self.compute.copy_(self.master.to(self.compute_dtype))
+
+    def zero_grad(self) -> None:
+        self.grad.zero_()
+        for p in self.params.values():
+            p.grad = None
+
+    def collect_autograd_grads(self) -> None:
+        """Fold gradients that autograd left in ``.grad`` into the flat accumulator."""
+
+        for p in self.params.values():
+            if p.grad is not None:
+                p.main_grad.add_(p.grad.to(torch.float32))
+                p.grad = None
+
+    def named_views(self, which: str = "master"):
+        buf = {"master": self.master, "grad": self.grad, "exp_avg": self.exp_avg,
+               "exp_avg_sq": self.exp_avg_sq}[which]
+        for slot in self.slots:
+            yield slot.name, buf[slot.offset:slot.offset + slot.numel].view(slot.shape)
+
+    def state_dict(self) -> dict[str, torch.Tensor]:
+        out = {"master": self.master, "exp_avg": self.exp_avg, "exp_avg_sq": self.exp_avg_sq}
+        return {k: v for k, v in out.items() if v is not None}
+
+    def load_state_dict(self, state: dict[str, torch.Tensor]) -> None:
+        for key, value in state.items():
+            getattr(self, key).copy_(value.to(self.device))
+        self.refresh_compute()
+
+
+__all__ = ["FlatParameterStore", "Slot"]

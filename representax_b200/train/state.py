@@ -1,0 +1,52 @@
+"""Train-state and step-result types (src/representax/train/state.py:12-36)."""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import torch
+
+
+@dataclass
+class StepMetrics:
+    """Device-resident step outputs; read them on the host one step later."""
+
+    loss: torch.Tensor
+    gradient_norm: torch.Tensor
+    finite: torch.Tensor
+    learning_rate: float
+    optimizer_step: torch.Tensor
+    metrics: dict[str, torch.Tensor] = field(default_factory=dict)
+
+    def to_host(self) -> dict[str, float]:
+        out = {
+            "loss": float(self.loss),
+            "gradient_norm": float(self.gradient_norm),
+            "finite": bool(self.finite),
+            "learning_rate": self.learning_rate,
+            "optimizer_step": int(self.optimizer_step),
+        }
+        out.update({k: float(v) for k, v in self.metrics.items()})
+        return out
+
+
+@dataclass
+class TrainState:
+    """Model (with its flat store) plus optimizer scalars and the step count."""
+
+    model: torch.nn.Module
+    store: object
+    scalars: torch.Tensor  # [8] fp32: clip coef, finite, step, norm, skipped
+
+    @property
+    def step(self) -> int:
+        return int(self.scalars[2].item())
+
+
+@dataclass
+class StepResult:
+    state: TrainState
+    metrics: StepMetrics
+
+
+__all__ = ["StepMetrics", "StepResult", "TrainState"]
