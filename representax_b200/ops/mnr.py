@@ -92,7 +92,7 @@ class _NativeMNR(torch.autograd.Function):
         else:
             reverse_loss = torch.zeros((), device=dev)
             grad_r = None
-            loss = forward_loss
+            loss = forward_loss.clone()
         ctx.save_for_backward(qn, dn, grad_f, grad_r if grad_r is not None else torch.empty(0, device=dev))
         ctx.symmetric = symmetric
         ctx.mark_non_differentiable(forward_loss, reverse_loss)

@@ -371,3 +371,28 @@ def test_adamw_clip_gate(C):
     C.adamw_step(p, g, m, v, copy, scalars, lr, b1, b2, eps, wd)
     assert torch.equal(p, before)
     assert scalars[2].item() == 3.0 and scalars[4].item() == 1.0
+
+
+@pytest.mark.parametrize("symmetric", [False, True])
+def test_native_mnr_loss_matches_reference(symmetric):
+    from representax_b200.ops.mnr import _NativeMNR, mnr_terms_reference, normalize
+
+    torch.manual_seed(12)
+    q = torch.randn(70, 96, device=_dev(), requires_grad=True)
+    d = torch.randn(70, 96, device=_dev(), requires_grad=True)
+    w = torch.eye(70, device=_dev())
+    w[3, 5] = 0.5
+    qv = torch.ones(70, dtype=torch.bool, device=_dev())
+    dv = torch.ones(70, dtype=torch.bool, device=_dev())
+    dv[7] = False
+    loss, fwd, rev = _NativeMNR.apply(normalize(q), normalize(d), w, qv, dv, 20.0, symmetric)
+    loss.backward()
+    gq, gd = q.grad.clone(), d.grad.clone()
+    q2 = q.detach().double().requires_grad_(True)
+    d2 = d.detach().double().requires_grad_(True)
+    ref, rf, rr, *_ = mnr_terms_reference(q2, d2, w.double(), qv, dv, 20.0, symmetric)
+    ref.backward()
+    assert abs(loss.item() - ref.item()) < 1e-4
+    assert abs(fwd.item() - rf.item()) < 1e-4
+    _close(gq, q2.grad, rtol=1e-3, atol=1e-5, what="dq")
+    _close(gd, d2.grad, rtol=1e-3, atol=1e-5, what="dd")
