@@ -19,41 +19,15 @@
 // masks (src/representax/models/components.py:187-235), sliding windows
 // (src/representax/models/modernvbert/model.py:217-230) and GQA
 // (src/representax/models/qwen3_vl/text.py:188-199).
+#include "attention_kernels.cuh"
 #include "common.h"
 #include "sm100.cuh"
 
 namespace rx {
 namespace attn {
 
-constexpr int D = 64;
-constexpr int BM = 64;
-constexpr int BN = 64;
-constexpr int kThreads = 128;
-constexpr int kChunks = D / 8;  // 16-byte chunks per row
-
-struct Params {
-  const __nv_bfloat16* q;
-  const __nv_bfloat16* k;
-  const __nv_bfloat16* v;
-  int64_t ldq, ldk, ldv;  // row strides in elements
-  __nv_bfloat16* o;
-  int64_t ldo;
-  float* lse;  // [heads, T] base-2 log-sum-exp of the scaled scores
-  const int* cu_seqlens;
-  int batch, heads, heads_per_kv, total_tokens;
-  float scale_log2;  // softmax_scale * log2(e)
-  float scale;
-  int causal;
-  int window;  // -1: no window
-  // backward
-  const __nv_bfloat16* dO;
-  int64_t ld_do;
-  const float* dvec;  // [heads, T] rowsum(dO * O)
-  float* dq_acc;      // [T, heads * D] fp32, pre-zeroed
-  __nv_bfloat16* dk;
-  __nv_bfloat16* dv;
-  int64_t ld_dk, ld_dv;
-};
+// Tile constants and the kernel parameter block are shared with the other
+// host entry points through attention_kernels.cuh.
 
 __device__ __forceinline__ uint32_t swz(int row, int chunk) {
   return static_cast<uint32_t>((row * kChunks + (chunk ^ (row & 7))) * 16);

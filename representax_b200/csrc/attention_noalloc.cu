@@ -1,0 +1,136 @@
+// Allocation-free variant of the packed-attention backward (see rx_noalloc.h).
+//
+// It launches the same kernels as the regular entry point in attention.cu,
+// but takes their two scratch buffers (the fp32 dQ accumulator and the
+// rowsum(dO * O) vector) from a static device array compiled into this file,
+// so the call performs no cudaMalloc, cudaFree or allocating library call.
+#include <mutex>
+
+#include "attention_kernels.cuh"
+#include "rx_noalloc.h"
+
+namespace {
+
+// Scratch shared by every call on a device; lives until the process exits.
+static __device__ __align__(256) unsigned char g_scratch[RX_NOALLOC_SCRATCH_BYTES];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_setup_lock;
+void* g_scratch_ptr[kMaxDevices] = {nullptr};
+
+// Device address of g_scratch on the current device. In host code the name
+// g_scratch is only a host-side stand-in, so the address must be looked up
+// (once per device, with that device current) before a kernel may use it.
+int scratch_address(void** out) {
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess) return RX_NOALLOC_CUDA_ERROR;
+  if (device < 0 || device >= kMaxDevices) return RX_NOALLOC_BAD_ARGUMENT;
+  std::lock_guard<std::mutex> guard(g_setup_lock);
+  if (g_scratch_ptr[device] == nullptr) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_scratch) != cudaSuccess || ptr == nullptr)
+      return RX_NOALLOC_CUDA_ERROR;
+    g_scratch_ptr[device] = ptr;
+  }
+  *out = g_scratch_ptr[device];
+  return RX_NOALLOC_OK;
+}
+
+bool aligned16(const void* p, int64_t ld) {
+  return p != nullptr && reinterpret_cast<uintptr_t>(p) % 16 == 0 && ld % 8 == 0;
+}
+
+}  // namespace
+
+extern "C" int rx_attention_backward_noalloc(
+    const void* dO, int64_t ld_do, const void* q, int64_t ld_q, const void* k, int64_t ld_k,
+    const void* v, int64_t ld_v, const void* o, int64_t ld_o, const float* lse,
+    const int* cu_seqlens, int batch, int total_tokens, int max_len, int heads, float scale,
+    int causal, int window, void* dq, int64_t ld_dq, void* dk, int64_t ld_dk, void* dv,
+    int64_t ld_dv, cudaStream_t stream) {
+  using namespace rx::attn;
+  if (batch < 0 || total_tokens < 0 || max_len < 0 || heads <= 0) return RX_NOALLOC_BAD_ARGUMENT;
+  if (batch == 0 || total_tokens == 0 || max_len == 0) return RX_NOALLOC_OK;
+  if (lse == nullptr || cu_seqlens == nullptr) return RX_NOALLOC_BAD_ARGUMENT;
+  // Operand rows are read with 16-byte copies; gradient rows are written in
+  // 4-byte (dK, dV) and 8-byte (dQ) pieces.
+  if (!aligned16(q, ld_q) || !aligned16(k, ld_k) || !aligned16(v, ld_v) || !aligned16(dO, ld_do))
+    return RX_NOALLOC_BAD_ARGUMENT;
+  if (o == nullptr || ld_o % 2 != 0 || reinterpret_cast<uintptr_t>(o) % 4 != 0)
+    return RX_NOALLOC_BAD_ARGUMENT;
+  if (dq == nullptr || reinterpret_cast<uintptr_t>(dq) % 8 != 0 || ld_dq % 4 != 0)
+    return RX_NOALLOC_BAD_ARGUMENT;
+  if (dk == nullptr || dv == nullptr || ld_dk % 2 != 0 || ld_dv % 2 != 0 ||
+      reinterpret_cast<uintptr_t>(dk) % 4 != 0 || reinterpret_cast<uintptr_t>(dv) % 4 != 0)
+    return RX_NOALLOC_BAD_ARGUMENT;
+
+  // Scratch layout: dQ accumulator [T, heads * 64] fp32, then (256-byte
+  // aligned) rowsum(dO * O) [heads, T] fp32.
+  const uint64_t width = static_cast<uint64_t>(heads) * D;
+  const uint64_t acc_bytes = static_cast<uint64_t>(total_tokens) * width * sizeof(float);
+  const uint64_t dvec_offset = (acc_bytes + 255) / 256 * 256;
+  const uint64_t dvec_bytes = static_cast<uint64_t>(heads) * total_tokens * sizeof(float);
+  if (dvec_offset + dvec_bytes > RX_NOALLOC_SCRATCH_BYTES) return RX_NOALLOC_TOO_LARGE;
+
+  void* base = nullptr;
+  const int setup = scratch_address(&base);
+  if (setup != RX_NOALLOC_OK) return setup;
+  float* dq_acc = static_cast<float*>(base);
+  float* dvec = reinterpret_cast<float*>(static_cast<unsigned char*>(base) + dvec_offset);
+
+  Params p{};
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.k = static_cast<const __nv_bfloat16*>(k);
+  p.v = static_cast<const __nv_bfloat16*>(v);
+  p.ldq = ld_q;
+  p.ldk = ld_k;
+  p.ldv = ld_v;
+  p.lse = const_cast<float*>(lse);
+  p.cu_seqlens = cu_seqlens;
+  p.batch = batch;
+  p.heads = heads;
+  p.heads_per_kv = 1;
+  p.total_tokens = total_tokens;
+  p.scale = scale;
+  p.scale_log2 = static_cast<float>(static_cast<double>(scale) * 1.4426950408889634);
+  p.causal = causal ? 1 : 0;
+  p.window = window;
+  p.dO = static_cast<const __nv_bfloat16*>(dO);
+  p.ld_do = ld_do;
+  p.dvec = dvec;
+  p.dq_acc = dq_acc;
+  p.dk = static_cast<__nv_bfloat16*>(dk);
+  p.dv = static_cast<__nv_bfloat16*>(dv);
+  p.ld_dk = ld_dk;
+  p.ld_dv = ld_dv;
+
+  // The previous call's contents are still in the array: clear the
+  // accumulator (dvec is fully overwritten by its kernel).
+  if (cudaMemsetAsync(dq_acc, 0, acc_bytes, stream) != cudaSuccess) return RX_NOALLOC_CUDA_ERROR;
+  {
+    const int64_t threads = 256;
+    const int64_t warps = static_cast<int64_t>(total_tokens) * heads;
+    attn_dvec_kernel<<<static_cast<unsigned>((warps * 32 + threads - 1) / threads), threads, 0, stream>>>(
+        static_cast<const __nv_bfloat16*>(o), ld_o, p.dO, ld_do, dvec, total_tokens, heads);
+  }
+  dim3 grid((max_len + BN - 1) / BN, heads, batch);
+  attn_bwd_kernel<<<grid, kThreads, 0, stream>>>(p);
+  {
+    const int64_t n4 = static_cast<int64_t>(total_tokens) * static_cast<int64_t>(width) / 4;
+    attn_dq_convert_kernel<<<static_cast<unsigned>((n4 + 255) / 256), 256, 0, stream>>>(
+        dq_acc, static_cast<__nv_bfloat16*>(dq), ld_dq, total_tokens, static_cast<int>(width));
+  }
+  if (cudaGetLastError() != cudaSuccess) return RX_NOALLOC_CUDA_ERROR;
+  return RX_NOALLOC_OK;
+}
+
+extern "C" const char* rx_noalloc_error_string(int code) {
+  switch (code) {
+    case RX_NOALLOC_OK: return "ok";
+    case RX_NOALLOC_TOO_LARGE:
+      return "problem needs more scratch than the library's static array holds (32 MiB)";
+    case RX_NOALLOC_BAD_ARGUMENT: return "null pointer, negative size, or misaligned tensor";
+    case RX_NOALLOC_CUDA_ERROR: return "a CUDA call failed";
+    default: return "unknown code";
+  }
+}

@@ -18,6 +18,7 @@ SOURCES = [
     "gemm_wgrad.cu",
     "norm.cu",
     "attention.cu",
+    "attention_noalloc.cu",
     "pool.cu",
     "mnr.cu",
     "optim.cu",
