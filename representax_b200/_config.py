@@ -86,10 +86,10 @@ def _project(model: BaseModel, dumped: dict[str, Any], role: ParameterRole) -> d
     return out
 
 
-def project_parameters(config: FrozenConfig, role: ParameterRole) -> dict[str, Any]:
+def project_parameters(config: FrozenConfig, role: ParameterRole | str) -> dict[str, Any]:
     """Project a config onto the fields carrying one intrinsic role."""
 
-    return _project(config, config.model_dump(mode="json"), role)
+    return _project(config, config.model_dump(mode="json"), ParameterRole(role))
 
 
 __all__ = [

@@ -373,6 +373,7 @@ class B200ExecutionConfig(FrozenConfig):
     overlap_gradient_reduction: bool = True
     gradient_bucket_bytes: PositiveInt = 64 * 2 ** 20
     cuda_graphs: bool = False
+    deterministic: bool = True
 
 
 class TrainingConfig(FrozenConfig):

@@ -1,0 +1,153 @@
+"""Packed INT4 base weights with trainable low-rank (LoRA) adapters.
+
+Parity: ``_pack_int4_rows`` / ``_unpack_int4_rows``, ``QuantizedLoRALinear``,
+``apply_quantized_lora``, ``merge_quantized_lora`` and
+``lora_parameter_filter`` of src/representax/models/adapters.py:30-267.
+
+The storage format is kept identical so adapter bundles interoperate: each
+output row has a symmetric bf16 scale ``max|w| / 7`` (stored as its uint16
+bit pattern), values are rounded and clipped to [-7, 7], and two 4-bit
+two's-complement values share one uint8 with the even column in the low
+nibble. ``lora_a [rank, in]`` starts ~ N(0, in^-1/2) (or the configured
+scale) and ``lora_b [out, rank]`` at zero, so the adapted model starts equal
+to the quantized base. The forward is
+``x W_q^T + ((x A^T) B^T) * alpha / rank (+ bias)``.
+
+Models in this package hold linear weights as ``<name>_weight`` parameters;
+``apply_quantized_lora`` swaps each matching 2-D weight for a
+:class:`QuantizedLoRAWeight` submodule under the same attribute name, and
+the models' linear helpers dispatch on it.
+"""
+
+from __future__ import annotations
+
+import re
+
+import torch
+from torch import nn
+
+
+def _bf16_bits(x: torch.Tensor) -> torch.Tensor:
+    return x.to(torch.bfloat16).view(torch.int16).view(torch.uint16) if hasattr(torch, "uint16") else \
+        x.to(torch.bfloat16).view(torch.int16)
+
+
+def _from_bf16_bits(bits: torch.Tensor) -> torch.Tensor:
+    return bits.view(torch.int16).view(torch.bfloat16) if bits.dtype != torch.int16 else bits.view(torch.bfloat16)
+
+
+def pack_int4_rows(weight: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Quantize ``[..., out, in]`` rows to packed int4 plus bf16 row scales."""
+
+    numeric = weight.to(torch.bfloat16)
+    maximum = numeric.abs().amax(dim=-1).to(torch.float32)
+    scale = torch.where(maximum > 0, maximum / 7.0, torch.ones_like(maximum)).to(torch.bfloat16)
+    q = torch.clamp(torch.round(numeric.float() / scale.float()[..., None]), -7, 7).to(torch.int8)
+    unsigned = (q & 0x0F).to(torch.uint8)
+    if unsigned.shape[-1] % 2:
+        unsigned = torch.nn.functional.pad(unsigned, (0, 1))
+    pairs = unsigned.reshape(*unsigned.shape[:-1], -1, 2)
+    packed = pairs[..., 0] | (pairs[..., 1] << 4)
+    return packed.contiguous(), _bf16_bits(scale)
+
+
+def unpack_int4_rows(packed: torch.Tensor, scale_bits: torch.Tensor, input_size: int) -> torch.Tensor:
+    low = packed & 0x0F
+    high = packed >> 4
+    unsigned = torch.stack((low, high), dim=-1).reshape(*packed.shape[:-1], -1)[..., :input_size].to(torch.int16)
+    signed = torch.where(unsigned < 8, unsigned, unsigned - 16)
+    scale = _from_bf16_bits(scale_bits)
+    return signed.to(torch.bfloat16) * scale[..., None]
+
+
+class QuantizedLoRAWeight(nn.Module):
+    """Frozen packed-int4 weight plus trainable fp32 LoRA factors."""
+
+    def __init__(self, weight: torch.Tensor, *, rank: int, alpha: float, seed: int = 0,
+                 initialization_scale: float | None = None) -> None:
+        super().__init__()
+        out_f, in_f = weight.shape[-2:]
+        if rank <= 0 or rank > min(out_f, in_f):
+            raise ValueError("adapter rank must fit both linear dimensions")
+        if alpha <= 0:
+            raise ValueError("adapter alpha must be positive")
+        packed, scales = pack_int4_rows(weight.detach())
+        self.register_buffer("packed_weight", packed)
+        self.register_buffer("scale_bits", scales)
+        g = torch.Generator().manual_seed(seed)
+        scale = in_f ** -0.5 if initialization_scale is None else initialization_scale
+        self.lora_a = nn.Parameter(scale * torch.randn(*weight.shape[:-2], rank, in_f, generator=g))
+        self.lora_b = nn.Parameter(torch.zeros(*weight.shape[:-2], out_f, rank))
+        self.input_size, self.output_size, self.rank, self.alpha = in_f, out_f, rank, float(alpha)
+        self.shape = tuple(weight.shape)
+
+    def base_weight(self) -> torch.Tensor:
+        return unpack_int4_rows(self.packed_weight, self.scale_bits, self.input_size)
+
+    def merged_weight(self) -> torch.Tensor:
+        return self.base_weight().float() + (self.lora_b @ self.lora_a) * (self.alpha / self.rank)
+
+    def linear(self, x: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
+        dtype = x.dtype
+        out = torch.nn.functional.linear(x, self.base_weight().to(dtype))
+        hidden = torch.nn.functional.linear(x, self.lora_a.to(dtype))
+        out = out + torch.nn.functional.linear(hidden, self.lora_b.to(dtype)) * (self.alpha / self.rank)
+        if bias is not None:
+            out = out + bias.to(dtype)
+        return out
+
+
+def linear(x: torch.Tensor, weight, bias: torch.Tensor | None = None) -> torch.Tensor:
+    """``x W^T + b`` for a plain weight or a :class:`QuantizedLoRAWeight`."""
+
+    if isinstance(weight, QuantizedLoRAWeight):
+        return weight.linear(x, bias)
+    return torch.nn.functional.linear(x, weight.to(x.dtype), None if bias is None else bias.to(x.dtype))
+
+
+def apply_quantized_lora(model: nn.Module, *, rank: int, alpha: float, seed: int = 0, target_pattern: str = ".*",
+                         initialization_scale: float | None = None) -> nn.Module:
+    """Quantize matching 2-D ``*_weight`` / ``weight`` parameters and freeze everything else."""
+
+    pattern = re.compile(target_pattern)
+    targets = []
+    for mod_name, module in model.named_modules():
+        for attr, p in list(module._parameters.items()):
+            if p is None or p.ndim != 2 or not (attr == "weight" or attr.endswith("_weight")):
+                continue
+            full = f"{mod_name}.{attr}" if mod_name else attr
+            if "embedding" in full or full.startswith("embeddings.") or ".word" in full:
+                continue
+            if pattern.fullmatch(full) or pattern.search(full):
+                targets.append((module, attr, full))
+    if not targets:
+        raise ValueError(f"no linear weights match adapter target_pattern {target_pattern!r}")
+    for p in model.parameters():
+        p.requires_grad_(False)
+    for i, (module, attr, _) in enumerate(targets):
+        weight = module._parameters.pop(attr)
+        adapter = QuantizedLoRAWeight(weight, rank=rank, alpha=alpha, seed=seed + i,
+                                      initialization_scale=initialization_scale)
+        module.add_module(attr, adapter)
+    return model
+
+
+def merge_quantized_lora(model: nn.Module) -> nn.Module:
+    """Replace every adapter by its merged fp32 weight (a plain parameter)."""
+
+    for module in list(model.modules()):
+        for name, child in list(module._modules.items()):
+            if isinstance(child, QuantizedLoRAWeight):
+                del module._modules[name]
+                module.register_parameter(name, nn.Parameter(child.merged_weight().detach().float()))
+    return model
+
+
+def lora_parameter_filter(model: nn.Module) -> dict[str, bool]:
+    """Trainability of every parameter: only LoRA factors train once adapted."""
+
+    return {name: ("lora_a" in name or "lora_b" in name) for name, _ in model.named_parameters()}
+
+
+__all__ = ["QuantizedLoRAWeight", "apply_quantized_lora", "linear", "lora_parameter_filter", "merge_quantized_lora",
+           "pack_int4_rows", "unpack_int4_rows"]

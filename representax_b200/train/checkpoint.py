@@ -152,7 +152,6 @@ class CheckpointManager:
                  scientific: str = "", data: str = "", rank: int = 0, world_size: int = 1,
                  metric_mode: str = "min") -> None:
         self.root = Path(root)
-        self.root.mkdir(parents=True, exist_ok=True)
         self.keep = keep
         self.keep_best = keep_best
         self.asynchronous = asynchronous
@@ -207,6 +206,7 @@ class CheckpointManager:
             self.wait()
 
     def _write(self, iteration: int, snapshot: dict[str, torch.Tensor], progress: dict, metric, best) -> None:
+        self.root.mkdir(parents=True, exist_ok=True)
         directory = self._dir(iteration)
         if self.rank == 0 and directory.exists():
             shutil.rmtree(directory)
@@ -240,6 +240,8 @@ class CheckpointManager:
 
     def _retain(self) -> None:
         complete = []
+        if not self.root.is_dir():
+            return
         for d in sorted(self.root.iterdir()):
             if d.is_dir() and (d / COMPLETE_MARKER).is_file():
                 complete.append(d)
