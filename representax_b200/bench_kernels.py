@@ -49,6 +49,9 @@ class Timer:
         return times[len(times) // 2]
 
 
+CASE_FILTER = None
+
+
 def bench_gemm(timer, hbm, flops_peak, tag, report):
     from representax_b200.ops import gemm as G
 
@@ -59,6 +62,8 @@ def bench_gemm(timer, hbm, flops_peak, tag, report):
         ("square_8k", 8192, 8192, 8192),
     ]
     for name, m, n, k in shapes:
+        if CASE_FILTER and CASE_FILTER not in name:
+            continue
         a = torch.randn(m, k, device="cuda").to(torch.bfloat16)
         b = torch.randn(n, k, device="cuda").to(torch.bfloat16)
         c = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
@@ -69,6 +74,8 @@ def bench_gemm(timer, hbm, flops_peak, tag, report):
                 "tflops": fl / t / 1e12, f"frac_of_{tag}_bf16": fl / t / flops_peak,
                 "cublas_ms": t_ref * 1e3})
     for name, t_, n, k in [("qkv", 18432, 2304, 768), ("ffn2", 18432, 768, 3072)]:
+        if CASE_FILTER:
+            continue
         dy = torch.randn(t_, n, device="cuda").to(torch.bfloat16)
         w = torch.randn(n, k, device="cuda").to(torch.bfloat16)
         x = torch.randn(t_, k, device="cuda").to(torch.bfloat16)
@@ -141,7 +148,10 @@ def main(argv=None):
     parser = argparse.ArgumentParser()
     parser.add_argument("--only", default="gemm,attention,norm")
     parser.add_argument("--out", default=None)
+    parser.add_argument("--case", default=None, help="run only GEMM cases whose name contains this")
     args = parser.parse_args(argv)
+    global CASE_FILTER
+    CASE_FILTER = args.case
     hbm, flops_peak, tag = _peaks()
     timer = Timer()
     rows = []

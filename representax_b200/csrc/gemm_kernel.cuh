@@ -13,8 +13,9 @@
 //   warp 1      owns TMEM (2 x BN fp32 columns = a double-buffered 128xBN
 //               accumulator) and one thread issues tcgen05.mma (M=128, K=16)
 //               and tcgen05.commit.
-//   warps 2-5   epilogue: tcgen05.ld of their 32-lane TMEM quadrant (one
-//               output row per thread), fused bias / GELU / GELU-backward /
+//   warps 2-9   epilogue: two warps per 32-lane TMEM quadrant, each taking half
+//               of the tile's columns; tcgen05.ld gives one output row per
+//               thread; fused bias / GELU / GELU-backward /
 //               residual, bf16 or fp32 stores, fp32 accumulate or split-K
 //               atomic reduction.
 // The double-buffered accumulator lets the epilogue of tile i overlap the
@@ -32,7 +33,8 @@ namespace gemm {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int kThreads = 192;
+constexpr int kEpilogueWarps = 8;  // two per TMEM lane quadrant, each owning half the columns
+constexpr int kThreads = 64 + 32 * kEpilogueWarps;
 
 enum Epi : int { EPI_BIAS = 1, EPI_GELU = 2, EPI_DGELU = 4, EPI_RESID = 8 };
 enum Out : int { OUT_BF16 = 0, OUT_F32 = 1, OUT_F32_ACC = 2, OUT_F32_ATOMIC = 3 };
@@ -220,7 +222,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 128);
+      mbar_init(&tempty[a], 32 * kEpilogueWarps);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -350,6 +352,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ epilogue
     const int quad = warp & 3;  // TMEM lanes this warp may access: [32*quad, 32*quad+32)
     const int row_local = quad * 32 + lane;
+    constexpr int kChunksPerWarp = BN / 32 / (kEpilogueWarps / 4);
+    const int chunk0 = ((warp - 2) / 4) * kChunksPerWarp;  // this warp's column half
     int local = 0;
     for (int u = blockIdx.x; u < p.num_units; u += gridDim.x, ++local) {
       int m0, n_t, kb0, kb1;
@@ -369,7 +373,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t t_row =
           tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = chunk0; c < chunk0 + kChunksPerWarp; ++c) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(t_row + c * 32, r);
         tmem_ld_wait();

@@ -132,8 +132,12 @@ __global__ void __launch_bounds__(kWarps * 32)
 // dgamma += sum dy*xhat, dbeta += sum dy, dbias_prev += sum dx.
 // When `word_grad` is non-null, x is rebuilt from the embedding tables and dx
 // is scattered into the fp32 table gradients instead of being stored.
+// Parameter-gradient partials (dgamma, dbeta, dbias_prev) live in shared
+// memory, one [3][H] region per warp; each lane only touches the columns it
+// owns, so no atomics are needed until the final per-CTA reduction. Keeping
+// them out of registers lets three 8-warp CTAs share an SM.
 template <int MAXV, bool RMS>
-__global__ void __launch_bounds__(kWarps * 32)
+__global__ void __launch_bounds__(kWarps * 32, (MAXV <= 4 ? 3 : 1))
     norm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
                     const float* __restrict__ mean_in, const float* __restrict__ rstd_in,
                     const __nv_bfloat16* __restrict__ gamma, __nv_bfloat16* __restrict__ dx,
@@ -145,22 +149,15 @@ __global__ void __launch_bounds__(kWarps * 32)
                     const __nv_bfloat16* __restrict__ pos, const __nv_bfloat16* __restrict__ type,
                     float* __restrict__ word_grad, float* __restrict__ pos_grad,
                     float* __restrict__ type_grad, int pad_id) {
-  extern __shared__ float red[];  // [3][kWarps][H] partial sums
+  extern __shared__ float red[];  // [kWarps][3][H] partial sums
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int nv = H >> 3;
-  // Per-lane parameter-gradient partials for the columns this lane owns.
-  float pg[MAXV][8], pb[MAXV][8], pd[MAXV][8];
-#pragma unroll
-  for (int i = 0; i < MAXV; ++i)
-#pragma unroll
-    for (int j = 0; j < 8; ++j) pg[i][j] = pb[i][j] = pd[i][j] = 0.f;
-  uint4 gpk[MAXV];
-#pragma unroll
-  for (int i = 0; i < MAXV; ++i) {
-    const int c = lane + 32 * i;
-    gpk[i] = c < nv ? reinterpret_cast<const uint4*>(gamma)[c] : make_uint4(0, 0, 0, 0);
-  }
+  float* pg = red + static_cast<size_t>(warp) * 3 * H;
+  float* pb = pg + H;
+  float* pd = pb + H;
+  for (int i = lane; i < 3 * H; i += 32) pg[i] = 0.f;
+  __syncwarp();
 
   for (int row = blockIdx.x * kWarps + warp; row < rows; row += gridDim.x * kWarps) {
     const float mean = RMS ? 0.f : mean_in[row];
@@ -185,16 +182,23 @@ __global__ void __launch_bounds__(kWarps * 32)
         dpk[i] = reinterpret_cast<const uint4*>(dy + static_cast<int64_t>(row) * H)[c];
         float d[8], g[8];
         unpack8(dpk[i], d);
-        unpack8(gpk[i], g);
+        unpack8(reinterpret_cast<const uint4*>(gamma)[c], g);
+        float4* gp = reinterpret_cast<float4*>(pg + c * 8);
+        float4* bp = reinterpret_cast<float4*>(pb + c * 8);
+        float4 g0 = gp[0], g1 = gp[1], b0 = bp[0], b1 = bp[1];
+        float xh[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const float xh = (xv[i][j] - mean) * rstd;
+          xh[j] = (xv[i][j] - mean) * rstd;
           const float dyg = d[j] * g[j];
           s1 += dyg;
-          s2 += dyg * xh;
-          pg[i][j] += d[j] * xh;
-          pb[i][j] += d[j];
+          s2 += dyg * xh[j];
         }
+        g0.x += d[0] * xh[0]; g0.y += d[1] * xh[1]; g0.z += d[2] * xh[2]; g0.w += d[3] * xh[3];
+        g1.x += d[4] * xh[4]; g1.y += d[5] * xh[5]; g1.z += d[6] * xh[6]; g1.w += d[7] * xh[7];
+        b0.x += d[0]; b0.y += d[1]; b0.z += d[2]; b0.w += d[3];
+        b1.x += d[4]; b1.y += d[5]; b1.z += d[6]; b1.w += d[7];
+        gp[0] = g0; gp[1] = g1; bp[0] = b0; bp[1] = b1;
       }
     }
     s1 = warp_sum(s1) / H;
@@ -205,12 +209,18 @@ __global__ void __launch_bounds__(kWarps * 32)
       if (c < nv) {
         float d[8], g[8], o[8];
         unpack8(dpk[i], d);
-        unpack8(gpk[i], g);
+        unpack8(reinterpret_cast<const uint4*>(gamma)[c], g);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const float xh = (xv[i][j] - mean) * rstd;
           o[j] = rstd * (d[j] * g[j] - (RMS ? 0.f : s1) - xh * s2);
-          pd[i][j] += o[j];
+        }
+        if (dbias_prev != nullptr) {
+          float4* dp = reinterpret_cast<float4*>(pd + c * 8);
+          float4 a0 = dp[0], a1 = dp[1];
+          a0.x += o[0]; a0.y += o[1]; a0.z += o[2]; a0.w += o[3];
+          a1.x += o[4]; a1.y += o[5]; a1.z += o[6]; a1.w += o[7];
+          dp[0] = a0; dp[1] = a1;
         }
         if (word_grad != nullptr) {
           const int id = ids[row];
@@ -230,30 +240,15 @@ __global__ void __launch_bounds__(kWarps * 32)
       }
     }
   }
-  // CTA reduction of the parameter-gradient partials.
-  float* rg = red;
-  float* rb = red + kWarps * H;
-  float* rd = red + 2 * kWarps * H;
-#pragma unroll
-  for (int i = 0; i < MAXV; ++i) {
-    const int c = lane + 32 * i;
-    if (c < nv) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        rg[warp * H + c * 8 + j] = pg[i][j];
-        rb[warp * H + c * 8 + j] = pb[i][j];
-        rd[warp * H + c * 8 + j] = pd[i][j];
-      }
-    }
-  }
   __syncthreads();
   for (int col = threadIdx.x; col < H; col += blockDim.x) {
     float a = 0.f, b = 0.f, d = 0.f;
 #pragma unroll
     for (int w = 0; w < kWarps; ++w) {
-      a += rg[w * H + col];
-      b += rb[w * H + col];
-      d += rd[w * H + col];
+      const float* base = red + static_cast<size_t>(w) * 3 * H;
+      a += base[col];
+      b += base[H + col];
+      d += base[2 * H + col];
     }
     if (dgamma) atomicAdd(dgamma + col, a);
     if (dbeta && !RMS) atomicAdd(dbeta + col, b);
@@ -363,7 +358,7 @@ void norm_backward(const at::Tensor& dy, const at::Tensor& x, const c10::optiona
   if (rows == 0) return;
   c10::cuda::CUDAGuard guard(x.get_device());
   const int sms = num_sms(x.get_device());
-  const int grid = static_cast<int>(std::min<int64_t>((rows + norm::kWarps - 1) / norm::kWarps, 2 * sms));
+  const int grid = static_cast<int>(std::min<int64_t>((rows + norm::kWarps - 1) / norm::kWarps, 3 * sms));
   const size_t smem = 3 * norm::kWarps * H * sizeof(float);
   auto st = at::cuda::getCurrentCUDAStream().stream();
   auto launch = rms ? norm::launch_bwd<true> : norm::launch_bwd<false>;
@@ -416,7 +411,7 @@ void embed_ln_backward(const at::Tensor& dy, const at::Tensor& ids, const at::Te
   if (rows == 0) return;
   c10::cuda::CUDAGuard guard(word.get_device());
   const int sms = num_sms(word.get_device());
-  const int grid = static_cast<int>(std::min<int64_t>((rows + norm::kWarps - 1) / norm::kWarps, 2 * sms));
+  const int grid = static_cast<int>(std::min<int64_t>((rows + norm::kWarps - 1) / norm::kWarps, 3 * sms));
   const size_t smem = 3 * norm::kWarps * H * sizeof(float);
   norm::launch_bwd<false>(
       maxv_for(H), grid, smem, at::cuda::getCurrentCUDAStream().stream(),

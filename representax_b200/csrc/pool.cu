@@ -135,22 +135,40 @@ __global__ void __launch_bounds__(kThreads)
 }
 
 // out[col] += sum_rows x[row, col]  (bf16 input, fp32 accumulator).
-__global__ void colsum_kernel(const __nv_bfloat16* __restrict__ x, int64_t ld, int rows, int cols,
-                              float* __restrict__ out) {
-  const int pair = blockIdx.x * blockDim.x + threadIdx.x;
-  if (pair * 2 >= cols) return;
-  const int rows_per = (rows + gridDim.y - 1) / gridDim.y;
-  const int r0 = blockIdx.y * rows_per;
-  const int r1 = min(rows, r0 + rows_per);
-  float a = 0.f, b = 0.f;
-  for (int r = r0; r < r1; ++r) {
-    const float2 f = __bfloat1622float2(
-        reinterpret_cast<const __nv_bfloat162*>(x + static_cast<int64_t>(r) * ld)[pair]);
-    a += f.x;
-    b += f.y;
+// Each thread owns one 16-byte column chunk (8 columns) and walks a strided
+// set of rows with vector loads, so a warp reads whole row segments; the CTA
+// then reduces its row groups in shared memory and adds one atomic per column.
+constexpr int kColsumThreads = 256;
+__global__ void __launch_bounds__(kColsumThreads)
+    colsum_kernel(const __nv_bfloat16* __restrict__ x, int64_t ld, int rows, int cols,
+                  float* __restrict__ out) {
+  extern __shared__ float part[];  // [groups][cols]
+  const int chunks = cols >> 3;
+  const int groups = kColsumThreads / chunks;  // row groups per CTA (>= 1)
+  const int tid = threadIdx.x;
+  const int c = tid % chunks;
+  const int grp = tid / chunks;
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (grp < groups) {
+    for (int r = blockIdx.x * groups + grp; r < rows; r += gridDim.x * groups) {
+      const uint4 w = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(r) * ld)[c];
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(h[j]);
+        acc[2 * j] += f.x;
+        acc[2 * j + 1] += f.y;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) part[grp * cols + c * 8 + j] = acc[j];
   }
-  atomicAdd(out + 2 * pair, a);
-  atomicAdd(out + 2 * pair + 1, b);
+  __syncthreads();
+  for (int col = tid; col < cols; col += kColsumThreads) {
+    float s = 0.f;
+    for (int g = 0; g < groups; ++g) s += part[g * cols + col];
+    atomicAdd(out + col, s);
+  }
 }
 
 __global__ void cast_bf16_kernel(const float* __restrict__ src, __nv_bfloat16* __restrict__ dst,
@@ -216,19 +234,32 @@ void pool_backward(const at::Tensor& dout, const at::Tensor& out, const at::Tens
 void colsum_accumulate(const at::Tensor& x, at::Tensor& out) {
   check_bf16(x, "x");
   check_f32(out, "out");
-  RX_CHECK(x.dim() == 2 && x.stride(1) == 1 && x.size(1) % 2 == 0 && x.stride(0) % 2 == 0,
-           "colsum needs a [rows, even cols] matrix");
+  RX_CHECK(x.dim() == 2 && x.stride(1) == 1 && x.size(1) % 8 == 0 && x.stride(0) % 8 == 0 &&
+               reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0,
+           "colsum needs a 16-byte aligned [rows, cols % 8 == 0] matrix");
   RX_CHECK(out.numel() == x.size(1) && out.is_contiguous(), "colsum output must be [cols]");
   const int rows = static_cast<int>(x.size(0)), cols = static_cast<int>(x.size(1));
   if (rows == 0) return;
+  constexpr int kMaxCols = pool::kColsumThreads * 8;
+  if (cols > kMaxCols) {  // wide matrices: independent column blocks
+    for (int c0 = 0; c0 < cols; c0 += kMaxCols) {
+      const int c1 = std::min(cols, c0 + kMaxCols);
+      at::Tensor xs = x.narrow(1, c0, c1 - c0);
+      at::Tensor os = out.narrow(0, c0, c1 - c0);
+      colsum_accumulate(xs, os);
+    }
+    return;
+  }
   c10::cuda::CUDAGuard guard(x.get_device());
-  const int threads = 128;
-  const int gx = (cols / 2 + threads - 1) / threads;
+  const int groups = pool::kColsumThreads / (cols / 8);
+  const size_t smem = static_cast<size_t>(groups) * cols * sizeof(float);
   const int sms = num_sms(x.get_device());
-  const int gy = std::max(1, std::min((rows + 63) / 64, (4 * sms + gx - 1) / gx));
-  pool::colsum_kernel<<<dim3(gx, gy), threads, 0, at::cuda::getCurrentCUDAStream().stream()>>>(
-      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0), rows, cols,
-      out.data_ptr<float>());
+  const int grid = std::max(1, std::min((rows + groups - 1) / groups, 2 * sms));
+  auto kern = pool::colsum_kernel;
+  if (smem > 48 * 1024)
+    RX_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+  kern<<<grid, pool::kColsumThreads, smem, at::cuda::getCurrentCUDAStream().stream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0), rows, cols, out.data_ptr<float>());
   RX_CUDA_CHECK(cudaGetLastError());
 }
 

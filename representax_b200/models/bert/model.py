@@ -133,10 +133,13 @@ class BertEncoder(nn.Module):
         states = [h] if all_layers else None
         for layer in self.layers:
             s1 = Fn.attention_block(h, layer.qkv_weight, layer.qkv_bias, layer.out_weight, layer.out_bias,
-                                    packed, heads=cfg.num_attention_heads)
-            h1 = Fn.layer_norm(s1, layer.attn_norm_weight, layer.attn_norm_bias, cfg.norm_epsilon)
-            s2 = Fn.mlp_block(h1, layer.ffn_in_weight, layer.ffn_in_bias, layer.ffn_out_weight, layer.ffn_out_bias)
-            h = Fn.layer_norm(s2, layer.out_norm_weight, layer.out_norm_bias, cfg.norm_epsilon)
+                                    packed, heads=cfg.num_attention_heads, out_bias_grad_fused=True)
+            h1 = Fn.layer_norm(s1, layer.attn_norm_weight, layer.attn_norm_bias, cfg.norm_epsilon,
+                               producer_bias=layer.out_bias)
+            s2 = Fn.mlp_block(h1, layer.ffn_in_weight, layer.ffn_in_bias, layer.ffn_out_weight, layer.ffn_out_bias,
+                              out_bias_grad_fused=True)
+            h = Fn.layer_norm(s2, layer.out_norm_weight, layer.out_norm_bias, cfg.norm_epsilon,
+                              producer_bias=layer.ffn_out_bias)
             if all_layers:
                 states.append(h)
         return (h, packed) if not all_layers else (states, packed)

@@ -77,7 +77,8 @@ def _colsum_into(x: torch.Tensor, sink: _GradSink) -> None:
 
 class AttentionBlockFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, w_qkv, b_qkv, w_o, b_o, cu_seqlens, max_len, heads, kv_heads, causal, window):
+    def forward(ctx, x, w_qkv, b_qkv, w_o, b_o, cu_seqlens, max_len, heads, kv_heads, causal, window,
+                out_bias_grad_fused=False):
         C = ext()
         T, H = x.shape
         head_dim = 64
@@ -93,6 +94,7 @@ class AttentionBlockFn(torch.autograd.Function):
         s = G.linear_forward(a, wo, bo, residual=x)
         ctx.save_for_backward(x, qkv, a, lse, cu_seqlens, w_qkv, b_qkv, w_o, b_o)
         ctx.meta = (max_len, heads, kv_heads, causal, window, scale)
+        ctx.out_bias_grad_fused = out_bias_grad_fused
         return s
 
     @staticmethod
@@ -106,7 +108,8 @@ class AttentionBlockFn(torch.autograd.Function):
         g_wo, g_bo, g_wqkv, g_bqkv = _GradSink(w_o), _GradSink(b_o), _GradSink(w_qkv), _GradSink(b_qkv)
         if g_wo.wanted:
             G.linear_wgrad(ds, a, g_wo.buffer())
-        _colsum_into(ds, g_bo)
+        if not ctx.out_bias_grad_fused:
+            _colsum_into(ds, g_bo)
         da = G.linear_dgrad(ds, compute_view(w_o))
         dqkv = torch.empty_like(qkv)
         q, k, v = qkv[:, :qd], qkv[:, qd:qd + kd], qkv[:, qd + kd:]
@@ -118,18 +121,20 @@ class AttentionBlockFn(torch.autograd.Function):
             G.linear_wgrad(dqkv, x, g_wqkv.buffer())
         _colsum_into(dqkv, g_bqkv)
         dx = G.linear_dgrad(dqkv, compute_view(w_qkv), residual=ds)
-        return dx, g_wqkv.result(), g_bqkv.result(), g_wo.result(), g_bo.result(), None, None, None, None, None, None
+        return (dx, g_wqkv.result(), g_bqkv.result(), g_wo.result(), g_bo.result(), None, None, None, None, None,
+                None, None)
 
 
 class MlpBlockFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, w1, b1, w2, b2):
+    def forward(ctx, x, w1, b1, w2, b2, out_bias_grad_fused=False):
         T = x.shape[0]
         inter = w1.shape[0]
         z = torch.empty(T, inter, dtype=torch.bfloat16, device=x.device)
         g = G.linear_forward(x, compute_view(w1), compute_view(b1), gelu_preact=z)
         s = G.linear_forward(g, compute_view(w2), compute_view(b2), residual=x)
         ctx.save_for_backward(x, z, g, w1, b1, w2, b2)
+        ctx.out_bias_grad_fused = out_bias_grad_fused
         return s
 
     @staticmethod
@@ -139,18 +144,19 @@ class MlpBlockFn(torch.autograd.Function):
         s_w1, s_b1, s_w2, s_b2 = _GradSink(w1), _GradSink(b1), _GradSink(w2), _GradSink(b2)
         if s_w2.wanted:
             G.linear_wgrad(ds, g, s_w2.buffer())
-        _colsum_into(ds, s_b2)
+        if not ctx.out_bias_grad_fused:
+            _colsum_into(ds, s_b2)
         dz = G.linear_dgrad(ds, compute_view(w2), gelu_preact=z)
         if s_w1.wanted:
             G.linear_wgrad(dz, x, s_w1.buffer())
         _colsum_into(dz, s_b1)
         dx = G.linear_dgrad(dz, compute_view(w1), residual=ds)
-        return dx, s_w1.result(), s_b1.result(), s_w2.result(), s_b2.result()
+        return dx, s_w1.result(), s_b1.result(), s_w2.result(), s_b2.result(), None
 
 
 class LayerNormFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, s, gamma, beta, eps, rms):
+    def forward(ctx, s, gamma, beta, eps, rms, producer_bias=None):
         C = ext()
         rows = s.shape[0]
         y = torch.empty_like(s)
@@ -158,7 +164,9 @@ class LayerNormFn(torch.autograd.Function):
         rstd = torch.empty(rows, dtype=torch.float32, device=s.device)
         C.norm_forward(s, compute_view(gamma), None if beta is None else compute_view(beta), y, mean, rstd, eps, rms)
         ctx.save_for_backward(s, mean if mean is not None else torch.empty(0, device=s.device), rstd, gamma,
-                              beta if beta is not None else torch.empty(0, device=s.device))
+                              beta if beta is not None else torch.empty(0, device=s.device),
+                              producer_bias if producer_bias is not None else torch.empty(0, device=s.device))
+        ctx.has_producer_bias = producer_bias is not None
         ctx.rms = rms
         ctx.has_beta = beta is not None
         return y
@@ -166,15 +174,18 @@ class LayerNormFn(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dy):
         C = ext()
-        s, mean, rstd, gamma, beta = ctx.saved_tensors
+        s, mean, rstd, gamma, beta, pbias = ctx.saved_tensors
         dy = dy.contiguous()
         sg = _GradSink(gamma)
         sb = _GradSink(beta) if ctx.has_beta else None
+        sp = _GradSink(pbias) if ctx.has_producer_bias else None
         dx = torch.empty_like(s)
         C.norm_backward(dy, s, None if ctx.rms else mean, rstd, compute_view(gamma), dx,
                         sg.buffer() if sg.wanted else None,
-                        sb.buffer() if (sb is not None and sb.wanted) else None, None, ctx.rms)
-        return dx, sg.result(), (sb.result() if sb is not None else None), None, None
+                        sb.buffer() if (sb is not None and sb.wanted) else None,
+                        sp.buffer() if (sp is not None and sp.wanted) else None, ctx.rms)
+        return (dx, sg.result(), (sb.result() if sb is not None else None), None, None,
+                sp.result() if sp is not None else None)
 
 
 class EmbedLayerNormFn(torch.autograd.Function):
@@ -230,17 +241,24 @@ class PoolFn(torch.autograd.Function):
         return dh, None, None, None
 
 
-def attention_block(x, w_qkv, b_qkv, w_o, b_o, packed: Packed, *, heads, kv_heads=None, causal=False, window=-1):
+def attention_block(x, w_qkv, b_qkv, w_o, b_o, packed: Packed, *, heads, kv_heads=None, causal=False, window=-1,
+                    out_bias_grad_fused: bool = False):
+    """``out_bias_grad_fused``: the following layer_norm was given ``producer_bias=b_o``
+    and reduces its gradient in its own backward kernel."""
+
     return AttentionBlockFn.apply(x, w_qkv, b_qkv, w_o, b_o, packed.cu_seqlens, packed.max_len, heads,
-                                  kv_heads or heads, causal, window)
+                                  kv_heads or heads, causal, window, out_bias_grad_fused)
 
 
-def mlp_block(x, w1, b1, w2, b2):
-    return MlpBlockFn.apply(x, w1, b1, w2, b2)
+def mlp_block(x, w1, b1, w2, b2, *, out_bias_grad_fused: bool = False):
+    return MlpBlockFn.apply(x, w1, b1, w2, b2, out_bias_grad_fused)
 
 
-def layer_norm(s, gamma, beta, eps: float, rms: bool = False):
-    return LayerNormFn.apply(s, gamma, beta, eps, rms)
+def layer_norm(s, gamma, beta, eps: float, rms: bool = False, *, producer_bias=None):
+    """``producer_bias``: bias of the linear layer that produced ``s``; its
+    gradient (the column sum of ds) is accumulated by the norm's backward."""
+
+    return LayerNormFn.apply(s, gamma, beta, eps, rms, producer_bias)
 
 
 def embed_layer_norm(ids, pos_ids, type_ids, word, pos, typ, gamma, beta, eps: float, pad_id: int):

@@ -285,10 +285,11 @@ def test_pool(C, mode):
 
 
 def test_colsum_and_cast(C):
-    x = _rand(1000, 768)
-    out = torch.ones(768, device=_dev())
-    C.colsum_accumulate(x, out)
-    _close(out, 1 + x.float().sum(0), rtol=1e-4, atol=1e-3, what="colsum")
+    for rows, cols in ((1000, 768), (37, 2304), (5000, 3072)):
+        x = _rand(rows, cols)
+        out = torch.ones(cols, device=_dev())
+        C.colsum_accumulate(x, out)
+        _close(out, 1 + x.float().sum(0), rtol=1e-4, atol=2e-3, what=f"colsum {cols}")
     src = torch.randn(1001, device=_dev())
     dst = torch.empty(1001, dtype=torch.bfloat16, device=_dev())
     C.cast_bf16(src, dst)
