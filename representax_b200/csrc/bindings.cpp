@@ -7,7 +7,7 @@ void gemm_tcgen05(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool 
                   const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& aux_in,
                   const c10::optional<at::Tensor>& aux_out,
                   const c10::optional<at::Tensor>& residual, const at::Tensor& status,
-                  int64_t split_k);
+                  int64_t split_k, int64_t variant);
 void norm_forward(const at::Tensor& x, const at::Tensor& gamma, const c10::optional<at::Tensor>& beta,
                   at::Tensor& y, const c10::optional<at::Tensor>& mean, at::Tensor& rstd,
                   double eps, bool rms);

@@ -14,7 +14,7 @@ void gemm_tcgen05(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool 
                   const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& aux_in,
                   const c10::optional<at::Tensor>& aux_out,
                   const c10::optional<at::Tensor>& residual, const at::Tensor& status,
-                  int64_t split_k) {
+                  int64_t split_k, int64_t variant) {
   using namespace gemm;
   check_bf16(A, "A");
   check_bf16(B, "B");
@@ -80,16 +80,21 @@ void gemm_tcgen05(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool 
     p.residual = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());
     p.ld_res = residual->stride(0);
   }
+  // variant: 1 = one CTA per 128x256 tile, 2 = CTA pair per 256x256 tile,
+  // 0 = pair whenever there are at least 256 rows.
+  const bool pair = variant == 2 || (variant == 0 && M >= 256);
   constexpr int BN = 256;
-  p.m_tiles = static_cast<int>((M + BM - 1) / BM);
+  const int tile_m = pair ? 2 * BM : BM;
+  p.m_tiles = static_cast<int>((M + tile_m - 1) / tile_m);
   p.n_tiles = static_cast<int>((N + BN - 1) / BN);
   p.kb_total = static_cast<int>((K + BK - 1) / BK);
   const int device = C.get_device();
   const int sms = num_sms(device);
+  const int workers = pair ? sms / 2 : sms;
   int splits = 1;
   const int tiles = p.m_tiles * p.n_tiles;
-  if (split_k == 0 && out_mode == OUT_F32_ATOMIC && tiles < sms) {
-    splits = std::max(1, std::min(p.kb_total / 4, (sms + tiles - 1) / tiles));
+  if (split_k == 0 && out_mode == OUT_F32_ATOMIC && tiles < workers) {
+    splits = std::max(1, std::min(p.kb_total / 4, (workers + tiles - 1) / tiles));
   } else if (split_k > 1) {
     RX_CHECK(out_mode == OUT_F32_ATOMIC, "split-K needs the atomic fp32 output mode");
     splits = static_cast<int>(std::min<int64_t>(split_k, p.kb_total));
@@ -98,17 +103,20 @@ void gemm_tcgen05(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool 
   p.splits = (p.kb_total + p.kb_per_split - 1) / p.kb_per_split;
   p.num_units = tiles * p.splits;
   LaunchFn fn = nullptr;
-  if (!a_mn && !b_mn) fn = pick_forward(static_cast<int>(epi), static_cast<int>(out_mode));
-  else if (!a_mn && b_mn) fn = pick_dgrad(static_cast<int>(epi), static_cast<int>(out_mode));
-  else if (a_mn && b_mn) fn = pick_wgrad(static_cast<int>(epi), static_cast<int>(out_mode));
+  const int e = static_cast<int>(epi), o = static_cast<int>(out_mode);
+  if (!a_mn && !b_mn) fn = pair ? pick_forward_pair(e, o) : pick_forward(e, o);
+  else if (!a_mn && b_mn) fn = pair ? pick_dgrad_pair(e, o) : pick_dgrad(e, o);
+  else if (a_mn && b_mn) fn = pair ? pick_wgrad_pair(e, o) : pick_wgrad(e, o);
   RX_CHECK(fn != nullptr, "unsupported gemm variant a_mn=", a_mn, " b_mn=", b_mn, " epi=", epi,
            " out=", out_mode);
   // A: K-major boxes [128 rows x 64 k]; MN-major boxes [64 k rows x 64 m].
+  // B: K-major boxes [BN rows x 64 k] (half of the pair tile per CTA);
+  //    MN-major boxes [64 k rows x 64 n].
   CUtensorMap ta = a_mn ? make_tmap_2d_bf16(A.data_ptr(), K, M, A.stride(0), 64, 64)
                         : make_tmap_2d_bf16(A.data_ptr(), M, K, A.stride(0), 64, BM);
   CUtensorMap tb = b_mn ? make_tmap_2d_bf16(B.data_ptr(), K, N, B.stride(0), 64, 64)
-                        : make_tmap_2d_bf16(B.data_ptr(), N, K, B.stride(0), 64, BN);
-  const int grid = std::min(p.num_units, sms);
+                        : make_tmap_2d_bf16(B.data_ptr(), N, K, B.stride(0), 64, pair ? BN / 2 : BN);
+  const int grid = pair ? 2 * std::min(p.num_units, workers) : std::min(p.num_units, sms);
   c10::cuda::CUDAGuard guard(device);
   fn(ta, tb, p, grid, at::cuda::getCurrentCUDAStream(device).stream(), device);
 }

@@ -22,5 +22,21 @@ LaunchFn pick_dgrad(int epi, int out) {
   }
 }
 
+LaunchFn pick_dgrad_pair(int epi, int out) {
+  if (epi == EPI_RESID && out == OUT_BF16) return launch_pair<false, true, EPI_RESID, OUT_BF16>;
+  if (epi != 0 && epi != EPI_DGELU) return nullptr;
+  const bool dgelu = epi == EPI_DGELU;
+  switch (out) {
+    case OUT_BF16:
+      return dgelu ? launch_pair<false, true, EPI_DGELU, OUT_BF16> : launch_pair<false, true, 0, OUT_BF16>;
+    case OUT_F32:
+      return dgelu ? launch_pair<false, true, EPI_DGELU, OUT_F32> : launch_pair<false, true, 0, OUT_F32>;
+    case OUT_F32_ACC:
+      return dgelu ? nullptr : launch_pair<false, true, 0, OUT_F32_ACC>;
+    default:
+      return nullptr;
+  }
+}
+
 }  // namespace gemm
 }  // namespace rx

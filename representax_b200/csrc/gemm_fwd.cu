@@ -24,5 +24,24 @@ LaunchFn pick_forward(int epi, int out) {
   return nullptr;
 }
 
+template <int OUT>
+static LaunchFn pick_epi_pair(int epi) {
+  switch (epi) {
+    case 0: return launch_pair<false, false, 0, OUT>;
+    case EPI_BIAS: return launch_pair<false, false, EPI_BIAS, OUT>;
+    case EPI_BIAS | EPI_GELU: return launch_pair<false, false, EPI_BIAS | EPI_GELU, OUT>;
+    case EPI_BIAS | EPI_RESID: return launch_pair<false, false, EPI_BIAS | EPI_RESID, OUT>;
+    case EPI_RESID: return launch_pair<false, false, EPI_RESID, OUT>;
+    default: return nullptr;
+  }
+}
+
+LaunchFn pick_forward_pair(int epi, int out) {
+  if (out == OUT_BF16) return pick_epi_pair<OUT_BF16>(epi);
+  if (out == OUT_F32) return pick_epi_pair<OUT_F32>(epi);
+  if (out == OUT_F32_ACC && epi == 0) return launch_pair<false, false, 0, OUT_F32_ACC>;
+  return nullptr;
+}
+
 }  // namespace gemm
 }  // namespace rx

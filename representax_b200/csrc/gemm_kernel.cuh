@@ -406,6 +406,271 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int g
   RX_CUDA_CHECK(cudaGetLastError());
 }
 
+// ============================================================================
+// CTA-pair variant (cta_group::2). A cluster of two CTAs owns a 256 x 256
+// output tile: CTA r loads A rows [128r, 128r + 128) and B rows
+// [128r, 128r + 128) of the tile into its own shared memory; the even CTA
+// issues one M=256, N=256 tcgen05.mma per K=16 step that reads both CTAs'
+// operands and leaves each CTA's 128 accumulator rows in its own TMEM. Each
+// CTA thus moves half the B tile per stage (32 KB instead of 48 KB), which
+// leaves room for 6 stages.
+//
+// Barriers: every stage's TMA loads (from both CTAs) complete on the even
+// CTA's full barrier; the MMA completion is committed to the empty / TMEM-full
+// / drain barriers of both CTAs; both CTAs' epilogue warps arrive on the even
+// CTA's TMEM-empty barrier.
+// ============================================================================
+constexpr int kPairStages = 6;
+
+template <bool A_MN, bool B_MN, int EPI, int OUT>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const Params p) {
+  constexpr int BN = 256;           // pair tile columns
+  constexpr int HALF_N = BN / 2;    // B rows loaded by each CTA
+  constexpr int STAGES = kPairStages;
+  constexpr int A_BYTES = BM * BK * 2;
+  constexpr int B_BYTES = HALF_N * BK * 2;
+  constexpr uint32_t TMEM_COLS = 2 * BN;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = base;
+  uint8_t* sB = base + STAGES * A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const uint32_t rank = cluster_ctarank();  // 0: issues the MMAs
+  const bool leader = rank == 0;
+  const int cluster = blockIdx.x >> 1;
+  const int clusters = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 2 * kEpilogueWarps);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_map(&tmA);
+    tma_prefetch_map(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barriers of both CTAs initialised before any remote use
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  auto decode = [&](int u, int& m0, int& n0, int& kb0, int& kb1) {
+    const int n_t = u % p.n_tiles;
+    const int t = u / p.n_tiles;
+    const int m_t = t % p.m_tiles;
+    const int split = t / p.m_tiles;
+    m0 = m_t * (2 * BM);
+    n0 = n_t * BN;
+    kb0 = split * p.kb_per_split;
+    kb1 = min(p.kb_total, kb0 + p.kb_per_split);
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const uint32_t full_leader0 = mapa_shared(smem_u32(&full[0]), 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int u = cluster; ok && u < p.num_units; u += clusters) {
+        int m0, n0, kb0, kb1;
+        decode(u, m0, n0, kb0, kb1);
+        const int my_m = m0 + static_cast<int>(rank) * BM;
+        const int my_n = n0 + static_cast<int>(rank) * HALF_N;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (*abort_flag) { ok = false; break; }
+          if (!mbar_wait(&empty[stage], phase ^ 1, p.timeout_ns)) {
+            report_status(p.status, kStatusTimeoutProducer);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          // The even CTA expects the bytes of both CTAs' loads.
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * (A_BYTES + B_BYTES));
+          const uint32_t bar = full_leader0 + stage * 8;
+          uint8_t* a_dst = sA + stage * A_BYTES;
+          uint8_t* b_dst = sB + stage * B_BYTES;
+          const int k0 = kb * BK;
+          if constexpr (A_MN) {
+            tma_load_2d_pair(a_dst, &tmA, bar, my_m, k0);
+            tma_load_2d_pair(a_dst + 8192, &tmA, bar, my_m + 64, k0);
+          } else {
+            tma_load_2d_pair(a_dst, &tmA, bar, k0, my_m);
+          }
+          if constexpr (B_MN) {
+            tma_load_2d_pair(b_dst, &tmB, bar, my_n, k0);
+            tma_load_2d_pair(b_dst + 8192, &tmB, bar, my_n + 64, k0);
+          } else {
+            tma_load_2d_pair(b_dst, &tmB, bar, k0, my_n);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // Every load issued by this CTA was consumed by an MMA before the MMA
+      // committed the stage's empty barrier; wait for the last commits.
+      for (int s = 0; s < STAGES; ++s) {
+        if (!mbar_wait(&empty[stage], phase ^ 1, p.timeout_ns)) {
+          report_status(p.status, kStatusTimeoutDrain);
+          break;
+        }
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (even CTA)
+    if (leader && lane == 0) {
+      constexpr uint32_t IDESC = idesc_bf16_f32(2 * BM, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int u = cluster; ok && u < p.num_units; u += clusters, ++local) {
+        int m0, n0, kb0, kb1;
+        decode(u, m0, n0, kb0, kb1);
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (*abort_flag || !mbar_wait(&tempty[acc], acc_phase ^ 1, p.timeout_ns)) {
+          report_status(p.status, kStatusTimeoutMma);
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (*abort_flag || !mbar_wait(&full[stage], phase, p.timeout_ns)) {
+            report_status(p.status, kStatusTimeoutMma);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + stage * A_BYTES);
+          const uint32_t b_addr = smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t ad = A_MN ? smem_desc_sw128(a_addr + kk * 2048, 8192, 1024)
+                                     : smem_desc_sw128(a_addr + kk * 32, 16, 1024);
+            const uint64_t bd = B_MN ? smem_desc_sw128(b_addr + kk * 2048, 8192, 1024)
+                                     : smem_desc_sw128(b_addr + kk * 32, 16, 1024);
+            umma_f16_ss_pair(d_tmem, ad, bd, IDESC, (kb > kb0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit_pair(&empty[stage], 0x3);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(&tfull[acc], 0x3);
+      }
+      // Signal both CTAs once every MMA of this pair has retired.
+      umma_commit_pair(drain, 0x3);
+    }
+    if (lane == 0 && !mbar_wait(drain, 0, p.timeout_ns)) report_status(p.status, kStatusTimeoutDrain);
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int quad = warp & 3;
+    const int row_local = quad * 32 + lane;
+    constexpr int kChunksPerWarp = BN / 32 / (kEpilogueWarps / 4);
+    const int chunk0 = ((warp - 2) / 4) * kChunksPerWarp;
+    const uint32_t tempty_leader = mapa_shared(smem_u32(&tempty[0]), 0);
+    int local = 0;
+    for (int u = cluster; u < p.num_units; u += clusters, ++local) {
+      int m0, n0, kb0, kb1;
+      decode(u, m0, n0, kb0, kb1);
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      bool ok = (*abort_flag == 0) && mbar_wait(&tfull[acc], acc_phase, p.timeout_ns);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) {
+        if (lane == 0) report_status(p.status, kStatusTimeoutEpilogue);
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const int m = m0 + static_cast<int>(rank) * BM + row_local;
+      const uint32_t t_row =
+          tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
+#pragma unroll 1
+      for (int c = chunk0; c < chunk0 + kChunksPerWarp; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(t_row + c * 32, r);
+        tmem_ld_wait();
+        const int n_base = n0 + c * 32;
+        if (m < p.M && n_base < p.N) epilogue_row32<EPI, OUT>(p, m, n_base, r);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty_leader + acc * 8);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // no CTA leaves while its peer may still signal it
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem_base, TMEM_COLS);
+}
+
+template <bool A_MN, bool B_MN, int EPI, int OUT>
+void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int grid,
+                 cudaStream_t stream, int device) {
+  auto kern = gemm_pair_kernel<A_MN, B_MN, EPI, OUT>;
+  constexpr size_t smem = 1024 + kPairStages * (BM * BK * 2 + 128 * BK * 2) + 256;
+  static bool configured[64] = {false};
+  if (device < 0 || device >= 64 || !configured[device]) {
+    RX_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem)));
+    if (device >= 0 && device < 64) configured[device] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  RX_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, p));
+}
+
 using LaunchFn = void (*)(const CUtensorMap&, const CUtensorMap&, const Params&, int, cudaStream_t,
                           int);
 
@@ -413,6 +678,9 @@ using LaunchFn = void (*)(const CUtensorMap&, const CUtensorMap&, const Params&,
 LaunchFn pick_forward(int epi, int out);
 LaunchFn pick_dgrad(int epi, int out);
 LaunchFn pick_wgrad(int epi, int out);
+LaunchFn pick_forward_pair(int epi, int out);
+LaunchFn pick_dgrad_pair(int epi, int out);
+LaunchFn pick_wgrad_pair(int epi, int out);
 
 }  // namespace gemm
 }  // namespace rx

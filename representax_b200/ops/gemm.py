@@ -23,6 +23,9 @@ OUT_F32 = 1
 OUT_F32_ACC = 2
 OUT_F32_ATOMIC = 3
 
+# Default tile variant for every GEMM (0 = automatic).
+GEMM_VARIANT = 0
+
 
 def gemm(
     a: torch.Tensor,
@@ -39,10 +42,14 @@ def gemm(
     aux_out: torch.Tensor | None = None,
     residual: torch.Tensor | None = None,
     split_k: int = 0,
+    variant: int | None = None,
 ) -> torch.Tensor:
+    """``variant``: 1 = one CTA per 128x256 tile, 2 = CTA pair per 256x256 tile
+    (cta_group::2), 0/None = the default (``GEMM_VARIANT``, pair for >= 256 rows)."""
+
     ext().gemm(
         a, b, out, a_mn, b_mn, epi, out_mode, alpha, bias, aux_in, aux_out, residual,
-        status(out.device), split_k,
+        status(out.device), split_k, GEMM_VARIANT if variant is None else variant,
     )
     return out
 

@@ -8,6 +8,14 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
+@pytest.fixture(params=[1, 2], ids=["cta1", "cta_pair"])
+def gemm_variant(request, monkeypatch):
+    from representax_b200.ops import gemm as G
+
+    monkeypatch.setattr(G, "GEMM_VARIANT", request.param)
+    return request.param
+
+
 @pytest.fixture(scope="module")
 def C():
     from representax_b200.ops._ext import ext
@@ -36,7 +44,7 @@ GEMM_SHAPES = [(128, 256, 64), (300, 520, 200), (2048, 768, 768), (1000, 2304, 7
 
 
 @pytest.mark.parametrize("m,n,k", GEMM_SHAPES)
-def test_gemm_forward_plain(m, n, k):
+def test_gemm_forward_plain(m, n, k, gemm_variant):
     from representax_b200.ops import gemm as G
     from representax_b200.ops._ext import check_status
 
@@ -52,7 +60,7 @@ def test_gemm_forward_plain(m, n, k):
 
 
 @pytest.mark.parametrize("m,n,k", [(333, 600, 256), (2048, 3072, 768)])
-def test_gemm_forward_epilogues(m, n, k):
+def test_gemm_forward_epilogues(m, n, k, gemm_variant):
     from representax_b200.ops import gemm as G
 
     torch.manual_seed(1)
@@ -73,7 +81,7 @@ def test_gemm_forward_epilogues(m, n, k):
 
 
 @pytest.mark.parametrize("m,n,k", [(300, 520, 200), (2048, 768, 3072)])
-def test_gemm_dgrad(m, n, k):
+def test_gemm_dgrad(m, n, k, gemm_variant):
     # dx[m, k] = dy[m, n] @ W[n, k]
     from representax_b200.ops import gemm as G
 
@@ -94,7 +102,7 @@ def test_gemm_dgrad(m, n, k):
 
 
 @pytest.mark.parametrize("t,n,k", [(300, 520, 200), (4096, 768, 768), (9000, 3072, 768)])
-def test_gemm_wgrad_accumulates(t, n, k):
+def test_gemm_wgrad_accumulates(t, n, k, gemm_variant):
     from representax_b200.ops import gemm as G
 
     torch.manual_seed(3)
