@@ -263,6 +263,9 @@ def main() -> None:
         }
         print(json.dumps(out), flush=True)
     if ctx.enabled:
+        from representax_b200.parallel.peer import close_peer_groups
+
+        close_peer_groups()
         torch.distributed.destroy_process_group()
 
 

@@ -54,6 +54,23 @@ void grad_norm_sq(const at::Tensor& grad, at::Tensor& out);
 void finalize_clip(const at::Tensor& norm_sq, at::Tensor& scalars, const at::Tensor& loss,
                    double max_norm, int64_t step_offset);
 void cast_bf16(const at::Tensor& src, at::Tensor& dst);
+int64_t ipc_malloc(int64_t nbytes, int64_t device);
+void ipc_free(int64_t ptr, int64_t device);
+at::Tensor ipc_handle(int64_t ptr, int64_t device);
+int64_t ipc_open(const at::Tensor& handle_bytes, int64_t device);
+void ipc_close(int64_t ptr, int64_t device);
+at::Tensor wrap_device_pointer(int64_t ptr, int64_t numel, int64_t dtype_code, int64_t device);
+void signal_barrier(const at::Tensor& pads, int64_t rank, int64_t world, int64_t epoch, const at::Tensor& status);
+void peer_sgemm(const at::Tensor& A, bool a_mn, const at::Tensor& b_ptrs, int64_t seg_b, int64_t ldb, bool b_mn,
+                bool b_seg_k, int64_t M, int64_t N, int64_t K, at::Tensor& C, const c10::optional<at::Tensor>& c_ptrs,
+                int64_t seg_c, int64_t c_slot, double alpha, bool accumulate);
+void slot_reduce(const at::Tensor& slots, int64_t world, at::Tensor& out, bool accumulate);
+void sharded_grad_reduce(const at::Tensor& grad_ptrs, int64_t world, int64_t off, int64_t n, at::Tensor& shard,
+                         at::Tensor& norm_sq);
+void sharded_adamw(const at::Tensor& shard_grad, int64_t off, int64_t n, const at::Tensor& master_ptrs,
+                   const c10::optional<at::Tensor>& copy_ptrs, int64_t world, int64_t rank, at::Tensor& exp_avg,
+                   at::Tensor& exp_avg_sq, const at::Tensor& scalars, double lr, double b1, double b2, double eps,
+                   double wd);
 }  // namespace rx
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -74,4 +91,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("grad_norm_sq", &rx::grad_norm_sq);
   m.def("finalize_clip", &rx::finalize_clip);
   m.def("cast_bf16", &rx::cast_bf16);
+  m.def("ipc_malloc", &rx::ipc_malloc);
+  m.def("ipc_free", &rx::ipc_free);
+  m.def("ipc_handle", &rx::ipc_handle);
+  m.def("ipc_open", &rx::ipc_open);
+  m.def("ipc_close", &rx::ipc_close);
+  m.def("wrap_device_pointer", &rx::wrap_device_pointer);
+  m.def("signal_barrier", &rx::signal_barrier);
+  m.def("peer_sgemm", &rx::peer_sgemm);
+  m.def("slot_reduce", &rx::slot_reduce);
+  m.def("sharded_grad_reduce", &rx::sharded_grad_reduce);
+  m.def("sharded_adamw", &rx::sharded_adamw);
 }

@@ -59,6 +59,24 @@ class RetrievalBatch:
             return mask.to(torch.float32)
         return torch.where(mask, self.positive_weights.to(torch.float32), torch.zeros((), device=mask.device))
 
+    def rows(self, start: int, stop: int) -> "RetrievalBatch":
+        """Rows [start, stop) of both columns, with the relation restricted to them."""
+
+        from representax_b200.tasks._batch import slice_rows
+
+        return RetrievalBatch(
+            query=slice_rows(self.query, start, stop),
+            document=slice_rows(self.document, start, stop),
+            positive_mask=self.positive_mask[start:stop, start:stop],
+            positive_weights=None if self.positive_weights is None else self.positive_weights[start:stop, start:stop],
+            query_valid=self.query_valid[start:stop],
+            document_valid=self.document_valid[start:stop],
+        )
+
+    @property
+    def batch_size(self) -> int:
+        return int(self.positive_mask.shape[0])
+
     def map_tensors(self, fn) -> "RetrievalBatch":
         return RetrievalBatch(
             query=map_tensors(self.query, fn),

@@ -105,6 +105,12 @@ class MNRTask:
                              row_chunk_size: int | None = None) -> LossOutput:
         if row_chunk_size is not None and row_chunk_size <= 0:
             raise ValueError("row_chunk_size must be positive when set")
+        from representax_b200.parallel.fused_mnr import ShardedRetrievalBatch, sharded_mnr_loss
+
+        if isinstance(batch, ShardedRetrievalBatch):
+            loss, forward, reverse = sharded_mnr_loss(query_embeddings, document_embeddings, batch,
+                                                      scale=self.scale, symmetric=self.symmetric)
+            return LossOutput(loss=loss, metrics={"forward_loss": forward, "reverse_loss": reverse})
         q, d, w, qv, dv = _canonical(query_embeddings, document_embeddings, batch.positive_mask,
                                      batch.positive_weights, batch.query_valid,
                                      batch.document_valid, self.scale)

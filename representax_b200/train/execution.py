@@ -33,7 +33,7 @@ def _detach(out: LossOutput) -> LossOutput:
     return LossOutput(loss=out.loss.detach(), metrics={k: v.detach() for k, v in out.metrics.items()})
 
 
-def _global_batch(batch, queries, documents, ctx: DistContext):
+def _global_batch(batch, queries, documents, ctx: DistContext, *, fused: bool = False, symmetric: bool = False):
     """Gather representations and the positive relation across ranks.
 
     A rank-local batch whose mask spans only its own documents is placed at
@@ -46,6 +46,10 @@ def _global_batch(batch, queries, documents, ctx: DistContext):
 
     if not ctx.enabled:
         return queries, documents, batch
+    if fused and queries.is_cuda:
+        from representax_b200.parallel.fused_mnr import ShardedRetrievalBatch
+
+        return queries, documents, ShardedRetrievalBatch.from_local(batch, ctx, symmetric=symmetric)
     local_d = documents.shape[0]
     global_d = local_d * ctx.world_size
     mask = batch.positive_mask
@@ -66,9 +70,23 @@ def _global_batch(batch, queries, documents, ctx: DistContext):
     return q_all, d_all, global_batch
 
 
+def _fusion(task, enabled: bool) -> dict:
+    """Use the fused cross-rank MNR kernels for MNR (and Matryoshka-wrapped MNR)."""
+
+    from representax_b200.tasks.modifiers import MatryoshkaTask
+    from representax_b200.tasks.retrieval import MNRTask
+
+    base = task.task if isinstance(task, MatryoshkaTask) else task
+    if enabled and isinstance(base, MNRTask) and base.negative_scope == "global":
+        return {"fused": True, "symmetric": base.symmetric}
+    return {"fused": False}
+
+
 @dataclass(frozen=True)
 class Direct:
     """Plain full-batch differentiation."""
+
+    fused: bool = True
 
     def validate(self, task: Any) -> None:
         return None
@@ -78,7 +96,7 @@ class Direct:
         if ctx.enabled and hasattr(base, "loss_from_representations") and hasattr(batch, "positive_mask"):
             gen = streams("direct")
             queries, documents = base.representations(model, batch, generator=gen, encode_fn=encode)
-            q_all, d_all, gbatch = _global_batch(batch, queries, documents, ctx)
+            q_all, d_all, gbatch = _global_batch(batch, queries, documents, ctx, **_fusion(task, self.fused))
             out = task.loss_from_representations((q_all, d_all), gbatch)
         else:
             out = evaluate_loss(task, model, batch, generator=streams("direct"))
@@ -114,6 +132,7 @@ class GradCache:
     query_chunk_size: int
     document_chunk_size: int | None = None
     loss_row_chunk_size: int | None = None
+    fused: bool = True
 
     def __post_init__(self) -> None:
         if self.query_chunk_size <= 0:
@@ -152,7 +171,7 @@ class GradCache:
         documents, _ = _encode_chunks(model, batch.document, Route.DOCUMENT, dc, streams, "document")
         queries.requires_grad_(True)
         documents.requires_grad_(True)
-        q_all, d_all, gbatch = _global_batch(batch, queries, documents, ctx)
+        q_all, d_all, gbatch = _global_batch(batch, queries, documents, ctx, **_fusion(task, self.fused))
         with torch.enable_grad():
             out = task.loss_from_representations((q_all, d_all), gbatch,
                                                  row_chunk_size=self.resolved_loss_row_chunk_size)

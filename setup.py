@@ -22,6 +22,7 @@ SOURCES = [
     "pool.cu",
     "mnr.cu",
     "optim.cu",
+    "comm.cu",
 ]
 
 NVCC_FLAGS = [

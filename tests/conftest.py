@@ -10,7 +10,7 @@ if ROOT not in sys.path:
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA (sm_100a) device and the built extension")
-    config.addinivalue_line("markers", "distributed: spawns several processes")
+    config.addinivalue_line("markers", "distributed: spawns several processes (CPU gloo ranks)")
 
 
 def pytest_collection_modifyitems(config, items):
