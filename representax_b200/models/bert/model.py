@@ -97,7 +97,8 @@ class BertEncoder(nn.Module):
 
     @staticmethod
     def make_batch(*, input_ids, attention_mask, token_type_ids=None) -> TokenBatch:
-        return TokenBatch(input_ids=input_ids, attention_mask=attention_mask, token_type_ids=token_type_ids)
+        return TokenBatch.from_arrays(input_ids=input_ids, attention_mask=attention_mask,
+                                      token_type_ids=token_type_ids)
 
     # ------------------------------------------------------------ dispatch
     def _dtype(self) -> torch.dtype:

@@ -154,6 +154,11 @@ class MPNetEncoder(nn.Module):
         self.pooling = pooling
         self.normalize = normalize
 
+    @staticmethod
+    def make_batch(*, input_ids, attention_mask, token_type_ids=None) -> TokenBatch:
+        del token_type_ids  # MPNet has no segment embeddings
+        return TokenBatch.from_arrays(input_ids=input_ids, attention_mask=attention_mask)
+
     def _dtype(self):
         return active_compute_dtype(self.compute_dtype)
 
@@ -250,7 +255,8 @@ class MPNetCheckpointAdapter:
         from representax_b200.integrations.huggingface import load_hf_config, load_safetensor_subset
 
         config = MPNetConfig.from_hf_config(load_hf_config(path))
-        model = MPNetEncoder(config, model_id=Path(path).name, **kwargs)
+        kwargs.setdefault("model_id", Path(path).name)
+        model = MPNetEncoder(config, **kwargs)
         names = set(cls.state_dict(model))
         return cls.from_state_dict(model, load_safetensor_subset(path, names, prefixes=("", "mpnet.")))
 

@@ -139,6 +139,18 @@ class TokenBatch:
     def batch_size(self) -> int:
         return self.attention_mask.shape[0]
 
+    @classmethod
+    def from_arrays(cls, *, input_ids, attention_mask, token_type_ids=None, position_ids=None) -> "TokenBatch":
+        """Build from numpy arrays or tensors (ids as int64, mask as int64)."""
+
+        def tensor(value):
+            if value is None:
+                return None
+            return torch.as_tensor(value).to(torch.int64)
+
+        return cls(input_ids=tensor(input_ids), attention_mask=tensor(attention_mask),
+                   token_type_ids=tensor(token_type_ids), position_ids=tensor(position_ids))
+
     def pack(self) -> "TokenBatch":
         """Attach the packed form (host tensors only; call before moving to the device)."""
 
