@@ -1,7 +1,7 @@
 // Variable-length (packed, padding-free) multi-head attention for sm_100a,
-// head dimension 64, bf16 operands, fp32 softmax and accumulation.
+// head dimension 64 or 128, bf16 operands, fp32 softmax and accumulation.
 //
-// Sequences are packed back to back ([T, heads * 64] rows addressed through
+// Sequences are packed back to back ([T, heads * D] rows addressed through
 // cu_seqlens), so no FLOP is spent on padding tokens. Supported masks: key
 // validity (sequence end), causal, and a symmetric sliding window
 // |i - j| <= window (ModernBERT local layers). Grouped-query attention maps
@@ -10,9 +10,10 @@
 // Forward: one CTA = 4 warps = 64 queries of one (sequence, head); key/value
 // tiles of 64 stream through double-buffered cp.async shared memory; online
 // softmax in base 2; the log-sum-exp is saved for the backward pass.
-// Backward: one CTA = 64 keys of one (sequence, head); loops over query tiles,
-// accumulates dK and dV in registers, and adds dQ partials with fp32 vector
-// atomics into a [T, heads * 64] accumulator.
+// Backward: one CTA = 64 keys of one (sequence, key/value head); loops over
+// the query heads of its group and their query tiles, accumulates dK and dV
+// in registers, and adds dQ partials with fp32 vector atomics into a
+// [T, heads * D] accumulator.
 // Warp-level math uses mma.sync m16n8k16 with ldmatrix fragment loads.
 //
 // Reference parity: `dot_product_attention` with padding / window / causal
@@ -29,8 +30,12 @@ namespace attn {
 // Tile constants and the kernel parameter block are shared with the other
 // host entry points through attention_kernels.cuh.
 
+// Byte offset of 16-byte chunk `chunk` of row `row` in a [rows][W] bf16 tile
+// whose chunks are XOR-swizzled by the row's low 3 bits (bank-conflict-free
+// ldmatrix).
+template <int W>
 __device__ __forceinline__ uint32_t swz(int row, int chunk) {
-  return static_cast<uint32_t>((row * kChunks + (chunk ^ (row & 7))) * 16);
+  return static_cast<uint32_t>((row * (W / 8) + (chunk ^ (row & 7))) * 16);
 }
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
@@ -71,10 +76,12 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// Load a [64 rows][64] bf16 tile (rows row0.. of a packed matrix) into
+// Load a [64 rows][D] bf16 tile (rows row0.. of a packed matrix) into
 // swizzled shared memory; rows at or beyond `rows_valid` are zero-filled.
+template <int D>
 __device__ __forceinline__ void load_tile(uint32_t smem, const __nv_bfloat16* base, int64_t ld,
                                           int row0, int rows_valid) {
+  constexpr int kChunks = D / 8;
 #pragma unroll
   for (int i = 0; i < (64 * kChunks) / kThreads; ++i) {
     const int idx = threadIdx.x + i * kThreads;
@@ -82,7 +89,7 @@ __device__ __forceinline__ void load_tile(uint32_t smem, const __nv_bfloat16* ba
     const int c = idx % kChunks;
     const bool valid = (row0 + r) < rows_valid;
     const __nv_bfloat16* src = base + static_cast<int64_t>(valid ? row0 + r : 0) * ld + c * 8;
-    cp_async16(smem + swz(r, c), src, valid);
+    cp_async16(smem + swz<D>(r, c), src, valid);
   }
 }
 
@@ -106,6 +113,7 @@ __device__ __forceinline__ void key_range(const Params& p, int q_lo, int q_hi, i
 }
 
 // ===================================================================== forward
+template <int D>
 __global__ void __launch_bounds__(kThreads) attn_fwd_kernel(const Params p) {
   const int qb = blockIdx.x;
   const int h = blockIdx.y;
@@ -115,7 +123,7 @@ __global__ void __launch_bounds__(kThreads) attn_fwd_kernel(const Params p) {
   if (qb * BM >= len) return;
   const int kvh = h / p.heads_per_kv;
 
-  __shared__ __align__(128) uint8_t smem[3 * 64 * D * 2 + 2 * 64 * D * 2];
+  extern __shared__ __align__(128) uint8_t smem[];
   const uint32_t sQ = smem_u32(smem);
   const uint32_t sK[2] = {sQ + 64 * D * 2, sQ + 2 * 64 * D * 2};
   const uint32_t sV[2] = {sQ + 3 * 64 * D * 2, sQ + 4 * 64 * D * 2};
@@ -133,10 +141,10 @@ __global__ void __launch_bounds__(kThreads) attn_fwd_kernel(const Params p) {
   const int kb_first = k_lo / BN;
   const int kb_last = (k_hi + BN - 1) / BN;  // exclusive
 
-  load_tile(sQ, qbase, p.ldq, q_lo, len);
+  load_tile<D>(sQ, qbase, p.ldq, q_lo, len);
   if (kb_first < kb_last) {
-    load_tile(sK[0], kbase, p.ldk, kb_first * BN, len);
-    load_tile(sV[0], vbase, p.ldv, kb_first * BN, len);
+    load_tile<D>(sK[0], kbase, p.ldk, kb_first * BN, len);
+    load_tile<D>(sV[0], vbase, p.ldv, kb_first * BN, len);
   }
   cp_async_commit();
 
@@ -152,8 +160,8 @@ __global__ void __launch_bounds__(kThreads) attn_fwd_kernel(const Params p) {
   for (int kb = kb_first; kb < kb_last; ++kb) {
     const int buf = (kb - kb_first) & 1;
     if (kb + 1 < kb_last) {
-      load_tile(sK[buf ^ 1], kbase, p.ldk, (kb + 1) * BN, len);
-      load_tile(sV[buf ^ 1], vbase, p.ldv, (kb + 1) * BN, len);
+      load_tile<D>(sK[buf ^ 1], kbase, p.ldk, (kb + 1) * BN, len);
+      load_tile<D>(sV[buf ^ 1], vbase, p.ldv, (kb + 1) * BN, len);
     }
     cp_async_commit();
     cp_async_wait<1>();
@@ -163,7 +171,7 @@ __global__ void __launch_bounds__(kThreads) attn_fwd_kernel(const Params p) {
       for (int kk = 0; kk < D / 16; ++kk) {
         const int r = warp * 16 + (lane & 15);
         const int c = kk * 2 + (lane >> 4);
-        ldsm_x4(sQ + swz(r, c), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
+        ldsm_x4(sQ + swz<D>(r, c), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
       }
     }
     // S = Q K^T for 16 rows x 64 keys.
@@ -176,7 +184,7 @@ __global__ void __launch_bounds__(kThreads) attn_fwd_kernel(const Params p) {
         uint32_t b0, b1, b2, b3;
         const int r = nb * 8 + (lane & 7);
         const int c = kk * 2 + (lane >> 3);
-        ldsm_x4(sK[buf] + swz(r, c), b0, b1, b2, b3);
+        ldsm_x4(sK[buf] + swz<D>(r, c), b0, b1, b2, b3);
         mma16816(s[nb], qf[kk], b0, b1);
         mma16816(s[nb], qf[kk + 1], b2, b3);
       }
@@ -244,7 +252,7 @@ __global__ void __launch_bounds__(kThreads) attn_fwd_kernel(const Params p) {
         uint32_t b0, b1, b2, b3;
         const int r = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
         const int c = nb + (lane >> 4);
-        ldsm_x4_t(sV[buf] + swz(r, c), b0, b1, b2, b3);
+        ldsm_x4_t(sV[buf] + swz<D>(r, c), b0, b1, b2, b3);
         mma16816(o_acc[nb], a, b0, b1);
         mma16816(o_acc[nb + 1], a, b2, b3);
       }
@@ -276,15 +284,19 @@ __global__ void __launch_bounds__(kThreads) attn_fwd_kernel(const Params p) {
 // dvec[h, t] = sum_d dO[t, h, d] * O[t, h, d]  (one warp per (t, h)).
 __global__ void attn_dvec_kernel(const __nv_bfloat16* __restrict__ o, int64_t ldo,
                                  const __nv_bfloat16* __restrict__ dO, int64_t ld_do,
-                                 float* __restrict__ dvec, int total, int heads) {
-  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+                                 float* __restrict__ dvec, int total, int heads, int head_dim) {
+  const int64_t gw = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  if (gw >= total * heads) return;
-  const int tok = gw / heads, h = gw % heads;
-  const __nv_bfloat162 a = reinterpret_cast<const __nv_bfloat162*>(o + tok * ldo + h * D)[lane];
-  const __nv_bfloat162 d = reinterpret_cast<const __nv_bfloat162*>(dO + tok * ld_do + h * D)[lane];
-  float2 fa = __bfloat1622float2(a), fd = __bfloat1622float2(d);
-  float s = fa.x * fd.x + fa.y * fd.y;
+  if (gw >= static_cast<int64_t>(total) * heads) return;
+  const int64_t tok = gw / heads;
+  const int h = static_cast<int>(gw % heads);
+  const __nv_bfloat162* a = reinterpret_cast<const __nv_bfloat162*>(o + tok * ldo + h * head_dim);
+  const __nv_bfloat162* d = reinterpret_cast<const __nv_bfloat162*>(dO + tok * ld_do + h * head_dim);
+  float s = 0.f;
+  for (int i = lane; i < head_dim / 2; i += 32) {
+    const float2 fa = __bfloat1622float2(a[i]), fd = __bfloat1622float2(d[i]);
+    s += fa.x * fd.x + fa.y * fd.y;
+  }
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
   if (lane == 0) dvec[static_cast<int64_t>(h) * total + tok] = s;
@@ -304,17 +316,17 @@ __global__ void attn_dq_convert_kernel(const float* __restrict__ acc, __nv_bfloa
 }
 
 // ==================================================================== backward
+template <int D>
 __global__ void __launch_bounds__(kThreads) attn_bwd_kernel(const Params p) {
   const int kbk = blockIdx.x;
-  const int h = blockIdx.y;
+  const int kvh = blockIdx.y;  // key/value head; its query heads are looped below
   const int b = blockIdx.z;
   const int start = p.cu_seqlens[b];
   const int len = p.cu_seqlens[b + 1] - start;
   if (kbk * BN >= len) return;
-  const int kvh = h / p.heads_per_kv;
 
   // K, V, Q, dO tiles + dS^T tile (bf16) + lse/dvec for 64 queries.
-  __shared__ __align__(128) uint8_t smem[5 * 64 * D * 2];
+  extern __shared__ __align__(128) uint8_t smem[];
   __shared__ float s_lse[64];
   __shared__ float s_dv[64];
   const uint32_t sK = smem_u32(smem);
@@ -340,11 +352,8 @@ __global__ void __launch_bounds__(kThreads) attn_bwd_kernel(const Params p) {
 
   const __nv_bfloat16* kbase = p.k + static_cast<int64_t>(start) * p.ldk + kvh * D;
   const __nv_bfloat16* vbase = p.v + static_cast<int64_t>(start) * p.ldv + kvh * D;
-  const __nv_bfloat16* qbase = p.q + static_cast<int64_t>(start) * p.ldq + h * D;
-  const __nv_bfloat16* dobase = p.dO + static_cast<int64_t>(start) * p.ld_do + h * D;
-
-  load_tile(sK, kbase, p.ldk, k_lo, len);
-  load_tile(sV, vbase, p.ldv, k_lo, len);
+  load_tile<D>(sK, kbase, p.ldk, k_lo, len);
+  load_tile<D>(sV, vbase, p.ldv, k_lo, len);
   cp_async_commit();
   cp_async_wait<0>();
   __syncthreads();
@@ -354,8 +363,8 @@ __global__ void __launch_bounds__(kThreads) attn_bwd_kernel(const Params p) {
   for (int kk = 0; kk < D / 16; ++kk) {
     const int r = warp * 16 + (lane & 15);
     const int c = kk * 2 + (lane >> 4);
-    ldsm_x4(sK + swz(r, c), kf[kk][0], kf[kk][1], kf[kk][2], kf[kk][3]);
-    ldsm_x4(sV + swz(r, c), vf[kk][0], vf[kk][1], vf[kk][2], vf[kk][3]);
+    ldsm_x4(sK + swz<D>(r, c), kf[kk][0], kf[kk][1], kf[kk][2], kf[kk][3]);
+    ldsm_x4(sV + swz<D>(r, c), vf[kk][0], vf[kk][1], vf[kk][2], vf[kk][3]);
   }
   float dk_acc[D / 8][4], dv_acc[D / 8][4];
 #pragma unroll
@@ -365,10 +374,13 @@ __global__ void __launch_bounds__(kThreads) attn_bwd_kernel(const Params p) {
 
   const int kj0 = k_lo + warp * 16 + g;  // this thread's key rows kj0, kj0 + 8
 
+  for (int h = kvh * p.heads_per_kv; h < (kvh + 1) * p.heads_per_kv; ++h)
   for (int qb = qb_first; qb < qb_last; ++qb) {
+    const __nv_bfloat16* qbase = p.q + static_cast<int64_t>(start) * p.ldq + h * D;
+    const __nv_bfloat16* dobase = p.dO + static_cast<int64_t>(start) * p.ld_do + h * D;
     const int q0 = qb * BM;
-    load_tile(sQ, qbase, p.ldq, q0, len);
-    load_tile(sdO, dobase, p.ld_do, q0, len);
+    load_tile<D>(sQ, qbase, p.ldq, q0, len);
+    load_tile<D>(sdO, dobase, p.ld_do, q0, len);
     cp_async_commit();
     if (threadIdx.x < 64) {
       const int i = q0 + threadIdx.x;
@@ -389,10 +401,10 @@ __global__ void __launch_bounds__(kThreads) attn_bwd_kernel(const Params p) {
         uint32_t b0, b1, b2, b3;
         const int r = nb * 8 + (lane & 7);
         const int c = kk * 2 + (lane >> 3);
-        ldsm_x4(sQ + swz(r, c), b0, b1, b2, b3);
+        ldsm_x4(sQ + swz<D>(r, c), b0, b1, b2, b3);
         mma16816(st[nb], kf[kk], b0, b1);
         mma16816(st[nb], kf[kk + 1], b2, b3);
-        ldsm_x4(sdO + swz(r, c), b0, b1, b2, b3);
+        ldsm_x4(sdO + swz<D>(r, c), b0, b1, b2, b3);
         mma16816(dpt[nb], vf[kk], b0, b1);
         mma16816(dpt[nb], vf[kk + 1], b2, b3);
       }
@@ -428,10 +440,10 @@ __global__ void __launch_bounds__(kThreads) attn_bwd_kernel(const Params p) {
         uint32_t b0, b1, b2, b3;
         const int r = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
         const int c = nb + (lane >> 4);
-        ldsm_x4_t(sdO + swz(r, c), b0, b1, b2, b3);
+        ldsm_x4_t(sdO + swz<D>(r, c), b0, b1, b2, b3);
         mma16816(dv_acc[nb], ap, b0, b1);
         mma16816(dv_acc[nb + 1], ap, b2, b3);
-        ldsm_x4_t(sQ + swz(r, c), b0, b1, b2, b3);
+        ldsm_x4_t(sQ + swz<D>(r, c), b0, b1, b2, b3);
         mma16816(dk_acc[nb], ad, b0, b1);
         mma16816(dk_acc[nb + 1], ad, b2, b3);
       }
@@ -439,10 +451,10 @@ __global__ void __launch_bounds__(kThreads) attn_bwd_kernel(const Params p) {
       const int key_r = warp * 16 + g;
       const int qcol = kk * 16 + 2 * t;  // element column within the 64-query row
       uint8_t* base = smem + 4 * 64 * D * 2;
-      *reinterpret_cast<uint32_t*>(base + swz(key_r, qcol >> 3) + (qcol & 7) * 2) = ad[0];
-      *reinterpret_cast<uint32_t*>(base + swz(key_r + 8, qcol >> 3) + (qcol & 7) * 2) = ad[1];
-      *reinterpret_cast<uint32_t*>(base + swz(key_r, (qcol + 8) >> 3) + (qcol & 7) * 2) = ad[2];
-      *reinterpret_cast<uint32_t*>(base + swz(key_r + 8, (qcol + 8) >> 3) + (qcol & 7) * 2) = ad[3];
+      *reinterpret_cast<uint32_t*>(base + swz<64>(key_r, qcol >> 3) + (qcol & 7) * 2) = ad[0];
+      *reinterpret_cast<uint32_t*>(base + swz<64>(key_r + 8, qcol >> 3) + (qcol & 7) * 2) = ad[1];
+      *reinterpret_cast<uint32_t*>(base + swz<64>(key_r, (qcol + 8) >> 3) + (qcol & 7) * 2) = ad[2];
+      *reinterpret_cast<uint32_t*>(base + swz<64>(key_r + 8, (qcol + 8) >> 3) + (qcol & 7) * 2) = ad[3];
     }
     __syncthreads();
     // dQ[64 q x D] += dS K : warp w handles queries w*16..w*16+15, k = keys.
@@ -457,14 +469,14 @@ __global__ void __launch_bounds__(kThreads) attn_bwd_kernel(const Params p) {
           const int mi = lane >> 3;
           const int r = kk * 16 + (lane & 7) + (mi >> 1) * 8;  // key row in dS^T
           const int c = warp * 2 + (mi & 1);                     // query chunk
-          ldsm_x4_t(sdS + swz(r, c), a[0], a[1], a[2], a[3]);
+          ldsm_x4_t(sdS + swz<64>(r, c), a[0], a[1], a[2], a[3]);
         }
 #pragma unroll
         for (int nb = 0; nb < D / 8; nb += 2) {
           uint32_t b0, b1, b2, b3;
           const int r = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
           const int c = nb + (lane >> 4);
-          ldsm_x4_t(sK + swz(r, c), b0, b1, b2, b3);
+          ldsm_x4_t(sK + swz<D>(r, c), b0, b1, b2, b3);
           mma16816(dq[nb], a, b0, b1);
           mma16816(dq[nb + 1], a, b2, b3);
         }
@@ -490,8 +502,8 @@ __global__ void __launch_bounds__(kThreads) attn_bwd_kernel(const Params p) {
   for (int r = 0; r < 2; ++r) {
     const int j = kj0 + r * 8;
     if (j >= len) continue;
-    __nv_bfloat16* dkrow = p.dk + static_cast<int64_t>(start + j) * p.ld_dk + h * D;
-    __nv_bfloat16* dvrow = p.dv + static_cast<int64_t>(start + j) * p.ld_dv + h * D;
+    __nv_bfloat16* dkrow = p.dk + static_cast<int64_t>(start + j) * p.ld_dk + kvh * D;
+    __nv_bfloat16* dvrow = p.dv + static_cast<int64_t>(start + j) * p.ld_dv + kvh * D;
 #pragma unroll
     for (int nb = 0; nb < D / 8; ++nb) {
       *reinterpret_cast<uint32_t*>(dkrow + nb * 8 + 2 * t) =
@@ -501,6 +513,11 @@ __global__ void __launch_bounds__(kThreads) attn_bwd_kernel(const Params p) {
     }
   }
 }
+
+template __global__ void attn_fwd_kernel<64>(const Params p);
+template __global__ void attn_fwd_kernel<128>(const Params p);
+template __global__ void attn_bwd_kernel<64>(const Params p);
+template __global__ void attn_bwd_kernel<128>(const Params p);
 
 }  // namespace attn
 
@@ -512,10 +529,12 @@ void fill_common(attn::Params& p, const at::Tensor& q, const at::Tensor& k, cons
   check_bf16(k, "k");
   check_bf16(v, "v");
   RX_CHECK(cu_seqlens.scalar_type() == at::kInt && cu_seqlens.is_cuda(), "cu_seqlens must be CUDA int32");
-  RX_CHECK(q.dim() == 2 && k.dim() == 2 && v.dim() == 2, "q/k/v must be [T, heads*64] views");
+  RX_CHECK(q.dim() == 2 && k.dim() == 2 && v.dim() == 2, "q/k/v must be [T, heads*D] views");
   RX_CHECK(q.stride(1) == 1 && k.stride(1) == 1 && v.stride(1) == 1, "unit inner stride required");
-  RX_CHECK(q.size(1) == heads * attn::D && k.size(1) == kv_heads * attn::D && v.size(1) == kv_heads * attn::D,
-           "head_dim must be 64");
+  RX_CHECK(heads > 0 && kv_heads > 0 && q.size(1) % heads == 0, "bad head counts");
+  const int64_t d = q.size(1) / heads;
+  RX_CHECK(d == 64 || d == 128, "head_dim must be 64 or 128");
+  RX_CHECK(k.size(1) == kv_heads * d && v.size(1) == kv_heads * d, "k/v widths do not match kv_heads*head_dim");
   RX_CHECK(heads % kv_heads == 0, "heads must be a multiple of kv_heads");
   for (const at::Tensor* t : {&q, &k, &v})
     RX_CHECK(t->stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(t->data_ptr()) % 16 == 0,
@@ -536,6 +555,12 @@ void fill_common(attn::Params& p, const at::Tensor& q, const at::Tensor& k, cons
   p.causal = causal ? 1 : 0;
   p.window = static_cast<int>(window);
 }
+
+template <typename Kernel>
+void set_smem(Kernel kernel, int bytes) {
+  if (bytes > 48 * 1024)
+    RX_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+}
 }  // namespace
 
 void attention_forward(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o,
@@ -553,7 +578,13 @@ void attention_forward(const at::Tensor& q, const at::Tensor& k, const at::Tenso
   if (p.batch == 0 || max_len == 0) return;
   c10::cuda::CUDAGuard guard(q.get_device());
   dim3 grid((max_len + attn::BM - 1) / attn::BM, heads, p.batch);
-  attn::attn_fwd_kernel<<<grid, attn::kThreads, 0, at::cuda::getCurrentCUDAStream().stream()>>>(p);
+  auto st = at::cuda::getCurrentCUDAStream().stream();
+  if (q.size(1) / heads == 64) {
+    attn::attn_fwd_kernel<64><<<grid, attn::kThreads, attn::fwd_smem_bytes<64>(), st>>>(p);
+  } else {
+    set_smem(attn::attn_fwd_kernel<128>, attn::fwd_smem_bytes<128>());
+    attn::attn_fwd_kernel<128><<<grid, attn::kThreads, attn::fwd_smem_bytes<128>(), st>>>(p);
+  }
   RX_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -565,11 +596,11 @@ void attention_backward(const at::Tensor& dO, const at::Tensor& q, const at::Ten
                         int64_t window) {
   attn::Params p{};
   fill_common(p, q, k, v, cu_seqlens, heads, kv_heads, scale, causal, window);
-  RX_CHECK(kv_heads == heads, "GQA backward is not supported yet");
+  const int d = static_cast<int>(q.size(1) / heads);
   check_bf16(dO, "dO");
   check_f32(dq_acc, "dq_acc");
   check_f32(dvec, "dvec");
-  RX_CHECK(dq_acc.is_contiguous() && dq_acc.numel() == q.size(0) * heads * attn::D, "bad dq_acc");
+  RX_CHECK(dq_acc.is_contiguous() && dq_acc.numel() == q.size(0) * heads * d, "bad dq_acc");
   p.dO = reinterpret_cast<const __nv_bfloat16*>(dO.data_ptr());
   p.ld_do = dO.stride(0);
   p.lse = lse.data_ptr<float>();
@@ -589,14 +620,19 @@ void attention_backward(const at::Tensor& dO, const at::Tensor& q, const at::Ten
     const int threads = 256;
     attn::attn_dvec_kernel<<<(warps * 32 + threads - 1) / threads, threads, 0, st>>>(
         reinterpret_cast<const __nv_bfloat16*>(o.data_ptr()), o.stride(0), p.dO, p.ld_do,
-        dvec.data_ptr<float>(), total, static_cast<int>(heads));
+        dvec.data_ptr<float>(), total, static_cast<int>(heads), d);
     RX_CUDA_CHECK(cudaGetLastError());
   }
-  dim3 grid((max_len + attn::BN - 1) / attn::BN, heads, p.batch);
-  attn::attn_bwd_kernel<<<grid, attn::kThreads, 0, st>>>(p);
+  dim3 grid((max_len + attn::BN - 1) / attn::BN, kv_heads, p.batch);
+  if (d == 64) {
+    attn::attn_bwd_kernel<64><<<grid, attn::kThreads, attn::bwd_smem_bytes<64>(), st>>>(p);
+  } else {
+    set_smem(attn::attn_bwd_kernel<128>, attn::bwd_smem_bytes<128>());
+    attn::attn_bwd_kernel<128><<<grid, attn::kThreads, attn::bwd_smem_bytes<128>(), st>>>(p);
+  }
   RX_CUDA_CHECK(cudaGetLastError());
   {
-    const int width = static_cast<int>(heads * attn::D);
+    const int width = static_cast<int>(heads * d);
     const int64_t n4 = static_cast<int64_t>(total) * width / 4;
     attn::attn_dq_convert_kernel<<<(n4 + 255) / 256, 256, 0, st>>>(
         p.dq_acc, reinterpret_cast<__nv_bfloat16*>(dq.data_ptr()), dq.stride(0), total, width);

@@ -9,11 +9,16 @@
 namespace rx {
 namespace attn {
 
-constexpr int D = 64;
+// Head dimension D (64 or 128) is a template parameter of the kernels.
 constexpr int BM = 64;
 constexpr int BN = 64;
 constexpr int kThreads = 128;
-constexpr int kChunks = D / 8;  // 16-byte chunks per row
+
+// Dynamic shared memory: forward Q + 2 x (K, V); backward K, V, Q, dO, dS^T.
+template <int D>
+constexpr int fwd_smem_bytes() { return 5 * 64 * D * 2; }
+template <int D>
+constexpr int bwd_smem_bytes() { return 4 * 64 * D * 2 + 64 * 64 * 2; }
 
 struct Params {
   const __nv_bfloat16* q;
@@ -24,7 +29,7 @@ struct Params {
   int64_t ldo;
   float* lse;  // [heads, T] base-2 log-sum-exp of the scaled scores
   const int* cu_seqlens;
-  int batch, heads, heads_per_kv, total_tokens;
+  int batch, heads, heads_per_kv, total_tokens;  // heads = query heads
   float scale_log2;  // softmax_scale * log2(e)
   float scale;
   int causal;
@@ -40,11 +45,18 @@ struct Params {
 };
 
 
+template <int D>
 __global__ void __launch_bounds__(kThreads) attn_fwd_kernel(const Params p);
+template <int D>
 __global__ void __launch_bounds__(kThreads) attn_bwd_kernel(const Params p);
+extern template __global__ void attn_fwd_kernel<64>(const Params p);
+extern template __global__ void attn_fwd_kernel<128>(const Params p);
+extern template __global__ void attn_bwd_kernel<64>(const Params p);
+extern template __global__ void attn_bwd_kernel<128>(const Params p);
+// dvec[h, t] = <dO[t, h, :], O[t, h, :]>, one warp per (t, h); D = 64 or 128.
 __global__ void attn_dvec_kernel(const __nv_bfloat16* __restrict__ o, int64_t ldo,
                                  const __nv_bfloat16* __restrict__ dO, int64_t ld_do,
-                                 float* __restrict__ dvec, int total, int heads);
+                                 float* __restrict__ dvec, int total, int heads, int head_dim);
 __global__ void attn_dq_convert_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ dq,
                                        int64_t ld_dq, int total, int width);
 

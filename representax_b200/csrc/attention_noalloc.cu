@@ -66,7 +66,7 @@ extern "C" int rx_attention_backward_noalloc(
 
   // Scratch layout: dQ accumulator [T, heads * 64] fp32, then (256-byte
   // aligned) rowsum(dO * O) [heads, T] fp32.
-  const uint64_t width = static_cast<uint64_t>(heads) * D;
+  const uint64_t width = static_cast<uint64_t>(heads) * 64;
   const uint64_t acc_bytes = static_cast<uint64_t>(total_tokens) * width * sizeof(float);
   const uint64_t dvec_offset = (acc_bytes + 255) / 256 * 256;
   const uint64_t dvec_bytes = static_cast<uint64_t>(heads) * total_tokens * sizeof(float);
@@ -111,10 +111,10 @@ extern "C" int rx_attention_backward_noalloc(
     const int64_t threads = 256;
     const int64_t warps = static_cast<int64_t>(total_tokens) * heads;
     attn_dvec_kernel<<<static_cast<unsigned>((warps * 32 + threads - 1) / threads), threads, 0, stream>>>(
-        static_cast<const __nv_bfloat16*>(o), ld_o, p.dO, ld_do, dvec, total_tokens, heads);
+        static_cast<const __nv_bfloat16*>(o), ld_o, p.dO, ld_do, dvec, total_tokens, heads, 64);
   }
   dim3 grid((max_len + BN - 1) / BN, heads, batch);
-  attn_bwd_kernel<<<grid, kThreads, 0, stream>>>(p);
+  attn_bwd_kernel<64><<<grid, kThreads, bwd_smem_bytes<64>(), stream>>>(p);
   {
     const int64_t n4 = static_cast<int64_t>(total_tokens) * static_cast<int64_t>(width) / 4;
     attn_dq_convert_kernel<<<static_cast<unsigned>((n4 + 255) / 256), 256, 0, stream>>>(

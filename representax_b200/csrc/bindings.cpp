@@ -2,6 +2,13 @@
 #include <torch/extension.h>
 
 namespace rx {
+void rope_forward(const at::Tensor& x, at::Tensor& y, const at::Tensor& pos, const c10::optional<at::Tensor>& axis_of,
+                  const at::Tensor& inv_freq, int64_t heads, const c10::optional<at::Tensor>& norm_w, double eps);
+void rope_backward(const at::Tensor& dy, at::Tensor& dx, const c10::optional<at::Tensor>& x, const at::Tensor& pos,
+                   const c10::optional<at::Tensor>& axis_of, const at::Tensor& inv_freq, int64_t heads,
+                   const c10::optional<at::Tensor>& norm_w, double eps, const c10::optional<at::Tensor>& dw);
+void activation_forward(const at::Tensor& z, at::Tensor& y, int64_t act, bool gated);
+void activation_backward(const at::Tensor& dy, const at::Tensor& z, at::Tensor& dz, int64_t act, bool gated);
 void gemm_tcgen05(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_mn, bool b_mn,
                   int64_t epi, int64_t out_mode, double alpha,
                   const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& aux_in,
@@ -102,4 +109,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("slot_reduce", &rx::slot_reduce);
   m.def("sharded_grad_reduce", &rx::sharded_grad_reduce);
   m.def("sharded_adamw", &rx::sharded_adamw);
+  m.def("rope_forward", &rx::rope_forward);
+  m.def("rope_backward", &rx::rope_backward);
+  m.def("activation_forward", &rx::activation_forward);
+  m.def("activation_backward", &rx::activation_backward);
 }

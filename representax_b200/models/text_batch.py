@@ -190,4 +190,27 @@ class TokenBatch:
         )
 
 
-__all__ = ["PackedTokens", "TokenBatch", "pack_tokens"]
+
+
+def packed_segments(batch: "TokenBatch", device: torch.device | str | None = None):
+    """(PackedTokens on ``device``, Segments) for a token batch.
+
+    Batches packed on the host by the loader carry ``packed`` already; a
+    batch without it is packed here (one device-to-host copy of the mask).
+    Positions are the column index of each token.
+    """
+
+    from representax_b200.ops.nn import Segments
+
+    device = torch.device(device) if device is not None else batch.attention_mask.device
+    pk = batch.packed
+    if pk is None:
+        ids = batch.input_ids if batch.input_ids is not None else torch.zeros_like(batch.attention_mask)
+        pk = pack_tokens(ids, batch.attention_mask, batch.token_type_ids, batch.position_ids)
+    if pk.input_ids.device != device:
+        pk = pk.map_tensors(lambda t: t.to(device, non_blocking=True))
+    seg = Segments([int(v) for v in pk.cu_host.tolist()], pk.cu_seqlens.to(device=device, dtype=torch.int32))
+    return pk, seg
+
+
+__all__ = ["PackedTokens", "TokenBatch", "pack_tokens", "packed_segments"]
