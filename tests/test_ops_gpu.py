@@ -1,0 +1,157 @@
+"""Native packed-row ops (bf16, sm_100a kernels) against their fp32 PyTorch statements."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from representax_b200.ops import nn as N
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _close(a, b, tol):
+    a, b = a.float(), b.float()
+    err = (a - b).abs().max().item()
+    scale = b.abs().max().item() + 1e-6
+    assert err <= tol * scale, f"max err {err:.3e} vs scale {scale:.3e}"
+
+
+def _pair(*shape, scale=1.0, seed=0):
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    x32 = (torch.randn(*shape, device=DEV, generator=g) * scale).requires_grad_()
+    x16 = x32.detach().to(torch.bfloat16).requires_grad_()
+    return x32, x16
+
+
+def _seg(lengths):
+    return N.Segments.from_lengths(lengths, DEV)
+
+
+@pytest.mark.parametrize("bias,residual", [(False, False), (True, True)])
+def test_linear(bias, residual):
+    x32, x16 = _pair(300, 256)
+    w = torch.nn.Parameter(torch.randn(384, 256, device=DEV) * 0.05)
+    b = torch.nn.Parameter(torch.randn(384, device=DEV)) if bias else None
+    r32, r16 = _pair(300, 384, seed=1) if residual else (None, None)
+    y32 = N.linear(x32, w, b, r32)
+    y16 = N.linear(x16, w, b, r16)
+    _close(y16, y32, 2e-2)
+    g = torch.randn_like(y32)
+    grads32 = torch.autograd.grad(y32, [x32, w] + ([b] if bias else []), g)
+    grads16 = torch.autograd.grad(y16, [x16, w] + ([b] if bias else []), g.to(torch.bfloat16))
+    for a, c in zip(grads16, grads32):
+        _close(a, c, 3e-2)
+
+
+@pytest.mark.parametrize("rms", [False, True])
+def test_norms(rms):
+    x32, x16 = _pair(257, 1024, scale=3.0)
+    w = torch.nn.Parameter(1 + 0.1 * torch.randn(1024, device=DEV))
+    f = (lambda x: N.rms_norm(x, w, 1e-6)) if rms else (lambda x: N.layer_norm(x, w, None, 1e-5))
+    y32, y16 = f(x32), f(x16)
+    _close(y16, y32, 2e-2)
+    g = torch.randn_like(y32)
+    a = torch.autograd.grad(y16, [x16, w], g.to(torch.bfloat16))
+    c = torch.autograd.grad(y32, [x32, w], g)
+    for u, v in zip(a, c):
+        _close(u, v, 3e-2)
+
+
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("axes,norm", [(1, False), (1, True), (3, False)])
+def test_rope(D, axes, norm):
+    heads, T = 3, 200
+    x32, x16 = _pair(T, heads * D, scale=2.0)
+    pos = torch.randint(0, 5000, (axes, T), device=DEV, dtype=torch.int32)
+    inv = N.rope_inv_freq(D, 10000.0, DEV)
+    axis = torch.tensor(N.mrope_axis_table(D, (D // 8, D // 8 * 3 // 2, D // 8 * 3 // 2), interleaved=True),
+                        device=DEV, dtype=torch.int32) if axes > 1 else None
+    w = torch.nn.Parameter(1 + 0.1 * torch.randn(D, device=DEV)) if norm else None
+    y32 = N.rope(x32, pos, inv, heads, axis_of=axis, norm_weight=w)
+    y16 = N.rope(x16, pos, inv, heads, axis_of=axis, norm_weight=w)
+    _close(y16, y32, 2e-2)
+    g = torch.randn_like(y32)
+    ins32 = [x32] + ([w] if norm else [])
+    ins16 = [x16] + ([w] if norm else [])
+    for a, c in zip(torch.autograd.grad(y16, ins16, g.to(torch.bfloat16)), torch.autograd.grad(y32, ins32, g)):
+        _close(a, c, 3e-2)
+
+
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("heads,kv,causal,window", [(4, 4, False, -1), (4, 2, True, -1), (4, 1, False, 20),
+                                                    (2, 2, False, 64)])
+def test_attention(D, heads, kv, causal, window):
+    lengths = [130, 1, 77, 256, 64]
+    T = sum(lengths)
+    seg = _seg(lengths)
+    q32, q16 = _pair(T, heads * D, seed=1)
+    k32, k16 = _pair(T, kv * D, seed=2)
+    v32, v16 = _pair(T, kv * D, seed=3)
+    o32 = N.attention(q32, k32, v32, seg, heads=heads, kv_heads=kv, causal=causal, window=window)
+    o16 = N.attention(q16, k16, v16, seg, heads=heads, kv_heads=kv, causal=causal, window=window)
+    _close(o16, o32, 2e-2)
+    g = torch.randn_like(o32)
+    a = torch.autograd.grad(o16, [q16, k16, v16], g.to(torch.bfloat16))
+    c = torch.autograd.grad(o32, [q32, k32, v32], g)
+    for u, w in zip(a, c):
+        _close(u, w, 4e-2)
+
+
+@pytest.mark.parametrize("D,heads,kv", [(64, 4, 4), (128, 4, 2)])
+def test_qkv_attention_with_rope_and_norm(D, heads, kv):
+    lengths = [100, 37, 128]
+    T = sum(lengths)
+    seg = _seg(lengths)
+    x32, x16 = _pair(T, (heads + 2 * kv) * D)
+    pos = torch.cat([torch.arange(n) for n in lengths]).to(DEV, torch.int32)
+    inv = N.rope_inv_freq(D, 1e6, DEV)
+    qn = torch.nn.Parameter(1 + 0.1 * torch.randn(D, device=DEV))
+    kn = torch.nn.Parameter(1 + 0.1 * torch.randn(D, device=DEV))
+    kw = dict(heads=heads, kv_heads=kv, pos=pos, inv_freq=inv, q_norm=qn, k_norm=kn, causal=True)
+    o32 = N.qkv_attention(x32, seg, **kw)
+    o16 = N.qkv_attention(x16, seg, **kw)
+    _close(o16, o32, 2e-2)
+    g = torch.randn_like(o32)
+    a = torch.autograd.grad(o16, [x16, qn, kn], g.to(torch.bfloat16))
+    c = torch.autograd.grad(o32, [x32, qn, kn], g)
+    for u, w in zip(a, c):
+        _close(u, w, 4e-2)
+
+
+@pytest.mark.parametrize("name", ["gelu", "gelu_pytorch_tanh", "silu", "quick_gelu"])
+@pytest.mark.parametrize("gated", [False, True])
+def test_activations(name, gated):
+    z32, z16 = _pair(123, 512, scale=2.0)
+    f = N.gated_activation if gated else N.activation
+    y32, y16 = f(z32, name), f(z16, name)
+    _close(y16, y32, 1e-2)
+    g = torch.randn_like(y32)
+    _close(torch.autograd.grad(y16, z16, g.to(torch.bfloat16))[0], torch.autograd.grad(y32, z32, g)[0], 2e-2)
+
+
+def test_modernvbert_native_matches_reference():
+    from representax_b200.models.modernvbert import ModernVBERTBatch, ModernVBERTConfig, ModernVBERTEncoder
+    from representax_b200.models.modernvbert.config import ModernVBERTTextConfig, SigLIPVisionConfig
+
+    cfg = ModernVBERTConfig(
+        text=ModernVBERTTextConfig(vocab_size=512, hidden_size=256, intermediate_size=384, num_hidden_layers=4,
+                                   num_attention_heads=4, local_attention=16, pad_token_id=0),
+        vision=SigLIPVisionConfig(hidden_size=256, intermediate_size=512, num_hidden_layers=2, num_attention_heads=4,
+                                  image_size=64, patch_size=16),
+        image_token_id=500, pixel_shuffle_factor=2)
+    m32 = ModernVBERTEncoder(cfg, seed=0).to(DEV)
+    m16 = ModernVBERTEncoder(cfg, seed=0, compute_dtype=torch.bfloat16).to(DEV)
+    ids = torch.randint(3, 490, (3, 40))
+    ids[:, 1:5] = 500
+    mask = torch.ones_like(ids)
+    mask[2, 30:] = 0
+    pixels = torch.randn(3, 1, 3, 64, 64)
+    b = ModernVBERTBatch(mask, ids, pixels).pack().map_tensors(lambda t: t.to(DEV))
+    e32 = m32.encode(b)
+    e16 = m16.encode(b)
+    cos = torch.nn.functional.cosine_similarity(e16.float(), e32.float(), dim=-1)
+    assert cos.min().item() > 0.995, cos
+    e16.sum().backward()
+    assert m16.vision.layers[0].qkv_w.grad is not None
