@@ -316,7 +316,7 @@ __global__ void attn_dq_convert_kernel(const float* __restrict__ acc, __nv_bfloa
 }
 
 // ==================================================================== backward
-template <int D>
+template <int D, bool GQA>
 __global__ void __launch_bounds__(kThreads) attn_bwd_kernel(const Params p) {
   const int kbk = blockIdx.x;
   const int kvh = blockIdx.y;  // key/value head; its query heads are looped below
@@ -374,7 +374,8 @@ __global__ void __launch_bounds__(kThreads) attn_bwd_kernel(const Params p) {
 
   const int kj0 = k_lo + warp * 16 + g;  // this thread's key rows kj0, kj0 + 8
 
-  for (int h = kvh * p.heads_per_kv; h < (kvh + 1) * p.heads_per_kv; ++h)
+  const int group = GQA ? p.heads_per_kv : 1;
+  for (int h = kvh * group; h < (kvh + 1) * group; ++h)
   for (int qb = qb_first; qb < qb_last; ++qb) {
     const __nv_bfloat16* qbase = p.q + static_cast<int64_t>(start) * p.ldq + h * D;
     const __nv_bfloat16* dobase = p.dO + static_cast<int64_t>(start) * p.ld_do + h * D;
@@ -516,8 +517,10 @@ __global__ void __launch_bounds__(kThreads) attn_bwd_kernel(const Params p) {
 
 template __global__ void attn_fwd_kernel<64>(const Params p);
 template __global__ void attn_fwd_kernel<128>(const Params p);
-template __global__ void attn_bwd_kernel<64>(const Params p);
-template __global__ void attn_bwd_kernel<128>(const Params p);
+template __global__ void attn_bwd_kernel<64, false>(const Params p);
+template __global__ void attn_bwd_kernel<128, false>(const Params p);
+template __global__ void attn_bwd_kernel<64, true>(const Params p);
+template __global__ void attn_bwd_kernel<128, true>(const Params p);
 
 }  // namespace attn
 
@@ -624,11 +627,16 @@ void attention_backward(const at::Tensor& dO, const at::Tensor& q, const at::Ten
     RX_CUDA_CHECK(cudaGetLastError());
   }
   dim3 grid((max_len + attn::BN - 1) / attn::BN, kv_heads, p.batch);
+  const bool gqa = kv_heads != heads;
   if (d == 64) {
-    attn::attn_bwd_kernel<64><<<grid, attn::kThreads, attn::bwd_smem_bytes<64>(), st>>>(p);
+    if (gqa) attn::attn_bwd_kernel<64, true><<<grid, attn::kThreads, attn::bwd_smem_bytes<64>(), st>>>(p);
+    else attn::attn_bwd_kernel<64, false><<<grid, attn::kThreads, attn::bwd_smem_bytes<64>(), st>>>(p);
+  } else if (gqa) {
+    set_smem(attn::attn_bwd_kernel<128, true>, attn::bwd_smem_bytes<128>());
+    attn::attn_bwd_kernel<128, true><<<grid, attn::kThreads, attn::bwd_smem_bytes<128>(), st>>>(p);
   } else {
-    set_smem(attn::attn_bwd_kernel<128>, attn::bwd_smem_bytes<128>());
-    attn::attn_bwd_kernel<128><<<grid, attn::kThreads, attn::bwd_smem_bytes<128>(), st>>>(p);
+    set_smem(attn::attn_bwd_kernel<128, false>, attn::bwd_smem_bytes<128>());
+    attn::attn_bwd_kernel<128, false><<<grid, attn::kThreads, attn::bwd_smem_bytes<128>(), st>>>(p);
   }
   RX_CUDA_CHECK(cudaGetLastError());
   {

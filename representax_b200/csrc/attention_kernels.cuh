@@ -47,12 +47,15 @@ struct Params {
 
 template <int D>
 __global__ void __launch_bounds__(kThreads) attn_fwd_kernel(const Params p);
-template <int D>
+// GQA: loop over the query heads of each key/value head (heads_per_kv > 1).
+template <int D, bool GQA>
 __global__ void __launch_bounds__(kThreads) attn_bwd_kernel(const Params p);
 extern template __global__ void attn_fwd_kernel<64>(const Params p);
 extern template __global__ void attn_fwd_kernel<128>(const Params p);
-extern template __global__ void attn_bwd_kernel<64>(const Params p);
-extern template __global__ void attn_bwd_kernel<128>(const Params p);
+extern template __global__ void attn_bwd_kernel<64, false>(const Params p);
+extern template __global__ void attn_bwd_kernel<128, false>(const Params p);
+extern template __global__ void attn_bwd_kernel<64, true>(const Params p);
+extern template __global__ void attn_bwd_kernel<128, true>(const Params p);
 // dvec[h, t] = <dO[t, h, :], O[t, h, :]>, one warp per (t, h); D = 64 or 128.
 __global__ void attn_dvec_kernel(const __nv_bfloat16* __restrict__ o, int64_t ldo,
                                  const __nv_bfloat16* __restrict__ dO, int64_t ld_do,

@@ -114,7 +114,7 @@ extern "C" int rx_attention_backward_noalloc(
         static_cast<const __nv_bfloat16*>(o), ld_o, p.dO, ld_do, dvec, total_tokens, heads, 64);
   }
   dim3 grid((max_len + BN - 1) / BN, heads, batch);
-  attn_bwd_kernel<64><<<grid, kThreads, bwd_smem_bytes<64>(), stream>>>(p);
+  attn_bwd_kernel<64, false><<<grid, kThreads, bwd_smem_bytes<64>(), stream>>>(p);
   {
     const int64_t n4 = static_cast<int64_t>(total_tokens) * static_cast<int64_t>(width) / 4;
     attn_dq_convert_kernel<<<static_cast<unsigned>((n4 + 255) / 256), 256, 0, stream>>>(

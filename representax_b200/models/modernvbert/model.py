@@ -166,9 +166,9 @@ class VisionLayer(nn.Module):
         self.fc1_w, self.fc1_b = _normal((inter, hidden), std, g), nn.Parameter(torch.zeros(inter))
         self.fc2_w, self.fc2_b = _normal((hidden, inter), std, g), nn.Parameter(torch.zeros(hidden))
 
-    def forward(self, h, seg, heads: int, eps: float, act: str):
+    def forward(self, h, seg, heads: int, eps: float, act: str, causal: bool = False):
         x = N.layer_norm(h, self.ln1_w, self.ln1_b, eps)
-        a = N.qkv_attention(N.linear(x, self.qkv_w, self.qkv_b), seg, heads=heads)
+        a = N.qkv_attention(N.linear(x, self.qkv_w, self.qkv_b), seg, heads=heads, causal=causal)
         h = N.linear(a, self.out_w, self.out_b, residual=h)
         x = N.layer_norm(h, self.ln2_w, self.ln2_b, eps)
         m = N.activation(N.linear(x, self.fc1_w, self.fc1_b), act)

@@ -155,3 +155,32 @@ def test_modernvbert_native_matches_reference():
     assert cos.min().item() > 0.995, cos
     e16.sum().backward()
     assert m16.vision.layers[0].qkv_w.grad is not None
+
+
+def test_qwen3_vl_native_matches_reference():
+    from representax_b200.models.qwen3 import Qwen3TextConfig
+    from representax_b200.models.qwen3_vl import Qwen3VLBatch, Qwen3VLConfig, Qwen3VLEncoder, Qwen3VLVisionConfig
+
+    cfg = Qwen3VLConfig(
+        text=Qwen3TextConfig(vocab_size=512, hidden_size=256, intermediate_size=512, num_hidden_layers=3,
+                             num_attention_heads=4, num_key_value_heads=2, head_dimension=64, mrope_section=(8, 12, 12),
+                             pad_token_id=0),
+        vision=Qwen3VLVisionConfig(depth=2, hidden_size=128, intermediate_size=256, num_heads=2, patch_size=8,
+                                   out_hidden_size=256, num_position_embeddings=64, deepstack_visual_indexes=(0,)),
+        image_token_id=500)
+    m32 = Qwen3VLEncoder(cfg, seed=0).to(DEV)
+    m16 = Qwen3VLEncoder(cfg, seed=0, compute_dtype=torch.bfloat16).to(DEV)
+    ids = torch.randint(1, 490, (2, 48))
+    ids[0, 2:18] = 500      # 8x8 patch grid -> 16 merged tokens
+    ids[1, 5:21] = 500
+    mask = torch.ones_like(ids)
+    mask[1, 40:] = 0
+    grid = torch.tensor([[1, 8, 8], [1, 8, 8]])
+    pixels = torch.randn(128, 3 * 2 * 8 * 8)
+    b = Qwen3VLBatch(ids, mask, pixels, grid).prepare(cfg)
+    e32 = m32.encode(b)
+    e16 = m16.encode(b)
+    cos = torch.nn.functional.cosine_similarity(e16.float(), e32.float(), dim=-1)
+    assert cos.min().item() > 0.99, cos
+    e16.sum().backward()
+    assert m16.text.layers[0].q_norm.grad is not None
