@@ -43,6 +43,8 @@ class Qwen3TextConfig(FrozenConfig):
     pad_token_id: int = 151643
     initializer_range: float = 0.02
     tie_word_embeddings: bool = True
+    qkv_bias: bool = False        # Qwen2 / Qwen2.5 projections carry biases
+    qk_norm: bool = True          # Qwen3 per-head RMSNorm on q and k
 
     @model_validator(mode="after")
     def _validate(self):
@@ -53,13 +55,13 @@ class Qwen3TextConfig(FrozenConfig):
         return self
 
     @classmethod
-    def from_hf_config(cls, value: Mapping[str, Any]) -> "Qwen3TextConfig":
+    def from_hf_config(cls, value: Mapping[str, Any], **overrides: Any) -> "Qwen3TextConfig":
         text = value.get("text_config", value)
         rope = text.get("rope_parameters") or text.get("rope_scaling") or {}
         theta = float(rope.get("rope_theta", text.get("rope_theta", 1_000_000.0)))
         section = rope.get("mrope_section")
         hidden, heads = int(text["hidden_size"]), int(text["num_attention_heads"])
-        return cls(
+        fields = dict(
             vocab_size=int(text["vocab_size"]), hidden_size=hidden, intermediate_size=int(text["intermediate_size"]),
             num_hidden_layers=int(text["num_hidden_layers"]), num_attention_heads=heads,
             num_key_value_heads=int(text.get("num_key_value_heads", heads)),
@@ -71,6 +73,8 @@ class Qwen3TextConfig(FrozenConfig):
             pad_token_id=int(text.get("pad_token_id") or 151643),
             tie_word_embeddings=bool(value.get("tie_word_embeddings", text.get("tie_word_embeddings", True))),
         )
+        fields.update(overrides)
+        return cls(**fields)
 
     def to_hf_config(self) -> dict[str, Any]:
         rope: dict[str, Any] = {"rope_type": "default", "rope_theta": self.rope_theta}
@@ -95,8 +99,9 @@ class Qwen3DecoderLayer(nn.Module):
         qd, kd = cfg.num_attention_heads * d, cfg.num_key_value_heads * d
         self.input_norm = nn.Parameter(torch.ones(h))
         self.qkv = _normal((qd + 2 * kd, h), std, g)       # [q; k; v] rows
-        self.q_norm = nn.Parameter(torch.ones(d))
-        self.k_norm = nn.Parameter(torch.ones(d))
+        self.qkv_bias = nn.Parameter(torch.zeros(qd + 2 * kd)) if cfg.qkv_bias else None
+        self.q_norm = nn.Parameter(torch.ones(d)) if cfg.qk_norm else None
+        self.k_norm = nn.Parameter(torch.ones(d)) if cfg.qk_norm else None
         self.o_proj = _normal((h, qd), std, g)
         self.post_norm = nn.Parameter(torch.ones(h))
         self.gate_up = _normal((2 * cfg.intermediate_size, h), std, g)  # [gate; up] rows
@@ -104,7 +109,7 @@ class Qwen3DecoderLayer(nn.Module):
 
     def forward(self, h, seg, pos, axis_of, inv_freq, cfg: Qwen3TextConfig):
         x = N.rms_norm(h, self.input_norm, cfg.norm_epsilon)
-        a = N.qkv_attention(N.linear(x, self.qkv), seg, heads=cfg.num_attention_heads,
+        a = N.qkv_attention(N.linear(x, self.qkv, self.qkv_bias), seg, heads=cfg.num_attention_heads,
                             kv_heads=cfg.num_key_value_heads, pos=pos, inv_freq=inv_freq, axis_of=axis_of,
                             q_norm=self.q_norm, k_norm=self.k_norm, norm_eps=cfg.norm_epsilon, causal=True)
         h = N.linear(a, self.o_proj, residual=h)
@@ -160,16 +165,23 @@ def qwen3_layer_state(layer: Qwen3DecoderLayer, cfg: Qwen3TextConfig, prefix: st
     qd, kd, inter = cfg.num_attention_heads * d, cfg.num_key_value_heads * d, cfg.intermediate_size
     w = layer.qkv.detach()
     gu = layer.gate_up.detach()
-    return {
+    out = {
         prefix + "input_layernorm.weight": layer.input_norm.detach(),
         prefix + "self_attn.q_proj.weight": w[:qd], prefix + "self_attn.k_proj.weight": w[qd:qd + kd],
         prefix + "self_attn.v_proj.weight": w[qd + kd:], prefix + "self_attn.o_proj.weight": layer.o_proj.detach(),
-        prefix + "self_attn.q_norm.weight": layer.q_norm.detach(),
-        prefix + "self_attn.k_norm.weight": layer.k_norm.detach(),
         prefix + "post_attention_layernorm.weight": layer.post_norm.detach(),
         prefix + "mlp.gate_proj.weight": gu[:inter], prefix + "mlp.up_proj.weight": gu[inter:],
         prefix + "mlp.down_proj.weight": layer.down.detach(),
     }
+    if layer.q_norm is not None:
+        out[prefix + "self_attn.q_norm.weight"] = layer.q_norm.detach()
+        out[prefix + "self_attn.k_norm.weight"] = layer.k_norm.detach()
+    if layer.qkv_bias is not None:
+        b = layer.qkv_bias.detach()
+        out[prefix + "self_attn.q_proj.bias"] = b[:qd]
+        out[prefix + "self_attn.k_proj.bias"] = b[qd:qd + kd]
+        out[prefix + "self_attn.v_proj.bias"] = b[qd + kd:]
+    return out
 
 
 def load_qwen3_layer(layer: Qwen3DecoderLayer, tensors: Mapping[str, torch.Tensor], prefix: str) -> None:
@@ -179,8 +191,12 @@ def load_qwen3_layer(layer: Qwen3DecoderLayer, tensors: Mapping[str, torch.Tenso
         layer.qkv.copy_(torch.cat([t("self_attn.q_proj.weight"), t("self_attn.k_proj.weight"),
                                    t("self_attn.v_proj.weight")]))
         layer.o_proj.copy_(t("self_attn.o_proj.weight"))
-        layer.q_norm.copy_(t("self_attn.q_norm.weight"))
-        layer.k_norm.copy_(t("self_attn.k_norm.weight"))
+        if layer.q_norm is not None:
+            layer.q_norm.copy_(t("self_attn.q_norm.weight"))
+            layer.k_norm.copy_(t("self_attn.k_norm.weight"))
+        if layer.qkv_bias is not None:
+            layer.qkv_bias.copy_(torch.cat([t("self_attn.q_proj.bias"), t("self_attn.k_proj.bias"),
+                                            t("self_attn.v_proj.bias")]))
         layer.post_norm.copy_(t("post_attention_layernorm.weight"))
         layer.gate_up.copy_(torch.cat([t("mlp.gate_proj.weight"), t("mlp.up_proj.weight")]))
         layer.down.copy_(t("mlp.down_proj.weight"))
