@@ -98,3 +98,24 @@ def test_qwen3_vl_matches_transformers(tmp_path):
     torch.testing.assert_close(got[mask.bool()], ref[mask.bool()], rtol=3e-4, atol=3e-4)
     s = Qwen3VLReranker(model, true_token_id=5, false_token_id=6).score(Qwen3VLBatch(ids, mask, pixels, grid))
     assert s.shape == (2,) and bool(((s > 0) & (s < 1)).all())
+
+
+def test_family_catalog_and_pinned_loaders(tmp_path):
+    from representax_b200.integrations import families as F
+    from representax_b200.integrations.pinned import load_modernvbert_text_encoder
+    from representax_b200.models.modernvbert import ModernVBERTCheckpointAdapter, ModernVBERTTextEncoder
+    from representax_b200.models.modernvbert.config import ModernVBERTTextConfig
+
+    assert F.get_model_type_family("qwen3_vl").name == "qwen3_vl"
+    arch = F.get_hugging_face_architecture("bert")
+    assert arch.family == "bert" and arch.has_auto_model
+    assert F.get_hugging_face_architecture("llama").support is F.ArchitectureSupport.CATALOGUED
+    for fam in F.MODEL_FAMILIES.values():
+        assert F.resolve_native_loader(fam.model_types[0]) is not None
+    text = ModernVBERTTextEncoder(ModernVBERTTextConfig(vocab_size=64, hidden_size=32, intermediate_size=48,
+                                                        num_hidden_layers=2, num_attention_heads=2,
+                                                        pad_token_id=0))
+    ModernVBERTCheckpointAdapter.save(text, tmp_path)
+    loaded = load_modernvbert_text_encoder(tmp_path)
+    for a, b in zip(text.parameters(), loaded.parameters()):
+        torch.testing.assert_close(a, b)
