@@ -50,6 +50,8 @@ def _args():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--global-batch", type=int, default=GLOBAL_BATCH)
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--retain-gb", type=float, default=None,
+                   help="GradCache graph-retention budget in GiB (default: free HBM minus a reserve; 0: replay all)")
     return p.parse_args()
 
 
@@ -147,7 +149,9 @@ def main() -> None:
     model = BertEncoder(config, seed=0, compute_dtype=torch.bfloat16)
     state = init_train_state(model, device=device, precision=BF16_MIXED_POLICY)
     step = TrainStep(state, MNRTask(scale=20.0), optimizer=AdamW(learning_rate=2e-5, weight_decay=0.01),
-                     precision=BF16_MIXED_POLICY, execution=GradCache(query_chunk_size=MINI_BATCH),
+                     precision=BF16_MIXED_POLICY,
+                     execution=GradCache(query_chunk_size=MINI_BATCH,
+                                         retain_bytes=None if args.retain_gb is None else int(args.retain_gb * 2**30)),
                      max_gradient_norm=1.0, dist=ctx, stochastic=False)
 
     # Host batches (pinned), distinct per step and per rank; same shapes every step.
@@ -248,6 +252,10 @@ def main() -> None:
                 "mini_batch": MINI_BATCH,
                 "seq_len": SEQ,
                 "valid_len": [MIN_LEN, SEQ],
+                "grad_cache": ("exact cached MNR; first-pass graphs of {retained_chunks} of {chunks} chunks kept in "
+                               "HBM ({gb:.0f} GB), their replay forward skipped; all other chunks replayed").format(
+                                   gb=step.execution.stats.get("retained_bytes", 0) / 2**30, **{
+                                       k: step.execution.stats.get(k, 0) for k in ("retained_chunks", "chunks")}),
                 "parallelism": f"dp{world}" + ("" if world == 1 else " with cross-rank negatives"),
                 "loss": "cached MNR (GradCache), scale 20, global negatives",
                 "optimizer": "AdamW lr 2e-5 wd 0.01, clip 1.0, fp32 master, bf16 compute",

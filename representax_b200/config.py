@@ -374,6 +374,10 @@ class B200ExecutionConfig(FrozenConfig):
     gradient_bucket_bytes: PositiveInt = 64 * 2 ** 20
     cuda_graphs: bool = False
     deterministic: bool = True
+    # GradCache: device bytes that first-pass chunk graphs may keep so their
+    # replay forward is skipped (exact same gradient). None = size from free
+    # HBM at run time; 0 = always replay.
+    grad_cache_retain_bytes: NonNegativeInt | None = None
 
 
 class TrainingConfig(FrozenConfig):

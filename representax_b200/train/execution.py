@@ -13,11 +13,17 @@ cross-rank negatives when distributed); then each chunk is re-encoded with
 autograd and back-propagated with its slice of the representation gradient.
 Replay draws the same random streams as the first pass, so the update equals
 the direct one.
+
+On a GPU with memory to spare, the first pass keeps the autograd graph of as
+many chunks as fit in ``retain_bytes`` (by default the free HBM minus a
+reserve for replaying the others): those chunks are back-propagated straight
+from their first-pass graph instead of being re-encoded. The gradient is the
+same; only the recomputation is skipped.
 """
 
 from __future__ import annotations
 
-from dataclasses import dataclass
+from dataclasses import dataclass, field
 from typing import Any
 
 import torch
@@ -104,20 +110,78 @@ class Direct:
         return _detach(out)
 
 
-def _encode_chunks(model, payload, route: Route, chunk: int, streams: StreamFactory, role: str):
+class RetainBudget:
+    """Decides which first-pass chunk graphs stay resident (CUDA only).
+
+    A chunk is kept while the memory already held by kept graphs plus the
+    largest graph seen so far fits in the budget; the remaining chunks run
+    without autograd state and are replayed later.
+    """
+
+    RESERVE = 12 * 2 ** 30
+
+    def __init__(self, limit: int | None, device: torch.device | None) -> None:
+        self.enabled = device is not None and device.type == "cuda" and limit != 0
+        self.device = device
+        if self.enabled and limit is None:
+            free, _ = torch.cuda.mem_get_info(device)
+            # blocks cached by the allocator but not in use are available too
+            free += torch.cuda.memory_reserved(device) - torch.cuda.memory_allocated(device)
+            limit = max(0, free - self.RESERVE)
+        self.limit = limit or 0
+        self.used = 0
+        self.largest = 0
+
+    def admit(self) -> bool:
+        return self.enabled and self.used + 2 * self.largest <= self.limit
+
+    def record(self, before: int) -> None:
+        size = max(0, torch.cuda.memory_allocated(self.device) - before)
+        self.used += size
+        self.largest = max(self.largest, size)
+
+
+def _model_device(model) -> torch.device | None:
+    for p in model.parameters():
+        return p.device
+    return None
+
+
+def _encode_chunks(model, payload, route: Route, chunk: int, streams: StreamFactory, role: str,
+                   budget: RetainBudget | None = None):
+    """Encode every chunk; returns (detached reps, rows, {start: (stop, graph reps)})."""
+
     rows = leading_rows(payload)
-    outs = []
-    with torch.no_grad():
-        for i, start in enumerate(range(0, rows, chunk)):
-            part = slice_rows(payload, start, min(rows, start + chunk))
-            outs.append(encode(model, part, route=route, generator=streams(role, i)))
-    return torch.cat(outs), rows
+    outs, kept = [], {}
+    for i, start in enumerate(range(0, rows, chunk)):
+        stop = min(rows, start + chunk)
+        part = slice_rows(payload, start, stop)
+        if budget is not None and budget.admit():
+            before = torch.cuda.memory_allocated(budget.device)
+            with torch.enable_grad():
+                reps = encode(model, part, route=route, generator=streams(role, i))
+            budget.record(before)
+            kept[start] = (stop, reps)
+            outs.append(reps.detach())
+        else:
+            with torch.no_grad():
+                outs.append(encode(model, part, route=route, generator=streams(role, i)))
+    return torch.cat(outs), rows, kept
 
 
 def _replay_chunks(model, payload, route: Route, chunk: int, grads: torch.Tensor, streams: StreamFactory,
-                   role: str) -> None:
+                   role: str, kept: dict | None = None) -> None:
     rows = leading_rows(payload)
+    kept = kept or {}
+    done = set(kept)
+    # Retained graphs first: their memory is released before any replay runs.
+    for start in sorted(kept):
+        stop, reps = kept.pop(start)
+        reps.backward(grads[start:stop])
+        del reps
     for i, start in enumerate(range(0, rows, chunk)):
+        if start in done:
+            continue
         stop = min(rows, start + chunk)
         part = slice_rows(payload, start, stop)
         with torch.enable_grad():
@@ -133,6 +197,8 @@ class GradCache:
     document_chunk_size: int | None = None
     loss_row_chunk_size: int | None = None
     fused: bool = True
+    retain_bytes: int | None = None
+    stats: dict = field(default_factory=dict, compare=False, repr=False)
 
     def __post_init__(self) -> None:
         if self.query_chunk_size <= 0:
@@ -167,17 +233,22 @@ class GradCache:
         if isinstance(base, GISTTask) and isinstance(batch, GISTBatch):
             return self._run_gist(task, base, model, batch, streams=streams, ctx=ctx)
         qc, dc = self.query_chunk_size, self.resolved_document_chunk_size
-        queries, _ = _encode_chunks(model, batch.query, Route.QUERY, qc, streams, "query")
-        documents, _ = _encode_chunks(model, batch.document, Route.DOCUMENT, dc, streams, "document")
+        budget = RetainBudget(self.retain_bytes, _model_device(model))
+        queries, _, kept_q = _encode_chunks(model, batch.query, Route.QUERY, qc, streams, "query", budget)
+        documents, _, kept_d = _encode_chunks(model, batch.document, Route.DOCUMENT, dc, streams, "document",
+                                              budget)
         queries.requires_grad_(True)
         documents.requires_grad_(True)
+        n_chunks = -(-queries.shape[0] // qc) + -(-documents.shape[0] // dc)
+        self.stats.update(retained_chunks=len(kept_q) + len(kept_d), chunks=n_chunks,
+                          retained_bytes=budget.used)
         q_all, d_all, gbatch = _global_batch(batch, queries, documents, ctx, **_fusion(task, self.fused))
         with torch.enable_grad():
             out = task.loss_from_representations((q_all, d_all), gbatch,
                                                  row_chunk_size=self.resolved_loss_row_chunk_size)
             out.loss.backward()
-        _replay_chunks(model, batch.query, Route.QUERY, qc, queries.grad, streams, "query")
-        _replay_chunks(model, batch.document, Route.DOCUMENT, dc, documents.grad, streams, "document")
+        _replay_chunks(model, batch.query, Route.QUERY, qc, queries.grad, streams, "query", kept_q)
+        _replay_chunks(model, batch.document, Route.DOCUMENT, dc, documents.grad, streams, "document", kept_d)
         return _detach(out)
 
     def _run_gist(self, task, base, model, batch, *, streams, ctx):
@@ -187,7 +258,7 @@ class GradCache:
         reps = {}
         for name, (payload, route) in roles.items():
             chunk = self.query_chunk_size if route == Route.QUERY else self.resolved_document_chunk_size
-            value, _ = _encode_chunks(model, payload, route, chunk, streams, name)
+            value, _, _ = _encode_chunks(model, payload, route, chunk, streams, name)
             reps[name] = value.requires_grad_(True)
         with torch.enable_grad():
             out = task.loss_from_representations(base.assemble(reps), batch,
@@ -200,4 +271,4 @@ class GradCache:
         return _detach(out)
 
 
-__all__ = ["Direct", "GradCache"]
+__all__ = ["Direct", "GradCache", "RetainBudget"]

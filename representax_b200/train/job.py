@@ -134,7 +134,9 @@ def build_execution(training: Any):
         g = training.grad_cache
         return GradCache(query_chunk_size=g.resolved_query_micro_batch_size,
                          document_chunk_size=g.resolved_document_micro_batch_size,
-                         loss_row_chunk_size=g.resolved_loss_row_chunk_size)
+                         loss_row_chunk_size=g.resolved_loss_row_chunk_size,
+                         fused=training.b200.fused_mnr_collectives,
+                         retain_bytes=training.b200.grad_cache_retain_bytes)
     if training.mega_batch_mining is not None:
         from .mega_batch import MegaBatchMining
 
