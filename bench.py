@@ -50,6 +50,9 @@ def _args():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--global-batch", type=int, default=GLOBAL_BATCH)
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--optimizer", choices=["sharded", "ddp"], default="sharded",
+                   help="N>1: sharded = peer-memory reduce-scatter + sharded AdamW + all-gather kernels; "
+                        "ddp = NCCL all-reduce + replicated AdamW")
     p.add_argument("--retain-gb", type=float, default=None,
                    help="GradCache graph-retention budget in GiB (default: free HBM minus a reserve; 0: replay all)")
     return p.parse_args()
@@ -147,7 +150,8 @@ def main() -> None:
 
     config = BertConfig.base(hidden_dropout_probability=0.0, attention_dropout_probability=0.0)
     model = BertEncoder(config, seed=0, compute_dtype=torch.bfloat16)
-    state = init_train_state(model, device=device, precision=BF16_MIXED_POLICY)
+    state = init_train_state(model, device=device, precision=BF16_MIXED_POLICY, dist=ctx,
+                             sharded_optimizer=args.optimizer == "sharded")
     step = TrainStep(state, MNRTask(scale=20.0), optimizer=AdamW(learning_rate=2e-5, weight_decay=0.01),
                      precision=BF16_MIXED_POLICY,
                      execution=GradCache(query_chunk_size=MINI_BATCH,

@@ -204,7 +204,8 @@ __global__ void rs_grad_kernel(const int64_t* __restrict__ grad_ptrs, int world,
 
 // Phase 2: clipped AdamW on the owned shard; the new fp32 master and bf16
 // compute values are stored into every rank's buffers (fused all-gather).
-// master_ptrs[r] / copy_ptrs[r]: rank r's flat master / compute buffers.
+// master_ptrs[r] / copy_ptrs[r]: rank r's flat master / compute buffers;
+// m / v hold only this rank's shard (indexed from 0).
 __global__ void adamw_shard_kernel(const float* __restrict__ shard_grad, int64_t off, int64_t n,
                                    const int64_t* __restrict__ master_ptrs, const int64_t* __restrict__ copy_ptrs,
                                    int world, int me, float* __restrict__ m, float* __restrict__ v,
@@ -220,10 +221,10 @@ __global__ void adamw_shard_kernel(const float* __restrict__ shard_grad, int64_t
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
     const int64_t gi = off + i;
     const float g = shard_grad[i] * coef;
-    const float mi = b1 * m[gi] + (1.f - b1) * g;
-    const float vi = b2 * v[gi] + (1.f - b2) * g * g;
-    m[gi] = mi;
-    v[gi] = vi;
+    const float mi = b1 * m[i] + (1.f - b1) * g;
+    const float vi = b2 * v[i] + (1.f - b2) * g * g;
+    m[i] = mi;
+    v[i] = vi;
     const float p = local[gi];
     const float np = p - lr * ((mi / bc1) / (sqrtf(vi / bc2) + eps) + wd * p);
     const __nv_bfloat16 nb = __float2bfloat16_rn(np);

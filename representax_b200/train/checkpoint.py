@@ -312,7 +312,12 @@ def training_tensors(state) -> dict[str, torch.Tensor]:
     out: dict[str, torch.Tensor] = {}
     for name, view in store.named_views("master"):
         out[f"model/{name}"] = view
-    if store.exp_avg is not None:
+    if store.exp_avg is not None and getattr(store, "sharded", False):
+        # sharded optimizer: each rank's file holds its own moment shard
+        out["optimizer/exp_avg_shard"] = store.exp_avg
+        out["optimizer/exp_avg_sq_shard"] = store.exp_avg_sq
+        out["optimizer/shard"] = torch.tensor([store.shard_offset, store.shard_numel, store.group.world])
+    elif store.exp_avg is not None:
         for name, view in store.named_views("exp_avg"):
             out[f"optimizer/exp_avg/{name}"] = view
         for name, view in store.named_views("exp_avg_sq"):
@@ -323,9 +328,18 @@ def training_tensors(state) -> dict[str, torch.Tensor]:
 
 def load_training_tensors(state, tensors: Mapping[str, torch.Tensor]) -> None:
     store = state.store
+    sharded = getattr(store, "sharded", False)
     with torch.no_grad():
-        for which, prefix in (("master", "model/"), ("exp_avg", "optimizer/exp_avg/"),
-                              ("exp_avg_sq", "optimizer/exp_avg_sq/")):
+        if sharded:
+            meta = tensors.get("optimizer/shard")
+            if meta is None or tuple(int(v) for v in meta) != (store.shard_offset, store.shard_numel,
+                                                                 store.group.world):
+                raise IncompleteCheckpointError("checkpoint optimizer shards do not match this run's sharding")
+            store.exp_avg.copy_(tensors["optimizer/exp_avg_shard"].to(store.device))
+            store.exp_avg_sq.copy_(tensors["optimizer/exp_avg_sq_shard"].to(store.device))
+        kinds = (("master", "model/"),) if sharded else (("master", "model/"), ("exp_avg", "optimizer/exp_avg/"),
+                                                          ("exp_avg_sq", "optimizer/exp_avg_sq/"))
+        for which, prefix in kinds:
             for name, view in store.named_views(which):
                 key = prefix + name
                 if key not in tensors:

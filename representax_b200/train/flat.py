@@ -34,8 +34,15 @@ def _align(n: int) -> int:
 
 
 class FlatParameterStore:
+    """``peer_group`` (CUDA, world > 1) selects the sharded-optimizer layout:
+    master, gradient and compute buffers live in peer (IPC) memory so one
+    kernel can reduce every rank's gradient for this rank's shard and
+    another can write the updated parameters into every rank; the AdamW
+    moments hold only this rank's shard ``[shard_offset, shard_offset +
+    shard_numel)``."""
+
     def __init__(self, model: nn.Module, *, device: torch.device, compute_dtype: torch.dtype = torch.float32,
-                 optimizer_state: bool = True) -> None:
+                 optimizer_state: bool = True, peer_group=None) -> None:
         self.device = torch.device(device)
         self.compute_dtype = compute_dtype
         self.slots: list[Slot] = []
@@ -44,13 +51,30 @@ class FlatParameterStore:
         for name, p in params:
             self.slots.append(Slot(name, offset, p.numel(), tuple(p.shape)))
             offset = _align(offset + p.numel())
-        self.numel = max(offset, ALIGN)
-        self.master = torch.zeros(self.numel, dtype=torch.float32, device=self.device)
-        self.grad = torch.zeros(self.numel, dtype=torch.float32, device=self.device)
-        self.exp_avg = torch.zeros(self.numel, dtype=torch.float32, device=self.device) if optimizer_state else None
-        self.exp_avg_sq = torch.zeros(self.numel, dtype=torch.float32, device=self.device) if optimizer_state else None
         self.mixed = compute_dtype != torch.float32
-        self.compute = torch.zeros(self.numel, dtype=compute_dtype, device=self.device) if self.mixed else None
+        self.group = peer_group
+        world = 1 if peer_group is None else peer_group.world
+        self.numel = max(_align(-(-offset // world)) * world, ALIGN * world)
+        shard = self.numel // world
+        rank = 0 if peer_group is None else peer_group.rank
+        self.shard_offset, self.shard_numel = rank * shard, shard
+        if peer_group is None:
+            self.master = torch.zeros(self.numel, dtype=torch.float32, device=self.device)
+            self.grad = torch.zeros(self.numel, dtype=torch.float32, device=self.device)
+            self.compute = torch.zeros(self.numel, dtype=compute_dtype, device=self.device) if self.mixed else None
+            moments = self.numel
+        else:
+            self._peer = {"master": peer_group.buffer(self.numel, torch.float32),
+                          "grad": peer_group.buffer(self.numel, torch.float32)}
+            if self.mixed:
+                self._peer["compute"] = peer_group.buffer(self.numel, compute_dtype)
+            for key, buf in self._peer.items():
+                buf.tensor.zero_()
+            self.master, self.grad = self._peer["master"].tensor, self._peer["grad"].tensor
+            self.compute = self._peer["compute"].tensor if self.mixed else None
+            moments = shard
+        self.exp_avg = torch.zeros(moments, dtype=torch.float32, device=self.device) if optimizer_state else None
+        self.exp_avg_sq = torch.zeros(moments, dtype=torch.float32, device=self.device) if optimizer_state else None
         self.params: dict[str, nn.Parameter] = {}
         modules = dict(model.named_modules())
         for slot, (name, p) in zip(self.slots, params):
@@ -99,6 +123,27 @@ class FlatParameterStore:
             if p.grad is not None:
                 p.main_grad.add_(p.grad.to(torch.float32))
                 p.grad = None
+
+    @property
+    def sharded(self) -> bool:
+        return self.group is not None
+
+    def peer_pointers(self, which: str) -> torch.Tensor:
+        return self._peer[which].ptrs
+
+    def full_moments(self, ctx) -> tuple[torch.Tensor, torch.Tensor]:
+        """AdamW moments over the whole flat buffer (all-gathered when sharded)."""
+
+        if not self.sharded:
+            return self.exp_avg, self.exp_avg_sq
+        import torch.distributed as dist
+
+        out = []
+        for m in (self.exp_avg, self.exp_avg_sq):
+            full = torch.empty(self.numel, dtype=m.dtype, device=m.device)
+            dist.all_gather_into_tensor(full, m.contiguous())
+            out.append(full)
+        return out[0], out[1]
 
     def named_views(self, which: str = "master"):
         buf = {"master": self.master, "grad": self.grad, "exp_avg": self.exp_avg,

@@ -173,7 +173,11 @@ def build_job_runtime(job: JobConfig, *, device: torch.device | str | None = Non
     precision = resolve_precision_policy(job.training.precision)
     if hasattr(model, "compute_dtype"):
         model.compute_dtype = precision.compute_dtype
-    state = init_train_state(model, device=device, precision=precision)
+    from representax_b200.parallel.sharding import plan_from_config
+
+    plan = plan_from_config(job.training.sharding, model, dist.world_size)
+    state = init_train_state(model, device=device, precision=precision, dist=dist,
+                             sharded_optimizer=plan.sharded_optimizer)
     optimizer = build_optimizer(job.optimization)
     execution = build_execution(job.training)
     if job.training.global_batch_size % dist.world_size:

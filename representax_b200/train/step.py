@@ -28,9 +28,19 @@ from .rng import StreamFactory
 from .state import StepMetrics, TrainState
 
 
-def init_train_state(model: torch.nn.Module, *, device, precision: PrecisionPolicy) -> TrainState:
+def init_train_state(model: torch.nn.Module, *, device, precision: PrecisionPolicy, dist: DistContext = LOCAL,
+                     sharded_optimizer: bool = False) -> TrainState:
+    """``sharded_optimizer`` (CUDA, world > 1): AdamW moments sharded over the
+    ranks, gradients reduce-scattered and parameters all-gathered by peer
+    memory kernels fused with the update (see ``TrainStep``)."""
+
     model.to(torch.float32)
-    store = FlatParameterStore(model, device=device, compute_dtype=precision.compute_dtype)
+    group = None
+    if sharded_optimizer and dist.enabled and torch.device(device).type == "cuda":
+        from representax_b200.parallel.peer import peer_group
+
+        group = peer_group(dist, torch.device(device))
+    store = FlatParameterStore(model, device=device, compute_dtype=precision.compute_dtype, peer_group=group)
     scalars = torch.zeros(8, dtype=torch.float32, device=store.device)
     return TrainState(model=model, store=store, scalars=scalars)
 
@@ -70,7 +80,7 @@ class TrainStep:
             else:
                 loss, metrics = self._accumulate(batch, streams)
         store.collect_autograd_grads()
-        if self.dist.enabled:
+        if self.dist.enabled and not store.sharded:
             all_reduce_sum_(store.grad, self.dist)
         return loss, metrics
 
@@ -105,6 +115,9 @@ class TrainStep:
         gate = loss.detach().reshape(1).to(torch.float32)
         for v in metrics.values():
             gate = gate + 0.0 * v.detach().reshape(-1)[:1].to(torch.float32)
+        if self._native and store.sharded:
+            self._sharded_update(gate, max_norm, lr)
+            return
         if self._native:
             from representax_b200.ops._ext import ext
 
@@ -135,6 +148,41 @@ class TrainStep:
             update = mhat / (vhat.sqrt() + opt.eps) + opt.weight_decay * store.master
             store.master.add_(update, alpha=-lr)
             store.refresh_compute()
+
+    def _sharded_update(self, gate: torch.Tensor, max_norm: float, lr: float) -> None:
+        """Fused reduce-scatter -> clipped AdamW on the shard -> all-gather.
+
+        1. device barrier: every rank's gradient accumulator is complete;
+        2. this rank sums all ranks' gradients for its shard by peer loads (in
+           rank order, deterministic) and accumulates the shard's squared norm;
+        3. the squared norm is summed over ranks (8-byte NCCL all-reduce) and
+           turned into the clip coefficient and finite gate on the device;
+        4. AdamW updates the shard and stores the new fp32 master and bf16
+           compute values into every rank's buffers (peer stores);
+        5. device barrier: the next forward reads complete parameters.
+        """
+
+        import torch.distributed as tdist
+
+        from representax_b200.ops._ext import ext
+
+        C = ext()
+        store: FlatParameterStore = self.state.store
+        s = self.state.scalars
+        opt = self.optimizer
+        group = store.group
+        if not hasattr(self, "_shard_grad"):
+            self._shard_grad = torch.empty(store.shard_numel, dtype=torch.float32, device=store.device)
+        group.barrier()
+        self._norm_sq.zero_()
+        C.sharded_grad_reduce(store.peer_pointers("grad"), group.world, store.shard_offset, store.shard_numel,
+                              self._shard_grad, self._norm_sq)
+        tdist.all_reduce(self._norm_sq)
+        C.finalize_clip(self._norm_sq, s, gate.contiguous(), max_norm, 1)
+        C.sharded_adamw(self._shard_grad, store.shard_offset, store.shard_numel, store.peer_pointers("master"),
+                        store.peer_pointers("compute") if store.mixed else None, group.world, group.rank,
+                        store.exp_avg, store.exp_avg_sq, s, lr, opt.b1, opt.b2, opt.eps, opt.weight_decay)
+        group.barrier()
 
     def __call__(self, batch: Any, iteration: int) -> StepMetrics:
         lr = self.optimizer.lr(iteration)

@@ -139,3 +139,59 @@ def test_fused_cross_rank_mnr_matches_gathered_reference(tmp_path, symmetric):
     assert abs(r["loss"] - float(loss)) < 1e-4
     assert torch.allclose(r["gq"].double(), q.grad, rtol=1e-3, atol=1e-6)
     assert torch.allclose(r["gd"].double(), d.grad, rtol=1e-3, atol=1e-6)
+
+
+def _sharded_worker(rank, world, port, out):
+    from representax_b200.data.synthetic import retrieval_pairs
+    from representax_b200.models.bert import BertEncoder
+    from representax_b200.precision import BF16_MIXED_POLICY
+    from representax_b200.tasks._batch import slice_rows, to_device
+    from representax_b200.tasks.retrieval import MNRTask
+    from representax_b200.train.execution import GradCache
+    from representax_b200.train.optimizer import AdamW
+    from representax_b200.train.step import TrainStep, init_train_state
+
+    ctx = _init(rank, world, port, "nccl")
+    dev = torch.device("cuda", rank)
+    full = retrieval_pairs(np.random.default_rng(0), 32, 48, vocab=2000, low=100, min_len=8)
+    local = to_device(slice_rows(full, rank * 16, rank * 16 + 16), dev)
+    local.positive_mask = torch.eye(16, dtype=torch.bool, device=dev)
+    results = {}
+    for sharded in (False, True):
+        state = init_train_state(BertEncoder(_tiny_cfg(), seed=0, compute_dtype=torch.bfloat16), device=dev,
+                                 precision=BF16_MIXED_POLICY, dist=ctx, sharded_optimizer=sharded)
+        assert state.store.sharded == sharded
+        step = TrainStep(state, MNRTask(scale=20.0), optimizer=AdamW(learning_rate=1e-3), precision=BF16_MIXED_POLICY,
+                         execution=GradCache(query_chunk_size=8), dist=ctx, stochastic=False)
+        for it in range(2):
+            m = step(local, it)
+        torch.cuda.synchronize()
+        m_full, v_full = state.store.full_moments(ctx)
+        results[sharded] = {"master": state.store.master[:state.store.numel].clone().cpu(), "m": m_full.cpu(),
+                            "compute": state.store.compute.float().cpu(), "loss": float(m.loss)}
+    if rank == 0:
+        torch.save(results, out)
+    dist.barrier()
+    from representax_b200.parallel.peer import close_peer_groups
+
+    close_peer_groups()
+    dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_sharded_optimizer_matches_ddp(tmp_path):
+    """Fused peer reduce-scatter + sharded AdamW + all-gather == NCCL all-reduce + replicated AdamW."""
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    out = str(tmp_path / "sharded.pt")
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    mp.spawn(_sharded_worker, args=(2, _port(), out), nprocs=2, join=True)
+    r = torch.load(out)
+    a, b = r[True], r[False]
+    assert abs(a["loss"] - b["loss"]) < 1e-3
+    n = min(a["master"].numel(), b["master"].numel())
+    diff = (a["master"][:n] - b["master"][:n]).abs()
+    assert diff.max() <= 4.1e-3                       # at most a couple of lr-sized sign flips
+    assert (diff <= 1e-5 + 1e-3 * b["master"][:n].abs()).float().mean() > 0.999
+    torch.testing.assert_close(a["compute"][:n], a["master"][:n].bfloat16().float())
