@@ -263,6 +263,9 @@ def main() -> None:
                 "parallelism": f"dp{world}" + ("" if world == 1 else " with cross-rank negatives"),
                 "loss": "cached MNR (GradCache), scale 20, global negatives",
                 "optimizer": "AdamW lr 2e-5 wd 0.01, clip 1.0, fp32 master, bf16 compute",
+                "optimizer_step": ("single-GPU fused norm/clip/AdamW kernels" if world == 1 else
+                                   "sharded: peer-memory gradient reduce-scatter + shard AdamW + parameter all-gather"
+                                   if args.optimizer == "sharded" else "NCCL all-reduce + replicated fused AdamW"),
                 "dropout": 0.0,
                 "padding": "packed (padding tokens are not computed)",
                 "l2": "per-step working set > 126 MB L2; no explicit flush",
