@@ -21,6 +21,12 @@ from pinned memory and the loss read back to the host.
 
 from __future__ import annotations
 
+import os
+
+# Retained GradCache graphs fill most of HBM; expandable segments keep the
+# caching allocator from fragmenting around them (must be set before CUDA init).
+os.environ.setdefault("PYTORCH_CUDA_ALLOC_CONF", "expandable_segments:True")
+
 import argparse
 import json
 import os

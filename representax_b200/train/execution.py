@@ -115,7 +115,10 @@ class RetainBudget:
 
     A chunk is kept while the memory already held by kept graphs plus the
     largest graph seen so far fits in the budget; the remaining chunks run
-    without autograd state and are replayed later.
+    without autograd state and are replayed later. Run the process with
+    ``PYTORCH_CUDA_ALLOC_CONF=expandable_segments:True``: with most of HBM
+    held by retained graphs, the default allocator fragments and the
+    replays slow down.
     """
 
     RESERVE = 12 * 2 ** 30
