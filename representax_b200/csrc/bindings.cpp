@@ -9,6 +9,13 @@ void rope_backward(const at::Tensor& dy, at::Tensor& dx, const c10::optional<at:
                    const c10::optional<at::Tensor>& norm_w, double eps, const c10::optional<at::Tensor>& dw);
 void activation_forward(const at::Tensor& z, at::Tensor& y, int64_t act, bool gated);
 void activation_backward(const at::Tensor& dy, const at::Tensor& z, at::Tensor& dz, int64_t act, bool gated);
+void fp8_scale(const at::Tensor& x, at::Tensor& scale, at::Tensor& amax_scratch, bool e5m2);
+void fp8_quantize(const at::Tensor& x, const at::Tensor& scale, at::Tensor& out, bool e5m2, bool transpose);
+void gemm_fp8(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, int64_t a_fmt, int64_t b_fmt,
+              int64_t epi, int64_t out_mode, double alpha, const at::Tensor& scales,
+              const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& residual,
+              const at::Tensor& status);
+void int4_dequantize(const at::Tensor& packed, const at::Tensor& scale_bits, at::Tensor& out);
 void gemm_tcgen05(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_mn, bool b_mn,
                   int64_t epi, int64_t out_mode, double alpha,
                   const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& aux_in,
@@ -109,6 +116,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("slot_reduce", &rx::slot_reduce);
   m.def("sharded_grad_reduce", &rx::sharded_grad_reduce);
   m.def("sharded_adamw", &rx::sharded_adamw);
+  m.def("int4_dequantize", &rx::int4_dequantize);
+  m.def("fp8_scale", &rx::fp8_scale);
+  m.def("fp8_quantize", &rx::fp8_quantize);
+  m.def("gemm_fp8", &rx::gemm_fp8);
   m.def("rope_forward", &rx::rope_forward);
   m.def("rope_backward", &rx::rope_backward);
   m.def("activation_forward", &rx::activation_forward);

@@ -88,6 +88,23 @@ inline CUtensorMap make_tmap_2d_bf16(const void* base, int64_t rows, int64_t col
   return map;
 }
 
+// 2-D tiled map of 8-bit elements with 128-byte rows per box (128 elements)
+// and the 128-byte swizzle (the same shared-memory geometry as 64 bf16).
+inline CUtensorMap make_tmap_2d_u8(const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+  RX_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0, "TMA base must be 16-byte aligned");
+  RX_CHECK(ld % 16 == 0, "8-bit TMA row stride must be a multiple of 16 elements");
+  CUtensorMap map;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld)};
+  cuuint32_t box[2] = {128u, static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t elem_strides[2] = {1, 1};
+  CUresult r = encode_tiled_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides,
+                                 box, elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  RX_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed with code ", static_cast<int>(r));
+  return map;
+}
+
 inline int num_sms(int device) {
   static int cached[64] = {0};
   if (device < 0 || device >= 64) return 148;

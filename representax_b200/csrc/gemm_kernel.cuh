@@ -52,9 +52,15 @@ struct Params {
   const __nv_bfloat16* residual;
   int64_t ld_res;
   float alpha;
+  const float* scales;  // fp8: device [2] per-tensor operand scales multiplied into alpha
   int* status;
   uint64_t timeout_ns;
 };
+
+// Operand kinds: 0 = bf16 x bf16 (kind::f16); 1.. = 8-bit floats
+// (kind::f8f6f4), KIND - 1 = (a_fmt | b_fmt << 1) with 0 = E4M3, 1 = E5M2.
+constexpr int kKindBf16 = 0;
+constexpr int fp8_kind(int a_fmt, int b_fmt) { return 1 + (a_fmt | (b_fmt << 1)); }
 
 __device__ __forceinline__ float gelu_erf(float x) {
   return 0.5f * x * (1.0f + erff(x * 0.70710678118654752440f));
@@ -189,10 +195,13 @@ __device__ __forceinline__ void decode_unit(const Params& p, int u, int& m0, int
   kb1 = min(p.kb_total, kb0 + p.kb_per_split);
 }
 
-template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, int OUT>
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, int OUT, int KIND = kKindBf16>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const Params p) {
+  // Both kinds move 128-byte K rows per stage: 64 bf16 or 128 8-bit values.
+  static_assert(KIND == kKindBf16 || (!A_MN && !B_MN), "8-bit operands are K-major only");
+  constexpr int K_ELEMS = KIND == kKindBf16 ? BK : 2 * BK;
   constexpr int A_BYTES = BM * BK * 2;
   constexpr int B_BYTES = BN * BK * 2;
   constexpr uint32_t TMEM_COLS = 2 * BN;
@@ -263,7 +272,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive_expect_tx(&full[stage], A_BYTES + B_BYTES);
           uint8_t* a_dst = sA + stage * A_BYTES;
           uint8_t* b_dst = sB + stage * B_BYTES;
-          const int k0 = kb * BK;
+          const int k0 = kb * K_ELEMS;
           if constexpr (A_MN) {
             tma_load_2d(a_dst, &tmA, &full[stage], m0, k0);
             tma_load_2d(a_dst + 8192, &tmA, &full[stage], m0 + 64, k0);
@@ -296,7 +305,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t IDESC = idesc_bf16_f32(BM, BN, A_MN, B_MN);
+      constexpr uint32_t IDESC = KIND == kKindBf16
+                                     ? idesc_bf16_f32(BM, BN, A_MN, B_MN)
+                                     : idesc_f8_f32(BM, BN, (KIND - 1) & 1, ((KIND - 1) >> 1) & 1);
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
@@ -330,7 +341,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                                      : smem_desc_sw128(a_addr + kk * 32, 16, 1024);
             const uint64_t bd = B_MN ? smem_desc_sw128(b_addr + kk * 2048, 8192, 1024)
                                      : smem_desc_sw128(b_addr + kk * 32, 16, 1024);
-            umma_f16_ss(d_tmem, ad, bd, IDESC, (kb > kb0 || kk > 0) ? 1u : 0u);
+            // One instruction consumes 32 bytes of K either way: K=16 bf16 or K=32 fp8.
+            if constexpr (KIND == kKindBf16)
+              umma_f16_ss(d_tmem, ad, bd, IDESC, (kb > kb0 || kk > 0) ? 1u : 0u);
+            else
+              umma_f8_ss(d_tmem, ad, bd, IDESC, (kb > kb0 || kk > 0) ? 1u : 0u);
           }
           issued_any = true;
           umma_commit(&empty[stage]);
@@ -355,6 +370,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr int kChunksPerWarp = BN / 32 / (kEpilogueWarps / 4);
     const int chunk0 = ((warp - 2) / 4) * kChunksPerWarp;  // this warp's column half
     int local = 0;
+    float operand_scale = 1.f;
+    if constexpr (KIND != kKindBf16) {
+      if (p.scales != nullptr) operand_scale = p.scales[0] * p.scales[1];
+    }
     for (int u = blockIdx.x; u < p.num_units; u += gridDim.x, ++local) {
       int m0, n_t, kb0, kb1;
       decode_unit(p, u, m0, n_t, kb0, kb1);
@@ -377,6 +396,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t r[32];
         tmem_ld_32x32b_x32(t_row + c * 32, r);
         tmem_ld_wait();
+        if constexpr (KIND != kKindBf16) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * operand_scale);
+        }
         const int n_base = n0 + c * 32;
         if (m < p.M && n_base < p.N) epilogue_row32<EPI, OUT>(p, m, n_base, r);
       }
@@ -391,10 +414,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) tmem_dealloc(tmem_base, TMEM_COLS);
 }
 
-template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, int OUT>
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, int OUT, int KIND = kKindBf16>
 void launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int grid,
             cudaStream_t stream, int device) {
-  auto kern = gemm_kernel<BN, STAGES, A_MN, B_MN, EPI, OUT>;
+  auto kern = gemm_kernel<BN, STAGES, A_MN, B_MN, EPI, OUT, KIND>;
   constexpr size_t smem = 1024 + STAGES * (BM * BK * 2 + BN * BK * 2) + 256;
   static bool configured[64] = {false};
   if (device < 0 || device >= 64 || !configured[device]) {

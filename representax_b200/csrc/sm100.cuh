@@ -137,6 +137,18 @@ __device__ __forceinline__ void umma_f16_ss(uint32_t d_tmem, uint64_t a_desc, ui
       : "memory");
 }
 
+// D[tmem] (+)= A[smem] * B[smem]^T with 8-bit float operands (E4M3 / E5M2 per
+// the instruction descriptor), fp32 accumulation; K = 32 per instruction.
+__device__ __forceinline__ void umma_f8_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                           uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive once on `bar` when every previously issued tcgen05.mma of this
 // thread has completed.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
@@ -188,6 +200,16 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int m, int n, bool a_mn_ma
          | (1u << 10)                               // B format: bf16
          | ((a_mn_major ? 1u : 0u) << 15)           // A major-ness
          | ((b_mn_major ? 1u : 0u) << 16)           // B major-ness
+         | (static_cast<uint32_t>(n >> 3) << 17)    // N / 8
+         | (static_cast<uint32_t>(m >> 4) << 24);   // M / 16
+}
+
+// kind::f8f6f4 descriptor, both operands K-major. Format codes: 0 = E4M3,
+// 1 = E5M2.
+__host__ __device__ constexpr uint32_t idesc_f8_f32(int m, int n, int a_fmt, int b_fmt) {
+  return (1u << 4)                                  // D format: f32
+         | (static_cast<uint32_t>(a_fmt) << 7)      // A format
+         | (static_cast<uint32_t>(b_fmt) << 10)     // B format
          | (static_cast<uint32_t>(n >> 3) << 17)    // N / 8
          | (static_cast<uint32_t>(m >> 4) << 24);   // M / 16
 }

@@ -87,6 +87,32 @@ class QuantizedLoRAWeight(nn.Module):
     def merged_weight(self) -> torch.Tensor:
         return self.base_weight().float() + (self.lora_b @ self.lora_a) * (self.alpha / self.rank)
 
+    def base_weight_bf16(self) -> torch.Tensor:
+        """The dequantised base weight (bf16); one kernel on CUDA."""
+
+        if self.packed_weight.is_cuda and self.input_size % 16 == 0 and self.packed_weight.dim() == 2:
+            from representax_b200.ops._ext import ext
+
+            out = torch.empty(self.output_size, self.input_size, dtype=torch.bfloat16, device=self.packed_weight.device)
+            ext().int4_dequantize(self.packed_weight, self.scale_bits, out)
+            return out
+        return self.base_weight().to(torch.bfloat16)
+
+    def linear_native(self, x: torch.Tensor, bias: torch.Tensor | None = None,
+                      residual: torch.Tensor | None = None) -> torch.Tensor:
+        """Packed-row bf16 path: ``x W_q^T + bias + residual + ((x A^T) * alpha / r) B^T``.
+
+        The LoRA product is added by the base GEMM's residual epilogue; the
+        base weight is dequantised by a kernel in the forward and again in the
+        backward (it is frozen, so only dx flows through it).
+        """
+
+        from representax_b200.ops import nn as N
+
+        u = N.linear(x, self.lora_a) * (self.alpha / self.rank)
+        lora = N.linear(u, self.lora_b, residual=residual)
+        return _FrozenLinearFn.apply(x, self, bias, lora)
+
     def linear(self, x: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
         dtype = x.dtype
         out = torch.nn.functional.linear(x, self.base_weight().to(dtype))
@@ -95,6 +121,35 @@ class QuantizedLoRAWeight(nn.Module):
         if bias is not None:
             out = out + bias.to(dtype)
         return out
+
+
+class _FrozenLinearFn(torch.autograd.Function):
+    """``x W^T (+ b) + residual`` with a frozen weight produced on demand (bf16)."""
+
+    @staticmethod
+    def forward(ctx, x, owner, bias, residual):
+        from representax_b200.ops import gemm as G
+        from representax_b200.ops.functional import compute_view
+
+        w = owner.base_weight_bf16()
+        y = G.linear_forward(x.contiguous(), w, None if bias is None else compute_view(bias), residual=residual)
+        ctx.owner = owner
+        ctx.save_for_backward(bias if bias is not None else torch.empty(0, device=x.device))
+        ctx.has_b = bias is not None
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        from representax_b200.ops import gemm as G
+        from representax_b200.ops.functional import _colsum_into, _GradSink
+
+        (bias,) = ctx.saved_tensors
+        dy = dy.contiguous()
+        dx = G.linear_dgrad(dy, ctx.owner.base_weight_bf16()) if ctx.needs_input_grad[0] else None
+        sb = _GradSink(bias) if ctx.has_b else None
+        if sb is not None:
+            _colsum_into(dy, sb)
+        return dx, None, (sb.result() if sb is not None else None), dy
 
 
 def linear(x: torch.Tensor, weight, bias: torch.Tensor | None = None) -> torch.Tensor:
@@ -111,12 +166,13 @@ def apply_quantized_lora(model: nn.Module, *, rank: int, alpha: float, seed: int
 
     pattern = re.compile(target_pattern)
     targets = []
+    skip = re.compile(r"embed|embeddings\.|\.word$|^word$|position|pos_embed|class_embedding|patch_w$|connector")
     for mod_name, module in model.named_modules():
         for attr, p in list(module._parameters.items()):
-            if p is None or p.ndim != 2 or not (attr == "weight" or attr.endswith("_weight")):
+            if p is None or p.ndim != 2:
                 continue
             full = f"{mod_name}.{attr}" if mod_name else attr
-            if "embedding" in full or full.startswith("embeddings.") or ".word" in full:
+            if skip.search(full):
                 continue
             if pattern.fullmatch(full) or pattern.search(full):
                 targets.append((module, attr, full))

@@ -92,10 +92,31 @@ class _LinearFn(torch.autograd.Function):
         return dx, sw.result(), (sb.result() if sb is not None else None), (dy if ctx.has_res else None)
 
 
+def _fp8_matrices() -> bool:
+    from representax_b200.precision import active_policy
+
+    return active_policy().matrix_dtype == torch.float8_e4m3fn
+
+
 def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None,
            residual: torch.Tensor | None = None) -> torch.Tensor:
-    """``x W^T (+ b) (+ residual)``; W in the Hugging Face ``[out, in]`` layout."""
+    """``x W^T (+ b) (+ residual)``; W in the Hugging Face ``[out, in]`` layout.
 
+    Under a precision policy whose matrix dtype is ``float8_e4m3fn`` the
+    native path runs the per-tensor-scaled FP8 GEMMs of ``ops.fp8``."""
+
+    from representax_b200.models.adapters import QuantizedLoRAWeight
+
+    if isinstance(weight, QuantizedLoRAWeight):
+        if native(x) and x.shape[1] % 16 == 0 and weight.output_size % 8 == 0:
+            return weight.linear_native(x.contiguous(), bias, residual)
+        y = weight.linear(x, bias)
+        return y if residual is None else y + residual
+    if native(x) and _fp8_matrices():
+        from .fp8 import fp8_supported, linear_fp8
+
+        if fp8_supported(x, weight):
+            return linear_fp8(x, weight, bias, residual)
     if native(x) and x.shape[1] % 8 == 0 and weight.shape[0] % 8 == 0:
         return _LinearFn.apply(x.contiguous(), weight, bias, residual)
     y = torch.nn.functional.linear(x, weight.to(x.dtype), None if bias is None else bias.to(x.dtype))

@@ -5,8 +5,9 @@ Parity: ``PrecisionPolicy``, ``resolve_precision_policy``,
 src/representax/precision.py:19-124. The B200 policy differs in mechanism, not
 meaning: fp32 master parameters live in one flat buffer with a bf16 compute
 copy refreshed by the fused optimizer kernel (instead of a cast per step), and
-``float8_e4m3fn`` matrices use block-scaled (1x32, UE8M0) operands rather than
-one per-tensor scale.
+a ``float8_e4m3fn`` matrix policy routes packed-row linear layers to
+tcgen05 FP8 GEMMs with the reference's per-tensor dynamic scaling (E4M3
+forward, E5M2 gradients, fp32 accumulation; ``ops.fp8``).
 """
 
 from __future__ import annotations
@@ -100,8 +101,13 @@ def loss_value(value: torch.Tensor) -> torch.Tensor:
     return value.to(active_policy().loss_dtype)
 
 
+FP8_MIXED_POLICY = PrecisionPolicy(
+    compute_dtype=torch.bfloat16, activation_dtype=torch.bfloat16, matrix_dtype=torch.float8_e4m3fn
+)
+
 __all__ = [
     "BF16_MIXED_POLICY",
+    "FP8_MIXED_POLICY",
     "FP32_POLICY",
     "PrecisionPolicy",
     "active_compute_dtype",

@@ -22,7 +22,7 @@ SOURCES = [
     "pool.cu",
     "mnr.cu",
     "optim.cu",
-    "comm.cu",
+    "comm.cu", "pointwise.cu", "gemm_fp8.cu", "int4.cu",
 ]
 
 NVCC_FLAGS = [

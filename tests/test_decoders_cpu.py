@@ -119,3 +119,33 @@ def test_family_catalog_and_pinned_loaders(tmp_path):
     loaded = load_modernvbert_text_encoder(tmp_path)
     for a, b in zip(text.parameters(), loaded.parameters()):
         torch.testing.assert_close(a, b)
+
+
+def test_quantized_lora_on_qwen3_vl_trains_only_adapters():
+    from representax_b200.models.adapters import QuantizedLoRAWeight, apply_quantized_lora, merge_quantized_lora
+    from representax_b200.models.qwen3 import Qwen3TextConfig
+    from representax_b200.models.qwen3_vl import Qwen3VLBatch, Qwen3VLConfig, Qwen3VLEncoder, Qwen3VLVisionConfig
+
+    cfg = Qwen3VLConfig(text=Qwen3TextConfig(vocab_size=128, hidden_size=64, intermediate_size=96, num_hidden_layers=2,
+                                             num_attention_heads=4, num_key_value_heads=2, head_dimension=16,
+                                             mrope_section=(2, 3, 3), pad_token_id=0),
+                        vision=Qwen3VLVisionConfig(depth=1, hidden_size=32, intermediate_size=64, num_heads=2,
+                                                   patch_size=4, out_hidden_size=64, num_position_embeddings=16,
+                                                   deepstack_visual_indexes=()),
+                        image_token_id=120)
+    model = Qwen3VLEncoder(cfg, seed=0)
+    apply_quantized_lora(model, rank=4, alpha=8.0, target_pattern=r"text\.layers\..*(qkv|o_proj|gate_up|down)$")
+    adapters = [m for m in model.modules() if isinstance(m, QuantizedLoRAWeight)]
+    assert len(adapters) == 8
+    ids = torch.randint(1, 100, (2, 9))
+    batch = Qwen3VLBatch(ids, torch.ones_like(ids))
+    e0 = model.encode(batch)
+    e0.sum().backward()
+    trained = {n for n, p in model.named_parameters() if p.grad is not None}
+    assert trained and all("lora_" in n for n in trained)
+    with torch.no_grad():
+        for a in adapters:
+            a.lora_b.normal_()
+    e1 = model.encode(batch)
+    merged = merge_quantized_lora(model)
+    torch.testing.assert_close(merged.encode(batch), e1, rtol=1e-4, atol=1e-5)

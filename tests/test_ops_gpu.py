@@ -184,3 +184,72 @@ def test_qwen3_vl_native_matches_reference():
     assert cos.min().item() > 0.99, cos
     e16.sum().backward()
     assert m16.text.layers[0].q_norm.grad is not None
+
+
+@pytest.mark.parametrize("bias", [False, True])
+def test_fp8_linear_matches_fake_quant_reference(bias):
+    from representax_b200.ops.fp8 import linear_fp8, linear_fp8_reference, quantize_reference
+
+    g = torch.Generator(device=DEV).manual_seed(3)
+    x = (torch.randn(500, 384, device=DEV, generator=g) * 2).to(torch.bfloat16).requires_grad_()
+    w = torch.nn.Parameter(torch.randn(640, 384, device=DEV, generator=g) * 0.05)
+    b = torch.nn.Parameter(torch.randn(640, device=DEV, generator=g)) if bias else None
+    # 500 rows: not a multiple of 16, exercising the padded transposed operands
+    y = linear_fp8(x, w, b)
+    ref = linear_fp8_reference(x.detach(), w.detach().to(torch.bfloat16), None if b is None else b.detach())
+    _close(y, ref, 1e-2)
+    # the fp8 product is close to the exact product too
+    _close(y, x.float() @ w.T.float() + (0 if b is None else b.float()), 8e-2)
+    dy = torch.randn_like(y)
+    dx, dw = torch.autograd.grad(y, [x, w], dy)
+    dyq, sdy = quantize_reference(dy, 1)
+    wq, sw = quantize_reference(w.detach().to(torch.bfloat16), 0)
+    xq, sx = quantize_reference(x.detach(), 0)
+    _close(dx, (dyq @ wq) * (sdy * sw), 2e-2)
+    _close(dw, (dyq.T @ xq) * (sdy * sx), 2e-2)
+
+
+def test_fp8_policy_routes_modernvbert_linears():
+    from representax_b200.models.modernvbert import ModernVBERTConfig, ModernVBERTEncoder
+    from representax_b200.models.modernvbert.config import ModernVBERTTextConfig, SigLIPVisionConfig
+    from representax_b200.models.text_batch import TokenBatch
+    from representax_b200.precision import BF16_MIXED_POLICY, FP8_MIXED_POLICY, precision_context
+
+    cfg = ModernVBERTConfig(
+        text=ModernVBERTTextConfig(vocab_size=512, hidden_size=256, intermediate_size=384, num_hidden_layers=2,
+                                   num_attention_heads=4, local_attention=16, pad_token_id=0),
+        vision=SigLIPVisionConfig(hidden_size=256, intermediate_size=512, num_hidden_layers=1, num_attention_heads=4,
+                                  image_size=64, patch_size=16), image_token_id=500, pixel_shuffle_factor=2)
+    m = ModernVBERTEncoder(cfg, seed=0, compute_dtype=torch.bfloat16).to(DEV)
+    ids = torch.randint(3, 490, (4, 64))
+    b = TokenBatch(attention_mask=torch.ones_like(ids), input_ids=ids).pack().map_tensors(lambda t: t.to(DEV))
+    with precision_context(BF16_MIXED_POLICY):
+        e16 = m.encode(b)
+    with precision_context(FP8_MIXED_POLICY):
+        e8 = m.encode(b)
+        e8.sum().backward()
+    cos = torch.nn.functional.cosine_similarity(e8.float(), e16.float(), dim=-1)
+    assert cos.min().item() > 0.98, cos
+    assert m.text.layers[0].Wqkv.grad is not None
+
+
+def test_int4_lora_linear_native_matches_reference():
+    from representax_b200.models.adapters import QuantizedLoRAWeight, unpack_int4_rows
+
+    g = torch.Generator().manual_seed(0)
+    w = torch.randn(384, 256, generator=g) * 0.05
+    q = QuantizedLoRAWeight(w, rank=16, alpha=32.0, seed=1).to(DEV)
+    with torch.no_grad():
+        q.lora_b.normal_(0, 0.02, generator=torch.Generator(device=DEV).manual_seed(2))
+    base = q.base_weight_bf16()
+    torch.testing.assert_close(base.float(), unpack_int4_rows(q.packed_weight, q.scale_bits, 256).float())
+    x32, x16 = _pair(300, 256)
+    bias = torch.nn.Parameter(torch.randn(384, device=DEV) * 0.1)
+    y32 = q.linear(x32, bias)
+    y16 = N.linear(x16, q, bias)
+    _close(y16, y32, 2e-2)
+    dy = torch.randn_like(y32)
+    a = torch.autograd.grad(y16, [x16, q.lora_a, q.lora_b, bias], dy.to(torch.bfloat16))
+    c = torch.autograd.grad(y32, [x32, q.lora_a, q.lora_b, bias], dy)
+    for u, v in zip(a, c):
+        _close(u, v, 4e-2)
