@@ -59,6 +59,9 @@ def _args():
     p.add_argument("--optimizer", choices=["sharded", "ddp"], default="sharded",
                    help="N>1: sharded = peer-memory reduce-scatter + sharded AdamW + all-gather kernels; "
                         "ddp = NCCL all-reduce + replicated AdamW")
+    p.add_argument("--kernel-table", default=None,
+                   help="after the timed steps, run one more step under torch.profiler (CUPTI) and write a "
+                        "per-kernel device-time table to this path (rank 0); not part of the timed number")
     p.add_argument("--retain-gb", type=float, default=None,
                    help="GradCache graph-retention budget in GiB (default: free HBM minus a reserve; 0: replay all)")
     return p.parse_args()
@@ -125,6 +128,41 @@ class ClockSampler:
         loaded = [x for x in sm if mx and x > 0.3 * mx] or sm
         return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": mx,
                 "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def _kernel_table(step, batch, it, path) -> None:
+    """Per-kernel device time of one training step (CUPTI via torch.profiler)."""
+
+    from torch.profiler import ProfilerActivity, profile
+
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        step(batch, it)
+        torch.cuda.synchronize()
+    rows = {}
+    for e in prof.events():
+        if e.device_type.name != "CUDA":
+            continue
+        name = e.name
+        for key, short in (("gemm_pair_kernel", "gemm_tcgen05_pair"), ("gemm_kernel", "gemm_tcgen05"),
+                           ("attn_fwd", "attention_fwd"), ("attn_bwd", "attention_bwd"), ("attn_dvec", "attention_dvec"),
+                           ("attn_dq_convert", "attention_dq_convert"), ("norm_fwd", "layernorm_fwd"),
+                           ("norm_bwd", "layernorm_bwd"), ("embed_ln", "embed_layernorm"), ("pool", "pool"),
+                           ("colsum", "colsum"), ("mnr", "mnr"), ("sgemm", "mnr_sgemm"), ("adamw", "adamw"),
+                           ("grad_norm", "grad_norm"), ("cast_bf16", "cast_bf16")):
+            if key in name:
+                name = short
+                break
+        else:
+            name = name[:60]
+        t, n = rows.get(name, (0.0, 0))
+        rows[name] = (t + e.device_time_total / 1e3, n + 1)
+    total = sum(t for t, _ in rows.values())
+    with open(path, "w") as f:
+        f.write("| kernel | launches | device ms | share |\n|---|---|---|---|\n")
+        for name, (t, n) in sorted(rows.items(), key=lambda kv: -kv[1][0]):
+            f.write(f"| {name} | {n} | {t:.2f} | {t / total:.1%} |\n")
+        f.write(f"| total | {sum(n for _, n in rows.values())} | {total:.2f} | 100% |\n")
 
 
 def main() -> None:
@@ -217,6 +255,13 @@ def main() -> None:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     elapsed = float(t)
     final_loss = float(metrics.loss)
+
+    if args.kernel_table and ctx.rank == 0:
+        _kernel_table(step, resident[it % n_host], it, args.kernel_table)
+        it += 1
+    elif args.kernel_table:
+        step(resident[it % n_host], it)
+        it += 1
 
     e2e = None
     if not args.no_e2e:
