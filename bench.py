@@ -59,6 +59,8 @@ def _args():
     p.add_argument("--optimizer", choices=["sharded", "ddp"], default="sharded",
                    help="N>1: sharded = peer-memory reduce-scatter + sharded AdamW + all-gather kernels; "
                         "ddp = NCCL all-reduce + replicated AdamW")
+    p.add_argument("--dropout", type=float, default=0.1,
+                   help="hidden and attention dropout (BERT-base default 0.1; native Philox masks)")
     p.add_argument("--kernel-table", default=None,
                    help="after the timed steps, run one more step under torch.profiler (CUPTI) and write a "
                         "per-kernel device-time table to this path (rank 0); not part of the timed number")
@@ -192,7 +194,7 @@ def main() -> None:
         raise SystemExit("global batch must divide evenly over ranks")
     local = args.global_batch // world
 
-    config = BertConfig.base(hidden_dropout_probability=0.0, attention_dropout_probability=0.0)
+    config = BertConfig.base(hidden_dropout_probability=args.dropout, attention_dropout_probability=args.dropout)
     model = BertEncoder(config, seed=0, compute_dtype=torch.bfloat16)
     state = init_train_state(model, device=device, precision=BF16_MIXED_POLICY, dist=ctx,
                              sharded_optimizer=args.optimizer == "sharded")
@@ -200,7 +202,7 @@ def main() -> None:
                      precision=BF16_MIXED_POLICY,
                      execution=GradCache(query_chunk_size=MINI_BATCH,
                                          retain_bytes=None if args.retain_gb is None else int(args.retain_gb * 2**30)),
-                     max_gradient_norm=1.0, dist=ctx, stochastic=False)
+                     max_gradient_norm=1.0, dist=ctx, stochastic=args.dropout > 0)
 
     # Host batches (pinned), distinct per step and per rank; same shapes every step.
     rng = np.random.default_rng(1234 + ctx.rank)
@@ -317,7 +319,7 @@ def main() -> None:
                 "optimizer_step": ("single-GPU fused norm/clip/AdamW kernels" if world == 1 else
                                    "sharded: peer-memory gradient reduce-scatter + shard AdamW + parameter all-gather"
                                    if args.optimizer == "sharded" else "NCCL all-reduce + replicated fused AdamW"),
-                "dropout": 0.0,
+                "dropout": args.dropout,
                 "padding": "packed (padding tokens are not computed)",
                 "l2": "per-step working set > 126 MB L2; no explicit flush",
             },

@@ -114,7 +114,7 @@ __device__ __forceinline__ void key_range(const Params& p, int q_lo, int q_hi, i
 
 // ===================================================================== forward
 template <int D>
-__global__ void __launch_bounds__(kThreads) attn_fwd_kernel(const Params p) {
+__global__ void __launch_bounds__(kThreads, D == 64 ? 4 : 1) attn_fwd_kernel(const Params p) {
   const int qb = blockIdx.x;
   const int h = blockIdx.y;
   const int b = blockIdx.z;
@@ -198,6 +198,9 @@ __global__ void __launch_bounds__(kThreads) attn_fwd_kernel(const Params p) {
         const int j = kb * BN + nb * 8 + 2 * t + (e & 1);
         const int i = qi0 + (e >> 1) * 8;
         float x = s[nb][e] * p.scale_log2;
+        if (p.rel_lut != nullptr)
+          x += __ldg(p.rel_lut + static_cast<int64_t>(h) * (2 * p.lut_len - 1) + (j - i + p.lut_len - 1)) *
+               1.4426950408889634f;
         if (!visible(p, i, j, len)) x = -INFINITY;
         s[nb][e] = x;
         mx[e >> 1] = fmaxf(mx[e >> 1], x);
@@ -223,7 +226,32 @@ __global__ void __launch_bounds__(kThreads) attn_fwd_kernel(const Params p) {
       for (int e = 0; e < 4; ++e) {
         const float pv = exp2f(s[nb][e] - m_use[e >> 1]);
         s[nb][e] = pv;
-        rs[e >> 1] += pv;
+        rs[e >> 1] += pv;  // the normaliser uses the probabilities before dropout
+      }
+    }
+    if (p.pdrop.threshold != 0u) {
+      // Rows qi0 and qi0 + 8 need two 2x2 blocks; the lanes of rows g and g ^ 1
+      // (lane ^ 4) need the same two blocks, so each lane generates one and
+      // the pair swaps halves: even-g lanes make the block of rows (qi0, qi0+1),
+      // odd-g lanes that of rows (qi0 + 7, qi0 + 8).
+      const bool odd = (g & 1) != 0;
+      const int i_sel = odd ? qi0 + 8 : qi0;
+#pragma unroll
+      for (int nb = 0; nb < BN / 8; ++nb) {
+        const int j = kb * BN + nb * 8 + 2 * t;  // even key index of this thread's pair
+        const Philox4 b = dropout_block(p.pdrop, static_cast<uint32_t>(start + (i_sel & ~1)),
+                                        (static_cast<uint32_t>(h) << 16) | static_cast<uint32_t>(j >> 1));
+        const uint32_t got0 = __shfl_xor_sync(0xffffffffu, odd ? b.x : b.z, 4);
+        const uint32_t got1 = __shfl_xor_sync(0xffffffffu, odd ? b.y : b.w, 4);
+        // words for (row qi0, cols j, j+1) and (row qi0 + 8, cols j, j+1)
+        const uint32_t w00 = odd ? got0 : b.x, w01 = odd ? got1 : b.y;
+        const uint32_t w10 = odd ? b.z : got0, w11 = odd ? b.w : got1;
+        const uint32_t th = p.pdrop.threshold;
+        const float sc = p.pdrop.scale;
+        s[nb][0] = w00 >= th ? s[nb][0] * sc : 0.f;
+        s[nb][1] = w01 >= th ? s[nb][1] * sc : 0.f;
+        s[nb][2] = w10 >= th ? s[nb][2] * sc : 0.f;
+        s[nb][3] = w11 >= th ? s[nb][3] * sc : 0.f;
       }
     }
 #pragma unroll
@@ -329,6 +357,7 @@ __global__ void __launch_bounds__(kThreads) attn_bwd_kernel(const Params p) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ float s_lse[64];
   __shared__ float s_dv[64];
+  __shared__ float s_diag[128];
   const uint32_t sK = smem_u32(smem);
   const uint32_t sV = sK + 64 * D * 2;
   const uint32_t sQ = sK + 2 * 64 * D * 2;
@@ -358,14 +387,9 @@ __global__ void __launch_bounds__(kThreads) attn_bwd_kernel(const Params p) {
   cp_async_wait<0>();
   __syncthreads();
 
-  uint32_t kf[D / 16][4], vf[D / 16][4];
-#pragma unroll
-  for (int kk = 0; kk < D / 16; ++kk) {
-    const int r = warp * 16 + (lane & 15);
-    const int c = kk * 2 + (lane >> 4);
-    ldsm_x4(sK + swz<D>(r, c), kf[kk][0], kf[kk][1], kf[kk][2], kf[kk][3]);
-    ldsm_x4(sV + swz<D>(r, c), vf[kk][0], vf[kk][1], vf[kk][2], vf[kk][3]);
-  }
+  // K and V fragments are re-read from shared memory per 32-wide k step of
+  // the first products instead of being held for the whole loop: the
+  // backward's accumulators already fill the register file.
   float dk_acc[D / 8][4], dv_acc[D / 8][4];
 #pragma unroll
   for (int i = 0; i < D / 8; ++i)
@@ -394,34 +418,97 @@ __global__ void __launch_bounds__(kThreads) attn_bwd_kernel(const Params p) {
     // S^T = K Q^T (16 keys x 64 queries per warp) and dP^T = V dO^T.
     float st[BM / 8][4], dpt[BM / 8][4];
 #pragma unroll
-    for (int nb = 0; nb < BM / 8; ++nb) {
+    for (int nb = 0; nb < BM / 8; ++nb)
 #pragma unroll
       for (int e = 0; e < 4; ++e) st[nb][e] = dpt[nb][e] = 0.f;
 #pragma unroll
-      for (int kk = 0; kk < D / 16; kk += 2) {
+    for (int kk = 0; kk < D / 16; kk += 2) {
+      uint32_t kf[2][4], vf[2][4];
+#pragma unroll
+      for (int h2 = 0; h2 < 2; ++h2) {
+        const int r = warp * 16 + (lane & 15);
+        const int c = (kk + h2) * 2 + (lane >> 4);
+        ldsm_x4(sK + swz<D>(r, c), kf[h2][0], kf[h2][1], kf[h2][2], kf[h2][3]);
+        ldsm_x4(sV + swz<D>(r, c), vf[h2][0], vf[h2][1], vf[h2][2], vf[h2][3]);
+      }
+#pragma unroll
+      for (int nb = 0; nb < BM / 8; ++nb) {
         uint32_t b0, b1, b2, b3;
         const int r = nb * 8 + (lane & 7);
         const int c = kk * 2 + (lane >> 3);
         ldsm_x4(sQ + swz<D>(r, c), b0, b1, b2, b3);
-        mma16816(st[nb], kf[kk], b0, b1);
-        mma16816(st[nb], kf[kk + 1], b2, b3);
+        mma16816(st[nb], kf[0], b0, b1);
+        mma16816(st[nb], kf[1], b2, b3);
         ldsm_x4(sdO + swz<D>(r, c), b0, b1, b2, b3);
-        mma16816(dpt[nb], vf[kk], b0, b1);
-        mma16816(dpt[nb], vf[kk + 1], b2, b3);
+        mma16816(dpt[nb], vf[0], b0, b1);
+        mma16816(dpt[nb], vf[1], b2, b3);
       }
     }
     // P^T and dS^T.
+    const bool drop = p.pdrop.threshold != 0u;
 #pragma unroll
     for (int nb = 0; nb < BM / 8; ++nb) {
+      // Keys kj0 and kj0 + 8 x queries i0, i0 + 1: two 2x2 blocks, shared with
+      // the lane of key row g ^ 1 (lane ^ 4) as in the forward. Words per key
+      // row: [0] = query i0, [1] = query i0 + 1.
+      uint32_t kw[2][2] = {{0u, 0u}, {0u, 0u}};
+      if (drop) {
+        const int i0 = q0 + nb * 8 + 2 * t;  // even query index of this thread's pair
+        const bool odd = (g & 1) != 0;
+        const int j_sel = odd ? kj0 + 8 : kj0;
+        const Philox4 b = dropout_block(p.pdrop, static_cast<uint32_t>(start + i0),
+                                        (static_cast<uint32_t>(h) << 16) | static_cast<uint32_t>(j_sel >> 1));
+        const uint32_t got0 = __shfl_xor_sync(0xffffffffu, odd ? b.x : b.y, 4);
+        const uint32_t got1 = __shfl_xor_sync(0xffffffffu, odd ? b.z : b.w, 4);
+        // word (i & 1) * 2 + (j & 1): even key -> x (i0), z (i0 + 1); odd key -> y, w
+        kw[0][0] = odd ? got0 : b.x;
+        kw[0][1] = odd ? got1 : b.z;
+        kw[1][0] = odd ? b.y : got0;
+        kw[1][1] = odd ? b.w : got1;
+      }
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int qi = nb * 8 + 2 * t + (e & 1);
         const int j = kj0 + (e >> 1) * 8;
         const int i = q0 + qi;
         float pv = 0.f;
-        if (i < len && visible(p, i, j, len)) pv = exp2f(st[nb][e] * p.scale_log2 - s_lse[qi]);
-        st[nb][e] = pv;
-        dpt[nb][e] = pv * (dpt[nb][e] - s_dv[qi]);
+        float bias = 0.f;
+        if (p.rel_lut != nullptr && i < len && j < len)
+          bias = __ldg(p.rel_lut + static_cast<int64_t>(h) * (2 * p.lut_len - 1) + (j - i + p.lut_len - 1)) *
+                 1.4426950408889634f;
+        if (i < len && visible(p, i, j, len)) pv = exp2f(st[nb][e] * p.scale_log2 + bias - s_lse[qi]);
+        if (drop) {
+          // dS = P * (mask * dP / (1 - p) - D); dV uses the dropped probabilities
+          const bool keep = kw[e >> 1][e & 1] >= p.pdrop.threshold;
+          const float dp = keep ? dpt[nb][e] * p.pdrop.scale : 0.f;
+          dpt[nb][e] = pv * (dp - s_dv[qi]);
+          st[nb][e] = keep ? pv * p.pdrop.scale : 0.f;
+        } else {
+          st[nb][e] = pv;
+          dpt[nb][e] = pv * (dpt[nb][e] - s_dv[qi]);
+        }
+      }
+    }
+    if (p.drel != nullptr) {
+      // dS summed along diagonals d = j - i (127 of them in a 64 x 64 tile)
+      // in shared memory, then one global atomic per diagonal.
+      for (int x = threadIdx.x; x < 128; x += blockDim.x) s_diag[x] = 0.f;
+      __syncthreads();
+      const int d0 = k_lo - q0 - 63;  // diagonal of (query q0 + 63, key k_lo)
+#pragma unroll
+      for (int nb = 0; nb < BM / 8; ++nb) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int i = q0 + nb * 8 + 2 * t + (e & 1);
+          const int j = kj0 + (e >> 1) * 8;
+          if (i < len && j < len && dpt[nb][e] != 0.f) atomicAdd(&s_diag[j - i - d0], dpt[nb][e]);
+        }
+      }
+      __syncthreads();
+      float* dst = p.drel + static_cast<int64_t>(h) * (2 * p.lut_len - 1) + p.lut_len - 1 + d0;
+      for (int x = threadIdx.x; x < 127; x += blockDim.x) {
+        const float v = s_diag[x];
+        if (v != 0.f) atomicAdd(dst + x, v);
       }
     }
     // dV += P^T dO ; dK += dS^T Q  (k = queries).
@@ -559,6 +646,22 @@ void fill_common(attn::Params& p, const at::Tensor& q, const at::Tensor& k, cons
   p.window = static_cast<int>(window);
 }
 
+void set_rel_bias(attn::Params& p, const c10::optional<at::Tensor>& lut, const c10::optional<at::Tensor>& grad,
+                  int64_t heads, int64_t max_len) {
+  if (!lut.has_value()) return;
+  check_f32(*lut, "rel_lut");
+  RX_CHECK(lut->dim() == 2 && lut->size(0) == heads && lut->is_contiguous() && lut->size(1) % 2 == 1,
+           "rel_lut must be contiguous fp32 [heads, 2 L - 1]");
+  p.lut_len = static_cast<int>((lut->size(1) + 1) / 2);
+  RX_CHECK(max_len <= p.lut_len, "rel_lut covers fewer distances than the longest sequence");
+  p.rel_lut = lut->data_ptr<float>();
+  if (grad.has_value()) {
+    check_f32(*grad, "drel");
+    RX_CHECK(grad->sizes() == lut->sizes() && grad->is_contiguous(), "drel must match rel_lut");
+    p.drel = grad->data_ptr<float>();
+  }
+}
+
 template <typename Kernel>
 void set_smem(Kernel kernel, int bytes) {
   if (bytes > 48 * 1024)
@@ -568,9 +671,15 @@ void set_smem(Kernel kernel, int bytes) {
 
 void attention_forward(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o,
                        at::Tensor& lse, const at::Tensor& cu_seqlens, int64_t max_len,
-                       int64_t heads, int64_t kv_heads, double scale, bool causal, int64_t window) {
+                       int64_t heads, int64_t kv_heads, double scale, bool causal, int64_t window,
+                       int64_t drop_seed, int64_t drop_stream, double drop_p,
+                       const c10::optional<at::Tensor>& rel_lut) {
   attn::Params p{};
   fill_common(p, q, k, v, cu_seqlens, heads, kv_heads, scale, causal, window);
+  RX_CHECK(drop_p >= 0.0 && drop_p < 1.0, "attention dropout must be in [0, 1)");
+  RX_CHECK(max_len < (1 << 17) && heads < (1 << 16), "dropout counters need max_len < 2^17, heads < 2^16");
+  p.pdrop = make_dropout_site(drop_seed, drop_stream, drop_p);
+  set_rel_bias(p, rel_lut, c10::nullopt, heads, max_len);
   check_bf16(o, "o");
   check_f32(lse, "lse");
   RX_CHECK(o.stride(1) == 1 && o.stride(0) % 2 == 0, "bad o layout");
@@ -596,9 +705,12 @@ void attention_backward(const at::Tensor& dO, const at::Tensor& q, const at::Ten
                         at::Tensor& dq, at::Tensor& dk, at::Tensor& dv, at::Tensor& dq_acc,
                         at::Tensor& dvec, const at::Tensor& cu_seqlens, int64_t max_len,
                         int64_t heads, int64_t kv_heads, double scale, bool causal,
-                        int64_t window) {
+                        int64_t window, int64_t drop_seed, int64_t drop_stream, double drop_p,
+                        const c10::optional<at::Tensor>& rel_lut, const c10::optional<at::Tensor>& drel) {
   attn::Params p{};
   fill_common(p, q, k, v, cu_seqlens, heads, kv_heads, scale, causal, window);
+  p.pdrop = make_dropout_site(drop_seed, drop_stream, drop_p);
+  set_rel_bias(p, rel_lut, drel, heads, max_len);
   const int d = static_cast<int>(q.size(1) / heads);
   check_bf16(dO, "dO");
   check_f32(dq_acc, "dq_acc");

@@ -6,6 +6,8 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include "philox.cuh"
+
 namespace rx {
 namespace attn {
 
@@ -34,6 +36,17 @@ struct Params {
   float scale;
   int causal;
   int window;  // -1: no window
+  // Attention-probability dropout (threshold 0 = off). Element (query i,
+  // key j) of head h in a sequence starting at token `start` uses word
+  // (i & 1) * 2 + (j & 1) of Philox block (start + (i & ~1), h << 16 | j >> 1):
+  // 2 x 2 blocks, so the forward (row-major) and backward (transposed) tiles
+  // both use two words of every block they generate.
+  DropoutSite pdrop;
+  // Relative position bias (MPNet): logits[h, i, j] += rel_lut[h, j - i + lut_len - 1]
+  // (fp32 [heads, 2 * lut_len - 1]); the backward adds dS into drel (same shape).
+  const float* rel_lut;
+  float* drel;
+  int lut_len;
   // backward
   const __nv_bfloat16* dO;
   int64_t ld_do;
@@ -45,8 +58,9 @@ struct Params {
 };
 
 
+// Four forward CTAs per SM at head dim 64 (<= 128 registers per thread).
 template <int D>
-__global__ void __launch_bounds__(kThreads) attn_fwd_kernel(const Params p);
+__global__ void __launch_bounds__(kThreads, D == 64 ? 4 : 1) attn_fwd_kernel(const Params p);
 // GQA: loop over the query heads of each key/value head (heads_per_kv > 1).
 template <int D, bool GQA>
 __global__ void __launch_bounds__(kThreads) attn_bwd_kernel(const Params p);

@@ -16,12 +16,13 @@ void gemm_fp8(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, int64_t a
               const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& residual,
               const at::Tensor& status);
 void int4_dequantize(const at::Tensor& packed, const at::Tensor& scale_bits, at::Tensor& out);
+void dropout_apply(const at::Tensor& x, at::Tensor& y, int64_t seed, int64_t stream, double p);
 void gemm_tcgen05(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_mn, bool b_mn,
                   int64_t epi, int64_t out_mode, double alpha,
                   const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& aux_in,
                   const c10::optional<at::Tensor>& aux_out,
                   const c10::optional<at::Tensor>& residual, const at::Tensor& status,
-                  int64_t split_k, int64_t variant);
+                  int64_t split_k, int64_t variant, int64_t drop_seed, int64_t drop_stream, double drop_p);
 void norm_forward(const at::Tensor& x, const at::Tensor& gamma, const c10::optional<at::Tensor>& beta,
                   at::Tensor& y, const c10::optional<at::Tensor>& mean, at::Tensor& rstd,
                   double eps, bool rms);
@@ -42,13 +43,16 @@ void embed_ln_backward(const at::Tensor& dy, const at::Tensor& ids, const at::Te
                        at::Tensor& dbeta, int64_t pad_id);
 void attention_forward(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o,
                        at::Tensor& lse, const at::Tensor& cu_seqlens, int64_t max_len,
-                       int64_t heads, int64_t kv_heads, double scale, bool causal, int64_t window);
+                       int64_t heads, int64_t kv_heads, double scale, bool causal, int64_t window,
+                       int64_t drop_seed, int64_t drop_stream, double drop_p,
+                       const c10::optional<at::Tensor>& rel_lut);
 void attention_backward(const at::Tensor& dO, const at::Tensor& q, const at::Tensor& k,
                         const at::Tensor& v, const at::Tensor& o, const at::Tensor& lse,
                         at::Tensor& dq, at::Tensor& dk, at::Tensor& dv, at::Tensor& dq_acc,
                         at::Tensor& dvec, const at::Tensor& cu_seqlens, int64_t max_len,
                         int64_t heads, int64_t kv_heads, double scale, bool causal,
-                        int64_t window);
+                        int64_t window, int64_t drop_seed, int64_t drop_stream, double drop_p,
+                        const c10::optional<at::Tensor>& rel_lut, const c10::optional<at::Tensor>& drel);
 void pool_forward(const at::Tensor& h, const at::Tensor& cu_seqlens, at::Tensor& out,
                   at::Tensor& norm, int64_t mode, bool normalize);
 void pool_backward(const at::Tensor& dout, const at::Tensor& out, const at::Tensor& norm,
@@ -117,6 +121,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sharded_grad_reduce", &rx::sharded_grad_reduce);
   m.def("sharded_adamw", &rx::sharded_adamw);
   m.def("int4_dequantize", &rx::int4_dequantize);
+  m.def("dropout_apply", &rx::dropout_apply);
   m.def("fp8_scale", &rx::fp8_scale);
   m.def("fp8_quantize", &rx::fp8_quantize);
   m.def("gemm_fp8", &rx::gemm_fp8);

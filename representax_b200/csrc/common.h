@@ -88,6 +88,23 @@ inline CUtensorMap make_tmap_2d_bf16(const void* base, int64_t rows, int64_t col
   return map;
 }
 
+// bf16 map for tile stores: boxes of 32 columns (64 bytes) x 32 rows with
+// the 64-byte swizzle (16-byte chunk index XOR (row / 2) % 4).
+inline CUtensorMap make_tmap_2d_bf16_store(const void* base, int64_t rows, int64_t cols, int64_t ld) {
+  RX_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0, "TMA base must be 16-byte aligned");
+  RX_CHECK((ld * 2) % 16 == 0, "TMA row stride must be a multiple of 16 bytes (ld % 8 == 0)");
+  CUtensorMap map;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
+  cuuint32_t box[2] = {32u, 32u};
+  cuuint32_t elem_strides[2] = {1, 1};
+  CUresult r = encode_tiled_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+                                 box, elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                                 CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  RX_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (store) failed with code ", static_cast<int>(r));
+  return map;
+}
+
 // 2-D tiled map of 8-bit elements with 128-byte rows per box (128 elements)
 // and the 128-byte swizzle (the same shared-memory geometry as 64 bf16).
 inline CUtensorMap make_tmap_2d_u8(const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows) {

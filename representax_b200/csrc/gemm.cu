@@ -14,7 +14,7 @@ void gemm_tcgen05(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool 
                   const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& aux_in,
                   const c10::optional<at::Tensor>& aux_out,
                   const c10::optional<at::Tensor>& residual, const at::Tensor& status,
-                  int64_t split_k, int64_t variant) {
+                  int64_t split_k, int64_t variant, int64_t drop_seed, int64_t drop_stream, double drop_p) {
   using namespace gemm;
   check_bf16(A, "A");
   check_bf16(B, "B");
@@ -80,6 +80,10 @@ void gemm_tcgen05(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool 
     p.residual = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());
     p.ld_res = residual->stride(0);
   }
+  if (epi & EPI_DROP) {
+    RX_CHECK(drop_p > 0.0 && drop_p < 1.0, "dropout probability must be in (0, 1)");
+    p.drop = make_dropout_site(drop_seed, drop_stream, drop_p);
+  }
   // variant: 1 = one CTA per 128x256 tile, 2 = CTA pair per 256x256 tile,
   // 0 = pair whenever there are at least 256 rows.
   const bool pair = variant == 2 || (variant == 0 && M >= 256);
@@ -94,7 +98,20 @@ void gemm_tcgen05(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool 
   int splits = 1;
   const int tiles = p.m_tiles * p.n_tiles;
   if (split_k == 0 && out_mode == OUT_F32_ATOMIC && tiles < workers) {
-    splits = std::max(1, std::min(p.kb_total / 4, (workers + tiles - 1) / tiles));
+    // Wave-aware split: among splits that leave >= 4 k-blocks each, take the
+    // one whose work units fill the persistent grid best (units / (waves *
+    // workers)), preferring fewer splits on ties (less atomic traffic).
+    double best = -1.0;
+    const int max_splits = std::max(1, std::min(16, p.kb_total / 4));
+    for (int s = 1; s <= max_splits; ++s) {
+      const int units = tiles * s;
+      const int waves = (units + workers - 1) / workers;
+      const double eff = static_cast<double>(units) / (static_cast<double>(waves) * workers);
+      if (eff > best + 1e-3) {
+        best = eff;
+        splits = s;
+      }
+    }
   } else if (split_k > 1) {
     RX_CHECK(out_mode == OUT_F32_ATOMIC, "split-K needs the atomic fp32 output mode");
     splits = static_cast<int>(std::min<int64_t>(split_k, p.kb_total));

@@ -13,6 +13,9 @@ static LaunchFn pick_epi(int epi) {
     case EPI_BIAS | EPI_GELU: return launch<BN, ST, false, false, EPI_BIAS | EPI_GELU, OUT>;
     case EPI_BIAS | EPI_RESID: return launch<BN, ST, false, false, EPI_BIAS | EPI_RESID, OUT>;
     case EPI_RESID: return launch<BN, ST, false, false, EPI_RESID, OUT>;
+    case EPI_BIAS | EPI_DROP | EPI_RESID:
+      if constexpr (OUT == OUT_BF16) return launch<BN, ST, false, false, EPI_BIAS | EPI_DROP | EPI_RESID, OUT>;
+      return nullptr;
     default: return nullptr;
   }
 }
@@ -32,6 +35,9 @@ static LaunchFn pick_epi_pair(int epi) {
     case EPI_BIAS | EPI_GELU: return launch_pair<false, false, EPI_BIAS | EPI_GELU, OUT>;
     case EPI_BIAS | EPI_RESID: return launch_pair<false, false, EPI_BIAS | EPI_RESID, OUT>;
     case EPI_RESID: return launch_pair<false, false, EPI_RESID, OUT>;
+    case EPI_BIAS | EPI_DROP | EPI_RESID:
+      if constexpr (OUT == OUT_BF16) return launch_pair<false, false, EPI_BIAS | EPI_DROP | EPI_RESID, OUT>;
+      return nullptr;
     default: return nullptr;
   }
 }

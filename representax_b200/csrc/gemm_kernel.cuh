@@ -26,6 +26,7 @@
 // backward; this kernel replaces both.
 #pragma once
 #include "common.h"
+#include "philox.cuh"
 #include "sm100.cuh"
 
 namespace rx {
@@ -36,7 +37,10 @@ constexpr int BK = 64;
 constexpr int kEpilogueWarps = 8;  // two per TMEM lane quadrant, each owning half the columns
 constexpr int kThreads = 64 + 32 * kEpilogueWarps;
 
-enum Epi : int { EPI_BIAS = 1, EPI_GELU = 2, EPI_DGELU = 4, EPI_RESID = 8 };
+// EPI_DROP: inverted dropout of the (biased) value before the residual add;
+// element (m, n) keeps its value when word (n & 3) of Philox block
+// (m, n >> 2) at the site is >= the threshold.
+enum Epi : int { EPI_BIAS = 1, EPI_GELU = 2, EPI_DGELU = 4, EPI_RESID = 8, EPI_DROP = 16 };
 enum Out : int { OUT_BF16 = 0, OUT_F32 = 1, OUT_F32_ACC = 2, OUT_F32_ATOMIC = 3 };
 
 struct Params {
@@ -53,6 +57,7 @@ struct Params {
   int64_t ld_res;
   float alpha;
   const float* scales;  // fp8: device [2] per-tensor operand scales multiplied into alpha
+  DropoutSite drop;
   int* status;
   uint64_t timeout_ns;
 };
@@ -99,6 +104,88 @@ __device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float (&
   }
 }
 
+// Epilogue values (bias / GELU / GELU' / dropout / residual) of one row
+// segment of 32 columns, for the staged tile store. Columns >= N and rows
+// >= M produce zeros and read nothing (the tile store clips them).
+template <int EPI>
+__device__ __forceinline__ void epilogue_values32(const Params& p, int m, int n_base, const uint32_t (&r)[32],
+                                                  float (&v)[32]) {
+  const bool row_ok = m < p.M;
+  const bool full = row_ok && (n_base + 32 <= p.N);
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * p.alpha;
+  if (full) {
+    if constexpr ((EPI & EPI_BIAS) != 0) {
+      float b[32];
+      load_bf16x32(p.bias + n_base, b);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] += b[i];
+    }
+    if constexpr ((EPI & EPI_DGELU) != 0) {
+      float z[32];
+      load_bf16x32(p.aux_in + static_cast<int64_t>(m) * p.ld_aux_in + n_base, z);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] *= gelu_erf_grad(z[i]);
+    }
+    if constexpr ((EPI & EPI_GELU) != 0) {
+      store_bf16x32(p.aux_out + static_cast<int64_t>(m) * p.ld_aux_out + n_base, v);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
+    }
+    if constexpr ((EPI & EPI_DROP) != 0) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const Philox4 rb = dropout_block(p.drop, static_cast<uint32_t>(m), static_cast<uint32_t>((n_base >> 2) + q));
+#pragma unroll
+        for (int w = 0; w < 4; ++w)
+          v[4 * q + w] = word_of(rb, w) >= p.drop.threshold ? v[4 * q + w] * p.drop.scale : 0.f;
+      }
+    }
+    if constexpr ((EPI & EPI_RESID) != 0) {
+      float res[32];
+      load_bf16x32(p.residual + static_cast<int64_t>(m) * p.ld_res + n_base, res);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] += res[i];
+    }
+    return;
+  }
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const int n = n_base + i;
+    if (!row_ok || n >= p.N) {
+      v[i] = 0.f;
+      continue;
+    }
+    float x = v[i];
+    if constexpr ((EPI & EPI_BIAS) != 0) x += __bfloat162float(p.bias[n]);
+    if constexpr ((EPI & EPI_DGELU) != 0)
+      x *= gelu_erf_grad(__bfloat162float(p.aux_in[static_cast<int64_t>(m) * p.ld_aux_in + n]));
+    if constexpr ((EPI & EPI_GELU) != 0) {
+      p.aux_out[static_cast<int64_t>(m) * p.ld_aux_out + n] = __float2bfloat16_rn(x);
+      x = gelu_erf(x);
+    }
+    if constexpr ((EPI & EPI_DROP) != 0) {
+      const Philox4 rb = dropout_block(p.drop, static_cast<uint32_t>(m), static_cast<uint32_t>(n >> 2));
+      x = word_of(rb, n & 3) >= p.drop.threshold ? x * p.drop.scale : 0.f;
+    }
+    if constexpr ((EPI & EPI_RESID) != 0) x += __bfloat162float(p.residual[static_cast<int64_t>(m) * p.ld_res + n]);
+    v[i] = x;
+  }
+}
+
+// Write one lane's 32 bf16 values as row `lane` of a 32 x 32 tile staged in
+// shared memory with the 64-byte swizzle of the store tensor map.
+__device__ __forceinline__ void stage_row32_sw64(uint8_t* buf, int lane, const float (&v)[32]) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint4 w;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&w);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) h[j] = __floats2bfloat162_rn(v[q * 8 + 2 * j], v[q * 8 + 2 * j + 1]);
+    *reinterpret_cast<uint4*>(buf + lane * 64 + ((q ^ ((lane >> 1) & 3)) * 16)) = w;
+  }
+}
+
 // Epilogue for one row segment of 32 columns [n_base, n_base + 32).
 template <int EPI, int OUT>
 __device__ __forceinline__ void epilogue_row32(const Params& p, int m, int n_base,
@@ -124,6 +211,15 @@ __device__ __forceinline__ void epilogue_row32(const Params& p, int m, int n_bas
       store_bf16x32(p.aux_out + static_cast<int64_t>(m) * p.ld_aux_out + n_base, v);
 #pragma unroll
       for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
+    }
+    if constexpr ((EPI & EPI_DROP) != 0) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const Philox4 r = dropout_block(p.drop, static_cast<uint32_t>(m), static_cast<uint32_t>((n_base >> 2) + q));
+#pragma unroll
+        for (int w = 0; w < 4; ++w)
+          v[4 * q + w] = word_of(r, w) >= p.drop.threshold ? v[4 * q + w] * p.drop.scale : 0.f;
+      }
     }
     if constexpr ((EPI & EPI_RESID) != 0) {
       float res[32];
@@ -165,6 +261,10 @@ __device__ __forceinline__ void epilogue_row32(const Params& p, int m, int n_bas
       if constexpr ((EPI & EPI_GELU) != 0) {
         p.aux_out[static_cast<int64_t>(m) * p.ld_aux_out + n] = __float2bfloat16_rn(x);
         x = gelu_erf(x);
+      }
+      if constexpr ((EPI & EPI_DROP) != 0) {
+        const Philox4 r = dropout_block(p.drop, static_cast<uint32_t>(m), static_cast<uint32_t>(n >> 2));
+        x = word_of(r, n & 3) >= p.drop.threshold ? x * p.drop.scale : 0.f;
       }
       if constexpr ((EPI & EPI_RESID) != 0)
         x += __bfloat162float(p.residual[static_cast<int64_t>(m) * p.ld_res + n]);
@@ -445,23 +545,32 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int g
 // ============================================================================
 constexpr int kPairStages = 6;
 
+// bf16 outputs leave through shared memory and TMA tile stores: each
+// epilogue warp stages its 32 x 32 piece (double-buffered, 64-byte swizzle)
+// and one lane issues the store, instead of 32 lanes writing 64 bytes to 32
+// different rows.
+template <int OUT>
+constexpr int pair_stage_bytes() { return OUT == OUT_BF16 ? kEpilogueWarps * 2 * 2048 : 0; }
+
 template <bool A_MN, bool B_MN, int EPI, int OUT>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     const Params p) {
+                     const __grid_constant__ CUtensorMap tmC, const Params p) {
   constexpr int BN = 256;           // pair tile columns
   constexpr int HALF_N = BN / 2;    // B rows loaded by each CTA
   constexpr int STAGES = kPairStages;
   constexpr int A_BYTES = BM * BK * 2;
   constexpr int B_BYTES = HALF_N * BK * 2;
   constexpr uint32_t TMEM_COLS = 2 * BN;
+  constexpr bool kTileStore = OUT == OUT_BF16;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* sA = base;
   uint8_t* sB = base + STAGES * A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint8_t* sC = sB + STAGES * B_BYTES;  // 1024-aligned staging for tile stores
+  uint64_t* full = reinterpret_cast<uint64_t*>(sC + pair_stage_bytes<OUT>());
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -493,6 +602,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_map(&tmA);
     tma_prefetch_map(&tmB);
+    if constexpr (kTileStore) tma_prefetch_map(&tmC);
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_slot, TMEM_COLS);
@@ -631,6 +741,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int chunk0 = ((warp - 2) / 4) * kChunksPerWarp;
     const uint32_t tempty_leader = mapa_shared(smem_u32(&tempty[0]), 0);
     int local = 0;
+    uint32_t store_seq = 0;
     for (int u = cluster; u < p.num_units; u += clusters, ++local) {
       int m0, n0, kb0, kb1;
       decode(u, m0, n0, kb0, kb1);
@@ -653,11 +764,33 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld_32x32b_x32(t_row + c * 32, r);
         tmem_ld_wait();
         const int n_base = n0 + c * 32;
-        if (m < p.M && n_base < p.N) epilogue_row32<EPI, OUT>(p, m, n_base, r);
+        if constexpr (kTileStore) {
+          if (n_base < p.N && m0 + static_cast<int>(rank) * BM + quad * 32 < p.M) {  // warp-uniform
+            float v[32];
+            epilogue_values32<EPI>(p, m, n_base, r, v);
+            uint8_t* buf = sC + ((warp - 2) * 2 + (store_seq & 1)) * 2048;
+            if (lane == 0) tma_store_wait_read<1>();  // the store that last read `buf` is done reading
+            __syncwarp();
+            stage_row32_sw64(buf, lane, v);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&tmC, buf, n_base, m0 + static_cast<int>(rank) * BM + quad * 32);
+              tma_store_commit();
+            }
+            ++store_seq;
+          }
+        } else {
+          if (m < p.M && n_base < p.N) epilogue_row32<EPI, OUT>(p, m, n_base, r);
+        }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader + acc * 8);
+    }
+    if constexpr (kTileStore) {
+      if (lane == 0) tma_store_wait<0>();  // every tile store has landed before the CTA exits
+      __syncwarp();
     }
   }
 
@@ -672,7 +805,11 @@ template <bool A_MN, bool B_MN, int EPI, int OUT>
 void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int grid,
                  cudaStream_t stream, int device) {
   auto kern = gemm_pair_kernel<A_MN, B_MN, EPI, OUT>;
-  constexpr size_t smem = 1024 + kPairStages * (BM * BK * 2 + 128 * BK * 2) + 256;
+  constexpr size_t smem = 1024 + kPairStages * (BM * BK * 2 + 128 * BK * 2) + pair_stage_bytes<OUT>() + 256;
+  static_assert(smem <= 232448, "pair GEMM shared memory exceeds the opt-in limit");
+  CUtensorMap tc{};
+  if constexpr (OUT == OUT_BF16)
+    tc = make_tmap_2d_bf16_store(p.C, p.M, p.N, p.ldc);
   static bool configured[64] = {false};
   if (device < 0 || device >= 64 || !configured[device]) {
     RX_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -691,7 +828,7 @@ void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, 
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  RX_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, p));
+  RX_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, tc, p));
 }
 
 using LaunchFn = void (*)(const CUtensorMap&, const CUtensorMap&, const Params&, int, cudaStream_t,

@@ -21,6 +21,7 @@
 // (src/representax/models/modernvbert/model.py:264-269,
 // src/representax/models/qwen3_vl/text.py:201-202).
 #include "common.h"
+#include "philox.cuh"
 
 #include <algorithm>
 
@@ -260,6 +261,31 @@ __global__ void act_bwd_kernel(const __nv_bfloat16* __restrict__ dy, int64_t ldd
   }
 }
 
+// y = x * keep(m, n) / (1 - p) over a [rows, cols] bf16 matrix (cols % 4 == 0);
+// one Philox block per 4 consecutive columns, the same mask as the GEMM
+// epilogue's EPI_DROP at the same site. x and y may alias.
+__global__ void dropout_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, __nv_bfloat16* y, int64_t ldy,
+                               int64_t rows, int64_t cols, DropoutSite site) {
+  const int64_t quads = cols / 4;
+  const int64_t n = rows * quads;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / quads, q = i % quads;
+    const Philox4 bits = dropout_block(site, static_cast<uint32_t>(r), static_cast<uint32_t>(q));
+    const uint2 in = *reinterpret_cast<const uint2*>(x + r * ldx + 4 * q);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&in);
+    const float2 a = __bfloat1622float2(h[0]), b = __bfloat1622float2(h[1]);
+    float v[4] = {a.x, a.y, b.x, b.y};
+#pragma unroll
+    for (int w = 0; w < 4; ++w) v[w] = word_of(bits, w) >= site.threshold ? v[w] * site.scale : 0.f;
+    uint2 out;
+    __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(&out);
+    o[0] = __floats2bfloat162_rn(v[0], v[1]);
+    o[1] = __floats2bfloat162_rn(v[2], v[3]);
+    *reinterpret_cast<uint2*>(y + r * ldy + 4 * q) = out;
+  }
+}
+
 }  // namespace pw
 
 namespace {
@@ -431,6 +457,25 @@ void activation_backward(const at::Tensor& dy, const at::Tensor& z, at::Tensor& 
     pw::act_bwd_kernel<false><<<grid, 256, 0, st>>>(gp, dy.stride(0), zp, z.stride(0), dp, dz.stride(0),
                                                      static_cast<int>(T), static_cast<int>(width),
                                                      static_cast<int>(act));
+  RX_CUDA_CHECK(cudaGetLastError());
+}
+
+void dropout_apply(const at::Tensor& x, at::Tensor& y, int64_t seed, int64_t stream, double p) {
+  check_bf16(x, "x");
+  check_bf16(y, "y");
+  RX_CHECK(x.dim() == 2 && y.sizes() == x.sizes() && x.stride(1) == 1 && y.stride(1) == 1, "dropout needs matrices");
+  RX_CHECK(x.size(1) % 4 == 0 && x.stride(0) % 4 == 0 && y.stride(0) % 4 == 0 &&
+               reinterpret_cast<uintptr_t>(x.data_ptr()) % 8 == 0 && reinterpret_cast<uintptr_t>(y.data_ptr()) % 8 == 0,
+           "dropout rows must be 8-byte aligned with width % 4 == 0");
+  RX_CHECK(p > 0.0 && p < 1.0, "dropout probability must be in (0, 1)");
+  const int64_t rows = x.size(0), cols = x.size(1);
+  if (rows == 0) return;
+  const int device = x.get_device();
+  c10::cuda::CUDAGuard guard(device);
+  const int grid = grid_for(rows * cols / 4, 256, device);
+  pw::dropout_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream(device).stream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0), reinterpret_cast<__nv_bfloat16*>(y.data_ptr()),
+      y.stride(0), rows, cols, make_dropout_site(seed, stream, p));
   RX_CUDA_CHECK(cudaGetLastError());
 }
 

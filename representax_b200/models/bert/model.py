@@ -112,35 +112,43 @@ class BertEncoder(nn.Module):
             return False
         if self.config.hidden_activation != "gelu":
             return False
-        dropout_active = generator is not None and (
-            self.config.hidden_dropout_probability > 0 or self.config.attention_dropout_probability > 0)
-        if dropout_active:
-            return False
         from representax_b200.ops import _ext
 
         _ext.ext()  # raises loudly if the extension is missing on a GPU box
         return True
 
     # ------------------------------------------------------------ native path
-    def _native_hidden(self, batch: TokenBatch, all_layers: bool = False):
+    def _native_hidden(self, batch: TokenBatch, all_layers: bool = False, generator=None):
         from representax_b200.ops import functional as Fn
 
         cfg = self.config
         pk = batch.packed
         packed = Fn.Packed(cu_seqlens=pk.cu_seqlens, max_len=pk.max_len, total=pk.total)
         e = self.embeddings
+        # Dropout masks come from counter-based Philox streams keyed by the
+        # generator's seed, so GradCache replays reproduce them exactly.
+        p_h, p_a = cfg.hidden_dropout_probability, cfg.attention_dropout_probability
+        seed = generator.initial_seed() if generator is not None and (p_h > 0 or p_a > 0) else None
+
+        def drop(site: int):
+            return None if seed is None else Fn.Dropout(seed, site, p_a, p_h)
+
         h = Fn.embed_layer_norm(pk.input_ids, pk.position_ids, pk.token_type_ids, e.word, e.position,
-                                e.token_type, e.norm_weight, e.norm_bias, cfg.norm_epsilon, cfg.pad_token_id)
+                                e.token_type, e.norm_weight, e.norm_bias, cfg.norm_epsilon, cfg.pad_token_id,
+                                dropout=drop(0))
         states = [h] if all_layers else None
-        for layer in self.layers:
+        fused_bias = seed is None or p_h == 0  # norm-fused bias gradient needs the undropped gradient
+        for i, layer in enumerate(self.layers):
+            site = 16 * (i + 1)
             s1 = Fn.attention_block(h, layer.qkv_weight, layer.qkv_bias, layer.out_weight, layer.out_bias,
-                                    packed, heads=cfg.num_attention_heads, out_bias_grad_fused=True)
+                                    packed, heads=cfg.num_attention_heads, out_bias_grad_fused=fused_bias,
+                                    dropout=drop(site))
             h1 = Fn.layer_norm(s1, layer.attn_norm_weight, layer.attn_norm_bias, cfg.norm_epsilon,
-                               producer_bias=layer.out_bias)
+                               producer_bias=layer.out_bias if fused_bias else None)
             s2 = Fn.mlp_block(h1, layer.ffn_in_weight, layer.ffn_in_bias, layer.ffn_out_weight, layer.ffn_out_bias,
-                              out_bias_grad_fused=True)
+                              out_bias_grad_fused=fused_bias, dropout=drop(site))
             h = Fn.layer_norm(s2, layer.out_norm_weight, layer.out_norm_bias, cfg.norm_epsilon,
-                              producer_bias=layer.ffn_out_bias)
+                              producer_bias=layer.ffn_out_bias if fused_bias else None)
             if all_layers:
                 states.append(h)
         return (h, packed) if not all_layers else (states, packed)
@@ -195,7 +203,7 @@ class BertEncoder(nn.Module):
         if not isinstance(inputs, TokenBatch):
             raise TypeError("BERT inputs must be TokenBatch")
         if self._native(inputs, generator):
-            h, _ = self._native_hidden(inputs)
+            h, _ = self._native_hidden(inputs, generator=generator)
             return _unpack(h, inputs)
         dtype = self._dtype()
         mask = inputs.attention_mask.bool()
@@ -221,7 +229,7 @@ class BertEncoder(nn.Module):
         if self._native(inputs, generator):
             from representax_b200.ops import functional as Fn
 
-            h, packed = self._native_hidden(inputs)
+            h, packed = self._native_hidden(inputs, generator=generator)
             return Fn.pool(h, packed, self.pooling, self.normalize)
         hidden = self.hidden_states(inputs, generator=generator)
         pooled = self._pool_reference(hidden, inputs.attention_mask)
@@ -241,7 +249,7 @@ class BertEncoder(nn.Module):
         if inputs.packed is not None and self._native(inputs, generator):
             from representax_b200.ops import functional as Fn
 
-            states, packed = self._native_hidden(inputs, all_layers=True)
+            states, packed = self._native_hidden(inputs, all_layers=True, generator=generator)
             return torch.stack([Fn.pool(s, packed, self.pooling, True) for s in states])
         hidden = self.hidden_states_by_layer(inputs, generator=generator)
         pooled = torch.stack([self._pool_reference(h, inputs.attention_mask) for h in hidden])

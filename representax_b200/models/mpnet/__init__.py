@@ -162,7 +162,61 @@ class MPNetEncoder(nn.Module):
     def _dtype(self):
         return active_compute_dtype(self.compute_dtype)
 
+    # ------------------------------------------------------------ native path
+    def _native(self, batch: TokenBatch) -> bool:
+        pk = batch.packed
+        return (pk is not None and pk.input_ids.is_cuda and self._dtype() == torch.bfloat16
+                and self.config.head_dimension == 64 and self.config.hidden_activation == "gelu")
+
+    def _rel_buckets(self, max_len: int, device) -> torch.Tensor:
+        cache = getattr(self, "_bucket_cache", {})
+        key = (max_len, str(device))
+        if key not in cache:
+            d = torch.arange(-(max_len - 1), max_len, device=device)
+            cache[key] = mpnet_relative_position_bucket(d, num_buckets=self.config.relative_attention_num_buckets)
+            self._bucket_cache = cache
+        return cache[key]
+
+    def _native_hidden(self, batch: TokenBatch, generator=None):
+        """Packed rows through the fused BERT-style blocks with the relative bias in the attention kernel."""
+
+        from representax_b200.ops import functional as Fn
+
+        cfg = self.config
+        pk = batch.packed
+        packed = Fn.Packed(cu_seqlens=pk.cu_seqlens, max_len=pk.max_len, total=pk.total)
+        # MPNet positions count valid tokens from padding_index + 1 (right padding: column + 2)
+        pos = pk.position_ids if batch.position_ids is not None else pk.position_ids + (cfg.pad_token_id + 1)
+        if not hasattr(self, "_zero_types") or self._zero_types.device != pk.input_ids.device:
+            self._zero_types = torch.zeros(1, cfg.hidden_size, device=pk.input_ids.device)
+        p_h, p_a = cfg.hidden_dropout_probability, cfg.attention_dropout_probability
+        seed = generator.initial_seed() if generator is not None and (p_h > 0 or p_a > 0) else None
+        drop = (lambda site: None if seed is None else Fn.Dropout(seed, site, p_a, p_h))  # noqa: E731
+        h = Fn.embed_layer_norm(pk.input_ids, pos, None, self.word, self.position, self._zero_types,
+                                self.emb_norm_weight, self.emb_norm_bias, cfg.norm_epsilon, cfg.pad_token_id,
+                                dropout=drop(0))
+        buckets = self._rel_buckets(max(pk.max_len, 1), pk.input_ids.device)
+        fused_bias = seed is None or p_h == 0
+        for i, layer in enumerate(self.layers):
+            s1 = Fn.attention_block(h, layer.qkv_weight, layer.qkv_bias, layer.out_weight, layer.out_bias, packed,
+                                    heads=cfg.num_attention_heads, out_bias_grad_fused=fused_bias,
+                                    dropout=drop(16 * (i + 1)), rel_table=self.relative_attention_bias,
+                                    rel_buckets=buckets)
+            h1 = Fn.layer_norm(s1, layer.attn_norm_weight, layer.attn_norm_bias, cfg.norm_epsilon,
+                               producer_bias=layer.out_bias if fused_bias else None)
+            s2 = Fn.mlp_block(h1, layer.ffn_in_weight, layer.ffn_in_bias, layer.ffn_out_weight, layer.ffn_out_bias,
+                              out_bias_grad_fused=fused_bias, dropout=drop(16 * (i + 1)))
+            h = Fn.layer_norm(s2, layer.out_norm_weight, layer.out_norm_bias, cfg.norm_epsilon,
+                              producer_bias=layer.ffn_out_bias if fused_bias else None)
+        return h, packed
+
     def hidden_states(self, batch: TokenBatch, *, generator=None) -> torch.Tensor:
+        if self._native(batch):
+            h, _ = self._native_hidden(batch, generator)
+            m = batch.attention_mask.to(h.device).bool()
+            out = h.new_zeros(m.shape + (h.shape[-1],))
+            out[m] = h
+            return out
         cfg = self.config
         dtype = self._dtype()
         ids = batch.input_ids.long()
@@ -199,6 +253,11 @@ class MPNetEncoder(nn.Module):
 
     def encode(self, inputs: TokenBatch, *, route: Route = Route.GENERIC, generator=None) -> torch.Tensor:
         del route
+        if self._native(inputs) and self.pooling in ("mean", "cls", "first", "last", "lasttoken"):
+            from representax_b200.ops import functional as Fn
+
+            h, packed = self._native_hidden(inputs, generator)
+            return Fn.pool(h, packed, self.pooling, self.normalize)
         hidden = self.hidden_states(inputs, generator=generator)
         mask = inputs.attention_mask
         if self.pooling == "mean":

@@ -75,10 +75,33 @@ def _colsum_into(x: torch.Tensor, sink: _GradSink) -> None:
         ext().colsum_accumulate(x, sink.buffer())
 
 
+@dataclass(frozen=True)
+class Dropout:
+    """Dropout of one block: Philox seed, the block's first site id, probabilities."""
+
+    seed: int
+    site: int
+    attention: float = 0.0
+    hidden: float = 0.0
+
+    def hidden_args(self, offset: int):
+        return (self.seed, self.site + offset, self.hidden) if self.hidden > 0 else None
+
+
+def _hidden_backward(ds: torch.Tensor, drop: "Dropout | None", offset: int) -> torch.Tensor:
+    """Gradient through an inverted-dropout site (the same Philox mask as the forward)."""
+
+    if drop is None or drop.hidden <= 0:
+        return ds
+    out = torch.empty_like(ds)
+    ext().dropout_apply(ds, out, drop.seed, drop.site + offset, drop.hidden)
+    return out
+
+
 class AttentionBlockFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, w_qkv, b_qkv, w_o, b_o, cu_seqlens, max_len, heads, kv_heads, causal, window,
-                out_bias_grad_fused=False):
+                out_bias_grad_fused=False, dropout=None, rel_table=None, rel_buckets=None):
         C = ext()
         T, H = x.shape
         head_dim = 64
@@ -90,11 +113,20 @@ class AttentionBlockFn(torch.autograd.Function):
         a = torch.empty(T, qd, dtype=torch.bfloat16, device=x.device)
         lse = torch.empty(heads, T, dtype=torch.float32, device=x.device)
         scale = head_dim ** -0.5
-        C.attention_forward(q, k, v, a, lse, cu_seqlens, max_len, heads, kv_heads, scale, causal, window)
-        s = G.linear_forward(a, wo, bo, residual=x)
+        pa = dropout.attention if dropout is not None else 0.0
+        seed = dropout.seed if dropout is not None else 0
+        site = dropout.site if dropout is not None else 0
+        lut = None
+        if rel_table is not None:  # [buckets, heads] -> [heads, 2 L - 1] over signed distances
+            lut = rel_table.detach().float()[rel_buckets].T.contiguous()
+        C.attention_forward(q, k, v, a, lse, cu_seqlens, max_len, heads, kv_heads, scale, causal, window, seed, site,
+                            pa, lut)
+        s = G.linear_forward(a, wo, bo, residual=x, dropout=None if dropout is None else dropout.hidden_args(1))
         ctx.save_for_backward(x, qkv, a, lse, cu_seqlens, w_qkv, b_qkv, w_o, b_o)
+        ctx.rel = (rel_table, rel_buckets, lut)
         ctx.meta = (max_len, heads, kv_heads, causal, window, scale)
         ctx.out_bias_grad_fused = out_bias_grad_fused
+        ctx.dropout = dropout
         return s
 
     @staticmethod
@@ -102,56 +134,70 @@ class AttentionBlockFn(torch.autograd.Function):
         C = ext()
         x, qkv, a, lse, cu, w_qkv, b_qkv, w_o, b_o = ctx.saved_tensors
         max_len, heads, kv_heads, causal, window, scale = ctx.meta
+        drop = ctx.dropout
         ds = ds.contiguous()
+        dpre = _hidden_backward(ds, drop, 1)  # gradient of the pre-dropout projection
         T = x.shape[0]
         qd, kd = heads * 64, kv_heads * 64
         g_wo, g_bo, g_wqkv, g_bqkv = _GradSink(w_o), _GradSink(b_o), _GradSink(w_qkv), _GradSink(b_qkv)
         if g_wo.wanted:
-            G.linear_wgrad(ds, a, g_wo.buffer())
+            G.linear_wgrad(dpre, a, g_wo.buffer())
         if not ctx.out_bias_grad_fused:
-            _colsum_into(ds, g_bo)
-        da = G.linear_dgrad(ds, compute_view(w_o))
+            _colsum_into(dpre, g_bo)
+        da = G.linear_dgrad(dpre, compute_view(w_o))
         dqkv = torch.empty_like(qkv)
         q, k, v = qkv[:, :qd], qkv[:, qd:qd + kd], qkv[:, qd + kd:]
         dq_acc = torch.empty(T, qd, dtype=torch.float32, device=x.device)
         dvec = torch.empty(heads, T, dtype=torch.float32, device=x.device)
+        rel_table, rel_buckets, lut = ctx.rel
+        drel = None if lut is None else torch.zeros_like(lut)
         C.attention_backward(da, q, k, v, a, lse, dqkv[:, :qd], dqkv[:, qd:qd + kd], dqkv[:, qd + kd:],
-                             dq_acc, dvec, cu, max_len, heads, kv_heads, scale, causal, window)
+                             dq_acc, dvec, cu, max_len, heads, kv_heads, scale, causal, window,
+                             drop.seed if drop is not None else 0, drop.site if drop is not None else 0,
+                             drop.attention if drop is not None else 0.0, lut, drel)
+        g_rel = None
+        if drel is not None and rel_table.requires_grad:
+            sink = _GradSink(rel_table)
+            sink.buffer().index_add_(0, rel_buckets, drel.T)
+            g_rel = sink.result()
         if g_wqkv.wanted:
             G.linear_wgrad(dqkv, x, g_wqkv.buffer())
         _colsum_into(dqkv, g_bqkv)
         dx = G.linear_dgrad(dqkv, compute_view(w_qkv), residual=ds)
         return (dx, g_wqkv.result(), g_bqkv.result(), g_wo.result(), g_bo.result(), None, None, None, None, None,
-                None, None)
+                None, None, None, g_rel, None)
 
 
 class MlpBlockFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, w1, b1, w2, b2, out_bias_grad_fused=False):
+    def forward(ctx, x, w1, b1, w2, b2, out_bias_grad_fused=False, dropout=None):
         T = x.shape[0]
         inter = w1.shape[0]
         z = torch.empty(T, inter, dtype=torch.bfloat16, device=x.device)
         g = G.linear_forward(x, compute_view(w1), compute_view(b1), gelu_preact=z)
-        s = G.linear_forward(g, compute_view(w2), compute_view(b2), residual=x)
+        s = G.linear_forward(g, compute_view(w2), compute_view(b2), residual=x,
+                             dropout=None if dropout is None else dropout.hidden_args(2))
         ctx.save_for_backward(x, z, g, w1, b1, w2, b2)
         ctx.out_bias_grad_fused = out_bias_grad_fused
+        ctx.dropout = dropout
         return s
 
     @staticmethod
     def backward(ctx, ds):
         x, z, g, w1, b1, w2, b2 = ctx.saved_tensors
         ds = ds.contiguous()
+        dpre = _hidden_backward(ds, ctx.dropout, 2)
         s_w1, s_b1, s_w2, s_b2 = _GradSink(w1), _GradSink(b1), _GradSink(w2), _GradSink(b2)
         if s_w2.wanted:
-            G.linear_wgrad(ds, g, s_w2.buffer())
+            G.linear_wgrad(dpre, g, s_w2.buffer())
         if not ctx.out_bias_grad_fused:
-            _colsum_into(ds, s_b2)
-        dz = G.linear_dgrad(ds, compute_view(w2), gelu_preact=z)
+            _colsum_into(dpre, s_b2)
+        dz = G.linear_dgrad(dpre, compute_view(w2), gelu_preact=z)
         if s_w1.wanted:
             G.linear_wgrad(dz, x, s_w1.buffer())
         _colsum_into(dz, s_b1)
         dx = G.linear_dgrad(dz, compute_view(w1), residual=ds)
-        return dx, s_w1.result(), s_b1.result(), s_w2.result(), s_b2.result(), None
+        return dx, s_w1.result(), s_b1.result(), s_w2.result(), s_b2.result(), None, None
 
 
 class LayerNormFn(torch.autograd.Function):
@@ -190,7 +236,7 @@ class LayerNormFn(torch.autograd.Function):
 
 class EmbedLayerNormFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, ids, pos_ids, type_ids, word, pos, typ, gamma, beta, eps, pad_id):
+    def forward(ctx, ids, pos_ids, type_ids, word, pos, typ, gamma, beta, eps, pad_id, dropout=None):
         C = ext()
         rows, H = ids.numel(), word.shape[1]
         y = torch.empty(rows, H, dtype=torch.bfloat16, device=ids.device)
@@ -198,6 +244,9 @@ class EmbedLayerNormFn(torch.autograd.Function):
         rstd = torch.empty(rows, dtype=torch.float32, device=ids.device)
         C.embed_ln_forward(ids, pos_ids, type_ids, compute_view(word), compute_view(pos), compute_view(typ),
                            compute_view(gamma), compute_view(beta), y, mean, rstd, eps)
+        ctx.dropout = dropout
+        if dropout is not None and dropout.hidden > 0:
+            C.dropout_apply(y, y, dropout.seed, dropout.site, dropout.hidden)
         ctx.save_for_backward(ids, pos_ids, type_ids if type_ids is not None else torch.empty(0, device=ids.device),
                               mean, rstd, word, pos, typ, gamma, beta)
         ctx.has_types = type_ids is not None
@@ -210,10 +259,11 @@ class EmbedLayerNormFn(torch.autograd.Function):
         ids, pos_ids, type_ids, mean, rstd, word, pos, typ, gamma, beta = ctx.saved_tensors
         sinks = [_GradSink(p) for p in (word, pos, typ, gamma, beta)]
         bufs = [s.buffer() for s in sinks]
-        C.embed_ln_backward(dy.contiguous(), ids, pos_ids, type_ids if ctx.has_types else None,
+        dy = _hidden_backward(dy.contiguous(), ctx.dropout, 0)
+        C.embed_ln_backward(dy, ids, pos_ids, type_ids if ctx.has_types else None,
                             compute_view(word), compute_view(pos), compute_view(typ), compute_view(gamma),
                             mean, rstd, bufs[0], bufs[1], bufs[2], bufs[3], bufs[4], ctx.pad_id)
-        return (None, None, None) + tuple(s.result() for s in sinks) + (None, None)
+        return (None, None, None) + tuple(s.result() for s in sinks) + (None, None, None)
 
 
 POOL_MODES = {"mean": 0, "first": 1, "cls": 1, "last": 2, "lasttoken": 2}
@@ -242,16 +292,23 @@ class PoolFn(torch.autograd.Function):
 
 
 def attention_block(x, w_qkv, b_qkv, w_o, b_o, packed: Packed, *, heads, kv_heads=None, causal=False, window=-1,
-                    out_bias_grad_fused: bool = False):
+                    out_bias_grad_fused: bool = False, dropout: Dropout | None = None, rel_table=None,
+                    rel_buckets=None):
     """``out_bias_grad_fused``: the following layer_norm was given ``producer_bias=b_o``
-    and reduces its gradient in its own backward kernel."""
+    and reduces its gradient in its own backward kernel (not with hidden dropout).
+    ``dropout``: attention-probability dropout (site) and output dropout (site + 1).
+    ``rel_table`` ([buckets, heads]) with ``rel_buckets`` (bucket of each signed
+    distance -(L-1)..L-1): an additive relative-position bias (MPNet)."""
 
     return AttentionBlockFn.apply(x, w_qkv, b_qkv, w_o, b_o, packed.cu_seqlens, packed.max_len, heads,
-                                  kv_heads or heads, causal, window, out_bias_grad_fused)
+                                  kv_heads or heads, causal, window, out_bias_grad_fused, dropout, rel_table,
+                                  rel_buckets)
 
 
-def mlp_block(x, w1, b1, w2, b2, *, out_bias_grad_fused: bool = False):
-    return MlpBlockFn.apply(x, w1, b1, w2, b2, out_bias_grad_fused)
+def mlp_block(x, w1, b1, w2, b2, *, out_bias_grad_fused: bool = False, dropout: Dropout | None = None):
+    """``dropout``: output dropout at site + 2."""
+
+    return MlpBlockFn.apply(x, w1, b1, w2, b2, out_bias_grad_fused, dropout)
 
 
 def layer_norm(s, gamma, beta, eps: float, rms: bool = False, *, producer_bias=None):
@@ -261,8 +318,9 @@ def layer_norm(s, gamma, beta, eps: float, rms: bool = False, *, producer_bias=N
     return LayerNormFn.apply(s, gamma, beta, eps, rms, producer_bias)
 
 
-def embed_layer_norm(ids, pos_ids, type_ids, word, pos, typ, gamma, beta, eps: float, pad_id: int):
-    return EmbedLayerNormFn.apply(ids, pos_ids, type_ids, word, pos, typ, gamma, beta, eps, pad_id)
+def embed_layer_norm(ids, pos_ids, type_ids, word, pos, typ, gamma, beta, eps: float, pad_id: int,
+                     dropout: Dropout | None = None):
+    return EmbedLayerNormFn.apply(ids, pos_ids, type_ids, word, pos, typ, gamma, beta, eps, pad_id, dropout)
 
 
 def pool(h, packed: Packed, mode: str = "mean", normalize: bool = True):
@@ -270,6 +328,7 @@ def pool(h, packed: Packed, mode: str = "mean", normalize: bool = True):
 
 
 __all__ = [
+    "Dropout",
     "Packed",
     "attention_block",
     "compute_view",

@@ -17,6 +17,7 @@ EPI_BIAS = 1
 EPI_GELU = 2
 EPI_DGELU = 4
 EPI_RESID = 8
+EPI_DROP = 16
 
 OUT_BF16 = 0
 OUT_F32 = 1
@@ -43,13 +44,17 @@ def gemm(
     residual: torch.Tensor | None = None,
     split_k: int = 0,
     variant: int | None = None,
+    dropout: tuple[int, int, float] | None = None,
 ) -> torch.Tensor:
     """``variant``: 1 = one CTA per 128x256 tile, 2 = CTA pair per 256x256 tile
     (cta_group::2), 0/None = the default (``GEMM_VARIANT``, pair for >= 256 rows)."""
 
+    seed, stream, p = dropout if dropout is not None else (0, 0, 0.0)
+    if dropout is not None:
+        epi |= EPI_DROP
     ext().gemm(
         a, b, out, a_mn, b_mn, epi, out_mode, alpha, bias, aux_in, aux_out, residual,
-        status(out.device), split_k, GEMM_VARIANT if variant is None else variant,
+        status(out.device), split_k, GEMM_VARIANT if variant is None else variant, seed, stream, p,
     )
     return out
 
@@ -62,8 +67,12 @@ def linear_forward(
     gelu_preact: torch.Tensor | None = None,
     residual: torch.Tensor | None = None,
     out: torch.Tensor | None = None,
+    dropout: tuple[int, int, float] | None = None,
 ) -> torch.Tensor:
-    """``y = x W^T (+ b) (-> gelu, storing the pre-activation) (+ residual)``."""
+    """``y = x W^T (+ b) (-> gelu, storing the pre-activation) (-> dropout) (+ residual)``.
+
+    ``dropout = (seed, stream, p)`` drops elements of the biased product
+    before the residual add (needs bias and residual)."""
 
     rows, n = x.shape[0], weight.shape[0]
     if out is None:
@@ -75,7 +84,7 @@ def linear_forward(
         epi |= EPI_GELU
     if residual is not None:
         epi |= EPI_RESID
-    return gemm(x, weight, out, epi=epi, bias=bias, aux_out=gelu_preact, residual=residual)
+    return gemm(x, weight, out, epi=epi, bias=bias, aux_out=gelu_preact, residual=residual, dropout=dropout)
 
 
 def linear_dgrad(

@@ -270,7 +270,7 @@ class _AttentionFn(torch.autograd.Function):
         T = q.shape[0]
         o = torch.empty(q.shape, dtype=torch.bfloat16, device=q.device)
         lse = torch.empty(heads, T, dtype=torch.float32, device=q.device)
-        C.attention_forward(q, k, v, o, lse, cu_seqlens, max_len, heads, kv_heads, scale, causal, window)
+        C.attention_forward(q, k, v, o, lse, cu_seqlens, max_len, heads, kv_heads, scale, causal, window, 0, 0, 0.0, None)
         ctx.save_for_backward(q, k, v, o, lse, cu_seqlens)
         ctx.meta = (max_len, heads, kv_heads, scale, causal, window)
         return o
@@ -285,7 +285,7 @@ class _AttentionFn(torch.autograd.Function):
         dq_acc = torch.empty(T, q.shape[1], dtype=torch.float32, device=q.device)
         dvec = torch.empty(heads, T, dtype=torch.float32, device=q.device)
         C.attention_backward(do.contiguous(), q, k, v, o, lse, dq, dk, dv, dq_acc, dvec, cu, max_len, heads, kv_heads,
-                             scale, causal, window)
+                             scale, causal, window, 0, 0, 0.0, None, None)
         return dq, dk, dv, None, None, None, None, None, None, None
 
 
@@ -348,7 +348,7 @@ class _QKVAttentionFn(torch.autograd.Function):
             q_r, k_r = q, k
         o = torch.empty(T, qd, dtype=qkv.dtype, device=qkv.device)
         lse = torch.empty(heads, T, dtype=torch.float32, device=qkv.device)
-        C.attention_forward(q_r, k_r, v, o, lse, cu_seqlens, max_len, heads, kv_heads, scale, causal, window)
+        C.attention_forward(q_r, k_r, v, o, lse, cu_seqlens, max_len, heads, kv_heads, scale, causal, window, 0, 0, 0.0, None)
         e = torch.empty(0, device=qkv.device)
         ctx.save_for_backward(qkv, q_r, k_r, o, lse, cu_seqlens, e if q_norm is None else q_norm,
                               e if k_norm is None else k_norm, e if pos is None else pos,
@@ -369,7 +369,7 @@ class _QKVAttentionFn(torch.autograd.Function):
         dq_acc = torch.empty(T, qd, dtype=torch.float32, device=qkv.device)
         dvec = torch.empty(heads, T, dtype=torch.float32, device=qkv.device)
         C.attention_backward(do.contiguous(), q_r, k_r, qkv[:, qd + kd:], o, lse, dq, dk, dv, dq_acc, dvec, cu,
-                             max_len, heads, kv_heads, scale, causal, window)
+                             max_len, heads, kv_heads, scale, causal, window, 0, 0, 0.0, None, None)
         grads = []
         if has_pos:
             axis = axis_of if has_axis else None

@@ -244,7 +244,7 @@ def test_attention_fwd_bwd(C, lens, heads, kv_heads, causal, window):
     scale = 1 / 8
     o = torch.empty(total, hd, dtype=torch.bfloat16, device=_dev())
     lse = torch.empty(heads, total, device=_dev())
-    C.attention_forward(q, k, v, o, lse, cu, max(lens), heads, kv_heads, scale, causal, window)
+    C.attention_forward(q, k, v, o, lse, cu, max(lens), heads, kv_heads, scale, causal, window, 0, 0, 0.0, None)
     qf = q.float().requires_grad_(True)
     kf = k.float().requires_grad_(True)
     vf = v.float().requires_grad_(True)
@@ -259,7 +259,7 @@ def test_attention_fwd_bwd(C, lens, heads, kv_heads, causal, window):
     dq_acc = torch.empty(total, hd, device=_dev())
     dvec = torch.empty(heads, total, device=_dev())
     C.attention_backward(do, q, k, v, o, lse, dq, dk, dv, dq_acc, dvec, cu, max(lens), heads,
-                         kv_heads, scale, causal, window)
+                         kv_heads, scale, causal, window, 0, 0, 0.0, None, None)
     _close(dq, qf.grad, rtol=3e-2, atol=3e-2, what="dq")
     _close(dk, kf.grad, rtol=3e-2, atol=3e-2, what="dk")
     _close(dv, vf.grad, rtol=3e-2, atol=3e-2, what="dv")

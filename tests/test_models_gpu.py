@@ -85,8 +85,7 @@ def test_grad_cache_retention_matches_replay():
     from representax_b200.train.step import init_train_state
 
     cfg = BertConfig(vocab_size=1000, hidden_size=256, num_hidden_layers=2, num_attention_heads=4,
-                     intermediate_size=512, max_position_embeddings=128, hidden_dropout_probability=0.0,
-                     attention_dropout_probability=0.0)
+                     intermediate_size=512, max_position_embeddings=128)  # dropout 0.1: replays must match
     dev = torch.device("cuda")
     batch = to_device(retrieval_pairs(np.random.default_rng(0), 64, 64, vocab=1000, low=10, min_len=8, max_len=64),
                       dev)
@@ -97,7 +96,7 @@ def test_grad_cache_retention_matches_replay():
         ex = GradCache(query_chunk_size=16, retain_bytes=retain)
         state.store.zero_grad()
         with precision_context(BF16_MIXED_POLICY):
-            ex.run(MNRTask(scale=20.0), state.model, batch, streams=StreamFactory(dev, 0, 0, enabled=False))
+            ex.run(MNRTask(scale=20.0), state.model, batch, streams=StreamFactory(dev, 0, 0, enabled=True))
         state.store.collect_autograd_grads()
         grads.append(state.store.grad.clone())
         assert ex.stats["retained_chunks"] == (0 if retain == 0 else ex.stats["chunks"])

@@ -253,3 +253,128 @@ def test_int4_lora_linear_native_matches_reference():
     c = torch.autograd.grad(y32, [x32, q.lora_a, q.lora_b, bias], dy)
     for u, v in zip(a, c):
         _close(u, v, 4e-2)
+
+
+def test_dropout_epilogue_and_pointwise_share_masks():
+    from representax_b200.ops import gemm as G
+    from representax_b200.ops._ext import ext
+
+    g = torch.Generator(device=DEV).manual_seed(0)
+    x = torch.randn(700, 256, device=DEV, generator=g).to(torch.bfloat16)
+    w = (torch.randn(384, 256, device=DEV, generator=g) * 0.05).to(torch.bfloat16)
+    b = torch.randn(384, device=DEV, generator=g).to(torch.bfloat16)
+    r = torch.randn(700, 384, device=DEV, generator=g).to(torch.bfloat16)
+    p = 0.25
+    y0 = G.linear_forward(x, w, b).float()
+    y1 = G.linear_forward(x, w, b, residual=r, dropout=(1234, 7, p)).float() - r.float()
+    ones = torch.ones(700, 384, device=DEV, dtype=torch.bfloat16)
+    mask = torch.empty_like(ones)
+    ext().dropout_apply(ones, mask, 1234, 7, p)
+    keep = mask.float() > 0
+    assert abs(1 - keep.float().mean().item() - p) < 0.01
+    torch.testing.assert_close(mask.float()[keep], torch.full_like(mask.float()[keep], 1 / (1 - p)), rtol=1e-2, atol=0)
+    _close(y1, y0 * keep / (1 - p), 3e-2)
+    other = torch.empty_like(ones)
+    ext().dropout_apply(ones, other, 1235, 7, p)
+    assert (other != mask).any()
+
+
+@pytest.mark.parametrize("D", [64, 128])
+def test_attention_dropout_gradient_is_consistent(D):
+    """Directional derivative of the dropped-out attention matches its backward (same Philox mask)."""
+
+    from representax_b200.ops._ext import ext
+
+    C = ext()
+    lengths = [90, 130, 33]
+    T, heads = sum(lengths), 2
+    seg = _seg(lengths)
+    g = torch.Generator(device=DEV).manual_seed(1)
+    q, k, v = (torch.randn(T, heads * D, device=DEV, generator=g) for _ in range(3))
+    do = torch.randn(T, heads * D, device=DEV, generator=g)
+    dirs = [torch.randn(T, heads * D, device=DEV, generator=g) for _ in range(3)]
+    scale, p, seed = D ** -0.5, 0.2, 99
+
+    def fwd(qq, kk, vv):
+        o = torch.empty(T, heads * D, device=DEV, dtype=torch.bfloat16)
+        lse = torch.empty(heads, T, device=DEV)
+        C.attention_forward(qq.bfloat16(), kk.bfloat16(), vv.bfloat16(), o, lse, seg.cu_seqlens, seg.max_len, heads,
+                            heads, scale, False, -1, seed, 3, p, None)
+        return o, lse
+
+    o, lse = fwd(q, k, v)
+    o_again, _ = fwd(q, k, v)
+    assert torch.equal(o, o_again)
+    dq, dk, dv = (torch.empty(T, heads * D, device=DEV, dtype=torch.bfloat16) for _ in range(3))
+    acc = torch.empty(T, heads * D, device=DEV)
+    dvec = torch.empty(heads, T, device=DEV)
+    C.attention_backward(do.bfloat16(), q.bfloat16(), k.bfloat16(), v.bfloat16(), o, lse, dq, dk, dv, acc, dvec,
+                         seg.cu_seqlens, seg.max_len, heads, heads, scale, False, -1, seed, 3, p, None, None)
+    eps = 0.25
+    base = [x.bfloat16().float() for x in (q, k, v)]
+    for i, grad in enumerate((dq, dk, dv)):
+        args_p, args_m = list(base), list(base)
+        # the perturbation actually seen by the bf16 kernel
+        plus = (base[i] + eps * dirs[i]).bfloat16().float()
+        minus = (base[i] - eps * dirs[i]).bfloat16().float()
+        args_p[i], args_m[i] = plus, minus
+        eff = (plus - minus) / (2 * eps)
+        num = ((fwd(*args_p)[0].float() - fwd(*args_m)[0].float()) * do).sum() / (2 * eps)
+        o_b, lse_b = fwd(*base)
+        C.attention_backward(do.bfloat16(), *(x.bfloat16() for x in base), o_b, lse_b, dq, dk, dv, acc, dvec,
+                             seg.cu_seqlens, seg.max_len, heads, heads, scale, False, -1, seed, 3, p, None, None)
+        ana = (grad.float() * eff).sum()
+        assert abs(num - ana) <= 0.1 * abs(ana) + 1.0, (i, float(num), float(ana))
+
+
+def test_bert_native_dropout_replays_exactly():
+    from representax_b200.models.bert import BertConfig, BertEncoder
+    from representax_b200.models.text_batch import TokenBatch
+    from representax_b200.train.rng import generator
+
+    cfg = BertConfig(vocab_size=1000, hidden_size=256, num_hidden_layers=2, num_attention_heads=4,
+                     intermediate_size=512, max_position_embeddings=128)   # dropout 0.1 / 0.1
+    m = BertEncoder(cfg, seed=0, compute_dtype=torch.bfloat16).to(DEV)
+    ids = torch.randint(5, 900, (6, 40))
+    mask = torch.ones_like(ids)
+    mask[3, 25:] = 0
+    b = TokenBatch(attention_mask=mask, input_ids=ids).pack().map_tensors(lambda t: t.to(DEV))
+    e1 = m.encode(b, generator=generator(DEV, 1, "x"))
+    e2 = m.encode(b, generator=generator(DEV, 1, "x"))
+    e3 = m.encode(b, generator=generator(DEV, 2, "x"))
+    e0 = m.encode(b)
+    assert torch.equal(e1, e2)
+    assert not torch.equal(e1, e3)
+    cos = torch.nn.functional.cosine_similarity(e1, e0, dim=-1)
+    assert 0.8 < cos.min().item() < 0.99999
+
+
+def test_mpnet_native_relative_bias_matches_reference():
+    from representax_b200.models.mpnet import MPNetConfig, MPNetEncoder
+    from representax_b200.models.text_batch import TokenBatch
+
+    cfg = MPNetConfig(vocab_size=600, hidden_size=256, num_hidden_layers=2, num_attention_heads=4,
+                      intermediate_size=512, max_position_embeddings=300, hidden_dropout_probability=0.0,
+                      attention_dropout_probability=0.0)
+    m32 = MPNetEncoder(cfg, seed=0).to(DEV)
+    m16 = MPNetEncoder(cfg, seed=0, compute_dtype=torch.bfloat16).to(DEV)
+    with torch.no_grad():  # a bias large enough to matter
+        for m in (m32, m16):
+            m.relative_attention_bias.normal_(0, 1.0, generator=torch.Generator(device=DEV).manual_seed(5))
+    ids = torch.randint(5, 590, (5, 200))
+    mask = torch.ones_like(ids)
+    mask[1, 150:] = 0
+    mask[4, 30:] = 0
+    ids[mask == 0] = cfg.pad_token_id
+    host = TokenBatch(attention_mask=mask, input_ids=ids)
+    e32 = m32.encode(host.map_tensors(lambda t: t.to(DEV)))
+    b16 = host.pack().map_tensors(lambda t: t.to(DEV))
+    assert m16._native(b16)
+    e16 = m16.encode(b16)
+    cos = torch.nn.functional.cosine_similarity(e16.float(), e32.float(), dim=-1)
+    assert cos.min().item() > 0.995, cos
+    (e32 * torch.arange(256, device=DEV)).sum().backward()
+    (e16 * torch.arange(256, device=DEV)).sum().backward()
+    g32 = m32.relative_attention_bias.grad
+    g16 = m16.relative_attention_bias.grad
+    assert torch.nn.functional.cosine_similarity(g16.flatten(), g32.flatten(), dim=0) > 0.98

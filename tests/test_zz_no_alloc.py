@@ -53,12 +53,12 @@ def _reference(C, qkv, do, cu, total, hd, heads, lens):
     q, k, v = qkv[:, :hd], qkv[:, hd:2 * hd], qkv[:, 2 * hd:]
     o = torch.empty(total, hd, dtype=torch.bfloat16, device=qkv.device)
     lse = torch.empty(heads, total, device=qkv.device)
-    C.attention_forward(q, k, v, o, lse, cu, max(lens), heads, heads, 0.125, False, -1)
+    C.attention_forward(q, k, v, o, lse, cu, max(lens), heads, heads, 0.125, False, -1, 0, 0, 0.0, None)
     dqkv = torch.empty_like(qkv)
     acc = torch.empty(total, hd, device=qkv.device)
     dvec = torch.empty(heads, total, device=qkv.device)
     C.attention_backward(do, q, k, v, o, lse, dqkv[:, :hd], dqkv[:, hd:2 * hd], dqkv[:, 2 * hd:], acc, dvec,
-                         cu, max(lens), heads, heads, 0.125, False, -1)
+                         cu, max(lens), heads, heads, 0.125, False, -1, 0, 0, 0.0, None, None)
     return o, lse, dqkv
 
 
