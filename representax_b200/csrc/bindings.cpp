@@ -16,13 +16,15 @@ void gemm_fp8(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, int64_t a
               const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& residual,
               const at::Tensor& status);
 void int4_dequantize(const at::Tensor& packed, const at::Tensor& scale_bits, at::Tensor& out);
-void dropout_apply(const at::Tensor& x, at::Tensor& y, int64_t seed, int64_t stream, double p);
+void dropout_apply(const at::Tensor& x, at::Tensor& y, int64_t seed, int64_t stream, double p,
+                   const c10::optional<at::Tensor>& colsum);
 void gemm_tcgen05(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_mn, bool b_mn,
                   int64_t epi, int64_t out_mode, double alpha,
                   const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& aux_in,
                   const c10::optional<at::Tensor>& aux_out,
                   const c10::optional<at::Tensor>& residual, const at::Tensor& status,
-                  int64_t split_k, int64_t variant, int64_t drop_seed, int64_t drop_stream, double drop_p);
+                  int64_t split_k, int64_t variant, int64_t drop_seed, int64_t drop_stream, double drop_p,
+                  const c10::optional<at::Tensor>& colsum);
 void norm_forward(const at::Tensor& x, const at::Tensor& gamma, const c10::optional<at::Tensor>& beta,
                   at::Tensor& y, const c10::optional<at::Tensor>& mean, at::Tensor& rstd,
                   double eps, bool rms);

@@ -5,6 +5,8 @@
 #include <algorithm>
 
 namespace rx {
+void colsum_accumulate(const at::Tensor& x, at::Tensor& out);
+
 // C = epilogue(alpha * A . B^T). Shapes: A is [M, K] (a_mn false) or [K, M]
 // (a_mn true); B is [N, K] (b_mn false) or [K, N] (b_mn true); C is [M, N].
 // `split_k` > 1 is allowed only with the atomic fp32 output mode; 0 picks a
@@ -14,7 +16,8 @@ void gemm_tcgen05(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool 
                   const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& aux_in,
                   const c10::optional<at::Tensor>& aux_out,
                   const c10::optional<at::Tensor>& residual, const at::Tensor& status,
-                  int64_t split_k, int64_t variant, int64_t drop_seed, int64_t drop_stream, double drop_p) {
+                  int64_t split_k, int64_t variant, int64_t drop_seed, int64_t drop_stream, double drop_p,
+                  const c10::optional<at::Tensor>& colsum) {
   using namespace gemm;
   check_bf16(A, "A");
   check_bf16(B, "B");
@@ -87,6 +90,16 @@ void gemm_tcgen05(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool 
   // variant: 1 = one CTA per 128x256 tile, 2 = CTA pair per 256x256 tile,
   // 0 = pair whenever there are at least 256 rows.
   const bool pair = variant == 2 || (variant == 0 && M >= 256);
+  bool colsum_after = false;
+  if (epi & EPI_COLSUM) {
+    RX_CHECK(colsum.has_value() && colsum->numel() == N, "the column-sum epilogue needs an fp32 [N] accumulator");
+    check_f32(*colsum, "colsum");
+    p.colsum = colsum->data_ptr<float>();
+    if (!pair) {  // only the tile-store epilogue sums columns; reduce afterwards instead
+      epi &= ~EPI_COLSUM;
+      colsum_after = true;
+    }
+  }
   constexpr int BN = 256;
   const int tile_m = pair ? 2 * BM : BM;
   p.m_tiles = static_cast<int>((M + tile_m - 1) / tile_m);
@@ -136,6 +149,10 @@ void gemm_tcgen05(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool 
   const int grid = pair ? 2 * std::min(p.num_units, workers) : std::min(p.num_units, sms);
   c10::cuda::CUDAGuard guard(device);
   fn(ta, tb, p, grid, at::cuda::getCurrentCUDAStream(device).stream(), device);
+  if (colsum_after) {
+    at::Tensor out = *colsum;
+    colsum_accumulate(C, out);
+  }
 }
 
 }  // namespace rx

@@ -24,6 +24,7 @@ LaunchFn pick_dgrad(int epi, int out) {
 
 LaunchFn pick_dgrad_pair(int epi, int out) {
   if (epi == EPI_RESID && out == OUT_BF16) return launch_pair<false, true, EPI_RESID, OUT_BF16>;
+  if (epi == (EPI_DGELU | EPI_COLSUM) && out == OUT_BF16) return launch_pair<false, true, EPI_DGELU | EPI_COLSUM, OUT_BF16>;
   if (epi != 0 && epi != EPI_DGELU) return nullptr;
   const bool dgelu = epi == EPI_DGELU;
   switch (out) {

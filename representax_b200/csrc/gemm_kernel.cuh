@@ -40,7 +40,10 @@ constexpr int kThreads = 64 + 32 * kEpilogueWarps;
 // EPI_DROP: inverted dropout of the (biased) value before the residual add;
 // element (m, n) keeps its value when word (n & 3) of Philox block
 // (m, n >> 2) at the site is >= the threshold.
-enum Epi : int { EPI_BIAS = 1, EPI_GELU = 2, EPI_DGELU = 4, EPI_RESID = 8, EPI_DROP = 16 };
+// EPI_COLSUM (tile-store path only): the column sums of the output are added
+// into p.colsum (fp32 [N]) with one atomic per column per 32-row warp piece
+// (the bias gradient of the layer whose input gradient is being computed).
+enum Epi : int { EPI_BIAS = 1, EPI_GELU = 2, EPI_DGELU = 4, EPI_RESID = 8, EPI_DROP = 16, EPI_COLSUM = 32 };
 enum Out : int { OUT_BF16 = 0, OUT_F32 = 1, OUT_F32_ACC = 2, OUT_F32_ATOMIC = 3 };
 
 struct Params {
@@ -58,6 +61,7 @@ struct Params {
   float alpha;
   const float* scales;  // fp8: device [2] per-tensor operand scales multiplied into alpha
   DropoutSite drop;
+  float* colsum;
   int* status;
   uint64_t timeout_ns;
 };
@@ -104,75 +108,6 @@ __device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float (&
   }
 }
 
-// Epilogue values (bias / GELU / GELU' / dropout / residual) of one row
-// segment of 32 columns, for the staged tile store. Columns >= N and rows
-// >= M produce zeros and read nothing (the tile store clips them).
-template <int EPI>
-__device__ __forceinline__ void epilogue_values32(const Params& p, int m, int n_base, const uint32_t (&r)[32],
-                                                  float (&v)[32]) {
-  const bool row_ok = m < p.M;
-  const bool full = row_ok && (n_base + 32 <= p.N);
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * p.alpha;
-  if (full) {
-    if constexpr ((EPI & EPI_BIAS) != 0) {
-      float b[32];
-      load_bf16x32(p.bias + n_base, b);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] += b[i];
-    }
-    if constexpr ((EPI & EPI_DGELU) != 0) {
-      float z[32];
-      load_bf16x32(p.aux_in + static_cast<int64_t>(m) * p.ld_aux_in + n_base, z);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] *= gelu_erf_grad(z[i]);
-    }
-    if constexpr ((EPI & EPI_GELU) != 0) {
-      store_bf16x32(p.aux_out + static_cast<int64_t>(m) * p.ld_aux_out + n_base, v);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
-    }
-    if constexpr ((EPI & EPI_DROP) != 0) {
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const Philox4 rb = dropout_block(p.drop, static_cast<uint32_t>(m), static_cast<uint32_t>((n_base >> 2) + q));
-#pragma unroll
-        for (int w = 0; w < 4; ++w)
-          v[4 * q + w] = word_of(rb, w) >= p.drop.threshold ? v[4 * q + w] * p.drop.scale : 0.f;
-      }
-    }
-    if constexpr ((EPI & EPI_RESID) != 0) {
-      float res[32];
-      load_bf16x32(p.residual + static_cast<int64_t>(m) * p.ld_res + n_base, res);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] += res[i];
-    }
-    return;
-  }
-#pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    const int n = n_base + i;
-    if (!row_ok || n >= p.N) {
-      v[i] = 0.f;
-      continue;
-    }
-    float x = v[i];
-    if constexpr ((EPI & EPI_BIAS) != 0) x += __bfloat162float(p.bias[n]);
-    if constexpr ((EPI & EPI_DGELU) != 0)
-      x *= gelu_erf_grad(__bfloat162float(p.aux_in[static_cast<int64_t>(m) * p.ld_aux_in + n]));
-    if constexpr ((EPI & EPI_GELU) != 0) {
-      p.aux_out[static_cast<int64_t>(m) * p.ld_aux_out + n] = __float2bfloat16_rn(x);
-      x = gelu_erf(x);
-    }
-    if constexpr ((EPI & EPI_DROP) != 0) {
-      const Philox4 rb = dropout_block(p.drop, static_cast<uint32_t>(m), static_cast<uint32_t>(n >> 2));
-      x = word_of(rb, n & 3) >= p.drop.threshold ? x * p.drop.scale : 0.f;
-    }
-    if constexpr ((EPI & EPI_RESID) != 0) x += __bfloat162float(p.residual[static_cast<int64_t>(m) * p.ld_res + n]);
-    v[i] = x;
-  }
-}
-
 // Write one lane's 32 bf16 values as row `lane` of a 32 x 32 tile staged in
 // shared memory with the 64-byte swizzle of the store tensor map.
 __device__ __forceinline__ void stage_row32_sw64(uint8_t* buf, int lane, const float (&v)[32]) {
@@ -183,6 +118,93 @@ __device__ __forceinline__ void stage_row32_sw64(uint8_t* buf, int lane, const f
 #pragma unroll
     for (int j = 0; j < 4; ++j) h[j] = __floats2bfloat162_rn(v[q * 8 + 2 * j], v[q * 8 + 2 * j + 1]);
     *reinterpret_cast<uint4*>(buf + lane * 64 + ((q ^ ((lane >> 1) & 3)) * 16)) = w;
+  }
+}
+
+// Coalesced load of a 32 x 32 bf16 tile (rows row0.., columns n_base..) into
+// `buf` with the 64-byte swizzle: 16-byte pieces, 4 lanes per 64-byte row
+// segment; rows >= rows_valid and columns >= cols_valid read as zero.
+__device__ __forceinline__ void warp_load_tile32_sw64(uint8_t* buf, const __nv_bfloat16* src, int64_t ld, int row0,
+                                                      int n_base, int rows_valid, int cols_valid, int lane) {
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {
+    const int c = lane + 32 * it;
+    const int row = c >> 2, piece = c & 3;
+    const int m = row0 + row, n = n_base + piece * 8;
+    uint4 w = make_uint4(0u, 0u, 0u, 0u);
+    if (m < rows_valid) {
+      const __nv_bfloat16* g = src + static_cast<int64_t>(m) * ld + n;
+      if (n + 8 <= cols_valid) {
+        w = *reinterpret_cast<const uint4*>(g);
+      } else {
+        __nv_bfloat16* e = reinterpret_cast<__nv_bfloat16*>(&w);
+        for (int k = 0; k < 8; ++k) e[k] = n + k < cols_valid ? g[k] : __float2bfloat16_rn(0.f);
+      }
+    }
+    *reinterpret_cast<uint4*>(buf + row * 64 + ((piece ^ ((row >> 1) & 3)) * 16)) = w;
+  }
+}
+
+// Row `lane` of a 64-byte-swizzled 32 x 32 bf16 tile as 32 floats.
+__device__ __forceinline__ void read_row32_sw64(const uint8_t* buf, int lane, float (&v)[32]) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint4 w = *reinterpret_cast<const uint4*>(buf + lane * 64 + ((q ^ ((lane >> 1) & 3)) * 16));
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __bfloat1622float2(h[j]);
+      v[q * 8 + 2 * j] = f.x;
+      v[q * 8 + 2 * j + 1] = f.y;
+    }
+  }
+}
+
+// Epilogue values of one row segment for the staged tile store, with the
+// residual (EPI_RESID) or GELU pre-activation input (EPI_DGELU) already in
+// `side`; with EPI_GELU the pre-activation is returned in `pre`.
+template <int EPI>
+__device__ __forceinline__ void epilogue_tile_values32(const Params& p, int m, int n_base, const uint32_t (&r)[32],
+                                                       const float (&side)[32], float (&v)[32], float (&pre)[32]) {
+  const bool row_ok = m < p.M;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * p.alpha;
+  if constexpr ((EPI & EPI_BIAS) != 0) {
+    if (n_base + 32 <= p.N) {
+      float b[32];
+      load_bf16x32(p.bias + n_base, b);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] += b[i];
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] += n_base + i < p.N ? __bfloat162float(p.bias[n_base + i]) : 0.f;
+    }
+  }
+  if constexpr ((EPI & EPI_DGELU) != 0) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] *= gelu_erf_grad(side[i]);
+  }
+  if constexpr ((EPI & EPI_GELU) != 0) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      pre[i] = v[i];
+      v[i] = gelu_erf(v[i]);
+    }
+  }
+  if constexpr ((EPI & EPI_DROP) != 0) {
+    if (row_ok) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const Philox4 rb = dropout_block(p.drop, static_cast<uint32_t>(m), static_cast<uint32_t>((n_base >> 2) + q));
+#pragma unroll
+        for (int w = 0; w < 4; ++w)
+          v[4 * q + w] = word_of(rb, w) >= p.drop.threshold ? v[4 * q + w] * p.drop.scale : 0.f;
+      }
+    }
+  }
+  if constexpr ((EPI & EPI_RESID) != 0) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] += side[i];
   }
 }
 
@@ -555,7 +577,8 @@ constexpr int pair_stage_bytes() { return OUT == OUT_BF16 ? kEpilogueWarps * 2 *
 template <bool A_MN, bool B_MN, int EPI, int OUT>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     const __grid_constant__ CUtensorMap tmC, const Params p) {
+                     const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmAux,
+                     const Params p) {
   constexpr int BN = 256;           // pair tile columns
   constexpr int HALF_N = BN / 2;    // B rows loaded by each CTA
   constexpr int STAGES = kPairStages;
@@ -603,6 +626,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_map(&tmA);
     tma_prefetch_map(&tmB);
     if constexpr (kTileStore) tma_prefetch_map(&tmC);
+    if constexpr (kTileStore && (EPI & EPI_GELU) != 0) tma_prefetch_map(&tmAux);
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_slot, TMEM_COLS);
@@ -765,17 +789,47 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld_wait();
         const int n_base = n0 + c * 32;
         if constexpr (kTileStore) {
-          if (n_base < p.N && m0 + static_cast<int>(rank) * BM + quad * 32 < p.M) {  // warp-uniform
-            float v[32];
-            epilogue_values32<EPI>(p, m, n_base, r, v);
+          const int row0 = m0 + static_cast<int>(rank) * BM + quad * 32;
+          if (n_base < p.N && row0 < p.M) {  // warp-uniform
             uint8_t* buf = sC + ((warp - 2) * 2 + (store_seq & 1)) * 2048;
             if (lane == 0) tma_store_wait_read<1>();  // the store that last read `buf` is done reading
             __syncwarp();
+            float side[32], v[32], pre[32];
+            if constexpr ((EPI & (EPI_RESID | EPI_DGELU)) != 0) {
+              const bool resid = (EPI & EPI_RESID) != 0;
+              warp_load_tile32_sw64(buf, resid ? p.residual : p.aux_in, resid ? p.ld_res : p.ld_aux_in, row0,
+                                    n_base, p.M, p.N, lane);
+              __syncwarp();
+              read_row32_sw64(buf, lane, side);
+              __syncwarp();  // every lane has its row before the buffer is overwritten
+            }
+            epilogue_tile_values32<EPI>(p, m, n_base, r, side, v, pre);
+            if constexpr ((EPI & EPI_GELU) != 0) {
+              stage_row32_sw64(buf, lane, pre);
+              fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0) {
+                tma_store_2d(&tmAux, buf, n_base, row0);
+                tma_store_commit();
+                tma_store_wait_read<0>();
+              }
+              __syncwarp();
+            }
             stage_row32_sw64(buf, lane, v);
             fence_proxy_async_smem();
             __syncwarp();
+            if constexpr ((EPI & EPI_COLSUM) != 0) {
+              // lane c sums column n_base + c over the piece's rows (rows >= M hold zeros)
+              float cs = 0.f;
+              const int piece = lane >> 3, within = (lane & 7) * 2;
+#pragma unroll 8
+              for (int rr = 0; rr < 32; ++rr)
+                cs += __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(
+                    buf + rr * 64 + ((piece ^ ((rr >> 1) & 3)) * 16) + within));
+              if (n_base + lane < p.N) atomicAdd(p.colsum + n_base + lane, cs);
+            }
             if (lane == 0) {
-              tma_store_2d(&tmC, buf, n_base, m0 + static_cast<int>(rank) * BM + quad * 32);
+              tma_store_2d(&tmC, buf, n_base, row0);
               tma_store_commit();
             }
             ++store_seq;
@@ -807,9 +861,11 @@ void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, 
   auto kern = gemm_pair_kernel<A_MN, B_MN, EPI, OUT>;
   constexpr size_t smem = 1024 + kPairStages * (BM * BK * 2 + 128 * BK * 2) + pair_stage_bytes<OUT>() + 256;
   static_assert(smem <= 232448, "pair GEMM shared memory exceeds the opt-in limit");
-  CUtensorMap tc{};
-  if constexpr (OUT == OUT_BF16)
+  CUtensorMap tc{}, taux{};
+  if constexpr (OUT == OUT_BF16) {
     tc = make_tmap_2d_bf16_store(p.C, p.M, p.N, p.ldc);
+    if constexpr ((EPI & EPI_GELU) != 0) taux = make_tmap_2d_bf16_store(p.aux_out, p.M, p.N, p.ld_aux_out);
+  }
   static bool configured[64] = {false};
   if (device < 0 || device >= 64 || !configured[device]) {
     RX_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -828,7 +884,7 @@ void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, 
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  RX_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, tc, p));
+  RX_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, tc, taux, p));
 }
 
 using LaunchFn = void (*)(const CUtensorMap&, const CUtensorMap&, const Params&, int, cudaStream_t,

@@ -88,13 +88,15 @@ class Dropout:
         return (self.seed, self.site + offset, self.hidden) if self.hidden > 0 else None
 
 
-def _hidden_backward(ds: torch.Tensor, drop: "Dropout | None", offset: int) -> torch.Tensor:
-    """Gradient through an inverted-dropout site (the same Philox mask as the forward)."""
+def _hidden_backward(ds: torch.Tensor, drop: "Dropout | None", offset: int,
+                     colsum: torch.Tensor | None = None) -> torch.Tensor:
+    """Gradient through an inverted-dropout site (the same Philox mask as the
+    forward); ``colsum`` also receives the result's column sums (a bias gradient)."""
 
     if drop is None or drop.hidden <= 0:
         return ds
     out = torch.empty_like(ds)
-    ext().dropout_apply(ds, out, drop.seed, drop.site + offset, drop.hidden)
+    ext().dropout_apply(ds, out, drop.seed, drop.site + offset, drop.hidden, colsum)
     return out
 
 
@@ -136,13 +138,15 @@ class AttentionBlockFn(torch.autograd.Function):
         max_len, heads, kv_heads, causal, window, scale = ctx.meta
         drop = ctx.dropout
         ds = ds.contiguous()
-        dpre = _hidden_backward(ds, drop, 1)  # gradient of the pre-dropout projection
         T = x.shape[0]
         qd, kd = heads * 64, kv_heads * 64
         g_wo, g_bo, g_wqkv, g_bqkv = _GradSink(w_o), _GradSink(b_o), _GradSink(w_qkv), _GradSink(b_qkv)
+        dropped = drop is not None and drop.hidden > 0
+        # gradient of the pre-dropout projection; its column sums are the out-bias gradient
+        dpre = _hidden_backward(ds, drop, 1, g_bo.buffer() if (dropped and g_bo.wanted) else None)
         if g_wo.wanted:
             G.linear_wgrad(dpre, a, g_wo.buffer())
-        if not ctx.out_bias_grad_fused:
+        if not ctx.out_bias_grad_fused and not dropped:
             _colsum_into(dpre, g_bo)
         da = G.linear_dgrad(dpre, compute_view(w_o))
         dqkv = torch.empty_like(qkv)
@@ -186,16 +190,17 @@ class MlpBlockFn(torch.autograd.Function):
     def backward(ctx, ds):
         x, z, g, w1, b1, w2, b2 = ctx.saved_tensors
         ds = ds.contiguous()
-        dpre = _hidden_backward(ds, ctx.dropout, 2)
         s_w1, s_b1, s_w2, s_b2 = _GradSink(w1), _GradSink(b1), _GradSink(w2), _GradSink(b2)
+        dropped = ctx.dropout is not None and ctx.dropout.hidden > 0
+        dpre = _hidden_backward(ds, ctx.dropout, 2, s_b2.buffer() if (dropped and s_b2.wanted) else None)
         if s_w2.wanted:
             G.linear_wgrad(dpre, g, s_w2.buffer())
-        if not ctx.out_bias_grad_fused:
+        if not ctx.out_bias_grad_fused and not dropped:
             _colsum_into(dpre, s_b2)
-        dz = G.linear_dgrad(dpre, compute_view(w2), gelu_preact=z)
+        # dz = (dpre W2) * gelu'(z); the GEMM epilogue also sums dz's columns (the ffn-in bias gradient)
+        dz = G.linear_dgrad(dpre, compute_view(w2), gelu_preact=z, colsum=s_b1.buffer() if s_b1.wanted else None)
         if s_w1.wanted:
             G.linear_wgrad(dz, x, s_w1.buffer())
-        _colsum_into(dz, s_b1)
         dx = G.linear_dgrad(dz, compute_view(w1), residual=ds)
         return dx, s_w1.result(), s_b1.result(), s_w2.result(), s_b2.result(), None, None
 
@@ -246,7 +251,7 @@ class EmbedLayerNormFn(torch.autograd.Function):
                            compute_view(gamma), compute_view(beta), y, mean, rstd, eps)
         ctx.dropout = dropout
         if dropout is not None and dropout.hidden > 0:
-            C.dropout_apply(y, y, dropout.seed, dropout.site, dropout.hidden)
+            C.dropout_apply(y, y, dropout.seed, dropout.site, dropout.hidden, None)
         ctx.save_for_backward(ids, pos_ids, type_ids if type_ids is not None else torch.empty(0, device=ids.device),
                               mean, rstd, word, pos, typ, gamma, beta)
         ctx.has_types = type_ids is not None

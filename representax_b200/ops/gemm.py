@@ -18,6 +18,7 @@ EPI_GELU = 2
 EPI_DGELU = 4
 EPI_RESID = 8
 EPI_DROP = 16
+EPI_COLSUM = 32
 
 OUT_BF16 = 0
 OUT_F32 = 1
@@ -45,16 +46,20 @@ def gemm(
     split_k: int = 0,
     variant: int | None = None,
     dropout: tuple[int, int, float] | None = None,
+    colsum: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """``variant``: 1 = one CTA per 128x256 tile, 2 = CTA pair per 256x256 tile
-    (cta_group::2), 0/None = the default (``GEMM_VARIANT``, pair for >= 256 rows)."""
+    (cta_group::2), 0/None = the default (``GEMM_VARIANT``, pair for >= 256 rows).
+    ``colsum`` (fp32 [N]): accumulate the output's column sums into it."""
 
     seed, stream, p = dropout if dropout is not None else (0, 0, 0.0)
     if dropout is not None:
         epi |= EPI_DROP
+    if colsum is not None:
+        epi |= EPI_COLSUM
     ext().gemm(
         a, b, out, a_mn, b_mn, epi, out_mode, alpha, bias, aux_in, aux_out, residual,
-        status(out.device), split_k, GEMM_VARIANT if variant is None else variant, seed, stream, p,
+        status(out.device), split_k, GEMM_VARIANT if variant is None else variant, seed, stream, p, colsum,
     )
     return out
 
@@ -94,8 +99,10 @@ def linear_dgrad(
     gelu_preact: torch.Tensor | None = None,
     residual: torch.Tensor | None = None,
     out: torch.Tensor | None = None,
+    colsum: torch.Tensor | None = None,
 ) -> torch.Tensor:
-    """``dx = dy W`` (times gelu'(preact) of the layer below) (+ residual)."""
+    """``dx = dy W`` (times gelu'(preact) of the layer below) (+ residual);
+    ``colsum``: also add dx's column sums into it (the lower layer's bias gradient)."""
 
     rows, k = dy.shape[0], weight.shape[1]
     if out is None:
@@ -106,7 +113,7 @@ def linear_dgrad(
     if residual is not None:
         epi |= EPI_RESID
     return gemm(
-        dy, weight, out, b_mn=True, epi=epi, aux_in=gelu_preact, residual=residual
+        dy, weight, out, b_mn=True, epi=epi, aux_in=gelu_preact, residual=residual, colsum=colsum
     )
 
 

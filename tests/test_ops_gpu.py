@@ -269,13 +269,13 @@ def test_dropout_epilogue_and_pointwise_share_masks():
     y1 = G.linear_forward(x, w, b, residual=r, dropout=(1234, 7, p)).float() - r.float()
     ones = torch.ones(700, 384, device=DEV, dtype=torch.bfloat16)
     mask = torch.empty_like(ones)
-    ext().dropout_apply(ones, mask, 1234, 7, p)
+    ext().dropout_apply(ones, mask, 1234, 7, p, None)
     keep = mask.float() > 0
     assert abs(1 - keep.float().mean().item() - p) < 0.01
     torch.testing.assert_close(mask.float()[keep], torch.full_like(mask.float()[keep], 1 / (1 - p)), rtol=1e-2, atol=0)
     _close(y1, y0 * keep / (1 - p), 3e-2)
     other = torch.empty_like(ones)
-    ext().dropout_apply(ones, other, 1235, 7, p)
+    ext().dropout_apply(ones, other, 1235, 7, p, None)
     assert (other != mask).any()
 
 
@@ -378,3 +378,27 @@ def test_mpnet_native_relative_bias_matches_reference():
     g32 = m32.relative_attention_bias.grad
     g16 = m16.relative_attention_bias.grad
     assert torch.nn.functional.cosine_similarity(g16.flatten(), g32.flatten(), dim=0) > 0.98
+
+
+def test_fused_column_sums_match():
+    from representax_b200.ops import gemm as G
+    from representax_b200.ops._ext import ext
+
+    g = torch.Generator(device=DEV).manual_seed(4)
+    dy = torch.randn(900, 768, device=DEV, generator=g).to(torch.bfloat16)
+    w = (torch.randn(768, 3072, device=DEV, generator=g) * 0.05).to(torch.bfloat16)
+    z = torch.randn(900, 3072, device=DEV, generator=g).to(torch.bfloat16)
+    cs = torch.zeros(3072, device=DEV)
+    dz = G.linear_dgrad(dy, w, gelu_preact=z, colsum=cs)
+    _close(cs, dz.float().sum(0), 2e-3)
+    small = torch.zeros(3072, device=DEV)  # < 256 rows: the column sums run after the GEMM
+    dz_s = G.linear_dgrad(dy[:100], w, gelu_preact=z[:100], colsum=small)
+    _close(small, dz_s.float().sum(0), 2e-3)
+    x = torch.randn(1000, 768, device=DEV, generator=g).to(torch.bfloat16)
+    out = torch.empty_like(x)
+    cs2 = torch.zeros(768, device=DEV)
+    ext().dropout_apply(x, out, 7, 3, 0.1, cs2)
+    ref = torch.empty_like(x)
+    ext().dropout_apply(x, ref, 7, 3, 0.1, None)
+    assert torch.equal(out, ref)
+    _close(cs2, out.float().sum(0), 2e-3)
