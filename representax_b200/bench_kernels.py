@@ -106,18 +106,28 @@ def bench_attention(timer, hbm, flops_peak, tag, report):
     o = torch.empty(total, 768, dtype=torch.bfloat16, device="cuda")
     lse = torch.empty(heads, total, device="cuda")
     fl = float(sum(4 * n * n * 64 * heads for n in lens.tolist()))
-    t = timer(lambda: C.attention_forward(q, k, v, o, lse, cu, 256, heads, heads, 0.125, False, -1, 0, 0, 0.0, None))
-    report({"kernel": "attention_fwd", "case": "bert_b128_len32-256", "ms": t * 1e3,
-            "tflops": fl / t / 1e12, f"frac_of_{tag}_bf16": fl / t / flops_peak})
     do = torch.randn(total, 768, device="cuda").to(torch.bfloat16)
     dqkv = torch.empty_like(qkv)
     acc = torch.empty(total, 768, device="cuda")
     dvec = torch.empty(heads, total, device="cuda")
-    t = timer(lambda: C.attention_backward(do, q, k, v, o, lse, dqkv[:, :768], dqkv[:, 768:1536],
-                                           dqkv[:, 1536:], acc, dvec, cu, 256, heads, heads, 0.125,
-                                           False, -1, 0, 0, 0.0, None, None))
-    report({"kernel": "attention_bwd", "case": "bert_b128_len32-256", "ms": t * 1e3,
-            "tflops": 2.5 * fl / t / 1e12, f"frac_of_{tag}_bf16": 2.5 * fl / t / flops_peak})
+    # Minimum DRAM traffic: forward reads Q, K, V and writes O (bf16); backward
+    # reads Q, K, V, O, dO and writes dQ, dK, dV (bf16).
+    fwd_bytes = 4 * total * 768 * 2
+    bwd_bytes = 8 * total * 768 * 2
+    for impl in ("tcgen05", "mma_sync"):
+        C.set_attention_tcgen05(impl == "tcgen05")
+        t = timer(lambda: C.attention_forward(q, k, v, o, lse, cu, 256, heads, heads, 0.125, False, -1, 0, 0, 0.0,
+                                              None))
+        report({"kernel": "attention_fwd", "impl": impl, "case": "bert_b128_len32-256", "ms": t * 1e3,
+                "tflops": fl / t / 1e12, f"frac_of_{tag}_bf16": fl / t / flops_peak,
+                f"frac_of_{tag}_hbm": fwd_bytes / t / hbm})
+        t = timer(lambda: C.attention_backward(do, q, k, v, o, lse, dqkv[:, :768], dqkv[:, 768:1536],
+                                               dqkv[:, 1536:], acc, dvec, cu, 256, heads, heads, 0.125,
+                                               False, -1, 0, 0, 0.0, None, None))
+        report({"kernel": "attention_bwd", "impl": impl, "case": "bert_b128_len32-256", "ms": t * 1e3,
+                "tflops": 2.5 * fl / t / 1e12, f"frac_of_{tag}_bf16": 2.5 * fl / t / flops_peak,
+                f"frac_of_{tag}_hbm": bwd_bytes / t / hbm})
+    C.set_attention_tcgen05(True)
 
 
 def bench_norm(timer, hbm, flops_peak, tag, report):

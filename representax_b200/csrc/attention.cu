@@ -609,9 +609,19 @@ template __global__ void attn_bwd_kernel<128, false>(const Params p);
 template __global__ void attn_bwd_kernel<64, true>(const Params p);
 template __global__ void attn_bwd_kernel<128, true>(const Params p);
 
+// tcgen05 kernels (attention_tc.cu): the path for head dims 64 / 128 without
+// relative position bias.
+bool tc_attention_enabled();
+void tc_forward(Params p, int d, int64_t max_len, cudaStream_t st, int device);
+void tc_backward(Params p, int d, int64_t max_len, cudaStream_t st, int device);
+
 }  // namespace attn
 
 namespace {
+bool aligned_rows(const at::Tensor& t) {
+  return t.stride(1) == 1 && t.stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0;
+}
+
 void fill_common(attn::Params& p, const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
                  const at::Tensor& cu_seqlens, int64_t heads, int64_t kv_heads, double scale,
                  bool causal, int64_t window) {
@@ -689,8 +699,12 @@ void attention_forward(const at::Tensor& q, const at::Tensor& k, const at::Tenso
   p.lse = lse.data_ptr<float>();
   if (p.batch == 0 || max_len == 0) return;
   c10::cuda::CUDAGuard guard(q.get_device());
-  dim3 grid((max_len + attn::BM - 1) / attn::BM, heads, p.batch);
   auto st = at::cuda::getCurrentCUDAStream().stream();
+  if (attn::tc_attention_enabled() && p.rel_lut == nullptr && aligned_rows(o)) {
+    attn::tc_forward(p, static_cast<int>(q.size(1) / heads), max_len, st, q.get_device());
+    return;
+  }
+  dim3 grid((max_len + attn::BM - 1) / attn::BM, heads, p.batch);
   if (q.size(1) / heads == 64) {
     attn::attn_fwd_kernel<64><<<grid, attn::kThreads, attn::fwd_smem_bytes<64>(), st>>>(p);
   } else {
@@ -740,7 +754,10 @@ void attention_backward(const at::Tensor& dO, const at::Tensor& q, const at::Ten
   }
   dim3 grid((max_len + attn::BN - 1) / attn::BN, kv_heads, p.batch);
   const bool gqa = kv_heads != heads;
-  if (d == 64) {
+  if (attn::tc_attention_enabled() && p.rel_lut == nullptr && aligned_rows(dO) &&
+      aligned_rows(dk) && aligned_rows(dv)) {
+    attn::tc_backward(p, d, max_len, st, q.get_device());
+  } else if (d == 64) {
     if (gqa) attn::attn_bwd_kernel<64, true><<<grid, attn::kThreads, attn::bwd_smem_bytes<64>(), st>>>(p);
     else attn::attn_bwd_kernel<64, false><<<grid, attn::kThreads, attn::bwd_smem_bytes<64>(), st>>>(p);
   } else if (gqa) {

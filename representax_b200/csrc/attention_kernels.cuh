@@ -55,6 +55,9 @@ struct Params {
   __nv_bfloat16* dk;
   __nv_bfloat16* dv;
   int64_t ld_dk, ld_dv;
+  // Bounded waits of the tcgen05 kernels (attention_tc.cu): error word and budget.
+  int* status;
+  uint64_t timeout_ns;
 };
 
 

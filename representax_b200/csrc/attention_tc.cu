@@ -1,0 +1,779 @@
+// Packed variable-length attention on the tcgen05 tensor cores (sm_100a).
+//
+// Same contract as the mma.sync kernels of attention.cu: packed [T, heads*D]
+// rows addressed through cu_seqlens (no FLOP spent on padding), key-validity /
+// causal / symmetric sliding-window masks, grouped-query heads, and the base-2
+// log-sum-exp of the scaled scores saved for the backward, and attention-
+// probability dropout with the same Philox counters (so either kernel family
+// can replay the other's masks). Covers head dimension 64 and 128 without
+// relative position bias (that variant stays on the mma.sync kernels).
+//
+// Forward: one CTA = 128 queries of one (sequence, head), 4 warps.
+//   Thread 0 issues TMA loads of Q (128 x D) and of 128-key blocks of K and V
+//   into 128-byte-swizzled shared memory and issues S = Q K^T (M=128, N=128)
+//   into TMEM. Each thread owns one query row (its TMEM lane): it reads its
+//   128 scores with tcgen05.ld, applies the masks and the online softmax in
+//   registers (no cross-thread reductions), and writes P as bf16 into
+//   swizzled shared memory; thread 0 then issues O += P V (M=128, N=D, V as an
+//   MN-major operand) into a second TMEM region. The running maximum only
+//   moves when a block raises it by more than 2^8, so the O rescale (a TMEM
+//   read-modify-write) is rare; O and the normaliser always share one maximum,
+//   so the result is exact.
+// Backward: one CTA = 128 keys of one (sequence, kv head), 4 warps; loops over
+//   the query heads of the group and 64-query blocks:
+//     S^T = K Q^T, dP^T = V dO^T                    (TMEM, M=128 keys, N=64)
+//     P^T = exp2(S^T * scale_log2 - lse), dS^T = P^T (dP^T - Dvec) * scale
+//                                                   (thread = key row, to smem)
+//     dV += P^T dO, dK += dS^T Q                     (TMEM accumulators)
+//     dQ  = dS K                                    (M=128: the upper 64 rows
+//                                                    read unrelated data and
+//                                                    are never used)
+//   and adds the 64 dQ rows into an fp32 accumulator with vector atomics.
+//
+// Every wait is bounded (%globaltimer); a wait that runs out records an error
+// code in the status word, the CTA drains its in-flight copies and MMAs,
+// frees its TMEM and returns.
+//
+// Reference parity: `dot_product_attention` with padding / window / causal
+// masks (src/representax/models/components.py:187-235), sliding windows
+// (src/representax/models/modernvbert/model.py:217-230) and GQA
+// (src/representax/models/qwen3_vl/text.py:188-199).
+#include "attention_kernels.cuh"
+#include "common.h"
+#include "sm100.cuh"
+
+namespace rx {
+namespace attn {
+namespace tc {
+
+constexpr int kThreads = 128;
+constexpr int FQ = 128;   // forward: queries per CTA (one per TMEM lane)
+constexpr int FK = 128;   // forward: keys per block
+constexpr int BKT = 128;  // backward: keys per CTA
+constexpr int BQB = 64;   // backward: queries per block
+constexpr uint32_t kSub128 = 128 * 128;  // [128 rows][64 bf16] swizzled sub-tile
+constexpr uint32_t kSub64 = 64 * 128;    // [64 rows][64 bf16]
+
+// Barrier slots (uint64) after the tiles.
+enum Bar : int { kBarQ = 0, kBarK, kBarV, kBarS, kBarO, kBarDrain, kNumBars };
+
+template <int D>
+struct FwdLayout {
+  static constexpr int DS = D / 64;
+  static constexpr uint32_t Q = 0;
+  static constexpr uint32_t K = Q + DS * kSub128;
+  static constexpr uint32_t V = K + DS * kSub128;
+  static constexpr uint32_t P = V + DS * kSub128;  // [128 q][128 keys] as two sub-tiles
+  static constexpr uint32_t BARS = P + 2 * kSub128;
+  static constexpr uint32_t BYTES = BARS + kNumBars * 8 + 16 + 1024;  // + TMEM slot + alignment slack
+  static constexpr uint32_t TMEM_COLS = 256;  // S: [0, 128), O: [128, 128 + D)
+};
+
+template <int D>
+struct BwdLayout {
+  static constexpr int DS = D / 64;
+  static constexpr uint32_t K = 0;
+  static constexpr uint32_t V = K + DS * kSub128;
+  static constexpr uint32_t Q = V + DS * kSub128;
+  static constexpr uint32_t DO = Q + DS * kSub64;
+  static constexpr uint32_t DST = DO + DS * kSub64;  // dS^T [128 keys][64 q]
+  static constexpr uint32_t PT = DST + kSub128;      // P^T  [128 keys][64 q]; must follow DST
+  static constexpr uint32_t LSE = PT + kSub128;      // 64 floats
+  static constexpr uint32_t DVEC = LSE + 256;        // 64 floats
+  static constexpr uint32_t BARS = DVEC + 256;
+  static constexpr uint32_t BYTES = BARS + kNumBars * 8 + 16 + 1024;
+  // S^T [0, 64), dP^T [64, 128), dV [128, 128 + D), dK [128 + D, 128 + 2D);
+  // dQ reuses [0, D) once S^T and dP^T have been read.
+  static constexpr uint32_t TMEM_COLS = D == 64 ? 256 : 512;
+};
+
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~static_cast<uintptr_t>(1023));
+}
+
+// Is key j visible from query i (both sequence-relative; j, i < len checked by the caller)?
+__device__ __forceinline__ bool mask_ok(const Params& p, int i, int j) {
+  if (p.causal && j > i) return false;
+  if (p.window >= 0 && (j - i > p.window || i - j > p.window)) return false;
+  return true;
+}
+
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// 2^x with the SFU instruction (relative error ~2^-22, far below bf16's
+// resolution); 2^-inf = 0.
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Row `row` of a K-major [rows][64] bf16 sub-tile with the 128-byte swizzle:
+// 16-byte chunk c of the row lives at chunk (c ^ (row & 7)).
+__device__ __forceinline__ void store_chunk_sw128(uint8_t* sub, int row, int chunk, uint4 w) {
+  *reinterpret_cast<uint4*>(sub + row * 128 + ((chunk ^ (row & 7)) << 4)) = w;
+}
+
+// Wait for an outstanding TMA phase (bounded), used when unwinding.
+__device__ __forceinline__ void drain_phase(uint64_t* bar, int issued, int waited, const Params& p) {
+  if (issued > waited && !mbar_wait(bar, static_cast<uint32_t>(waited & 1), p.timeout_ns))
+    report_status(p.status, kStatusTimeoutDrain);
+}
+
+// Attention-probability dropout shares the mma.sync kernels' counter layout:
+// element (query i, key j) of query head h in a sequence starting at token
+// `start` uses word (i & 1) * 2 + (j & 1) of Philox block
+// (start + (i & ~1), h << 16 | j >> 1). Two adjacent lanes own rows of the
+// same parity pair, so each generates every other block and the pair swaps
+// the halves the other needs.
+//
+// Forward (lane = query i; lanes i and i ^ 1 share blocks): keep bits of keys
+// [k0, k0 + 128) for this lane's query, bit c = key k0 + c.
+__device__ __forceinline__ void fwd_keep_bits(const DropoutSite& site, int start, int i, int h, int k0,
+                                              int lane, uint32_t (&keep)[4]) {
+  keep[0] = keep[1] = keep[2] = keep[3] = 0u;
+  const bool odd = (lane & 1) != 0;
+  const uint32_t a = static_cast<uint32_t>(start + (i & ~1));
+  const int b0 = k0 >> 1;
+#pragma unroll 1
+  for (int t = 0; t < 66; t += 2) {
+    const Philox4 r = dropout_block(site, a, (static_cast<uint32_t>(h) << 16) | static_cast<uint32_t>(b0 + t + (odd ? 1 : 0)));
+    // even lane keeps (x, y) of block t and sends (z, w); odd lane keeps
+    // (z, w) of block t + 1 and sends (x, y).
+    const uint32_t s0 = __shfl_xor_sync(0xffffffffu, odd ? r.x : r.z, 1);
+    const uint32_t s1 = __shfl_xor_sync(0xffffffffu, odd ? r.y : r.w, 1);
+    uint32_t w[4];  // words for keys 2 (b0 + t) + 0..3
+    w[0] = odd ? s0 : r.x;
+    w[1] = odd ? s1 : r.y;
+    w[2] = odd ? r.z : s0;
+    w[3] = odd ? r.w : s1;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int c = 2 * (b0 + t) + e - k0;
+      if (c >= 0 && c < 128 && w[e] >= site.threshold) keep[c >> 5] |= 1u << (c & 31);
+    }
+  }
+}
+
+// Backward (lane = key j; lanes j and j ^ 1 share blocks): keep bits of
+// queries [q0, q0 + 64) for this lane's key, bit c = query q0 + c.
+__device__ __forceinline__ void bwd_keep_bits(const DropoutSite& site, int start, int j, int h, int q0,
+                                              int lane, uint32_t (&keep)[2]) {
+  keep[0] = keep[1] = 0u;
+  const bool odd = (lane & 1) != 0;
+  const uint32_t bcol = (static_cast<uint32_t>(h) << 16) | static_cast<uint32_t>(j >> 1);
+  const int a0 = q0 >> 1;
+#pragma unroll 1
+  for (int t = 0; t < 34; t += 2) {
+    const Philox4 r = dropout_block(site, static_cast<uint32_t>(start + 2 * (a0 + t + (odd ? 1 : 0))), bcol);
+    // even key needs words x (even query), z (odd query); odd key y, w.
+    const uint32_t s0 = __shfl_xor_sync(0xffffffffu, odd ? r.x : r.y, 1);
+    const uint32_t s1 = __shfl_xor_sync(0xffffffffu, odd ? r.z : r.w, 1);
+    uint32_t w[4];  // words for queries 2 (a0 + t) + 0..3
+    w[0] = odd ? s0 : r.x;
+    w[1] = odd ? s1 : r.z;
+    w[2] = odd ? r.y : s0;
+    w[3] = odd ? r.w : s1;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int c = 2 * (a0 + t) + e - q0;
+      if (c >= 0 && c < 64 && w[e] >= site.threshold) keep[c >> 5] |= 1u << (c & 31);
+    }
+  }
+}
+
+// ===================================================================== forward
+template <int D>
+__global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
+    attn_tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                       const __grid_constant__ CUtensorMap tmV, const Params p) {
+  using L = FwdLayout<D>;
+  constexpr int DS = L::DS;
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int start = p.cu_seqlens[b];
+  const int len = p.cu_seqlens[b + 1] - start;
+  const int q_lo = blockIdx.x * FQ;
+  if (q_lo >= len) return;
+  const int q_hi = min(len, q_lo + FQ);
+  const int kvh = h / p.heads_per_kv;
+  int k_lo = 0, k_hi = len;
+  if (p.causal) k_hi = min(k_hi, q_hi);
+  if (p.window >= 0) {
+    k_lo = max(0, q_lo - p.window);
+    k_hi = min(k_hi, q_hi + p.window);
+  }
+  const int nblk = (k_hi - k_lo + FK - 1) / FK;  // >= 1: query q_lo always sees itself
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = align1024(smem_raw);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + L::BARS);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t sQ = smem_u32(base + L::Q), sK = smem_u32(base + L::K), sV = smem_u32(base + L::V),
+                 sP = smem_u32(base + L::P);
+
+  // Thread 0's TMA bookkeeping (issued / waited phases per barrier).
+  int k_issued = 0, k_waited = 0, v_issued = 0, v_waited = 0, q_waited = 0;
+  if (tid == 0) {
+    for (int i = 0; i < kNumBars; ++i) mbar_init(&bars[i], 1);
+    fence_mbarrier_init();
+    mbar_arrive_expect_tx(&bars[kBarQ], DS * kSub128);
+    for (int s = 0; s < DS; ++s) tma_load_2d(base + L::Q + s * kSub128, &tmQ, &bars[kBarQ], h * D + 64 * s, start + q_lo);
+    mbar_arrive_expect_tx(&bars[kBarK], DS * kSub128);
+    for (int s = 0; s < DS; ++s) tma_load_2d(base + L::K + s * kSub128, &tmK, &bars[kBarK], kvh * D + 64 * s, start + k_lo);
+    mbar_arrive_expect_tx(&bars[kBarV], DS * kSub128);
+    for (int s = 0; s < DS; ++s) tma_load_2d(base + L::V + s * kSub128, &tmV, &bars[kBarV], kvh * D + 64 * s, start + k_lo);
+    k_issued = v_issued = 1;
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, L::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem, tO = tmem + 128;
+  const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+  const int row = warp * 32 + lane;
+  const int i = q_lo + row;  // this thread's query (sequence-relative)
+  const bool warp_live = q_lo + warp * 32 < len;
+  constexpr uint32_t IDESC_O = idesc_bf16_f32(128, D, false, true);
+
+  float m_run = -INFINITY, l_run = 0.f;
+  bool ok = true, mma_issued = false;
+  for (int j = 0; j < nblk; ++j) {
+    const int k0 = k_lo + j * FK;
+    const uint32_t ph = static_cast<uint32_t>(j & 1);
+    // Keys of this block that can be visible, rounded up to the MMA's N / K step.
+    const int n16 = (min(FK, k_hi - k0) + 15) & ~15;
+    bool issue_ok = true;
+    if (tid == 0) {
+      if (j == 0) {
+        issue_ok = mbar_wait(&bars[kBarQ], 0, p.timeout_ns);
+        q_waited = issue_ok ? 1 : 0;
+      }
+      if (issue_ok) {
+        issue_ok = mbar_wait(&bars[kBarK], static_cast<uint32_t>(k_waited & 1), p.timeout_ns);
+        if (issue_ok) ++k_waited;
+      }
+      if (issue_ok) {
+        tc_fence_after();
+        const uint32_t idesc_s = idesc_bf16_f32(128, n16, false, false);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * kSub128 + (kk & 3) * 32;
+          umma_f16_ss(tS, smem_desc_sw128(sQ + off, 16, 1024), smem_desc_sw128(sK + off, 16, 1024), idesc_s,
+                      kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&bars[kBarS]);
+        mma_issued = true;
+      } else {
+        report_status(p.status, kStatusTimeoutMma);
+      }
+    }
+    bool got = issue_ok && mbar_wait(&bars[kBarS], ph, p.timeout_ns);
+    if (__syncthreads_or(!got)) {
+      if (tid == 0) report_status(p.status, kStatusTimeoutEpilogue);
+      ok = false;
+      break;
+    }
+    tc_fence_after();
+    // The S MMA has retired, so the K buffer is free for the next block.
+    if (tid == 0 && j + 1 < nblk) {
+      mbar_arrive_expect_tx(&bars[kBarK], DS * kSub128);
+      for (int s = 0; s < DS; ++s)
+        tma_load_2d(base + L::K + s * kSub128, &tmK, &bars[kBarK], kvh * D + 64 * s, start + k0 + FK);
+      ++k_issued;
+    }
+
+    __syncwarp();  // warp 0 may have diverged around thread 0's TMA issue
+    if (warp_live) {
+      uint32_t r[4][32];
+      const int nch = (n16 + 31) >> 5;  // 32-column TMEM chunks holding scores
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        if (c < nch) tmem_ld_32x32b_x32(tS + lane_off + c * 32, r[c]);
+      tmem_ld_wait();
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        if (c >= nch) break;
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int key = k0 + c * 32 + e;
+          float x = __uint_as_float(r[c][e]) * p.scale_log2;
+          if (key >= k_hi || !mask_ok(p, i, key)) x = -INFINITY;
+          r[c][e] = __float_as_uint(x);
+          mx = fmaxf(mx, x);
+        }
+      }
+      float alpha = 1.f;
+      bool rescale = false;
+      if (mx > -INFINITY) {
+        if (m_run == -INFINITY) {
+          m_run = mx;  // the row of O is still zero: earlier blocks contributed nothing
+        } else if (mx > m_run + 8.f) {
+          alpha = ex2(m_run - mx);
+          m_run = mx;
+          l_run *= alpha;
+          rescale = true;
+        }
+      }
+      if (__any_sync(0xffffffffu, rescale)) {
+        // The previous P V has retired (waited below), so O is stable in TMEM.
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld_32x32b_x32(tO + lane_off + c * 32, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+          tmem_st_32x32b_x32(tO + lane_off + c * 32, o);
+        }
+        tmem_st_wait();
+      }
+      const float m_use = m_run == -INFINITY ? 0.f : m_run;
+      const bool drop = p.pdrop.threshold != 0u;
+      uint32_t keep[4] = {0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu};
+      if (drop) fwd_keep_bits(p.pdrop, start, i, h, k0, lane, keep);
+      const float dscale = drop ? p.pdrop.scale : 1.f;
+      float rs = 0.f;
+      uint8_t* prow = base + L::P;
+#pragma unroll
+      for (int ch = 0; ch < FK / 8; ++ch) {
+        if (ch * 8 >= n16) break;
+        float e8[8];
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          const int c = ch * 8 + t;
+          const float e = ex2(__uint_as_float(r[c >> 5][c & 31]) - m_use);
+          rs += e;  // the normaliser uses the probabilities before dropout
+          e8[t] = ((keep[c >> 5] >> (c & 31)) & 1u) ? e * dscale : 0.f;
+        }
+        const uint4 w = make_uint4(pack2(e8[0], e8[1]), pack2(e8[2], e8[3]), pack2(e8[4], e8[5]),
+                                   pack2(e8[6], e8[7]));
+        store_chunk_sw128(prow + (ch >> 3) * kSub128, row, ch & 7, w);
+      }
+      l_run += rs;
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+
+    if (tid == 0) {
+      tc_fence_after();
+      issue_ok = mbar_wait(&bars[kBarV], static_cast<uint32_t>(v_waited & 1), p.timeout_ns);
+      if (issue_ok) {
+        ++v_waited;
+        for (int kk = 0; kk < n16 / 16; ++kk) {
+          const uint32_t a_off = (kk >> 2) * kSub128 + (kk & 3) * 32;
+          umma_f16_ss(tO, smem_desc_sw128(sP + a_off, 16, 1024), smem_desc_sw128(sV + kk * 2048, kSub128, 1024),
+                      IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&bars[kBarO]);
+      } else {
+        report_status(p.status, kStatusTimeoutMma);
+      }
+    }
+    got = issue_ok && mbar_wait(&bars[kBarO], ph, p.timeout_ns);
+    if (__syncthreads_or(!got)) {
+      if (tid == 0) report_status(p.status, kStatusTimeoutEpilogue);
+      ok = false;
+      break;
+    }
+    tc_fence_after();
+    // P V has retired: V (and P) are free.
+    if (tid == 0 && j + 1 < nblk) {
+      mbar_arrive_expect_tx(&bars[kBarV], DS * kSub128);
+      for (int s = 0; s < DS; ++s)
+        tma_load_2d(base + L::V + s * kSub128, &tmV, &bars[kBarV], kvh * D + 64 * s, start + k0 + FK);
+      ++v_issued;
+    }
+  }
+
+  __syncwarp();
+  if (ok && warp_live) {
+    const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+    __nv_bfloat16* orow = p.o + static_cast<int64_t>(start + i) * p.ldo + h * D;
+#pragma unroll 1
+    for (int c = 0; c < D / 32; ++c) {
+      uint32_t o[32];
+      tmem_ld_32x32b_x32(tO + lane_off + c * 32, o);
+      tmem_ld_wait();
+      if (i < len) {
+        uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float* f = reinterpret_cast<const float*>(o + q * 8);
+          dst[q] = make_uint4(pack2(f[0] * inv, f[1] * inv), pack2(f[2] * inv, f[3] * inv),
+                              pack2(f[4] * inv, f[5] * inv), pack2(f[6] * inv, f[7] * inv));
+        }
+      }
+    }
+    if (i < len)
+      p.lse[static_cast<int64_t>(h) * p.total_tokens + start + i] = l_run > 0.f ? m_run + log2f(l_run) : INFINITY;
+  }
+
+  if (!ok && tid == 0) {
+    // Unwind: no TMA write may still be landing and no MMA may still be
+    // writing TMEM when the CTA releases them.
+    if (q_waited == 0) drain_phase(&bars[kBarQ], 1, 0, p);
+    drain_phase(&bars[kBarK], k_issued, k_waited, p);
+    drain_phase(&bars[kBarV], v_issued, v_waited, p);
+    if (mma_issued) {
+      umma_commit(&bars[kBarDrain]);
+      if (!mbar_wait(&bars[kBarDrain], 0, p.timeout_ns)) report_status(p.status, kStatusTimeoutDrain);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tmem, L::TMEM_COLS);
+}
+
+// ==================================================================== backward
+template <int D>
+__global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
+    attn_tc_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                       const Params p) {
+  using L = BwdLayout<D>;
+  constexpr int DS = L::DS;
+  const int kvh = blockIdx.y, b = blockIdx.z;
+  const int start = p.cu_seqlens[b];
+  const int len = p.cu_seqlens[b + 1] - start;
+  const int kt0 = blockIdx.x * BKT;
+  if (kt0 >= len) return;
+  const int kt_hi = min(len, kt0 + BKT);
+  const int nk16 = (kt_hi - kt0 + 15) & ~15;  // key rows in use (the dQ MMA's K)
+  // Queries that can see a key of this tile.
+  int q_first = 0, q_end = len;
+  if (p.causal) q_first = kt0;
+  if (p.window >= 0) {
+    q_first = max(q_first, kt0 - p.window);
+    q_end = min(q_end, kt_hi + p.window);
+  }
+  const int nqb = q_end > q_first ? (q_end - q_first + BQB - 1) / BQB : 0;
+  const int total_it = nqb * p.heads_per_kv;
+  const int width_q = p.heads * D;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = align1024(smem_raw);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + L::BARS);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
+  float* s_lse = reinterpret_cast<float*>(base + L::LSE);
+  float* s_dvec = reinterpret_cast<float*>(base + L::DVEC);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t sK = smem_u32(base + L::K), sV = smem_u32(base + L::V), sQ = smem_u32(base + L::Q),
+                 sDO = smem_u32(base + L::DO), sDST = smem_u32(base + L::DST), sPT = smem_u32(base + L::PT);
+
+  int kv_waited = 0, qd_issued = 0, qd_waited = 0;
+  auto issue_qd = [&](int it) {
+    const int hq = kvh * p.heads_per_kv + it / nqb;
+    const int q0 = q_first + (it % nqb) * BQB;
+    mbar_arrive_expect_tx(&bars[kBarQ], 2 * DS * kSub64);
+    for (int s = 0; s < DS; ++s) {
+      tma_load_2d(base + L::Q + s * kSub64, &tmQ, &bars[kBarQ], hq * D + 64 * s, start + q0);
+      tma_load_2d(base + L::DO + s * kSub64, &tmDO, &bars[kBarQ], hq * D + 64 * s, start + q0);
+    }
+  };
+  if (tid == 0) {
+    for (int i = 0; i < kNumBars; ++i) mbar_init(&bars[i], 1);
+    fence_mbarrier_init();
+    if (total_it > 0) {
+      mbar_arrive_expect_tx(&bars[kBarK], 2 * DS * kSub128);
+      for (int s = 0; s < DS; ++s) {
+        tma_load_2d(base + L::K + s * kSub128, &tmK, &bars[kBarK], kvh * D + 64 * s, start + kt0);
+        tma_load_2d(base + L::V + s * kSub128, &tmV, &bars[kBarK], kvh * D + 64 * s, start + kt0);
+      }
+      issue_qd(0);
+      qd_issued = 1;
+    }
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, L::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem, tDP = tmem + 64, tDV = tmem + 128, tDK = tmem + 128 + D, tDQ = tmem;
+  const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+  const int krow = warp * 32 + lane;
+  const int key = kt0 + krow;  // this thread's key (sequence-relative)
+  const bool warp_live = kt0 + warp * 32 < len;
+  constexpr uint32_t IDESC_KV = idesc_bf16_f32(128, D, false, true);
+  constexpr uint32_t IDESC_Q = idesc_bf16_f32(128, D, true, true);
+
+  bool ok = true, mma_issued = false;
+  for (int it = 0; it < total_it; ++it) {
+    const int hq = kvh * p.heads_per_kv + it / nqb;
+    const int q0 = q_first + (it % nqb) * BQB;
+    const uint32_t ph = static_cast<uint32_t>(it & 1);
+    const int nq16 = (min(BQB, q_end - q0) + 15) & ~15;  // query columns in use
+    if (tid < BQB) {
+      const int q = q0 + tid;
+      const int64_t at = static_cast<int64_t>(hq) * p.total_tokens + start + q;
+      s_lse[tid] = q < len ? p.lse[at] : INFINITY;
+      s_dvec[tid] = q < len ? p.dvec[at] : 0.f;
+    }
+    __syncthreads();
+    bool issue_ok = true;
+    if (tid == 0) {
+      if (it == 0) {
+        issue_ok = mbar_wait(&bars[kBarK], 0, p.timeout_ns);
+        kv_waited = issue_ok ? 1 : 0;
+      }
+      if (issue_ok) {
+        issue_ok = mbar_wait(&bars[kBarQ], static_cast<uint32_t>(qd_waited & 1), p.timeout_ns);
+        if (issue_ok) ++qd_waited;
+      }
+      if (issue_ok) {
+        tc_fence_after();
+        const uint32_t idesc_s = idesc_bf16_f32(128, nq16, false, false);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off128 = (kk >> 2) * kSub128 + (kk & 3) * 32;
+          const uint32_t off64 = (kk >> 2) * kSub64 + (kk & 3) * 32;
+          umma_f16_ss(tS, smem_desc_sw128(sK + off128, 16, 1024), smem_desc_sw128(sQ + off64, 16, 1024), idesc_s,
+                      kk > 0 ? 1u : 0u);
+          umma_f16_ss(tDP, smem_desc_sw128(sV + off128, 16, 1024), smem_desc_sw128(sDO + off64, 16, 1024), idesc_s,
+                      kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&bars[kBarS]);
+        mma_issued = true;
+      } else {
+        report_status(p.status, kStatusTimeoutMma);
+      }
+    }
+    bool got = issue_ok && mbar_wait(&bars[kBarS], ph, p.timeout_ns);
+    if (__syncthreads_or(!got)) {
+      if (tid == 0) report_status(p.status, kStatusTimeoutEpilogue);
+      ok = false;
+      break;
+    }
+    tc_fence_after();
+
+    uint8_t* pt = base + L::PT;
+    uint8_t* dst = base + L::DST;
+    __syncwarp();
+    if (warp_live) {
+      uint32_t rs[2][32], rd[2][32];
+      tmem_ld_32x32b_x32(tS + lane_off, rs[0]);
+      tmem_ld_32x32b_x32(tDP + lane_off, rd[0]);
+      if (nq16 > 32) {
+        tmem_ld_32x32b_x32(tS + lane_off + 32, rs[1]);
+        tmem_ld_32x32b_x32(tDP + lane_off + 32, rd[1]);
+      }
+      tmem_ld_wait();
+      const bool key_ok = key < len;
+      const bool drop = p.pdrop.threshold != 0u;
+      uint32_t keep[2] = {0xffffffffu, 0xffffffffu};
+      if (drop) bwd_keep_bits(p.pdrop, start, key, hq, q0, lane, keep);
+      const float dscale = drop ? p.pdrop.scale : 1.f;
+#pragma unroll
+      for (int ch = 0; ch < BQB / 8; ++ch) {
+        if (ch * 8 >= nq16) break;
+        float pv[8], dv[8];
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          const int c = ch * 8 + t;
+          const int q = q0 + c;
+          const bool vis = key_ok && q < len && mask_ok(p, q, key);
+          const float s = __uint_as_float(rs[c >> 5][c & 31]);
+          const float pr = vis ? ex2(s * p.scale_log2 - s_lse[c]) : 0.f;
+          // With dropout: dV uses the dropped probabilities, and
+          // dS = P * (mask * dP / (1 - p) - Dvec).
+          const bool kept = ((keep[c >> 5] >> (c & 31)) & 1u) != 0u;
+          const float dp = kept ? __uint_as_float(rd[c >> 5][c & 31]) * dscale : 0.f;
+          pv[t] = kept ? pr * dscale : 0.f;
+          dv[t] = pr * (dp - s_dvec[c]) * p.scale;
+        }
+        store_chunk_sw128(pt, krow, ch,
+                          make_uint4(pack2(pv[0], pv[1]), pack2(pv[2], pv[3]), pack2(pv[4], pv[5]), pack2(pv[6], pv[7])));
+        store_chunk_sw128(dst, krow, ch,
+                          make_uint4(pack2(dv[0], dv[1]), pack2(dv[2], dv[3]), pack2(dv[4], dv[5]), pack2(dv[6], dv[7])));
+      }
+    } else {
+      // Keys past the sequence: zero rows (dS^T rows enter dQ = dS K).
+#pragma unroll
+      for (int ch = 0; ch < BQB / 8; ++ch) {
+        store_chunk_sw128(pt, krow, ch, make_uint4(0u, 0u, 0u, 0u));
+        store_chunk_sw128(dst, krow, ch, make_uint4(0u, 0u, 0u, 0u));
+      }
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+
+    if (tid == 0) {
+      tc_fence_after();
+      for (int kk = 0; kk < nq16 / 16; ++kk) {
+        const uint32_t acc = (it > 0 || kk > 0) ? 1u : 0u;
+        umma_f16_ss(tDV, smem_desc_sw128(sPT + kk * 32, 16, 1024), smem_desc_sw128(sDO + kk * 2048, kSub64, 1024),
+                    IDESC_KV, acc);
+        umma_f16_ss(tDK, smem_desc_sw128(sDST + kk * 32, 16, 1024), smem_desc_sw128(sQ + kk * 2048, kSub64, 1024),
+                    IDESC_KV, acc);
+      }
+      // dQ = dS K: A = dS (M = queries, MN-major view of dS^T; its second
+      // 64-row chunk is the P^T buffer, whose output rows are ignored).
+      for (int kk = 0; kk < nk16 / 16; ++kk) {
+        umma_f16_ss(tDQ, smem_desc_sw128(sDST + kk * 2048, L::PT - L::DST, 1024),
+                    smem_desc_sw128(sK + kk * 2048, kSub128, 1024), IDESC_Q, kk > 0 ? 1u : 0u);
+      }
+      umma_commit(&bars[kBarO]);
+    }
+    got = mbar_wait(&bars[kBarO], ph, p.timeout_ns);
+    if (__syncthreads_or(!got)) {
+      if (tid == 0) report_status(p.status, kStatusTimeoutEpilogue);
+      ok = false;
+      break;
+    }
+    tc_fence_after();
+    // Q and dO are free: fetch the next block while this one's dQ drains.
+    if (tid == 0 && it + 1 < total_it) {
+      issue_qd(it + 1);
+      ++qd_issued;
+    }
+    __syncwarp();
+    if (warp < BQB / 32) {
+      const int q = q0 + warp * 32 + lane;
+      float* dq = p.dq_acc + static_cast<int64_t>(start + q) * width_q + hq * D;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld_32x32b_x32(tDQ + lane_off + c * 32, o);
+        tmem_ld_wait();
+        // Only queries that can see this key tile have dS rows written this
+        // iteration (q_end <= len).
+        if (q < q_end) {
+          float4* d4 = reinterpret_cast<float4*>(dq + c * 32);
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            atomicAdd(d4 + e, make_float4(__uint_as_float(o[4 * e]), __uint_as_float(o[4 * e + 1]),
+                                          __uint_as_float(o[4 * e + 2]), __uint_as_float(o[4 * e + 3])));
+        }
+      }
+    }
+    tc_fence_before();
+  }
+
+  __syncwarp();
+  if (ok && warp_live) {
+    const bool have = total_it > 0;
+    __nv_bfloat16* dk_row = p.dk + static_cast<int64_t>(start + key) * p.ld_dk + kvh * D;
+    __nv_bfloat16* dv_row = p.dv + static_cast<int64_t>(start + key) * p.ld_dv + kvh * D;
+#pragma unroll 1
+    for (int which = 0; which < 2; ++which) {
+      const uint32_t t_acc = which == 0 ? tDK : tDV;
+      __nv_bfloat16* out = which == 0 ? dk_row : dv_row;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        if (have) {
+          tmem_ld_32x32b_x32(t_acc + lane_off + c * 32, o);
+          tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = 0u;
+        }
+        if (key < len) {
+          uint4* d = reinterpret_cast<uint4*>(out + c * 32);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float* f = reinterpret_cast<const float*>(o + q * 8);
+            d[q] = make_uint4(pack2(f[0], f[1]), pack2(f[2], f[3]), pack2(f[4], f[5]), pack2(f[6], f[7]));
+          }
+        }
+      }
+    }
+  }
+
+  if (!ok && tid == 0) {
+    if (total_it > 0 && kv_waited == 0) drain_phase(&bars[kBarK], 1, 0, p);
+    drain_phase(&bars[kBarQ], qd_issued, qd_waited, p);
+    if (mma_issued) {
+      umma_commit(&bars[kBarDrain]);
+      if (!mbar_wait(&bars[kBarDrain], 0, p.timeout_ns)) report_status(p.status, kStatusTimeoutDrain);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tmem, L::TMEM_COLS);
+}
+
+template <typename Kernel>
+void configure(Kernel kernel, uint32_t bytes, int device, bool (&done)[64]) {
+  if (device < 0 || device >= 64 || !done[device]) {
+    RX_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes)));
+    if (device >= 0 && device < 64) done[device] = true;
+  }
+}
+
+}  // namespace tc
+
+// ------------------------------------------------------------------- host side
+namespace {
+bool g_tc_enabled = true;
+int* g_status[64] = {nullptr};
+}  // namespace
+
+bool tc_attention_enabled() { return g_tc_enabled; }
+void set_tc_attention_enabled(bool on) { g_tc_enabled = on; }
+void register_tc_status(int device, int* status) {
+  if (device >= 0 && device < 64) g_status[device] = status;
+}
+
+// Launch the tcgen05 forward for a filled parameter block (no dropout, no bias).
+void tc_forward(Params p, int d, int64_t max_len, cudaStream_t st, int device) {
+  p.status = (device >= 0 && device < 64) ? g_status[device] : nullptr;
+  p.timeout_ns = kWaitBudgetNs;
+  const int64_t T = p.total_tokens;
+  const int kv_heads = p.heads / p.heads_per_kv;
+  const CUtensorMap tq = make_tmap_2d_bf16(p.q, T, static_cast<int64_t>(p.heads) * d, p.ldq, 64, tc::FQ);
+  const CUtensorMap tk = make_tmap_2d_bf16(p.k, T, static_cast<int64_t>(kv_heads) * d, p.ldk, 64, tc::FK);
+  const CUtensorMap tv = make_tmap_2d_bf16(p.v, T, static_cast<int64_t>(kv_heads) * d, p.ldv, 64, tc::FK);
+  dim3 grid(static_cast<unsigned>((max_len + tc::FQ - 1) / tc::FQ), p.heads, p.batch);
+  if (d == 64) {
+    static bool done[64] = {false};
+    tc::configure(tc::attn_tc_fwd_kernel<64>, tc::FwdLayout<64>::BYTES, device, done);
+    tc::attn_tc_fwd_kernel<64><<<grid, tc::kThreads, tc::FwdLayout<64>::BYTES, st>>>(tq, tk, tv, p);
+  } else {
+    static bool done[64] = {false};
+    tc::configure(tc::attn_tc_fwd_kernel<128>, tc::FwdLayout<128>::BYTES, device, done);
+    tc::attn_tc_fwd_kernel<128><<<grid, tc::kThreads, tc::FwdLayout<128>::BYTES, st>>>(tq, tk, tv, p);
+  }
+  RX_CUDA_CHECK(cudaGetLastError());
+}
+
+// Launch the tcgen05 backward (dq_acc zeroed and dvec computed by the caller).
+void tc_backward(Params p, int d, int64_t max_len, cudaStream_t st, int device) {
+  p.status = (device >= 0 && device < 64) ? g_status[device] : nullptr;
+  p.timeout_ns = kWaitBudgetNs;
+  const int64_t T = p.total_tokens;
+  const int kv_heads = p.heads / p.heads_per_kv;
+  const CUtensorMap tq = make_tmap_2d_bf16(p.q, T, static_cast<int64_t>(p.heads) * d, p.ldq, 64, tc::BQB);
+  const CUtensorMap tdo = make_tmap_2d_bf16(p.dO, T, static_cast<int64_t>(p.heads) * d, p.ld_do, 64, tc::BQB);
+  const CUtensorMap tk = make_tmap_2d_bf16(p.k, T, static_cast<int64_t>(kv_heads) * d, p.ldk, 64, tc::BKT);
+  const CUtensorMap tv = make_tmap_2d_bf16(p.v, T, static_cast<int64_t>(kv_heads) * d, p.ldv, 64, tc::BKT);
+  dim3 grid(static_cast<unsigned>((max_len + tc::BKT - 1) / tc::BKT), kv_heads, p.batch);
+  if (d == 64) {
+    static bool done[64] = {false};
+    tc::configure(tc::attn_tc_bwd_kernel<64>, tc::BwdLayout<64>::BYTES, device, done);
+    tc::attn_tc_bwd_kernel<64><<<grid, tc::kThreads, tc::BwdLayout<64>::BYTES, st>>>(tq, tk, tv, tdo, p);
+  } else {
+    static bool done[64] = {false};
+    tc::configure(tc::attn_tc_bwd_kernel<128>, tc::BwdLayout<128>::BYTES, device, done);
+    tc::attn_tc_bwd_kernel<128><<<grid, tc::kThreads, tc::BwdLayout<128>::BYTES, st>>>(tq, tk, tv, tdo, p);
+  }
+  RX_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace attn
+}  // namespace rx

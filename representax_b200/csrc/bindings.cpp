@@ -93,6 +93,14 @@ void sharded_adamw(const at::Tensor& shard_grad, int64_t off, int64_t n, const a
                    double wd);
 }  // namespace rx
 
+namespace rx {
+namespace attn {
+bool tc_attention_enabled();
+void set_tc_attention_enabled(bool on);
+void register_tc_status(int device, int* status);
+}  // namespace attn
+}  // namespace rx
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "representax_b200 sm_100a kernels";
   m.def("gemm", &rx::gemm_tcgen05, "tcgen05 GEMM with fused epilogue");
@@ -102,6 +110,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embed_ln_backward", &rx::embed_ln_backward);
   m.def("attention_forward", &rx::attention_forward);
   m.def("attention_backward", &rx::attention_backward);
+  m.def("set_attention_tcgen05", &rx::attn::set_tc_attention_enabled,
+        "route eligible attention calls (no dropout, no relative bias) to the tcgen05 kernels");
+  m.def("attention_tcgen05_enabled", &rx::attn::tc_attention_enabled);
+  m.def("register_status_word", [](const at::Tensor& status) {
+    TORCH_CHECK(status.is_cuda() && status.scalar_type() == at::kInt, "status must be CUDA int32");
+    rx::attn::register_tc_status(status.get_device(), status.data_ptr<int>());
+  }, "status word that kernels without a status argument report bounded-wait failures to");
   m.def("pool_forward", &rx::pool_forward);
   m.def("pool_backward", &rx::pool_backward);
   m.def("colsum_accumulate", &rx::colsum_accumulate);

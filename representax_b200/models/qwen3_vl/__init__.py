@@ -188,6 +188,7 @@ class Qwen3VLBatch:
     position_ids: torch.Tensor | None = None       # [3, B, S]
     packed: PackedTokens | None = None
     packed_positions: torch.Tensor | None = None   # [3, T] int32
+    images_per_row: torch.Tensor | None = None     # [B] int64 on the host (set by prepare)
 
     def __post_init__(self) -> None:
         if self.input_ids.shape != self.attention_mask.shape:
@@ -212,14 +213,52 @@ class Qwen3VLBatch:
         packed = pack_tokens(self.input_ids, self.attention_mask)
         rows, cols = np.nonzero(mask)
         ppos = torch.from_numpy(np.ascontiguousarray(pos[:, rows, cols]).astype(np.int32))
+        per_row = None
+        if self.image_grid_thw is not None:
+            # Images are consumed in order by the rows' image-token runs.
+            merge = config.vision.spatial_merge_size ** 2
+            tokens = [int(t * h * w) // merge for t, h, w in self.image_grid_thw.tolist()]
+            counts = ((ids == config.image_token_id) & mask).sum(1)
+            per_row = np.zeros(len(counts), dtype=np.int64)
+            image = 0
+            for r, need in enumerate(counts.tolist()):
+                while need > 0 and image < len(tokens):
+                    need -= tokens[image]
+                    image += 1
+                    per_row[r] += 1
+            per_row = torch.from_numpy(per_row)
         return Qwen3VLBatch(self.input_ids, self.attention_mask, self.pixel_values, self.image_grid_thw,
-                            torch.from_numpy(pos), packed, ppos)
+                            torch.from_numpy(pos), packed, ppos, per_row)
+
+    def rows(self, start: int, stop: int) -> "Qwen3VLBatch":
+        """Rows [start, stop) with their images' patches (for chunked encoders such as GradCache)."""
+
+        if self.packed is None or self.packed_positions is None:
+            raise ValueError("call prepare() before slicing a Qwen3-VL batch")
+        t0, t1 = int(self.packed.cu_host[start]), int(self.packed.cu_host[stop])
+        pixels, grid, per_row = None, None, None
+        if self.image_grid_thw is not None:
+            if self.images_per_row is None:
+                raise ValueError("prepare() did not record the images of each row")
+            first = int(self.images_per_row[:start].sum())
+            last = first + int(self.images_per_row[start:stop].sum())
+            patches = (self.image_grid_thw[:, 0] * self.image_grid_thw[:, 1] * self.image_grid_thw[:, 2]).tolist()
+            p0, p1 = int(sum(patches[:first])), int(sum(patches[:last]))
+            pixels = self.pixel_values[p0:p1]
+            grid = self.image_grid_thw[first:last]
+            per_row = self.images_per_row[start:stop]
+            if last == first:
+                pixels, grid = None, None
+        pos = None if self.position_ids is None else self.position_ids[:, start:stop]
+        return Qwen3VLBatch(self.input_ids[start:stop], self.attention_mask[start:stop], pixels, grid, pos,
+                            self.packed.rows(start, stop), self.packed_positions[:, t0:t1], per_row)
 
     def map_tensors(self, fn) -> "Qwen3VLBatch":
         opt = lambda t: None if t is None else fn(t)  # noqa: E731
         return Qwen3VLBatch(fn(self.input_ids), fn(self.attention_mask), opt(self.pixel_values),
                             self.image_grid_thw, opt(self.position_ids),
-                            None if self.packed is None else self.packed.map_tensors(fn), opt(self.packed_positions))
+                            None if self.packed is None else self.packed.map_tensors(fn), opt(self.packed_positions),
+                            self.images_per_row)
 
 
 # ------------------------------------------------------------------ vision

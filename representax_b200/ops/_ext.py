@@ -6,6 +6,7 @@ machine with a GPU the ops raise instead of silently falling back to PyTorch.
 
 from __future__ import annotations
 
+import os
 import threading
 
 import torch
@@ -68,6 +69,8 @@ def ext():
                         "representax_b200 CUDA extension is not built; run "
                         "`python setup.py build_ext --inplace` (sm_100a)"
                     ) from error
+                if os.environ.get("RX_ATTENTION_TC", "1") == "0":
+                    _C.set_attention_tcgen05(False)
                 _module = _CountingModule(_C)
     return _module
 
@@ -96,6 +99,7 @@ def status(device: torch.device | int) -> torch.Tensor:
     if tensor is None:
         tensor = torch.zeros(4, dtype=torch.int32, device=torch.device("cuda", index))
         _status[index] = tensor
+        ext().register_status_word(tensor)
     return tensor
 
 

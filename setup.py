@@ -19,6 +19,7 @@ SOURCES = [
     "norm.cu",
     "attention.cu",
     "attention_noalloc.cu",
+    "attention_tc.cu",
     "pool.cu",
     "mnr.cu",
     "optim.cu",

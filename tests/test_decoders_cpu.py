@@ -149,3 +149,32 @@ def test_quantized_lora_on_qwen3_vl_trains_only_adapters():
     e1 = model.encode(batch)
     merged = merge_quantized_lora(model)
     torch.testing.assert_close(merged.encode(batch), e1, rtol=1e-4, atol=1e-5)
+
+
+def test_qwen3_vl_batch_rows_slice_images(tmp_path):
+    """Row slices carry their own images' patches, so chunked encoding equals whole-batch encoding."""
+    from representax_b200.models.qwen3_vl import Qwen3VLBatch, Qwen3VLCheckpointAdapter
+
+    _tiny_qwen3_vl(tmp_path)
+    model = Qwen3VLCheckpointAdapter.load(tmp_path)
+    g = torch.Generator().manual_seed(5)
+    ids = torch.randint(1, 240, (3, 20), generator=g)
+    mask = torch.ones_like(ids)
+    ids[0, 3:7] = 250             # one 4x4 image
+    ids[1, 1:5] = 250             # two images: 4x4 and 4x8
+    ids[1, 8:16] = 250
+    ids[2, 2:10] = 250            # one 4x8 image
+    mask[2, 17:] = 0
+    grid = torch.tensor([[1, 4, 4], [1, 4, 4], [1, 4, 8], [1, 4, 8]])
+    patches = int((grid[:, 0] * grid[:, 1] * grid[:, 2]).sum())
+    pixels = torch.randn(patches, 3 * 2 * 4 * 4, generator=g)
+    full = Qwen3VLBatch(ids, mask, pixels, grid).prepare(model.config)
+    assert full.images_per_row.tolist() == [1, 2, 1]
+    part = full.rows(1, 3)
+    assert part.image_grid_thw.tolist() == [[1, 4, 4], [1, 4, 8], [1, 4, 8]]
+    assert part.pixel_values.shape[0] == 16 + 32 + 32
+    torch.testing.assert_close(part.pixel_values, pixels[16:])
+    with torch.no_grad():
+        whole = model.encode(full)
+        chunks = torch.cat([model.encode(full.rows(0, 1)), model.encode(full.rows(1, 3))])
+    torch.testing.assert_close(chunks, whole, rtol=1e-5, atol=1e-5)

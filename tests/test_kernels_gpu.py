@@ -203,10 +203,9 @@ def test_embedding_ln(C):
     _close(dg, gf.grad, rtol=1e-3, atol=5e-2, what="dgamma")
 
 
-def _attn_ref(q, k, v, lens, heads, kv_heads, scale, causal, window):
+def _attn_ref(q, k, v, lens, heads, kv_heads, scale, causal, window, d=64):
     outs = []
     start = 0
-    d = 64
     for n in lens:
         qs = q[start:start + n].float().view(n, heads, d).transpose(0, 1)
         ks = k[start:start + n].float().view(n, kv_heads, d).transpose(0, 1)
@@ -229,29 +228,43 @@ def _attn_ref(q, k, v, lens, heads, kv_heads, scale, causal, window):
     return torch.cat(outs)
 
 
+@pytest.fixture(params=["tcgen05", "mma_sync"])
+def attn_impl(request, C):
+    C.set_attention_tcgen05(request.param == "tcgen05")
+    yield request.param
+    C.set_attention_tcgen05(True)
+
+
 @pytest.mark.parametrize(
-    "lens,heads,kv_heads,causal,window",
-    [([1, 17, 64, 65, 200, 256], 12, 12, False, -1), ([300, 129], 4, 4, False, 64), ([100, 257], 4, 2, True, -1)],
+    "lens,heads,kv_heads,causal,window,d,q_gain",
+    [
+        ([1, 17, 64, 65, 200, 256], 12, 12, False, -1, 64, 1.0),
+        ([300, 129], 4, 4, False, 64, 64, 1.0),
+        ([100, 257], 4, 2, True, -1, 64, 1.0),
+        # several key blocks with sharp scores: exercises the running-max moves
+        ([513, 40, 384], 2, 2, False, -1, 64, 4.0),
+        ([1, 130, 256], 4, 4, False, -1, 128, 1.0),
+        ([200, 77, 300], 4, 2, True, -1, 128, 2.0),
+    ],
 )
-def test_attention_fwd_bwd(C, lens, heads, kv_heads, causal, window):
+def test_attention_fwd_bwd(C, attn_impl, lens, heads, kv_heads, causal, window, d, q_gain):
     torch.manual_seed(7)
     total = sum(lens)
-    hd = heads * 64
-    kvd = kv_heads * 64
+    hd = heads * d
+    kvd = kv_heads * d
     qkv = _rand(total, hd + 2 * kvd)
+    qkv[:, :hd] = (qkv[:, :hd].float() * q_gain).to(torch.bfloat16)
     q, k, v = qkv[:, :hd], qkv[:, hd:hd + kvd], qkv[:, hd + kvd:]
     cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), dtype=torch.int32, device=_dev())
-    scale = 1 / 8
+    scale = 1 / math.sqrt(d)
     o = torch.empty(total, hd, dtype=torch.bfloat16, device=_dev())
     lse = torch.empty(heads, total, device=_dev())
     C.attention_forward(q, k, v, o, lse, cu, max(lens), heads, kv_heads, scale, causal, window, 0, 0, 0.0, None)
     qf = q.float().requires_grad_(True)
     kf = k.float().requires_grad_(True)
     vf = v.float().requires_grad_(True)
-    ref = _attn_ref(qf, kf, vf, lens, heads, kv_heads, scale, causal, window)
-    _close(o, ref, rtol=2e-2, atol=2e-2, what="attn fwd")
-    if kv_heads != heads:
-        return
+    ref = _attn_ref(qf, kf, vf, lens, heads, kv_heads, scale, causal, window, d)
+    _close(o, ref, rtol=2e-2, atol=2e-2, what=f"attn fwd ({attn_impl})")
     do = _rand(total, hd)
     ref.backward(do.float())
     dqkv = torch.empty_like(qkv)
@@ -260,9 +273,47 @@ def test_attention_fwd_bwd(C, lens, heads, kv_heads, causal, window):
     dvec = torch.empty(heads, total, device=_dev())
     C.attention_backward(do, q, k, v, o, lse, dq, dk, dv, dq_acc, dvec, cu, max(lens), heads,
                          kv_heads, scale, causal, window, 0, 0, 0.0, None, None)
-    _close(dq, qf.grad, rtol=3e-2, atol=3e-2, what="dq")
-    _close(dk, kf.grad, rtol=3e-2, atol=3e-2, what="dk")
-    _close(dv, vf.grad, rtol=3e-2, atol=3e-2, what="dv")
+    torch.cuda.synchronize()
+    gain = max(1.0, q_gain)
+    _close(dq, qf.grad, rtol=3e-2, atol=3e-2 * gain, what=f"dq ({attn_impl})")
+    _close(dk, kf.grad, rtol=3e-2, atol=3e-2 * gain, what=f"dk ({attn_impl})")
+    _close(dv, vf.grad, rtol=3e-2, atol=3e-2 * gain, what=f"dv ({attn_impl})")
+
+
+@pytest.mark.parametrize("d", [64, 128])
+def test_attention_dropout_masks_match_across_kernels(C, d):
+    """The tcgen05 and mma.sync kernels draw the same Philox dropout masks."""
+    torch.manual_seed(11)
+    lens, heads = [90, 130, 33, 257], 2
+    total = sum(lens)
+    hd = heads * d
+    qkv = _rand(total, 3 * hd)
+    q, k, v = qkv[:, :hd], qkv[:, hd:2 * hd], qkv[:, 2 * hd:]
+    do = _rand(total, hd)
+    cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), dtype=torch.int32, device=_dev())
+    results = {}
+    for impl in ("tcgen05", "mma_sync"):
+        C.set_attention_tcgen05(impl == "tcgen05")
+        o = torch.empty(total, hd, dtype=torch.bfloat16, device=_dev())
+        lse = torch.empty(heads, total, device=_dev())
+        C.attention_forward(q, k, v, o, lse, cu, max(lens), heads, heads, d ** -0.5, False, -1, 4321, 5, 0.15, None)
+        dqkv = torch.empty_like(qkv)
+        acc = torch.empty(total, hd, device=_dev())
+        dvec = torch.empty(heads, total, device=_dev())
+        C.attention_backward(do, q, k, v, o, lse, dqkv[:, :hd], dqkv[:, hd:2 * hd], dqkv[:, 2 * hd:], acc, dvec, cu,
+                             max(lens), heads, heads, d ** -0.5, False, -1, 4321, 5, 0.15, None, None)
+        results[impl] = (o.float(), dqkv.float())
+    C.set_attention_tcgen05(True)
+    _close(results["tcgen05"][0], results["mma_sync"][0], rtol=2e-2, atol=2e-2, what="dropout fwd")
+    _close(results["tcgen05"][1], results["mma_sync"][1], rtol=3e-2, atol=3e-2, what="dropout grads")
+
+
+def test_attention_tcgen05_is_default(C):
+    import os
+
+    if os.environ.get("RX_ATTENTION_TC", "1") == "0":
+        pytest.skip("tcgen05 attention switched off by RX_ATTENTION_TC=0")
+    assert C.attention_tcgen05_enabled()
 
 
 @pytest.mark.parametrize("mode", [0, 1, 2])
