@@ -128,6 +128,15 @@ def bench_attention(timer, hbm, flops_peak, tag, report):
                 "tflops": 2.5 * fl / t / 1e12, f"frac_of_{tag}_bf16": 2.5 * fl / t / flops_peak,
                 f"frac_of_{tag}_hbm": bwd_bytes / t / hbm})
     C.set_attention_tcgen05(True)
+    # Attention-probability dropout 0.1 (Philox masks regenerated in both passes).
+    t = timer(lambda: C.attention_forward(q, k, v, o, lse, cu, 256, heads, heads, 0.125, False, -1, 7, 1, 0.1, None))
+    report({"kernel": "attention_fwd", "impl": "tcgen05", "case": "bert_b128_len32-256_dropout0.1", "ms": t * 1e3,
+            "tflops": fl / t / 1e12, f"frac_of_{tag}_hbm": fwd_bytes / t / hbm})
+    t = timer(lambda: C.attention_backward(do, q, k, v, o, lse, dqkv[:, :768], dqkv[:, 768:1536], dqkv[:, 1536:],
+                                           acc, dvec, cu, 256, heads, heads, 0.125, False, -1, 7, 1, 0.1, None,
+                                           None))
+    report({"kernel": "attention_bwd", "impl": "tcgen05", "case": "bert_b128_len32-256_dropout0.1", "ms": t * 1e3,
+            "tflops": 2.5 * fl / t / 1e12, f"frac_of_{tag}_hbm": bwd_bytes / t / hbm})
 
 
 def bench_norm(timer, hbm, flops_peak, tag, report):

@@ -609,8 +609,7 @@ template __global__ void attn_bwd_kernel<128, false>(const Params p);
 template __global__ void attn_bwd_kernel<64, true>(const Params p);
 template __global__ void attn_bwd_kernel<128, true>(const Params p);
 
-// tcgen05 kernels (attention_tc.cu): the path for head dims 64 / 128 without
-// relative position bias.
+// tcgen05 kernels (attention_tc.cu): the default path for head dims 64 / 128.
 bool tc_attention_enabled();
 void tc_forward(Params p, int d, int64_t max_len, cudaStream_t st, int device);
 void tc_backward(Params p, int d, int64_t max_len, cudaStream_t st, int device);
@@ -700,7 +699,7 @@ void attention_forward(const at::Tensor& q, const at::Tensor& k, const at::Tenso
   if (p.batch == 0 || max_len == 0) return;
   c10::cuda::CUDAGuard guard(q.get_device());
   auto st = at::cuda::getCurrentCUDAStream().stream();
-  if (attn::tc_attention_enabled() && p.rel_lut == nullptr && aligned_rows(o)) {
+  if (attn::tc_attention_enabled() && aligned_rows(o)) {
     attn::tc_forward(p, static_cast<int>(q.size(1) / heads), max_len, st, q.get_device());
     return;
   }
@@ -754,7 +753,7 @@ void attention_backward(const at::Tensor& dO, const at::Tensor& q, const at::Ten
   }
   dim3 grid((max_len + attn::BN - 1) / attn::BN, kv_heads, p.batch);
   const bool gqa = kv_heads != heads;
-  if (attn::tc_attention_enabled() && p.rel_lut == nullptr && aligned_rows(dO) &&
+  if (attn::tc_attention_enabled() && aligned_rows(dO) &&
       aligned_rows(dk) && aligned_rows(dv)) {
     attn::tc_backward(p, d, max_len, st, q.get_device());
   } else if (d == 64) {

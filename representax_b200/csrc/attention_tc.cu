@@ -5,8 +5,10 @@
 // causal / symmetric sliding-window masks, grouped-query heads, and the base-2
 // log-sum-exp of the scaled scores saved for the backward, and attention-
 // probability dropout with the same Philox counters (so either kernel family
-// can replay the other's masks). Covers head dimension 64 and 128 without
-// relative position bias (that variant stays on the mma.sync kernels).
+// can replay the other's masks), and MPNet's relative position bias (a
+// per-head table over signed distances, added to the logits; its gradient is
+// summed per diagonal in shared memory, then one global add per diagonal).
+// Head dimension 64 and 128.
 //
 // Forward: one CTA = 128 queries of one (sequence, head), 4 warps.
 //   Thread 0 issues TMA loads of Q (128 x D) and of 128-key blocks of K and V
@@ -53,6 +55,7 @@ constexpr int BKT = 128;  // backward: keys per CTA
 constexpr int BQB = 64;   // backward: queries per block
 constexpr uint32_t kSub128 = 128 * 128;  // [128 rows][64 bf16] swizzled sub-tile
 constexpr uint32_t kSub64 = 64 * 128;    // [64 rows][64 bf16]
+constexpr float kLog2e = 1.4426950408889634f;
 
 // Barrier slots (uint64) after the tiles.
 enum Bar : int { kBarQ = 0, kBarK, kBarV, kBarS, kBarO, kBarDrain, kNumBars };
@@ -80,7 +83,8 @@ struct BwdLayout {
   static constexpr uint32_t PT = DST + kSub128;      // P^T  [128 keys][64 q]; must follow DST
   static constexpr uint32_t LSE = PT + kSub128;      // 64 floats
   static constexpr uint32_t DVEC = LSE + 256;        // 64 floats
-  static constexpr uint32_t BARS = DVEC + 256;
+  static constexpr uint32_t DIAG = DVEC + 256;       // 192 floats: relative-bias gradient per diagonal
+  static constexpr uint32_t BARS = DIAG + 768;
   static constexpr uint32_t BYTES = BARS + kNumBars * 8 + 16 + 1024;
   // S^T [0, 64), dP^T [64, 128), dV [128, 128 + D), dK [128 + D, 128 + 2D);
   // dQ reuses [0, D) once S^T and dP^T have been read.
@@ -128,41 +132,43 @@ __device__ __forceinline__ void drain_phase(uint64_t* bar, int issued, int waite
 // `start` uses word (i & 1) * 2 + (j & 1) of Philox block
 // (start + (i & ~1), h << 16 | j >> 1). Two adjacent lanes own rows of the
 // same parity pair, so each generates every other block and the pair swaps
-// the halves the other needs.
+// the halves the other needs. Keep bits live in 64-bit registers (bit c =
+// column c), never in an indexed array.
 //
-// Forward (lane = query i; lanes i and i ^ 1 share blocks): keep bits of keys
-// [k0, k0 + 128) for this lane's query, bit c = key k0 + c.
+// Forward (lane = query i; lanes i and i ^ 1 share blocks): keys
+// [k0, k0 + 128), bit c of (lo, hi) = key k0 + c.
 __device__ __forceinline__ void fwd_keep_bits(const DropoutSite& site, int start, int i, int h, int k0,
-                                              int lane, uint32_t (&keep)[4]) {
-  keep[0] = keep[1] = keep[2] = keep[3] = 0u;
+                                              int lane, uint64_t& lo, uint64_t& hi) {
+  lo = hi = 0ull;
   const bool odd = (lane & 1) != 0;
   const uint32_t a = static_cast<uint32_t>(start + (i & ~1));
   const int b0 = k0 >> 1;
 #pragma unroll 1
   for (int t = 0; t < 66; t += 2) {
-    const Philox4 r = dropout_block(site, a, (static_cast<uint32_t>(h) << 16) | static_cast<uint32_t>(b0 + t + (odd ? 1 : 0)));
+    const Philox4 r =
+        dropout_block(site, a, (static_cast<uint32_t>(h) << 16) | static_cast<uint32_t>(b0 + t + (odd ? 1 : 0)));
     // even lane keeps (x, y) of block t and sends (z, w); odd lane keeps
     // (z, w) of block t + 1 and sends (x, y).
     const uint32_t s0 = __shfl_xor_sync(0xffffffffu, odd ? r.x : r.z, 1);
     const uint32_t s1 = __shfl_xor_sync(0xffffffffu, odd ? r.y : r.w, 1);
-    uint32_t w[4];  // words for keys 2 (b0 + t) + 0..3
-    w[0] = odd ? s0 : r.x;
-    w[1] = odd ? s1 : r.y;
-    w[2] = odd ? r.z : s0;
-    w[3] = odd ? r.w : s1;
+    const uint32_t w0 = odd ? s0 : r.x, w1 = odd ? s1 : r.y, w2 = odd ? r.z : s0, w3 = odd ? r.w : s1;
+    const int c0 = 2 * (b0 + t) - k0;  // column of w0; w1..w3 follow
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      const int c = 2 * (b0 + t) + e - k0;
-      if (c >= 0 && c < 128 && w[e] >= site.threshold) keep[c >> 5] |= 1u << (c & 31);
+      const uint32_t w = e == 0 ? w0 : (e == 1 ? w1 : (e == 2 ? w2 : w3));
+      const int c = c0 + e;
+      if (c >= 0 && c < 128 && w >= site.threshold) {
+        if (c < 64) lo |= 1ull << c;
+        else hi |= 1ull << (c - 64);
+      }
     }
   }
 }
 
-// Backward (lane = key j; lanes j and j ^ 1 share blocks): keep bits of
-// queries [q0, q0 + 64) for this lane's key, bit c = query q0 + c.
-__device__ __forceinline__ void bwd_keep_bits(const DropoutSite& site, int start, int j, int h, int q0,
-                                              int lane, uint32_t (&keep)[2]) {
-  keep[0] = keep[1] = 0u;
+// Backward (lane = key j; lanes j and j ^ 1 share blocks): queries
+// [q0, q0 + 64), bit c = query q0 + c.
+__device__ __forceinline__ uint64_t bwd_keep_bits(const DropoutSite& site, int start, int j, int h, int q0, int lane) {
+  uint64_t keep = 0ull;
   const bool odd = (lane & 1) != 0;
   const uint32_t bcol = (static_cast<uint32_t>(h) << 16) | static_cast<uint32_t>(j >> 1);
   const int a0 = q0 >> 1;
@@ -172,17 +178,16 @@ __device__ __forceinline__ void bwd_keep_bits(const DropoutSite& site, int start
     // even key needs words x (even query), z (odd query); odd key y, w.
     const uint32_t s0 = __shfl_xor_sync(0xffffffffu, odd ? r.x : r.y, 1);
     const uint32_t s1 = __shfl_xor_sync(0xffffffffu, odd ? r.z : r.w, 1);
-    uint32_t w[4];  // words for queries 2 (a0 + t) + 0..3
-    w[0] = odd ? s0 : r.x;
-    w[1] = odd ? s1 : r.z;
-    w[2] = odd ? r.y : s0;
-    w[3] = odd ? r.w : s1;
+    const uint32_t w0 = odd ? s0 : r.x, w1 = odd ? s1 : r.z, w2 = odd ? r.y : s0, w3 = odd ? r.w : s1;
+    const int c0 = 2 * (a0 + t) - q0;
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      const int c = 2 * (a0 + t) + e - q0;
-      if (c >= 0 && c < 64 && w[e] >= site.threshold) keep[c >> 5] |= 1u << (c & 31);
+      const uint32_t w = e == 0 ? w0 : (e == 1 ? w1 : (e == 2 ? w2 : w3));
+      const int c = c0 + e;
+      if (c >= 0 && c < 64 && w >= site.threshold) keep |= 1ull << c;
     }
   }
+  return keep;
 }
 
 // ===================================================================== forward
@@ -215,7 +220,9 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
   const uint32_t sQ = smem_u32(base + L::Q), sK = smem_u32(base + L::K), sV = smem_u32(base + L::V),
                  sP = smem_u32(base + L::P);
 
-  // Thread 0's TMA bookkeeping (issued / waited phases per barrier).
+  // Thread 0 issues every copy and MMA and is the only thread that waits on
+  // their mbarriers; the others meet it at a block barrier. Bookkeeping of
+  // issued / waited phases lets an aborting CTA drain what is in flight.
   int k_issued = 0, k_waited = 0, v_issued = 0, v_waited = 0, q_waited = 0;
   if (tid == 0) {
     for (int i = 0; i < kNumBars; ++i) mbar_init(&bars[i], 1);
@@ -242,25 +249,40 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
   const int i = q_lo + row;  // this thread's query (sequence-relative)
   const bool warp_live = q_lo + warp * 32 < len;
   constexpr uint32_t IDESC_O = idesc_bf16_f32(128, D, false, true);
+  const float sl2 = p.scale_log2;
+  // Keys this query may see: [vis_lo, vis_hi) (sequence-relative).
+  int vis_lo = 0, vis_hi = len;
+  if (p.causal) vis_hi = min(vis_hi, i + 1);
+  if (p.window >= 0) {
+    vis_lo = max(0, i - p.window);
+    vis_hi = min(vis_hi, i + p.window + 1);
+  }
+  // Relative position bias (MPNet): logits[h, i, j] += rel_lut[h, j - i + lut_len - 1],
+  // folded into the raw score as bias / scale.
+  const float* lut_h =
+      p.rel_lut == nullptr ? nullptr : p.rel_lut + static_cast<int64_t>(h) * (2 * p.lut_len - 1) + (p.lut_len - 1);
+  const float inv_scale = 1.f / p.scale;
+  const bool drop = p.pdrop.threshold != 0u;
 
-  float m_run = -INFINITY, l_run = 0.f;
+  float m_run = -INFINITY, l_run = 0.f;  // in scaled base-2 units
   bool ok = true, mma_issued = false;
   for (int j = 0; j < nblk; ++j) {
     const int k0 = k_lo + j * FK;
     const uint32_t ph = static_cast<uint32_t>(j & 1);
     // Keys of this block that can be visible, rounded up to the MMA's N / K step.
     const int n16 = (min(FK, k_hi - k0) + 15) & ~15;
-    bool issue_ok = true;
+    const int nch = (n16 + 31) >> 5;  // 32-column TMEM chunks holding scores
+    bool ok0 = true;
     if (tid == 0) {
       if (j == 0) {
-        issue_ok = mbar_wait(&bars[kBarQ], 0, p.timeout_ns);
-        q_waited = issue_ok ? 1 : 0;
+        ok0 = mbar_wait(&bars[kBarQ], 0, p.timeout_ns);
+        q_waited = ok0 ? 1 : 0;
       }
-      if (issue_ok) {
-        issue_ok = mbar_wait(&bars[kBarK], static_cast<uint32_t>(k_waited & 1), p.timeout_ns);
-        if (issue_ok) ++k_waited;
+      if (ok0) {
+        ok0 = mbar_wait(&bars[kBarK], static_cast<uint32_t>(k_waited & 1), p.timeout_ns);
+        if (ok0) ++k_waited;
       }
-      if (issue_ok) {
+      if (ok0) {
         tc_fence_after();
         const uint32_t idesc_s = idesc_bf16_f32(128, n16, false, false);
 #pragma unroll
@@ -271,46 +293,69 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
         }
         umma_commit(&bars[kBarS]);
         mma_issued = true;
-      } else {
-        report_status(p.status, kStatusTimeoutMma);
       }
     }
-    bool got = issue_ok && mbar_wait(&bars[kBarS], ph, p.timeout_ns);
-    if (__syncthreads_or(!got)) {
-      if (tid == 0) report_status(p.status, kStatusTimeoutEpilogue);
+    // Dropout keep bits depend only on coordinates: draw them while the
+    // copies and the S MMA are in flight.
+    uint64_t keep_lo = ~0ull, keep_hi = ~0ull;
+    __syncwarp();
+    if (drop && warp_live) fwd_keep_bits(p.pdrop, start, i, h, k0, lane, keep_lo, keep_hi);
+    if (tid == 0) {
+      if (ok0) ok0 = mbar_wait(&bars[kBarS], ph, p.timeout_ns);
+      if (!ok0) report_status(p.status, kStatusTimeoutMma);
+      // The S MMA has retired, so the K buffer is free for the next block.
+      if (ok0 && j + 1 < nblk) {
+        mbar_arrive_expect_tx(&bars[kBarK], DS * kSub128);
+        for (int s = 0; s < DS; ++s)
+          tma_load_2d(base + L::K + s * kSub128, &tmK, &bars[kBarK], kvh * D + 64 * s, start + k0 + FK);
+        ++k_issued;
+      }
+    }
+    if (__syncthreads_or(!ok0)) {
       ok = false;
       break;
     }
     tc_fence_after();
-    // The S MMA has retired, so the K buffer is free for the next block.
-    if (tid == 0 && j + 1 < nblk) {
-      mbar_arrive_expect_tx(&bars[kBarK], DS * kSub128);
-      for (int s = 0; s < DS; ++s)
-        tma_load_2d(base + L::K + s * kSub128, &tmK, &bars[kBarK], kvh * D + 64 * s, start + k0 + FK);
-      ++k_issued;
-    }
 
-    __syncwarp();  // warp 0 may have diverged around thread 0's TMA issue
+    __syncwarp();
     if (warp_live) {
       uint32_t r[4][32];
-      const int nch = (n16 + 31) >> 5;  // 32-column TMEM chunks holding scores
 #pragma unroll
       for (int c = 0; c < 4; ++c)
         if (c < nch) tmem_ld_32x32b_x32(tS + lane_off + c * 32, r[c]);
       tmem_ld_wait();
+      const int clo = vis_lo - k0, chi = vis_hi - k0;  // visible columns of this block
       float mx = -INFINITY;
+      if (lut_h == nullptr) {
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        if (c >= nch) break;
+        for (int c = 0; c < 4; ++c) {
+          if (c < nch) {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int key = k0 + c * 32 + e;
-          float x = __uint_as_float(r[c][e]) * p.scale_log2;
-          if (key >= k_hi || !mask_ok(p, i, key)) x = -INFINITY;
-          r[c][e] = __float_as_uint(x);
-          mx = fmaxf(mx, x);
+            for (int e = 0; e < 32; ++e) {
+              const int col = c * 32 + e;
+              const float v = (col >= clo && col < chi) ? __uint_as_float(r[c][e]) : -INFINITY;
+              r[c][e] = __float_as_uint(v);
+              mx = fmaxf(mx, v);
+            }
+          }
+        }
+      } else {
+        const float* lut_row = lut_h + (k0 - i);  // bias of column c at lut_row[c]
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          if (c < nch) {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              const int col = c * 32 + e;
+              const bool vis = col >= clo && col < chi && i < len;
+              const float v = vis ? __uint_as_float(r[c][e]) + __ldg(lut_row + col) * inv_scale : -INFINITY;
+              r[c][e] = __float_as_uint(v);
+              mx = fmaxf(mx, v);
+            }
+          }
         }
       }
+      mx *= sl2;  // scaled base-2 units (-inf stays -inf)
       float alpha = 1.f;
       bool rescale = false;
       if (mx > -INFINITY) {
@@ -336,27 +381,44 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
         }
         tmem_st_wait();
       }
-      const float m_use = m_run == -INFINITY ? 0.f : m_run;
-      const bool drop = p.pdrop.threshold != 0u;
-      uint32_t keep[4] = {0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu};
-      if (drop) fwd_keep_bits(p.pdrop, start, i, h, k0, lane, keep);
-      const float dscale = drop ? p.pdrop.scale : 1.f;
+      const float neg_m = m_run == -INFINITY ? 0.f : -m_run;
       float rs = 0.f;
       uint8_t* prow = base + L::P;
+      if (!drop) {
 #pragma unroll
-      for (int ch = 0; ch < FK / 8; ++ch) {
-        if (ch * 8 >= n16) break;
-        float e8[8];
+        for (int ch = 0; ch < FK / 8; ++ch) {
+          if (ch * 8 < n16) {
+            float e8[8];
 #pragma unroll
-        for (int t = 0; t < 8; ++t) {
-          const int c = ch * 8 + t;
-          const float e = ex2(__uint_as_float(r[c >> 5][c & 31]) - m_use);
-          rs += e;  // the normaliser uses the probabilities before dropout
-          e8[t] = ((keep[c >> 5] >> (c & 31)) & 1u) ? e * dscale : 0.f;
+            for (int t = 0; t < 8; ++t) {
+              const int c = ch * 8 + t;
+              e8[t] = ex2(fmaf(__uint_as_float(r[c >> 5][c & 31]), sl2, neg_m));
+              rs += e8[t];
+            }
+            store_chunk_sw128(prow + (ch >> 3) * kSub128, row, ch & 7,
+                              make_uint4(pack2(e8[0], e8[1]), pack2(e8[2], e8[3]), pack2(e8[4], e8[5]),
+                                         pack2(e8[6], e8[7])));
+          }
         }
-        const uint4 w = make_uint4(pack2(e8[0], e8[1]), pack2(e8[2], e8[3]), pack2(e8[4], e8[5]),
-                                   pack2(e8[6], e8[7]));
-        store_chunk_sw128(prow + (ch >> 3) * kSub128, row, ch & 7, w);
+      } else {
+        const float dscale = p.pdrop.scale;
+#pragma unroll
+        for (int ch = 0; ch < FK / 8; ++ch) {
+          if (ch * 8 < n16) {
+            float e8[8];
+#pragma unroll
+            for (int t = 0; t < 8; ++t) {
+              const int c = ch * 8 + t;
+              const float e = ex2(fmaf(__uint_as_float(r[c >> 5][c & 31]), sl2, neg_m));
+              rs += e;  // the normaliser uses the probabilities before dropout
+              const uint64_t bit = c < 64 ? (keep_lo >> c) : (keep_hi >> (c - 64));
+              e8[t] = (bit & 1ull) ? e * dscale : 0.f;
+            }
+            store_chunk_sw128(prow + (ch >> 3) * kSub128, row, ch & 7,
+                              make_uint4(pack2(e8[0], e8[1]), pack2(e8[2], e8[3]), pack2(e8[4], e8[5]),
+                                         pack2(e8[6], e8[7])));
+          }
+        }
       }
       l_run += rs;
     }
@@ -366,8 +428,8 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
 
     if (tid == 0) {
       tc_fence_after();
-      issue_ok = mbar_wait(&bars[kBarV], static_cast<uint32_t>(v_waited & 1), p.timeout_ns);
-      if (issue_ok) {
+      ok0 = mbar_wait(&bars[kBarV], static_cast<uint32_t>(v_waited & 1), p.timeout_ns);
+      if (ok0) {
         ++v_waited;
         for (int kk = 0; kk < n16 / 16; ++kk) {
           const uint32_t a_off = (kk >> 2) * kSub128 + (kk & 3) * 32;
@@ -375,24 +437,22 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
                       IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(&bars[kBarO]);
-      } else {
-        report_status(p.status, kStatusTimeoutMma);
+        ok0 = mbar_wait(&bars[kBarO], ph, p.timeout_ns);
+      }
+      if (!ok0) report_status(p.status, kStatusTimeoutMma);
+      // P V has retired: V (and P) are free.
+      if (ok0 && j + 1 < nblk) {
+        mbar_arrive_expect_tx(&bars[kBarV], DS * kSub128);
+        for (int s = 0; s < DS; ++s)
+          tma_load_2d(base + L::V + s * kSub128, &tmV, &bars[kBarV], kvh * D + 64 * s, start + k0 + FK);
+        ++v_issued;
       }
     }
-    got = issue_ok && mbar_wait(&bars[kBarO], ph, p.timeout_ns);
-    if (__syncthreads_or(!got)) {
-      if (tid == 0) report_status(p.status, kStatusTimeoutEpilogue);
+    if (__syncthreads_or(!ok0)) {
       ok = false;
       break;
     }
     tc_fence_after();
-    // P V has retired: V (and P) are free.
-    if (tid == 0 && j + 1 < nblk) {
-      mbar_arrive_expect_tx(&bars[kBarV], DS * kSub128);
-      for (int s = 0; s < DS; ++s)
-        tma_load_2d(base + L::V + s * kSub128, &tmV, &bars[kBarV], kvh * D + 64 * s, start + k0 + FK);
-      ++v_issued;
-    }
   }
 
   __syncwarp();
@@ -465,8 +525,9 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
   uint8_t* base = align1024(smem_raw);
   uint64_t* bars = reinterpret_cast<uint64_t*>(base + L::BARS);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
-  float* s_lse = reinterpret_cast<float*>(base + L::LSE);
-  float* s_dvec = reinterpret_cast<float*>(base + L::DVEC);
+  float* s_nlse = reinterpret_cast<float*>(base + L::LSE);   // -lse of the block's queries
+  float* s_dvs = reinterpret_cast<float*>(base + L::DVEC);   // Dvec * scale
+  float* s_diag = p.drel != nullptr ? reinterpret_cast<float*>(base + L::DIAG) : nullptr;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t sK = smem_u32(base + L::K), sV = smem_u32(base + L::V), sQ = smem_u32(base + L::Q),
                  sDO = smem_u32(base + L::DO), sDST = smem_u32(base + L::DST), sPT = smem_u32(base + L::PT);
@@ -481,6 +542,8 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
       tma_load_2d(base + L::DO + s * kSub64, &tmDO, &bars[kBarQ], hq * D + 64 * s, start + q0);
     }
   };
+  if (s_diag != nullptr)
+    for (int t = tid; t < BKT + BQB; t += kThreads) s_diag[t] = 0.f;
   if (tid == 0) {
     for (int i = 0; i < kNumBars; ++i) mbar_init(&bars[i], 1);
     fence_mbarrier_init();
@@ -509,6 +572,16 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
   const bool warp_live = kt0 + warp * 32 < len;
   constexpr uint32_t IDESC_KV = idesc_bf16_f32(128, D, false, true);
   constexpr uint32_t IDESC_Q = idesc_bf16_f32(128, D, true, true);
+  const float sl2 = p.scale_log2, scale = p.scale;
+  // Queries that may see this key: [vis_lo, vis_hi) (empty past the sequence end).
+  int vis_lo = 0, vis_hi = key < len ? len : 0;
+  if (p.causal) vis_lo = key;
+  if (p.window >= 0) {
+    vis_lo = max(vis_lo, key - p.window);
+    vis_hi = min(vis_hi, key + p.window + 1);
+  }
+  const bool drop = p.pdrop.threshold != 0u;
+  const bool general = drop || p.rel_lut != nullptr;
 
   bool ok = true, mma_issued = false;
   for (int it = 0; it < total_it; ++it) {
@@ -519,21 +592,20 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
     if (tid < BQB) {
       const int q = q0 + tid;
       const int64_t at = static_cast<int64_t>(hq) * p.total_tokens + start + q;
-      s_lse[tid] = q < len ? p.lse[at] : INFINITY;
-      s_dvec[tid] = q < len ? p.dvec[at] : 0.f;
+      s_nlse[tid] = q < len ? -p.lse[at] : -INFINITY;
+      s_dvs[tid] = q < len ? p.dvec[at] * scale : 0.f;
     }
-    __syncthreads();
-    bool issue_ok = true;
+    bool ok0 = true;
     if (tid == 0) {
       if (it == 0) {
-        issue_ok = mbar_wait(&bars[kBarK], 0, p.timeout_ns);
-        kv_waited = issue_ok ? 1 : 0;
+        ok0 = mbar_wait(&bars[kBarK], 0, p.timeout_ns);
+        kv_waited = ok0 ? 1 : 0;
       }
-      if (issue_ok) {
-        issue_ok = mbar_wait(&bars[kBarQ], static_cast<uint32_t>(qd_waited & 1), p.timeout_ns);
-        if (issue_ok) ++qd_waited;
+      if (ok0) {
+        ok0 = mbar_wait(&bars[kBarQ], static_cast<uint32_t>(qd_waited & 1), p.timeout_ns);
+        if (ok0) ++qd_waited;
       }
-      if (issue_ok) {
+      if (ok0) {
         tc_fence_after();
         const uint32_t idesc_s = idesc_bf16_f32(128, nq16, false, false);
 #pragma unroll
@@ -547,13 +619,19 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
         }
         umma_commit(&bars[kBarS]);
         mma_issued = true;
-      } else {
-        report_status(p.status, kStatusTimeoutMma);
       }
     }
-    bool got = issue_ok && mbar_wait(&bars[kBarS], ph, p.timeout_ns);
-    if (__syncthreads_or(!got)) {
-      if (tid == 0) report_status(p.status, kStatusTimeoutEpilogue);
+    // Dropout keep bits depend only on coordinates: draw them while the
+    // S^T / dP^T MMAs are in flight.
+    uint64_t keep = ~0ull;
+    __syncwarp();
+    if (drop && warp_live) keep = bwd_keep_bits(p.pdrop, start, key, hq, q0, lane);
+    if (tid == 0) {
+      if (ok0) ok0 = mbar_wait(&bars[kBarS], ph, p.timeout_ns);
+      if (!ok0) report_status(p.status, kStatusTimeoutMma);
+    }
+    // Also publishes this block's -lse / Dvec rows to every thread.
+    if (__syncthreads_or(!ok0)) {
       ok = false;
       break;
     }
@@ -571,33 +649,62 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
         tmem_ld_32x32b_x32(tDP + lane_off + 32, rd[1]);
       }
       tmem_ld_wait();
-      const bool key_ok = key < len;
-      const bool drop = p.pdrop.threshold != 0u;
-      uint32_t keep[2] = {0xffffffffu, 0xffffffffu};
-      if (drop) bwd_keep_bits(p.pdrop, start, key, hq, q0, lane, keep);
-      const float dscale = drop ? p.pdrop.scale : 1.f;
+      const int clo = vis_lo - q0, chi = vis_hi - q0;  // visible query columns of this block
+      if (!general) {
 #pragma unroll
-      for (int ch = 0; ch < BQB / 8; ++ch) {
-        if (ch * 8 >= nq16) break;
-        float pv[8], dv[8];
+        for (int ch = 0; ch < BQB / 8; ++ch) {
+          if (ch * 8 < nq16) {
+            float pv[8], dv[8];
 #pragma unroll
-        for (int t = 0; t < 8; ++t) {
-          const int c = ch * 8 + t;
-          const int q = q0 + c;
-          const bool vis = key_ok && q < len && mask_ok(p, q, key);
-          const float s = __uint_as_float(rs[c >> 5][c & 31]);
-          const float pr = vis ? ex2(s * p.scale_log2 - s_lse[c]) : 0.f;
-          // With dropout: dV uses the dropped probabilities, and
-          // dS = P * (mask * dP / (1 - p) - Dvec).
-          const bool kept = ((keep[c >> 5] >> (c & 31)) & 1u) != 0u;
-          const float dp = kept ? __uint_as_float(rd[c >> 5][c & 31]) * dscale : 0.f;
-          pv[t] = kept ? pr * dscale : 0.f;
-          dv[t] = pr * (dp - s_dvec[c]) * p.scale;
+            for (int t = 0; t < 8; ++t) {
+              const int c = ch * 8 + t;
+              const float s = __uint_as_float(rs[c >> 5][c & 31]);
+              const float dp = __uint_as_float(rd[c >> 5][c & 31]);
+              const float pr = (c >= clo && c < chi) ? ex2(fmaf(s, sl2, s_nlse[c])) : 0.f;
+              pv[t] = pr;
+              dv[t] = pr * fmaf(dp, scale, -s_dvs[c]);  // P (dP - Dvec) * scale
+            }
+            store_chunk_sw128(pt, krow, ch, make_uint4(pack2(pv[0], pv[1]), pack2(pv[2], pv[3]),
+                                                       pack2(pv[4], pv[5]), pack2(pv[6], pv[7])));
+            store_chunk_sw128(dst, krow, ch, make_uint4(pack2(dv[0], dv[1]), pack2(dv[2], dv[3]),
+                                                        pack2(dv[4], dv[5]), pack2(dv[6], dv[7])));
+          }
         }
-        store_chunk_sw128(pt, krow, ch,
-                          make_uint4(pack2(pv[0], pv[1]), pack2(pv[2], pv[3]), pack2(pv[4], pv[5]), pack2(pv[6], pv[7])));
-        store_chunk_sw128(dst, krow, ch,
-                          make_uint4(pack2(dv[0], dv[1]), pack2(dv[2], dv[3]), pack2(dv[4], dv[5]), pack2(dv[6], dv[7])));
+      } else {
+        // Dropout and / or relative bias: dV uses the dropped probabilities and
+        // dS = P * (mask * dP / (1 - p) - Dvec); the bias gradient is dS summed
+        // along each diagonal.
+        const float dscale = drop ? p.pdrop.scale : 1.f;
+        const float* lut_col =
+            p.rel_lut == nullptr ? nullptr
+                                 : p.rel_lut + static_cast<int64_t>(hq) * (2 * p.lut_len - 1) + (p.lut_len - 1) +
+                                       (key - q0);  // bias of column c at lut_col[-c]
+        const float inv_scale = 1.f / scale;
+#pragma unroll
+        for (int ch = 0; ch < BQB / 8; ++ch) {
+          if (ch * 8 < nq16) {
+            float pv[8], dv[8];
+#pragma unroll
+            for (int t = 0; t < 8; ++t) {
+              const int c = ch * 8 + t;
+              const bool vis = c >= clo && c < chi;
+              float s = __uint_as_float(rs[c >> 5][c & 31]);
+              if (vis && lut_col != nullptr) s += __ldg(lut_col - c) * inv_scale;
+              const float pr = vis ? ex2(fmaf(s, sl2, s_nlse[c])) : 0.f;
+              const bool kept = ((keep >> c) & 1ull) != 0ull;
+              const float dp = kept ? __uint_as_float(rd[c >> 5][c & 31]) * dscale : 0.f;
+              const float ds = pr * fmaf(dp, scale, -s_dvs[c]);
+              pv[t] = kept ? pr * dscale : 0.f;
+              dv[t] = ds;
+              // diagonal key - q, offset so the tile's smallest (key kt0, query q0 + 63) is 0
+              if (s_diag != nullptr && ds != 0.f) atomicAdd(s_diag + (krow - c + BQB - 1), ds * inv_scale);
+            }
+            store_chunk_sw128(pt, krow, ch, make_uint4(pack2(pv[0], pv[1]), pack2(pv[2], pv[3]),
+                                                       pack2(pv[4], pv[5]), pack2(pv[6], pv[7])));
+            store_chunk_sw128(dst, krow, ch, make_uint4(pack2(dv[0], dv[1]), pack2(dv[2], dv[3]),
+                                                        pack2(dv[4], dv[5]), pack2(dv[6], dv[7])));
+          }
+        }
       }
     } else {
       // Keys past the sequence: zero rows (dS^T rows enter dQ = dS K).
@@ -610,6 +717,17 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
     fence_proxy_async_smem();
     tc_fence_before();
     __syncthreads();
+    if (s_diag != nullptr) {
+      // One global add per diagonal of the tile; the buffer is cleared for the next block.
+      float* drel_h = p.drel + static_cast<int64_t>(hq) * (2 * p.lut_len - 1) + (p.lut_len - 1);
+      for (int t = tid; t < BKT + BQB - 1; t += kThreads) {
+        const float v = s_diag[t];
+        if (v != 0.f) {
+          atomicAdd(drel_h + (kt0 - (q0 + BQB - 1) + t), v);
+          s_diag[t] = 0.f;
+        }
+      }
+    }
 
     if (tid == 0) {
       tc_fence_after();
@@ -627,19 +745,19 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
                     smem_desc_sw128(sK + kk * 2048, kSub128, 1024), IDESC_Q, kk > 0 ? 1u : 0u);
       }
       umma_commit(&bars[kBarO]);
+      ok0 = mbar_wait(&bars[kBarO], ph, p.timeout_ns);
+      if (!ok0) report_status(p.status, kStatusTimeoutMma);
+      // Q and dO are free: fetch the next block while this one's dQ drains.
+      if (ok0 && it + 1 < total_it) {
+        issue_qd(it + 1);
+        ++qd_issued;
+      }
     }
-    got = mbar_wait(&bars[kBarO], ph, p.timeout_ns);
-    if (__syncthreads_or(!got)) {
-      if (tid == 0) report_status(p.status, kStatusTimeoutEpilogue);
+    if (__syncthreads_or(!ok0)) {
       ok = false;
       break;
     }
     tc_fence_after();
-    // Q and dO are free: fetch the next block while this one's dQ drains.
-    if (tid == 0 && it + 1 < total_it) {
-      issue_qd(it + 1);
-      ++qd_issued;
-    }
     __syncwarp();
     if (warp < BQB / 32) {
       const int q = q0 + warp * 32 + lane;

@@ -94,7 +94,8 @@ class MatryoshkaTask:
         weights = torch.tensor(self.weights, dtype=torch.float32, device=stacked.device)
         weights = torch.where(selected.to(stacked.device), weights, torch.zeros_like(weights))
         return LossOutput(loss=(weights * stacked).sum(),
-                          metrics={"dimension_losses": stacked.detach(), "selected_dimensions": selected})
+                          metrics={"dimension_losses": stacked.detach(),
+                                   "selected_dimensions": selected.to(stacked.device)})
 
 
 @dataclass

@@ -114,7 +114,7 @@ class TrainStep:
         max_norm = float(self.max_gradient_norm or 0.0)
         gate = loss.detach().reshape(1).to(torch.float32)
         for v in metrics.values():
-            gate = gate + 0.0 * v.detach().reshape(-1)[:1].to(torch.float32)
+            gate = gate + 0.0 * v.detach().reshape(-1)[:1].to(gate.device, torch.float32)
         if self._native and store.sharded:
             self._sharded_update(gate, max_norm, lr)
             return

@@ -281,8 +281,10 @@ def test_attention_fwd_bwd(C, attn_impl, lens, heads, kv_heads, causal, window, 
 
 
 @pytest.mark.parametrize("d", [64, 128])
-def test_attention_dropout_masks_match_across_kernels(C, d):
-    """The tcgen05 and mma.sync kernels draw the same Philox dropout masks."""
+@pytest.mark.parametrize("variant", ["dropout", "relative_bias"])
+def test_attention_variants_match_across_kernels(C, d, variant):
+    """The tcgen05 and mma.sync kernels agree on dropout masks (same Philox counters) and on
+    MPNet's relative position bias and its gradient."""
     torch.manual_seed(11)
     lens, heads = [90, 130, 33, 257], 2
     total = sum(lens)
@@ -291,21 +293,27 @@ def test_attention_dropout_masks_match_across_kernels(C, d):
     q, k, v = qkv[:, :hd], qkv[:, hd:2 * hd], qkv[:, 2 * hd:]
     do = _rand(total, hd)
     cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), dtype=torch.int32, device=_dev())
+    drop = 0.15 if variant == "dropout" else 0.0
+    lut = torch.randn(heads, 2 * 300 - 1, device=_dev()) if variant == "relative_bias" else None
     results = {}
     for impl in ("tcgen05", "mma_sync"):
         C.set_attention_tcgen05(impl == "tcgen05")
         o = torch.empty(total, hd, dtype=torch.bfloat16, device=_dev())
         lse = torch.empty(heads, total, device=_dev())
-        C.attention_forward(q, k, v, o, lse, cu, max(lens), heads, heads, d ** -0.5, False, -1, 4321, 5, 0.15, None)
+        C.attention_forward(q, k, v, o, lse, cu, max(lens), heads, heads, d ** -0.5, False, -1, 4321, 5, drop, lut)
         dqkv = torch.empty_like(qkv)
         acc = torch.empty(total, hd, device=_dev())
         dvec = torch.empty(heads, total, device=_dev())
+        drel = None if lut is None else torch.zeros_like(lut)
         C.attention_backward(do, q, k, v, o, lse, dqkv[:, :hd], dqkv[:, hd:2 * hd], dqkv[:, 2 * hd:], acc, dvec, cu,
-                             max(lens), heads, heads, d ** -0.5, False, -1, 4321, 5, 0.15, None, None)
-        results[impl] = (o.float(), dqkv.float())
+                             max(lens), heads, heads, d ** -0.5, False, -1, 4321, 5, drop, lut, drel)
+        results[impl] = (o.float(), dqkv.float(), drel)
     C.set_attention_tcgen05(True)
-    _close(results["tcgen05"][0], results["mma_sync"][0], rtol=2e-2, atol=2e-2, what="dropout fwd")
-    _close(results["tcgen05"][1], results["mma_sync"][1], rtol=3e-2, atol=3e-2, what="dropout grads")
+    _close(results["tcgen05"][0], results["mma_sync"][0], rtol=2e-2, atol=2e-2, what=f"{variant} fwd")
+    _close(results["tcgen05"][1], results["mma_sync"][1], rtol=3e-2, atol=3e-2, what=f"{variant} grads")
+    if lut is not None:
+        ref = results["mma_sync"][2]
+        _close(results["tcgen05"][2], ref, rtol=2e-2, atol=2e-2 * float(ref.abs().max()), what="relative-bias grad")
 
 
 def test_attention_tcgen05_is_default(C):
