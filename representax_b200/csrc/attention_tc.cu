@@ -4,7 +4,7 @@
 // rows addressed through cu_seqlens (no FLOP spent on padding), key-validity /
 // causal / symmetric sliding-window masks, grouped-query heads, and the base-2
 // log-sum-exp of the scaled scores saved for the backward, attention-
-// probability dropout (Philox masks with 16-bit decisions, regenerated in the
+// probability dropout (Philox masks with 8-bit decisions, regenerated in the
 // backward; see below), and MPNet's relative position bias (a
 // per-head table over signed distances, added to the logits; its gradient is
 // summed per diagonal in shared memory, then one global add per diagonal).
@@ -127,111 +127,102 @@ __device__ __forceinline__ void drain_phase(uint64_t* bar, int issued, int waite
     report_status(p.status, kStatusTimeoutDrain);
 }
 
-// Attention-probability dropout with 16-bit keep decisions (eight per Philox
-// block): element (query i, key j) of query head h in a sequence starting at
-// token `start` keeps its probability when half (j & 1) of word
-// (i & 1) * 2 + ((j >> 1) & 1) of Philox block (start + (i & ~1), h << 16 | j >> 2)
-// is >= t16 = round(p * 2^16); kept values are scaled by 2^16 / (2^16 - t16),
-// which keeps the expectation exact for the quantised probability (within
-// 2^-17 of p). Both kernels draw the same mask from these coordinates, so
-// nothing is stored between the forward and the backward. Keep bits live in
-// 64-bit registers (bit c = column c), never in an indexed array.
-struct Drop16 {
-  uint32_t t16;  // 0: off
+// Attention-probability dropout with 8-bit keep decisions (sixteen per
+// Philox block, as FlashAttention does): element (query i, key j) of query
+// head h in a sequence starting at token `start` keeps its probability when
+// byte (j & 3) of word (i & 1) * 2 + ((j >> 2) & 1) of Philox block
+// (start + (i & ~1), h << 16 | j >> 3) is >= t8 = round(p * 256); kept values
+// are scaled by 256 / (256 - t8), which keeps the expectation exact for the
+// quantised probability t8 / 256. Both passes draw the mask from these
+// coordinates, so nothing is stored between them. Keep bits live in 64-bit
+// registers (bit c = column c), never in an indexed array.
+struct Drop8 {
+  uint32_t t8;  // 0: off
   float scale;
 };
 
-__device__ __forceinline__ Drop16 drop16(const DropoutSite& site) {
-  Drop16 d{0u, 1.f};
+__device__ __forceinline__ Drop8 drop8(const DropoutSite& site) {
+  Drop8 d{0u, 1.f};
   if (site.threshold == 0u) return d;
-  d.t16 = min((site.threshold + 32768u) >> 16, 65535u);
-  d.scale = 65536.f / static_cast<float>(65536u - d.t16);
+  d.t8 = min((site.threshold + (1u << 23)) >> 24, 255u);
+  if (d.t8 == 0u) d.t8 = 1u;  // a requested dropout never rounds to none
+  d.scale = 256.f / static_cast<float>(256u - d.t8);
   return d;
 }
 
-__device__ __forceinline__ bool keep16(uint32_t word, int high, uint32_t t16) {
-  return (high ? (word >> 16) : (word & 0xffffu)) >= t16;
+// Keep decisions of the four bytes of a word, as a nibble (bit b = byte b).
+__device__ __forceinline__ uint32_t keep_nibble(uint32_t w, uint32_t t8) {
+  return static_cast<uint32_t>((w & 0xffu) >= t8) | (static_cast<uint32_t>(((w >> 8) & 0xffu) >= t8) << 1) |
+         (static_cast<uint32_t>(((w >> 16) & 0xffu) >= t8) << 2) | (static_cast<uint32_t>((w >> 24) >= t8) << 3);
+}
+
+// OR `n` bits of `bits` into the 128-bit (lo, hi) at column c (c may be
+// negative: columns below 0 and above 127 are dropped).
+__device__ __forceinline__ void put_bits(uint64_t& lo, uint64_t& hi, uint32_t bits, int n, int c) {
+  if (c < 0) {
+    if (-c >= n) return;
+    bits >>= -c;
+    c = 0;
+  }
+  const uint64_t v = static_cast<uint64_t>(bits);
+  if (c < 64) {
+    lo |= v << c;
+    if (c + n > 64) hi |= v >> (64 - c);
+  } else if (c < 128) {
+    hi |= v << (c - 64);
+  }
 }
 
 // Forward (lane = query i; lanes i and i ^ 1 share blocks): keys
-// [k0, k0 + nkeys), bit c of (lo, hi) = key k0 + c (c < 128). Four
-// independent Philox blocks are in flight per step (their 7-round chains
-// are latency-bound otherwise).
-__device__ __forceinline__ void fwd_keep_bits(const DropoutSite& site, uint32_t t16, int start, int i, int h, int k0,
+// [k0, k0 + nkeys), bit c of (lo, hi) = key k0 + c (c < 128).
+__device__ __forceinline__ void fwd_keep_bits(const DropoutSite& site, uint32_t t8, int start, int i, int h, int k0,
                                               int nkeys, int lane, uint64_t& lo, uint64_t& hi) {
   lo = hi = 0ull;
   const bool odd = (lane & 1) != 0;
   const uint32_t a = static_cast<uint32_t>(start + (i & ~1));
-  const int b0 = k0 >> 2;
-  const int nb = ((k0 + nkeys - 1) >> 2) - b0 + 1;  // blocks covering the keys (<= 33)
   const uint32_t hb = static_cast<uint32_t>(h) << 16;
+  const int b0 = k0 >> 3;
+  const int nb = ((k0 + nkeys - 1) >> 3) - b0 + 1;  // blocks covering the keys (<= 17)
 #pragma unroll 1
-  for (int t0 = 0; t0 < nb; t0 += 8) {
-    Philox4 r[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u)
-      r[u] = dropout_block(site, a, hb | static_cast<uint32_t>(b0 + t0 + 2 * u + (odd ? 1 : 0)));
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int t = t0 + 2 * u;
-      if (t >= nb) break;
-      // even lane keeps (x, y) of block t and sends (z, w); odd lane keeps
-      // (z, w) of block t + 1 and sends (x, y).
-      const uint32_t s0 = __shfl_xor_sync(0xffffffffu, odd ? r[u].x : r[u].z, 1);
-      const uint32_t s1 = __shfl_xor_sync(0xffffffffu, odd ? r[u].y : r[u].w, 1);
-      // this lane's row: words of block t (keys 4 (b0 + t) + 0..3) and block t + 1
-      const uint32_t wa0 = odd ? s0 : r[u].x, wa1 = odd ? s1 : r[u].y;
-      const uint32_t wb0 = odd ? r[u].z : s0, wb1 = odd ? r[u].w : s1;
-      const int c0 = 4 * (b0 + t) - k0;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const uint32_t w = e < 2 ? wa0 : (e < 4 ? wa1 : (e < 6 ? wb0 : wb1));
-        const int c = c0 + e;
-        if (c >= 0 && c < 128 && keep16(w, e & 1, t16)) {
-          if (c < 64) lo |= 1ull << c;
-          else hi |= 1ull << (c - 64);
-        }
-      }
-    }
+  for (int t = 0; t < nb; t += 2) {
+    const Philox4 r = dropout_block(site, a, hb | static_cast<uint32_t>(b0 + t + (odd ? 1 : 0)));
+    // even lane keeps (x, y) of block t and sends (z, w); odd lane keeps
+    // (z, w) of block t + 1 and sends (x, y).
+    const uint32_t s0 = __shfl_xor_sync(0xffffffffu, odd ? r.x : r.z, 1);
+    const uint32_t s1 = __shfl_xor_sync(0xffffffffu, odd ? r.y : r.w, 1);
+    // this lane's row: keys 8 (b0 + t) + 0..7 (block t) and + 8..15 (block t + 1)
+    const uint32_t wa0 = odd ? s0 : r.x, wa1 = odd ? s1 : r.y;
+    const uint32_t wb0 = odd ? r.z : s0, wb1 = odd ? r.w : s1;
+    const uint32_t bits = keep_nibble(wa0, t8) | (keep_nibble(wa1, t8) << 4) | (keep_nibble(wb0, t8) << 8) |
+                          (keep_nibble(wb1, t8) << 12);
+    put_bits(lo, hi, bits, 16, 8 * (b0 + t) - k0);
   }
 }
 
-// Backward (lane = key j; the four lanes of keys 4k .. 4k + 3 share blocks,
-// each generating every fourth query pair): queries [q0, q0 + nq), bit c =
-// query q0 + c (c < 64). Up to three blocks per lane are in flight.
-__device__ __forceinline__ uint64_t bwd_keep_bits(const DropoutSite& site, uint32_t t16, int start, int j, int h,
+// Backward (lane = key j; the eight lanes of keys 8k .. 8k + 7 share blocks,
+// each generating every eighth query pair and broadcasting its 16 decisions):
+// queries [q0, q0 + nq), bit c = query q0 + c (c < 64).
+__device__ __forceinline__ uint64_t bwd_keep_bits(const DropoutSite& site, uint32_t t8, int start, int j, int h,
                                                   int q0, int nq, int lane) {
-  uint64_t keep = 0ull;
-  const int r = lane & 3, src0 = lane & ~3;
-  const bool wsel = ((j >> 1) & 1) != 0;  // word y / w (keys 4k + 2, 4k + 3) instead of x / z
-  const int half = j & 1;
-  const uint32_t bcol = (static_cast<uint32_t>(h) << 16) | static_cast<uint32_t>(j >> 2);
+  uint64_t keep = 0ull, unused = 0ull;
+  const int r = lane & 7, src0 = lane & ~7, koff = j & 7;
+  const uint32_t bcol = (static_cast<uint32_t>(h) << 16) | static_cast<uint32_t>(j >> 3);
   const int a0 = q0 >> 1;
   const int npairs = ((q0 + nq - 1) >> 1) - a0 + 1;  // <= 33
 #pragma unroll 1
-  for (int t0 = 0; t0 < npairs; t0 += 12) {
-    Philox4 blk[3];
+  for (int t0 = 0; t0 < npairs; t0 += 8) {
+    const Philox4 blk = dropout_block(site, static_cast<uint32_t>(start + 2 * (a0 + t0 + r)), bcol);
+    // bit (8 * (query & 1) + key offset) of the pair's 16 decisions
+    const uint32_t dec = keep_nibble(blk.x, t8) | (keep_nibble(blk.y, t8) << 4) | (keep_nibble(blk.z, t8) << 8) |
+                         (keep_nibble(blk.w, t8) << 12);
+    uint32_t g = 0u;  // 16 queries: bit 2 s = even query of pair s, bit 2 s + 1 = odd
 #pragma unroll
-    for (int u = 0; u < 3; ++u)
-      blk[u] = dropout_block(site, static_cast<uint32_t>(start + 2 * (a0 + t0 + 4 * u + r)), bcol);
-#pragma unroll
-    for (int u = 0; u < 3; ++u) {
-      const int t = t0 + 4 * u;
-      if (t >= npairs) break;
-#pragma unroll
-      for (int s = 0; s < 4; ++s) {
-        // A shuffle sends the source lane's register, so fetch all four words
-        // and pick this key's pair here.
-        const uint32_t x = __shfl_sync(0xffffffffu, blk[u].x, src0 + s);
-        const uint32_t y = __shfl_sync(0xffffffffu, blk[u].y, src0 + s);
-        const uint32_t z = __shfl_sync(0xffffffffu, blk[u].z, src0 + s);
-        const uint32_t w = __shfl_sync(0xffffffffu, blk[u].w, src0 + s);
-        const uint32_t ev = wsel ? y : x, od = wsel ? w : z;
-        const int c = 2 * (a0 + t + s) - q0;  // even query of the pair
-        if (c >= 0 && c < 64 && keep16(ev, half, t16)) keep |= 1ull << c;
-        if (c + 1 >= 0 && c + 1 < 64 && keep16(od, half, t16)) keep |= 1ull << (c + 1);
-      }
+    for (int s = 0; s < 8; ++s) {
+      const uint32_t d = __shfl_sync(0xffffffffu, dec, src0 + s);
+      g |= ((d >> koff) & 1u) << (2 * s);
+      g |= ((d >> (8 + koff)) & 1u) << (2 * s + 1);
     }
+    put_bits(keep, unused, g, 16, 2 * (a0 + t0) - q0);
   }
   return keep;
 }
@@ -308,8 +299,8 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
   const float* lut_h =
       p.rel_lut == nullptr ? nullptr : p.rel_lut + static_cast<int64_t>(h) * (2 * p.lut_len - 1) + (p.lut_len - 1);
   const float inv_scale = 1.f / p.scale;
-  const Drop16 dr = drop16(p.pdrop);
-  const bool drop = dr.t16 != 0u;
+  const Drop8 dr = drop8(p.pdrop);
+  const bool drop = dr.t8 != 0u;
 
   float m_run = -INFINITY, l_run = 0.f;  // in scaled base-2 units
   bool ok = true, mma_issued = false;
@@ -346,7 +337,7 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
     // copies and the S MMA are in flight.
     uint64_t keep_lo = ~0ull, keep_hi = ~0ull;
     __syncwarp();
-    if (drop && warp_live) fwd_keep_bits(p.pdrop, dr.t16, start, i, h, k0, n16, lane, keep_lo, keep_hi);
+    if (drop && warp_live) fwd_keep_bits(p.pdrop, dr.t8, start, i, h, k0, n16, lane, keep_lo, keep_hi);
     if (tid == 0) {
       if (ok0) ok0 = mbar_wait(&bars[kBarS], ph, p.timeout_ns);
       if (!ok0) report_status(p.status, kStatusTimeoutMma);
@@ -627,8 +618,8 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
     vis_lo = max(vis_lo, key - p.window);
     vis_hi = min(vis_hi, key + p.window + 1);
   }
-  const Drop16 dr = drop16(p.pdrop);
-  const bool drop = dr.t16 != 0u;
+  const Drop8 dr = drop8(p.pdrop);
+  const bool drop = dr.t8 != 0u;
   const bool general = drop || p.rel_lut != nullptr;
 
   bool ok = true, mma_issued = false;
@@ -673,7 +664,7 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
     // S^T / dP^T MMAs are in flight.
     uint64_t keep = ~0ull;
     __syncwarp();
-    if (drop && warp_live) keep = bwd_keep_bits(p.pdrop, dr.t16, start, key, hq, q0, nq16, lane);
+    if (drop && warp_live) keep = bwd_keep_bits(p.pdrop, dr.t8, start, key, hq, q0, nq16, lane);
     if (tid == 0) {
       if (ok0) ok0 = mbar_wait(&bars[kBarS], ph, p.timeout_ns);
       if (!ok0) report_status(p.status, kStatusTimeoutMma);
