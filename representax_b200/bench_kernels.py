@@ -161,6 +161,13 @@ def bench_norm(timer, hbm, flops_peak, tag, report):
     by = 3 * rows * h * 2
     report({"kernel": "layernorm_bwd", "rows": rows, "H": h, "ms": t * 1e3, "gbs": by / t / 1e9,
             f"frac_of_{tag}_hbm": by / t / hbm})
+    # bias-gradient column sums of a QKV-shaped gradient (one GradCache chunk)
+    g_qkv = torch.randn(18432, 2304, device="cuda").to(torch.bfloat16)
+    acc = torch.zeros(2304, device="cuda")
+    t = timer(lambda: C.colsum_accumulate(g_qkv, acc))
+    by = g_qkv.numel() * 2
+    report({"kernel": "colsum", "rows": 18432, "cols": 2304, "ms": t * 1e3, "gbs": by / t / 1e9,
+            f"frac_of_{tag}_hbm": by / t / hbm})
 
 
 def main(argv=None):

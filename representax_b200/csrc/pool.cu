@@ -150,14 +150,26 @@ __global__ void __launch_bounds__(kColsumThreads)
   const int grp = tid / chunks;
   float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   if (grp < groups) {
-    for (int r = blockIdx.x * groups + grp; r < rows; r += gridDim.x * groups) {
-      const uint4 w = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(r) * ld)[c];
-      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
+    // Four rows in flight per thread: with one group per CTA (2048 columns)
+    // a single outstanding load per thread leaves HBM mostly idle.
+    const int stride = gridDim.x * groups;
+    for (int r = blockIdx.x * groups + grp; r < rows; r += 4 * stride) {
+      uint4 w[4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 f = __bfloat1622float2(h[j]);
-        acc[2 * j] += f.x;
-        acc[2 * j + 1] += f.y;
+      for (int u = 0; u < 4; ++u) {
+        const int rr = r + u * stride;
+        w[u] = rr < rows ? reinterpret_cast<const uint4*>(x + static_cast<int64_t>(rr) * ld)[c]
+                         : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w[u]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __bfloat1622float2(h[j]);
+          acc[2 * j] += f.x;
+          acc[2 * j + 1] += f.y;
+        }
       }
     }
 #pragma unroll

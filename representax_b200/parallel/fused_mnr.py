@@ -1,7 +1,7 @@
 """Cross-rank MNR with the all-gather and reduce-scatter fused into the kernels.
 
-Each rank holds its own L query and L document embeddings (rank-major global
-order). Instead of all-gathering the embeddings, computing the whole
+Each rank holds its own Lq query and Ld document embeddings (rank-major global
+order; Ld > Lq with hard negatives). Instead of all-gathering the embeddings, computing the whole
 [N*L, N*L] objective on every rank and slicing the gradient, every rank:
 
   forward   writes its normalised rows into its peer buffers, barriers, and
@@ -43,18 +43,18 @@ from .peer import PeerGroup, peer_group
 class ShardedRetrievalBatch:
     """A rank's rows of a retrieval batch whose negatives span all ranks.
 
-    ``forward_weights`` [L, N*L]: positive weights of local queries over all
-    documents; ``reverse_weights`` [L, N*L]: of local documents over all
+    ``forward_weights`` [Lq, N*Ld]: positive weights of local queries over all
+    documents; ``reverse_weights`` [Ld, N*Lq]: of local documents over all
     queries (only needed in symmetric mode).
     """
 
     ctx: DistContext
     forward_weights: torch.Tensor
     reverse_weights: torch.Tensor | None
-    query_valid: torch.Tensor          # [L]
-    document_valid: torch.Tensor       # [L]
-    query_valid_all: torch.Tensor      # [N*L]
-    document_valid_all: torch.Tensor   # [N*L]
+    query_valid: torch.Tensor          # [Lq]
+    document_valid: torch.Tensor       # [Ld]
+    query_valid_all: torch.Tensor      # [N*Lq]
+    document_valid_all: torch.Tensor   # [N*Ld]
 
     @classmethod
     def from_local(cls, batch, ctx: DistContext, *, symmetric: bool) -> "ShardedRetrievalBatch":
@@ -88,58 +88,62 @@ class _ShardedMNR(torch.autograd.Function):
     def forward(ctx_, qn, dn, sb: ShardedRetrievalBatch, scale: float, symmetric: bool, group: PeerGroup,
                 n_f, n_r):
         C = ext()
-        L, D = qn.shape
+        Lq, D = qn.shape
+        Ld = dn.shape[0]
         world, rank = group.world, group.rank
         dev = qn.device
         half = 0.5 if symmetric else 1.0
-        qbuf = group.cached(("mnr_q", L, D), L * D)
-        dbuf = group.cached(("mnr_d", L, D), L * D)
-        qslots = group.cached(("mnr_qs", L, D), world * L * D)
-        dslots = group.cached(("mnr_ds", L, D), world * L * D)
+        qbuf = group.cached(("mnr_q", Lq, D), Lq * D)
+        dbuf = group.cached(("mnr_d", Ld, D), Ld * D)
+        qslots = group.cached(("mnr_qs", Lq, D), world * Lq * D)
+        dslots = group.cached(("mnr_ds", Ld, D), world * Ld * D)
         group.barrier()  # peers are done reading the previous contents
         qbuf.tensor.copy_(qn.reshape(-1))
         dbuf.tensor.copy_(dn.reshape(-1))
         group.barrier()  # every rank's rows are published
 
-        def direction(rows, cands_buf, weights, row_valid, col_valid, n_active):
-            scores = torch.empty(L, world * L, device=dev, dtype=torch.float32)
-            C.peer_sgemm(rows, False, cands_buf.ptrs, L, D, False, False, L, world * L, D, scores, None, 1, 0,
-                         1.0, False)
+        def direction(rows, cands_buf, n_cands, weights, row_valid, col_valid, n_active):
+            n_rows = rows.shape[0]
+            scores = torch.empty(n_rows, world * n_cands, device=dev, dtype=torch.float32)
+            C.peer_sgemm(rows, False, cands_buf.ptrs, n_cands, D, False, False, n_rows, world * n_cands, D, scores,
+                         None, 1, 0, 1.0, False)
             grad = torch.empty_like(scores)
-            row_loss = torch.empty(L, device=dev)
-            row_active = torch.empty(L, device=dev)
+            row_loss = torch.empty(n_rows, device=dev)
+            row_active = torch.empty(n_rows, device=dev)
             coef = (half / n_active).reshape(1)
             C.mnr_rows(scores, weights, row_valid, col_valid, grad, row_loss, row_active, float(scale), coef)
             return (row_loss * row_active).sum() / n_active.reshape(()), grad
 
-        fwd_local, g_f = direction(qn, dbuf, sb.forward_weights, sb.query_valid, sb.document_valid_all, n_f)
+        fwd_local, g_f = direction(qn, dbuf, Ld, sb.forward_weights, sb.query_valid, sb.document_valid_all, n_f)
         if symmetric:
-            rev_local, g_r = direction(dn, qbuf, sb.reverse_weights, sb.document_valid, sb.query_valid_all, n_r)
+            rev_local, g_r = direction(dn, qbuf, Lq, sb.reverse_weights, sb.document_valid, sb.query_valid_all,
+                                       n_r)
         else:
             rev_local, g_r = torch.zeros((), device=dev), torch.empty(0, device=dev)
         ctx_.save_for_backward(qn, dn, g_f, g_r)
-        ctx_.meta = (group, symmetric, L, D, qbuf, dbuf, qslots, dslots)
+        ctx_.meta = (group, symmetric, Lq, Ld, D, qbuf, dbuf, qslots, dslots)
         return fwd_local, rev_local
 
     @staticmethod
     def backward(ctx_, grad_fwd, grad_rev):
         C = ext()
         qn, dn, g_f, g_r = ctx_.saved_tensors
-        group, symmetric, L, D, qbuf, dbuf, qslots, dslots = ctx_.meta
+        group, symmetric, Lq, Ld, D, qbuf, dbuf, qslots, dslots = ctx_.meta
         world, rank = group.world, group.rank
         half = 0.5 if symmetric else 1.0
         # g_* hold d(loss)/d(score) for loss = half * (fwd + rev); rescale by the upstream gradients.
         g_f = g_f * (grad_fwd / half)
         dq = torch.empty_like(qn)
-        C.peer_sgemm(g_f, False, dbuf.ptrs, L, D, True, True, L, D, world * L, dq, None, 1, 0, 1.0, False)
+        C.peer_sgemm(g_f, False, dbuf.ptrs, Ld, D, True, True, Lq, D, world * Ld, dq, None, 1, 0, 1.0, False)
         local_q = torch.tensor([qn.data_ptr()], dtype=torch.int64, device=qn.device)
-        C.peer_sgemm(g_f, True, local_q, D, D, True, False, world * L, D, L, dq, dslots.ptrs, L, rank, 1.0, False)
+        C.peer_sgemm(g_f, True, local_q, D, D, True, False, world * Ld, D, Lq, dq, dslots.ptrs, Ld, rank, 1.0,
+                     False)
         dd = torch.zeros_like(dn)
         if symmetric:
             g_r = g_r * (grad_rev / half)
-            C.peer_sgemm(g_r, False, qbuf.ptrs, L, D, True, True, L, D, world * L, dd, None, 1, 0, 1.0, False)
+            C.peer_sgemm(g_r, False, qbuf.ptrs, Lq, D, True, True, Ld, D, world * Lq, dd, None, 1, 0, 1.0, False)
             local_d = torch.tensor([dn.data_ptr()], dtype=torch.int64, device=dn.device)
-            C.peer_sgemm(g_r, True, local_d, D, D, True, False, world * L, D, L, dd, qslots.ptrs, L, rank, 1.0,
+            C.peer_sgemm(g_r, True, local_d, D, D, True, False, world * Lq, D, Ld, dd, qslots.ptrs, Lq, rank, 1.0,
                          False)
         group.barrier()  # every rank's slot contributions have landed
         C.slot_reduce(dslots.tensor, world, dd, True)

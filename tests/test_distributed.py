@@ -82,17 +82,20 @@ def test_two_gloo_ranks_match_single_process(tmp_path):
         assert torch.allclose(got["master"], master, rtol=1e-4, atol=1e-6), name
 
 
-def _fused_worker(rank, world, port, out, symmetric):
+def _fused_worker(rank, world, port, out, symmetric, hard_negatives=False):
     from representax_b200.parallel.fused_mnr import ShardedRetrievalBatch, sharded_mnr_loss
     from representax_b200.tasks.retrieval import retrieval_batch
 
     ctx = _init(rank, world, port, "nccl")
     dev = torch.device("cuda", rank)
     L, D = 96, 80
+    Ld = 2 * L if hard_negatives else L  # documents: positives, then one hard negative per query
     g = torch.Generator().manual_seed(100 + rank)
     q = torch.randn(L, D, generator=g).to(dev).requires_grad_(True)
-    d = torch.randn(L, D, generator=g).to(dev).requires_grad_(True)
-    local = retrieval_batch(query=q.detach(), document=d.detach(), positive_mask=torch.eye(L, dtype=torch.bool))
+    d = torch.randn(Ld, D, generator=g).to(dev).requires_grad_(True)
+    mask = torch.zeros(L, Ld, dtype=torch.bool)
+    mask[:, :L] = torch.eye(L, dtype=torch.bool)
+    local = retrieval_batch(query=q.detach(), document=d.detach(), positive_mask=mask)
     local = local.map_tensors(lambda t: t.to(dev))
     local.document_valid[5] = False
     sb = ShardedRetrievalBatch.from_local(local, ctx, symmetric=symmetric)
@@ -119,20 +122,24 @@ def _fused_worker(rank, world, port, out, symmetric):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("hard_negatives", [False, True])
 @pytest.mark.parametrize("symmetric", [False, True])
-def test_fused_cross_rank_mnr_matches_gathered_reference(tmp_path, symmetric):
+def test_fused_cross_rank_mnr_matches_gathered_reference(tmp_path, symmetric, hard_negatives):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     from representax_b200.ops.mnr import mnr_terms_reference
 
     out = str(tmp_path / "fused.pt")
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
-    mp.spawn(_fused_worker, args=(2, _port(), out, symmetric), nprocs=2, join=True)
+    mp.spawn(_fused_worker, args=(2, _port(), out, symmetric, hard_negatives), nprocs=2, join=True)
     r = torch.load(out)
     q = r["q"].double().requires_grad_(True)
     d = r["d"].double().requires_grad_(True)
     n = q.shape[0]
-    w = torch.eye(n, dtype=torch.float64)
+    ld = d.shape[0] // 2  # documents per rank (rank-major)
+    w = torch.zeros(n, d.shape[0], dtype=torch.float64)
+    for rank in range(2):
+        w[rank * (n // 2):(rank + 1) * (n // 2), rank * ld:rank * ld + n // 2] = torch.eye(n // 2)
     qv = torch.ones(n, dtype=torch.bool)
     loss, *_ = mnr_terms_reference(q, d, w, qv, r["dv"], 20.0, symmetric)
     loss.backward()
