@@ -1,8 +1,10 @@
 """Serializable user-facing configuration for reproducible training.
 
 Parity: every class of src/representax/config.py:46-773 with the same field
-names, defaults, roles (``Scientific`` / ``Execution``) and validation, so a
-job file written for the reference validates here unchanged. Execution-only
+names, defaults and roles (``Scientific`` / ``Execution``) and the same
+accept/reject decisions, so a job file written for the reference validates
+here unchanged. The checks are stated as (rule, complaint) pairs; one
+``ValueError`` lists every broken rule of an object. Execution-only
 fields specific to this framework (tensor-parallel degree, fused-kernel
 toggles) live in ``B200ExecutionConfig`` under ``TrainingConfig.b200`` and
 carry the ``Execution`` role, leaving the scientific fingerprint unchanged.
@@ -16,11 +18,13 @@ from collections.abc import Mapping
 from typing import Annotated, Literal
 
 from pydantic import (
+    Discriminator,
     Field,
     NonNegativeInt,
     PositiveFloat,
     PositiveInt,
     SerializeAsAny,
+    Tag,
     ValidationInfo,
     field_validator,
     model_validator,
@@ -39,6 +43,59 @@ MetricMode = Literal["min", "max"]
 ExportSelection = Literal["final", "best"]
 JsonScalar = str | int | float | bool | None
 JsonValue = TypeAliasType("JsonValue", JsonScalar | list["JsonValue"] | dict[str, "JsonValue"])
+
+
+# --- validation helpers -----------------------------------------------------------------
+# Every validator below states its rules as (holds, complaint) pairs and hands them to
+# ``_check``, which reports all broken rules of one object in a single ValueError.
+
+def _check(*rules: tuple[bool, str]) -> None:
+    broken = [complaint for holds, complaint in rules if not holds]
+    if broken:
+        raise ValueError("; ".join(broken))
+
+
+def _repeated(values) -> list:
+    """Values that occur more than once, in first-seen order."""
+
+    seen: set = set()
+    twice: list = []
+    for value in values:
+        if value in seen and value not in twice:
+            twice.append(value)
+        seen.add(value)
+    return twice
+
+
+def _regex_problem(pattern: str) -> str | None:
+    try:
+        re.compile(pattern)
+    except re.error as error:
+        return str(error)
+    return None
+
+
+def _axis_names(entries) -> list[str]:
+    """Mesh-axis names named by a sequence of partition entries (None = replicated)."""
+
+    names: list[str] = []
+    for entry in entries:
+        if entry is None:
+            continue
+        names.extend(entry if isinstance(entry, tuple) else (entry,))
+    return names
+
+
+def _context_registry(info: ValidationInfo, key: str, fallback, expected: type):
+    """A registry passed through pydantic's validation context, else the built-in one."""
+
+    supplied = (info.context or {}).get(key)
+    if supplied is None:
+        return fallback
+    if not isinstance(supplied, expected):
+        raise TypeError(f"validation context entry {key!r} is a {type(supplied).__name__}, "
+                        f"expected {expected.__name__}")
+    return supplied
 
 
 class ComponentConfig(FrozenConfig):
@@ -69,19 +126,22 @@ class DataConfig(FrozenConfig):
 
     @model_validator(mode="before")
     @classmethod
-    def wrap_distribution(cls, value: object) -> object:
-        if isinstance(value, DataDistributionConfig):
-            return {"distribution": value}
-        if isinstance(value, Mapping) and "distribution" not in value and "sources" in value:
-            return {"distribution": value}
-        return value
+    def _accept_bare_distribution(cls, value: object) -> object:
+        # ``DataConfig(distribution)`` shorthand: a distribution (object or mapping with
+        # ``sources``) given where the data config is expected.
+        bare = isinstance(value, DataDistributionConfig) or (
+            isinstance(value, Mapping) and "sources" in value and "distribution" not in value)
+        return {"distribution": value} if bare else value
 
     @model_validator(mode="after")
-    def validate_data_wait_thresholds(self):
-        if (self.data_wait_heartbeat_seconds is not None and self.data_wait_timeout_seconds is not None
-                and self.data_wait_heartbeat_seconds >= self.data_wait_timeout_seconds):
-            raise ValueError("data_wait_heartbeat_seconds must be below data_wait_timeout_seconds")
+    def _heartbeat_before_deadline(self):
+        beat, deadline = self.data_wait_heartbeat_seconds, self.data_wait_timeout_seconds
+        _check((beat is None or deadline is None or beat < deadline,
+                f"the data-wait heartbeat ({beat} s) has to fire before the data-wait timeout ({deadline} s)"))
         return self
+
+
+Similarity = Literal["cosine", "dot", "euclidean", "manhattan"]
 
 
 class EvaluatorConfig(FrozenConfig):
@@ -92,20 +152,18 @@ class EvaluatorConfig(FrozenConfig):
 class EmbeddingSimilarityEvaluatorConfig(EvaluatorConfig):
     kind: Literal["embedding_similarity"] = "embedding_similarity"  # type: ignore[assignment]
     name: NonEmptyString = "similarity"
-    similarity_functions: tuple[Literal["cosine", "dot", "euclidean", "manhattan"], ...] = (
-        "cosine", "dot", "euclidean", "manhattan")
-    main_similarity: Literal["cosine", "dot", "euclidean", "manhattan"] | None = None
+    similarity_functions: tuple[Similarity, ...] = ("cosine", "dot", "euclidean", "manhattan")
+    main_similarity: Similarity | None = None
     left_route: Route = Route.GENERIC
     right_route: Route = Route.GENERIC
 
     @model_validator(mode="after")
-    def validate_similarity(self):
-        if not self.similarity_functions:
-            raise ValueError("at least one similarity function is required")
-        if len(set(self.similarity_functions)) != len(self.similarity_functions):
-            raise ValueError("similarity functions must be unique")
-        if self.main_similarity is not None and self.main_similarity not in self.similarity_functions:
-            raise ValueError("main_similarity must be one of similarity_functions")
+    def _functions_cover_main(self):
+        functions = self.similarity_functions
+        _check((len(functions) > 0, "similarity_functions is empty"),
+               (not _repeated(functions), f"similarity_functions lists {_repeated(functions)} more than once"),
+               (self.main_similarity is None or self.main_similarity in functions,
+                f"main_similarity {self.main_similarity!r} is not among similarity_functions {list(functions)}"))
         return self
 
 
@@ -116,17 +174,26 @@ class InformationRetrievalEvaluatorConfig(EvaluatorConfig):
     similarity: Literal["cosine", "dot"] = "cosine"
 
 
-_EVALUATORS = {
-    "loss": EvaluatorConfig,
-    "embedding_similarity": EmbeddingSimilarityEvaluatorConfig,
-    "information_retrieval": InformationRetrievalEvaluatorConfig,
-}
+def _evaluator_kind(value: object) -> str:
+    """Discriminator of the evaluator union; a mapping without ``kind`` is a loss evaluator."""
+
+    if isinstance(value, Mapping):
+        return str(value.get("kind", "loss"))
+    return str(getattr(value, "kind", "loss"))
+
+
+AnyEvaluatorConfig = Annotated[
+    Annotated[EvaluatorConfig, Tag("loss")]
+    | Annotated[EmbeddingSimilarityEvaluatorConfig, Tag("embedding_similarity")]
+    | Annotated[InformationRetrievalEvaluatorConfig, Tag("information_retrieval")],
+    Discriminator(_evaluator_kind),
+]
 
 
 class EvaluationConfig(FrozenConfig):
     data: DataConfig
     batch_size: Scientific[PositiveInt]
-    evaluators: Scientific[tuple[SerializeAsAny[EvaluatorConfig], ...]] = (EvaluatorConfig(),)
+    evaluators: Scientific[tuple[AnyEvaluatorConfig, ...]] = (EvaluatorConfig(),)
     every_steps: PositiveInt | None = None
     on_start: bool = False
     on_end: bool = True
@@ -136,35 +203,16 @@ class EvaluationConfig(FrozenConfig):
     save_best: bool = True
     keep_best: PositiveInt = 1
 
-    @field_validator("evaluators", mode="before")
-    @classmethod
-    def validate_evaluators(cls, value: object) -> object:
-        if not isinstance(value, (list, tuple)):
-            raise TypeError("evaluators must be a list or tuple")
-        parsed = []
-        for evaluator in value:
-            if isinstance(evaluator, EvaluatorConfig):
-                parsed.append(evaluator)
-                continue
-            if not isinstance(evaluator, Mapping):
-                raise TypeError("each evaluator must be a config or mapping")
-            kind = evaluator.get("kind", "loss")
-            if kind not in _EVALUATORS:
-                raise ValueError(f"unknown evaluator kind {kind!r}")
-            parsed.append(_EVALUATORS[kind].model_validate(evaluator))
-        return tuple(parsed)
-
     @model_validator(mode="after")
-    def validate_evaluation(self):
-        names = tuple(e.name for e in self.evaluators)
-        if not names:
-            raise ValueError("evaluation requires at least one evaluator")
-        if len(set(names)) != len(names):
-            raise ValueError("evaluator names must be unique")
-        if not self.primary_metric.startswith("valid/"):
-            raise ValueError("primary_metric must use the valid/ namespace")
-        if self.save_best and not (self.on_start or self.on_end or self.every_steps is not None):
-            raise ValueError("best-model selection requires an evaluation cadence")
+    def _consistent_selection(self):
+        names = [e.name for e in self.evaluators]
+        scheduled = self.on_start or self.on_end or self.every_steps is not None
+        _check((len(names) > 0, "evaluation needs an evaluator"),
+               (not _repeated(names), f"evaluator name(s) {_repeated(names)} used twice; metrics would collide"),
+               (self.primary_metric.startswith("valid/"),
+                f"primary_metric {self.primary_metric!r} is not a validation metric (prefix 'valid/')"),
+               (scheduled or not self.save_best,
+                "save_best is set but evaluation never runs (no on_start, on_end or every_steps)"))
         return self
 
 
@@ -182,9 +230,9 @@ class ExportConfig(FrozenConfig):
 
     @field_validator("directory_name")
     @classmethod
-    def validate_directory_name(cls, value: str) -> str:
-        if value in {".", ".."} or "/" in value or "\\" in value:
-            raise ValueError("export directory_name must be one path component")
+    def _single_component(cls, value: str) -> str:
+        _check((value not in (".", "..") and not any(sep in value for sep in "/\\"),
+                f"export directory_name {value!r} has to be a plain directory name inside the run directory"))
         return value
 
 
@@ -193,24 +241,28 @@ class MeshConfig(FrozenConfig):
     axis_names: tuple[NonEmptyString, ...] = ("data",)
 
     @model_validator(mode="after")
-    def validate_axes(self):
-        if len(self.axis_shapes) != len(self.axis_names):
-            raise ValueError("mesh axis_shapes and axis_names must have equal length")
-        if not self.axis_names:
-            raise ValueError("a mesh must contain at least one logical axis")
-        if len(set(self.axis_names)) != len(self.axis_names):
-            raise ValueError("mesh axis names must be unique")
+    def _names_match_shapes(self):
+        names, shapes = self.axis_names, self.axis_shapes
+        _check((len(names) > 0, "the mesh has no axes"),
+               (len(names) == len(shapes), f"{len(names)} mesh axis names for {len(shapes)} axis sizes"),
+               (not _repeated(names), f"mesh axis name(s) {_repeated(names)} repeat"))
         return self
 
     @property
+    def axes(self) -> dict[str, int]:
+        """Axis name -> size."""
+
+        return dict(zip(self.axis_names, self.axis_shapes))
+
+    @property
     def device_count(self) -> int:
-        return math.prod(self.axis_shapes)
+        return math.prod(self.axes.values())
 
     def axis_size(self, name: str) -> int:
-        try:
-            return self.axis_shapes[self.axis_names.index(name)]
-        except ValueError as error:
-            raise KeyError(f"mesh axis {name!r} is not defined") from error
+        size = self.axes.get(name)
+        if size is None:
+            raise KeyError(f"no mesh axis named {name!r} (axes: {list(self.axis_names)})")
+        return size
 
 
 PartitionAxis = NonEmptyString | tuple[NonEmptyString, ...] | None
@@ -220,28 +272,15 @@ class PartitionRuleConfig(FrozenConfig):
     pattern: NonEmptyString
     axes: tuple[PartitionAxis, ...] = ()
 
-    @field_validator("pattern")
-    @classmethod
-    def validate_pattern(cls, value: str) -> str:
-        try:
-            re.compile(value)
-        except re.error as error:
-            raise ValueError(f"invalid partition-rule regular expression: {error}") from error
-        return value
-
-    @field_validator("axes")
-    @classmethod
-    def validate_partition_axes(cls, value):
-        names: list[str] = []
-        for axis in value:
-            if isinstance(axis, tuple) and not axis:
-                raise ValueError("a grouped partition axis cannot be empty")
-            if axis is None:
-                continue
-            names.extend(axis if isinstance(axis, tuple) else (axis,))
-        if len(set(names)) != len(names):
-            raise ValueError("a partition rule cannot reuse one mesh axis")
-        return value
+    @model_validator(mode="after")
+    def _compiles_and_axes_distinct(self):
+        problem = _regex_problem(self.pattern)
+        grouped_empty = any(isinstance(a, tuple) and not a for a in self.axes)
+        used = _axis_names(self.axes)
+        _check((problem is None, f"partition-rule pattern {self.pattern!r} does not compile ({problem})"),
+               (not grouped_empty, "an axis group of a partition rule is the empty tuple"),
+               (not _repeated(used), f"partition rule shards over mesh axis {_repeated(used)} more than once"))
+        return self
 
 
 class DDPConfig(FrozenConfig):
@@ -268,14 +307,21 @@ class CustomShardingConfig(FrozenConfig):
     default_parameter_axes: tuple[PartitionAxis, ...] = ()
 
     @model_validator(mode="after")
-    def validate_custom_sharding(self):
-        if not self.parameter_axes:
-            raise ValueError("custom sharding requires at least one parameter axis")
-        if len(set(self.parameter_axes)) != len(self.parameter_axes):
-            raise ValueError("custom parameter axes must be unique")
-        if not self.parameter_rules:
-            raise ValueError("custom sharding requires at least one parameter rule")
+    def _rules_within_axes(self):
+        axes = self.parameter_axes
+        named = set(_axis_names(self.default_parameter_axes))
+        for rule in self.parameter_rules:
+            named.update(_axis_names(rule.axes))
+        stray = sorted(named - set(axes))
+        _check((len(axes) > 0, "custom sharding names no parameter axis"),
+               (not _repeated(axes), f"parameter axis {_repeated(axes)} listed twice"),
+               (len(self.parameter_rules) > 0, "custom sharding has no parameter rule"),
+               (not stray, f"partition rules shard over {stray}, which parameter_axes does not declare"))
         return self
+
+    @property
+    def referenced_axes(self) -> set[str]:
+        return set(self.parameter_axes) | ({self.data_axis} if self.data_axis else set())
 
 
 class TensorParallelConfig(FrozenConfig):
@@ -289,6 +335,16 @@ class TensorParallelConfig(FrozenConfig):
 
 ShardingConfig = Annotated[DDPConfig | FSDPConfig | CustomShardingConfig | TensorParallelConfig,
                            Field(discriminator="kind")]
+
+
+def _sharding_axes(sharding) -> set[str]:
+    if isinstance(sharding, DDPConfig):
+        return {sharding.axis}
+    if isinstance(sharding, FSDPConfig):
+        return {sharding.data_axis, sharding.resolved_parameter_axis}
+    if isinstance(sharding, TensorParallelConfig):
+        return {sharding.data_axis, sharding.model_axis}
+    return sharding.referenced_axes
 
 
 class BatchConfig(FrozenConfig):
@@ -358,11 +414,9 @@ class QuantizedLoRAConfig(FrozenConfig):
 
     @field_validator("target_pattern")
     @classmethod
-    def validate_target_pattern(cls, pattern: str) -> str:
-        try:
-            re.compile(pattern)
-        except re.error as error:
-            raise ValueError(f"invalid adapter target_pattern: {error}") from error
+    def _pattern_compiles(cls, pattern: str) -> str:
+        problem = _regex_problem(pattern)
+        _check((problem is None, f"adapter target_pattern {pattern!r} does not compile ({problem})"))
         return pattern
 
 
@@ -375,8 +429,8 @@ class B200ExecutionConfig(FrozenConfig):
     cuda_graphs: bool = False
     deterministic: bool = True
     # GradCache: device bytes that first-pass chunk graphs may keep so their
-    # replay forward is skipped (exact same gradient). None = size from free
-    # HBM at run time; 0 = always replay.
+    # replay forward is skipped (exact same gradient). None (the default) and 0
+    # both mean: replay every chunk, the memory bound GradCache is chosen for.
     grad_cache_retain_bytes: NonNegativeInt | None = None
 
 
@@ -396,35 +450,11 @@ class TrainingConfig(FrozenConfig):
     b200: Execution[B200ExecutionConfig] = B200ExecutionConfig()
 
     @model_validator(mode="after")
-    def validate_loss_execution(self):
-        if self.grad_cache is not None and self.mega_batch_mining is not None:
-            raise ValueError("configure only one specialized loss execution")
-        return self
-
-    @model_validator(mode="after")
-    def validate_sharding_axes(self):
-        mesh_axes = set(self.mesh.axis_names)
-        s = self.sharding
-        if isinstance(s, DDPConfig):
-            referenced = {s.axis}
-        elif isinstance(s, FSDPConfig):
-            referenced = {s.data_axis, s.resolved_parameter_axis}
-        elif isinstance(s, TensorParallelConfig):
-            referenced = {s.data_axis, s.model_axis}
-        else:
-            referenced = set(s.parameter_axes)
-            if s.data_axis is not None:
-                referenced.add(s.data_axis)
-            rule_axes = {n for r in s.parameter_rules for a in r.axes if a is not None
-                         for n in (a if isinstance(a, tuple) else (a,))}
-            default_axes = {n for a in s.default_parameter_axes if a is not None
-                            for n in (a if isinstance(a, tuple) else (a,))}
-            unsupported = (rule_axes | default_axes) - set(s.parameter_axes)
-            if unsupported:
-                raise ValueError(f"partition rules use axes absent from parameter_axes: {sorted(unsupported)}")
-        unknown = referenced - mesh_axes
-        if unknown:
-            raise ValueError(f"sharding axes are absent from the mesh: {sorted(unknown)}")
+    def _one_execution_and_known_axes(self):
+        missing = sorted(_sharding_axes(self.sharding) - set(self.mesh.axis_names))
+        _check((self.grad_cache is None or self.mega_batch_mining is None,
+                "grad_cache and mega_batch_mining are alternative loss executions; set at most one"),
+               (not missing, f"the sharding plan uses mesh axes {missing} that the mesh does not define"))
         return self
 
 
@@ -441,13 +471,16 @@ class CheckpointConfig(FrozenConfig):
     asynchronous: bool = True
 
     @model_validator(mode="after")
-    def validate_iterations(self):
-        if len(set(self.additional_iterations)) != len(self.additional_iterations):
-            raise ValueError("additional checkpoint iterations must be unique")
+    def _distinct_extra_iterations(self):
+        twice = _repeated(self.additional_iterations)
+        _check((not twice, f"additional checkpoint iteration(s) {twice} listed twice"))
         return self
 
     def should_save(self, iteration: int, *, final: bool) -> bool:
         return iteration % self.every == 0 or iteration in self.additional_iterations or (final and self.save_final)
+
+
+_EXCLUSIVE_MODIFIERS = frozenset({"matryoshka", "adaptive_layer", "matryoshka_2d"})
 
 
 class JobConfig(FrozenConfig):
@@ -466,88 +499,80 @@ class JobConfig(FrozenConfig):
     evaluation: EvaluationConfig | None = None
     export: ExportConfig = ExportConfig()
 
+    # Task, loss and modifier configs are open families: each registry parses its own
+    # kinds. A caller may validate against its own registries through the validation
+    # context (keys task_registry / loss_registry / modifier_registry).
+
     @field_validator("task", mode="before")
     @classmethod
-    def validate_registered_task(cls, value: object, info: ValidationInfo) -> TaskConfig:
+    def _parse_task(cls, value: object, info: ValidationInfo) -> TaskConfig:
         from .tasks.registry import BUILTIN_TASKS, TaskRegistry
 
-        registry = None if info.context is None else info.context.get("task_registry")
-        registry = BUILTIN_TASKS if registry is None else registry
-        if not isinstance(registry, TaskRegistry):
-            raise TypeError("task_registry validation context must be a TaskRegistry")
-        return registry.parse(value)
+        return _context_registry(info, "task_registry", BUILTIN_TASKS, TaskRegistry).parse(value)
 
     @field_validator("loss", mode="before")
     @classmethod
-    def validate_registered_loss(cls, value: object, info: ValidationInfo) -> LossConfig:
+    def _parse_loss(cls, value: object, info: ValidationInfo) -> LossConfig:
         from .tasks.registry import BUILTIN_LOSSES, LossRegistry
 
-        registry = None if info.context is None else info.context.get("loss_registry")
-        registry = BUILTIN_LOSSES if registry is None else registry
-        if not isinstance(registry, LossRegistry):
-            raise TypeError("loss_registry validation context must be a LossRegistry")
-        return registry.parse(value)
+        return _context_registry(info, "loss_registry", BUILTIN_LOSSES, LossRegistry).parse(value)
 
     @field_validator("loss_modifiers", mode="before")
     @classmethod
-    def validate_registered_loss_modifiers(cls, value: object, info: ValidationInfo):
+    def _parse_modifiers(cls, value: object, info: ValidationInfo):
         from .tasks.registry import BUILTIN_LOSS_MODIFIERS, LossModifierRegistry
 
-        registry = None if info.context is None else info.context.get("modifier_registry")
-        registry = BUILTIN_LOSS_MODIFIERS if registry is None else registry
-        if not isinstance(registry, LossModifierRegistry):
-            raise TypeError("modifier_registry validation context must be a LossModifierRegistry")
-        if not isinstance(value, (list, tuple)):
-            raise TypeError("loss_modifiers must be a list or tuple")
-        parsed = tuple(registry.parse(m) for m in value)
-        kinds = tuple(m.kind for m in parsed)
-        if len(set(kinds)) != len(kinds):
-            raise ValueError("loss modifier kinds must be unique")
-        if len(parsed) > 1 and any(k in {"matryoshka", "adaptive_layer", "matryoshka_2d"} for k in kinds):
-            raise ValueError("dimension/layer modifiers are mutually exclusive; use matryoshka_2d for their "
-                             "joint objective")
+        registry = _context_registry(info, "modifier_registry", BUILTIN_LOSS_MODIFIERS, LossModifierRegistry)
+        if isinstance(value, (str, bytes, Mapping)) or not isinstance(value, (list, tuple)):
+            raise TypeError(f"loss_modifiers takes a sequence of modifier configs, got {type(value).__name__}")
+        parsed = tuple(registry.parse(item) for item in value)
+        kinds = [m.kind for m in parsed]
+        _check((not _repeated(kinds), f"loss modifier(s) {_repeated(kinds)} applied twice"),
+               (len(kinds) < 2 or not _EXCLUSIVE_MODIFIERS.intersection(kinds),
+                f"modifiers {kinds} cannot be stacked: matryoshka, adaptive_layer and matryoshka_2d each "
+                "rewrite the representation; matryoshka_2d is the combined dimension x layer objective"))
         return parsed
 
     @model_validator(mode="after")
-    def validate_loss_capabilities(self, info: ValidationInfo):
-        from .tasks.registry import BUILTIN_LOSS_MODIFIERS, BUILTIN_LOSSES
+    def _loss_supports_plan(self, info: ValidationInfo):
+        from .tasks.registry import BUILTIN_LOSS_MODIFIERS, BUILTIN_LOSSES, LossModifierRegistry, LossRegistry
 
-        losses = (info.context or {}).get("loss_registry") or BUILTIN_LOSSES
-        definition = losses.definition(self.loss.kind)
-        if self.task.kind not in definition.task_kinds:
-            raise ValueError(f"loss {self.loss.kind!r} does not support task {self.task.kind!r}")
+        losses = _context_registry(info, "loss_registry", BUILTIN_LOSSES, LossRegistry)
+        modifiers = _context_registry(info, "modifier_registry", BUILTIN_LOSS_MODIFIERS, LossModifierRegistry)
+        loss = losses.definition(self.loss.kind)
         strategy = self.training_strategy
-        if strategy not in definition.training_strategies:
-            raise ValueError(f"loss {self.loss.kind!r} does not support training strategy {strategy!r}")
-        steps = self.training.batch.gradient_accumulation_steps
-        if steps > 1:
-            if strategy != "direct":
-                raise ValueError("gradient accumulation composes only with direct execution; GradCache and "
-                                 "mega-batch execution already own their logical batch decomposition")
-            if not definition.microbatch_accumulation:
-                raise ValueError(f"loss {self.loss.kind!r} does not decompose exactly across "
-                                 "gradient-accumulation microbatches")
-        modifiers = (info.context or {}).get("modifier_registry") or BUILTIN_LOSS_MODIFIERS
+        accumulating = self.training.batch.gradient_accumulation_steps > 1
+        rules = [
+            (self.task.kind in loss.task_kinds,
+             f"loss {self.loss.kind!r} is defined for tasks {sorted(loss.task_kinds)}, not {self.task.kind!r}"),
+            (strategy in loss.training_strategies,
+             f"loss {self.loss.kind!r} cannot run under the {strategy!r} execution"),
+            (not accumulating or strategy == "direct",
+             f"gradient_accumulation_steps > 1 needs direct execution; {strategy!r} already splits the "
+             "logical batch into its own chunks"),
+            (not accumulating or loss.microbatch_accumulation,
+             f"loss {self.loss.kind!r} couples examples across the batch, so microbatch accumulation would "
+             "change its value"),
+        ]
         for modifier in self.loss_modifiers:
-            md = modifiers.definition(modifier.kind)
-            if strategy not in md.training_strategies:
-                raise ValueError(f"loss modifier {modifier.kind!r} does not support training strategy "
-                                 f"{strategy!r}")
-            if steps > 1 and not md.microbatch_accumulation:
-                raise ValueError(f"loss modifier {modifier.kind!r} does not decompose exactly across "
-                                 "gradient-accumulation microbatches")
+            spec = modifiers.definition(modifier.kind)
+            rules.append((strategy in spec.training_strategies,
+                          f"modifier {modifier.kind!r} cannot run under the {strategy!r} execution"))
+            rules.append((not accumulating or spec.microbatch_accumulation,
+                          f"modifier {modifier.kind!r} is not exact under microbatch accumulation"))
+        _check(*rules)
         return self
 
     @model_validator(mode="after")
-    def validate_checkpoint_schedule(self):
-        if self.checkpointing is not None and any(
-                i > self.training.max_steps for i in self.checkpointing.additional_iterations):
-            raise ValueError("additional checkpoint iterations cannot exceed training.max_steps")
-        if self.evaluation is not None and self.evaluation.save_best and self.checkpointing is None:
-            raise ValueError("best-model selection requires checkpointing")
-        if (self.export.enabled and self.export.selection == "best"
-                and (self.evaluation is None or not self.evaluation.save_best)):
-            raise ValueError("best-model export requires evaluation.save_best")
+    def _schedules_fit(self):
+        extra = () if self.checkpointing is None else self.checkpointing.additional_iterations
+        late = sorted(i for i in extra if i > self.training.max_steps)
+        selects_best = self.evaluation is not None and self.evaluation.save_best
+        _check((not late, f"checkpoint iteration(s) {late} come after the last step {self.training.max_steps}"),
+               (not selects_best or self.checkpointing is not None,
+                "evaluation.save_best keeps the best checkpoint, so checkpointing must be configured"),
+               (not (self.export.enabled and self.export.selection == "best") or selects_best,
+                "export.selection='best' needs evaluation with save_best"))
         return self
 
     @property
@@ -563,10 +588,10 @@ class JobConfig(FrozenConfig):
 
 
 __all__ = [
-    "B200ExecutionConfig", "BatchConfig", "CheckpointConfig", "ComponentConfig", "CustomShardingConfig", "DDPConfig",
-    "DataConfig", "EmbeddingSimilarityEvaluatorConfig", "EvaluationConfig", "EvaluatorConfig", "ExportConfig",
-    "FSDPConfig", "GradCacheConfig", "HuggingFaceExportConfig", "InformationRetrievalEvaluatorConfig", "JobConfig",
-    "LoggingConfig", "MegaBatchMiningConfig", "MeshConfig", "ModelConfig", "OptimizationConfig", "ParameterRole",
-    "PartitionAxis", "PartitionRuleConfig", "PrecisionConfig", "QuantizedLoRAConfig", "RematerializationPolicy",
-    "ShardingConfig", "TensorParallelConfig", "TrainingConfig",
+    "AnyEvaluatorConfig", "B200ExecutionConfig", "BatchConfig", "CheckpointConfig", "ComponentConfig",
+    "CustomShardingConfig", "DDPConfig", "DataConfig", "EmbeddingSimilarityEvaluatorConfig", "EvaluationConfig",
+    "EvaluatorConfig", "ExportConfig", "FSDPConfig", "GradCacheConfig", "HuggingFaceExportConfig",
+    "InformationRetrievalEvaluatorConfig", "JobConfig", "LoggingConfig", "MegaBatchMiningConfig", "MeshConfig",
+    "ModelConfig", "OptimizationConfig", "ParameterRole", "PartitionAxis", "PartitionRuleConfig", "PrecisionConfig",
+    "QuantizedLoRAConfig", "RematerializationPolicy", "ShardingConfig", "TensorParallelConfig", "TrainingConfig",
 ]

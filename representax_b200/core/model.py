@@ -39,15 +39,14 @@ class Modality(str):
     AUDIO: ClassVar["Modality"]
     VIDEO: ClassVar["Modality"]
 
-    _NAME = re.compile(r"^[a-z][a-z0-9]*(?:[._/-][a-z0-9]+)*$")
+    # lowercase word, optionally continued by '.', '/', '_' or '-' separated words
+    _NAME = re.compile(r"[a-z][a-z0-9]*(?:[._/-][a-z0-9]+)*")
 
     def __new__(cls, value: str) -> "Modality":
-        if not isinstance(value, str) or not cls._NAME.fullmatch(value):
-            raise ValueError(
-                "modality names must be lowercase identifiers optionally "
-                "separated by '.', '/', '_', or '-'"
-            )
-        return str.__new__(cls, value)
+        if isinstance(value, str) and cls._NAME.fullmatch(value):
+            return str.__new__(cls, value)
+        raise ValueError(f"{value!r} is not a modality name: use lowercase words such as 'text' or "
+                         "'image/depth' (separators '.', '/', '_', '-')")
 
     @property
     def value(self) -> str:
@@ -72,16 +71,15 @@ class EncoderMetadata:
     modalities: frozenset = field(default_factory=lambda: frozenset({Modality.TEXT}))
 
     def __post_init__(self) -> None:
-        if not self.model_id:
-            raise ValueError("model_id must be non-empty")
-        if not self.revision:
-            raise ValueError("revision must be non-empty")
-        if self.output_dimension <= 0:
-            raise ValueError("output_dimension must be positive")
-        if not self.routes:
-            raise ValueError("an encoder must support at least one route")
-        if not self.modalities:
-            raise ValueError("an encoder must support at least one modality")
+        problems = [text for bad, text in (
+            (not self.model_id, "empty model_id"),
+            (not self.revision, "empty revision"),
+            (self.output_dimension < 1, f"output_dimension {self.output_dimension} < 1"),
+            (not self.routes, "no route"),
+            (not self.modalities, "no modality"),
+        ) if bad]
+        if problems:
+            raise ValueError("EncoderMetadata: " + ", ".join(problems))
 
 
 @runtime_checkable
@@ -101,66 +99,66 @@ class LayerwiseEncoder(Encoder, Protocol):
 
 
 def _metadata(model: Any) -> EncoderMetadata:
-    if not isinstance(model, torch.nn.Module):
-        raise TypeError("encoders must be torch.nn.Module trees")
+    """The metadata of an object that satisfies the encoder contract (module + metadata + encode)."""
+
     metadata = getattr(model, "metadata", None)
-    if not isinstance(metadata, EncoderMetadata):
-        raise TypeError("encoders must expose EncoderMetadata")
-    if not callable(getattr(model, "encode", None)):
-        raise TypeError("encoders must implement encode")
+    missing = [what for ok, what in (
+        (isinstance(model, torch.nn.Module), "is not a torch.nn.Module"),
+        (isinstance(metadata, EncoderMetadata), "has no EncoderMetadata"),
+        (callable(getattr(model, "encode", None)), "has no encode()"),
+    ) if not ok]
+    if missing:
+        raise TypeError(f"{type(model).__name__} is not an encoder: it " + " and ".join(missing))
     return metadata
 
 
 def _check_route(metadata: EncoderMetadata, route: Route | str) -> Route:
-    route = Route(route)
-    if route not in metadata.routes:
-        raise ValueError(f"{metadata.model_id} does not support route {route.value!r}")
-    return route
+    chosen = Route(route)
+    if chosen in metadata.routes:
+        return chosen
+    offered = sorted(r.value for r in metadata.routes)
+    raise ValueError(f"route {chosen.value!r} is not offered by {metadata.model_id} (routes: {offered})")
+
+
+def _contract(metadata: EncoderMetadata, result: Any, layout: tuple[str, ...]) -> torch.Tensor:
+    """Check an encoder output against ``layout`` (axis names, last = dimension) and cast it."""
+
+    where = f"{metadata.model_id} output"
+    if not torch.is_tensor(result):
+        raise TypeError(f"{where} is a {type(result).__name__}, not a tensor")
+    if not result.is_floating_point():
+        raise TypeError(f"{where} has integer dtype {result.dtype}")
+    if result.ndim != len(layout):
+        raise ValueError(f"{where} has {result.ndim} axes; expected [{', '.join(layout)}]")
+    if layout[0] == "layer" and result.shape[0] < 2:
+        raise ValueError(f"{where} holds {result.shape[0]} layer(s); layerwise outputs need at least an "
+                         "earlier and the final layer")
+    width = result.shape[-1]
+    if width != metadata.output_dimension:
+        raise ValueError(f"{where} is {width} wide but the metadata declares {metadata.output_dimension}")
+    return result.to(active_policy().accumulation_dtype)
 
 
 def encode(model: Encoder, inputs: Any, *, route: Route | str = Route.GENERIC,
            generator: Any = None) -> torch.Tensor:
-    """Encode one batch and enforce the shared representation contract."""
+    """Encode one batch as ``[batch, dimension]`` in the accumulation dtype."""
 
     metadata = _metadata(model)
-    route = _check_route(metadata, route)
-    result = model.encode(inputs, route=route, generator=generator)
-    if not isinstance(result, torch.Tensor):
-        raise TypeError("encoder output must be a tensor")
-    if result.ndim != 2:
-        raise ValueError("encoder output must have shape [batch, dimension]")
-    if not result.is_floating_point():
-        raise TypeError("encoder output must have a floating dtype")
-    if result.shape[1] != metadata.output_dimension:
-        raise ValueError(
-            f"{metadata.model_id} declares output_dimension="
-            f"{metadata.output_dimension} but returned {result.shape[1]}"
-        )
-    return result.to(active_policy().accumulation_dtype)
+    chosen = _check_route(metadata, route)
+    return _contract(metadata, model.encode(inputs, route=chosen, generator=generator), ("batch", "dimension"))
 
 
 def encode_layers(model: LayerwiseEncoder, inputs: Any, *, route: Route | str = Route.GENERIC,
                   generator: Any = None) -> torch.Tensor:
-    """Encode every available depth with a stable layer-major contract."""
+    """Encode every available depth as ``[layer, batch, dimension]``."""
 
     metadata = _metadata(model)
-    route = _check_route(metadata, route)
+    chosen = _check_route(metadata, route)
     layerwise = getattr(model, "encode_layers", None)
     if not callable(layerwise):
-        raise TypeError(f"{metadata.model_id} does not expose layerwise representations")
-    result = layerwise(inputs, route=route, generator=generator)
-    if result.ndim != 3:
-        raise ValueError("layerwise encoder output must have shape [layer, batch, dimension]")
-    if not result.is_floating_point():
-        raise TypeError("layerwise encoder output must have a floating dtype")
-    if result.shape[0] < 2:
-        raise ValueError("layerwise encoders must expose a prior and final layer")
-    if result.shape[2] != metadata.output_dimension:
-        raise ValueError(
-            f"{metadata.model_id} declares output_dimension="
-            f"{metadata.output_dimension} but returned {result.shape[2]}"
-        )
-    return result.to(active_policy().accumulation_dtype)
+        raise TypeError(f"{metadata.model_id} has no encode_layers()")
+    return _contract(metadata, layerwise(inputs, route=chosen, generator=generator),
+                     ("layer", "batch", "dimension"))
 
 
 class BoundEncoder:

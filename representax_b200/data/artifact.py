@@ -48,15 +48,14 @@ class Artifact:
             raise ValueError("a referenced artifact needs a non-empty uri")
         if inline and any(v is not None for v in (self.revision, self.etag, self.archive_member, self.byte_range)):
             raise ValueError("inline artifacts take no reference selectors")
-        for name in ("revision", "etag", "archive_member", "checksum"):
-            value = getattr(self, name)
-            if value is not None and not value:
-                raise ValueError(f"artifact {name} must be non-empty or None")
+        blank = [n for n in ("revision", "etag", "archive_member", "checksum") if getattr(self, n) == ""]
+        if blank:
+            raise ValueError(f"artifact selectors {blank} are empty strings; use None to leave them unset")
         if self.byte_range is not None:
-            start, stop = self.byte_range
-            if start < 0 or stop <= start:
-                raise ValueError("byte_range must be a non-empty [start, stop) span")
-            object.__setattr__(self, "byte_range", (int(start), int(stop)))
+            lo, hi = (int(v) for v in self.byte_range)
+            if not 0 <= lo < hi:
+                raise ValueError(f"byte_range {self.byte_range} is not a non-empty [start, stop) span")
+            object.__setattr__(self, "byte_range", (lo, hi))
         if self.checksum is not None:
             algorithm, sep, digest = self.checksum.partition(":")
             if algorithm != "sha256" or not sep or len(digest) != 64 or not set(digest) <= _HEX:

@@ -78,23 +78,26 @@ def _export_huggingface(model, job, target: Path) -> None:
         target.mkdir(parents=True)
     adapter.save(model, target)
     if config.verify_reload:
-        restored = adapter.load(target)
-        expected = adapter.state_dict(model)
-        actual = adapter.state_dict(restored)
-        if set(actual) != set(expected):
-            raise ValueError("Hugging Face export changed checkpoint tensor names")
-        for name in sorted(expected):
-            if not torch.equal(actual[name], expected[name]):
-                raise ValueError(f"Hugging Face export failed exact reload verification: {name}")
+        _check_reload(adapter.state_dict(model), adapter.state_dict(adapter.load(target)), target)
+
+
+def _check_reload(written: dict[str, torch.Tensor], reread: dict[str, torch.Tensor], where: Path) -> None:
+    """The checkpoint read back from ``where`` has to equal what was written, bit for bit."""
+
+    lost, gained = sorted(set(written) - set(reread)), sorted(set(reread) - set(written))
+    differing = [name for name in sorted(set(written) & set(reread)) if not torch.equal(written[name], reread[name])]
+    if lost or gained or differing:
+        raise ValueError(f"the Hugging Face checkpoint at {where} does not read back as written: "
+                         f"lost {lost[:3]}, gained {gained[:3]}, changed {differing[:3]}")
 
 
 def export_inference_bundle(model: torch.nn.Module, job: Any, directory: str | Path, *,
                             iteration: int | None) -> InferenceBundle:
-    if iteration is None or iteration < 0:
-        raise ValueError("export iteration must be non-negative")
+    if not (isinstance(iteration, int) and iteration >= 0):
+        raise ValueError(f"export needs the iteration the weights come from (an int >= 0), got {iteration!r}")
     target = Path(directory).expanduser().resolve()
     if target.exists():
-        raise FileExistsError(f"inference bundle already exists: {target}")
+        raise FileExistsError(f"refusing to overwrite {target}: bundles are written once")
     target.parent.mkdir(parents=True, exist_ok=True)
     temporary = Path(tempfile.mkdtemp(prefix=f".{target.name}-", dir=target.parent)).resolve()
     try:
@@ -126,6 +129,25 @@ def export_inference_bundle(model: torch.nn.Module, job: Any, directory: str | P
                            None if job.export.huggingface is None else target / "huggingface", iteration)
 
 
+def _verified_manifest(bundle: Path) -> dict[str, Any]:
+    """Read a bundle's manifest after checking marker, schema, fingerprint and weight digest."""
+
+    try:
+        manifest = json.loads((bundle / "manifest.json").read_text())
+        marker = (bundle / COMPLETE_MARKER).read_text().strip()
+    except FileNotFoundError as error:
+        raise FileNotFoundError(f"{bundle} is not a finished bundle ({Path(error.filename).name} absent)") from None
+    stated = manifest.pop("fingerprint", None)
+    if manifest.get("schema_version") != EXPORT_SCHEMA:
+        raise ValueError(f"{bundle}: schema {manifest.get('schema_version')!r}, expected {EXPORT_SCHEMA!r}")
+    if not (stated == marker == _fingerprint(manifest)):
+        raise ValueError(f"{bundle}: the manifest fingerprint, the marker and the manifest content disagree")
+    weights = bundle / manifest["native"]["model"]
+    if _sha256(weights) != manifest["native"]["model_sha256"]:
+        raise ValueError(f"{weights} changed after export (sha256 differs from the manifest)")
+    return manifest
+
+
 def load_inference_bundle(directory: str | Path):
     """Rebuild the model from ``job.json`` and load the digest-checked weights."""
 
@@ -133,27 +155,15 @@ def load_inference_bundle(directory: str | Path):
     from representax_b200.train.job import load_model, prepare_model
 
     bundle = Path(directory).expanduser().resolve()
-    manifest_path = bundle / "manifest.json"
-    complete = bundle / COMPLETE_MARKER
-    if not manifest_path.is_file() or not complete.is_file():
-        raise FileNotFoundError(f"inference bundle is incomplete: {bundle}")
-    manifest = json.loads(manifest_path.read_text())
-    fingerprint = manifest.pop("fingerprint", None)
-    if (manifest.get("schema_version") != EXPORT_SCHEMA or fingerprint != _fingerprint(manifest)
-            or complete.read_text().strip() != fingerprint):
-        raise ValueError(f"inference bundle manifest is invalid: {bundle}")
-    model_path = bundle / manifest["native"]["model"]
-    if _sha256(model_path) != manifest["native"]["model_sha256"]:
-        raise ValueError(f"native model digest differs: {model_path}")
+    manifest = _verified_manifest(bundle)
     job = JobConfig.model_validate_json((bundle / manifest["native"]["config"]).read_text())
     model = prepare_model(load_model(job), job)
+    model_path = bundle / manifest["native"]["model"]
     state = load_file(str(model_path))
     current = model.state_dict()
-    missing = set(current) - set(state)
-    unexpected = set(state) - set(current)
-    if missing or unexpected:
-        raise ValueError(f"native bundle does not match the model: missing={sorted(missing)[:5]}, "
-                         f"unexpected={sorted(unexpected)[:5]}")
+    if set(state) != set(current):
+        raise ValueError(f"{model_path} holds other tensors than the model built from job.json: "
+                         f"absent {sorted(set(current) - set(state))[:5]}, extra {sorted(set(state) - set(current))[:5]}")
     model.load_state_dict({k: v.to(current[k].dtype) for k, v in state.items()})
     return model, job
 

@@ -32,21 +32,25 @@ from representax_b200.core.model import Modality, Route
 from representax_b200.data.artifact import Artifact
 
 
-def _shape(value: Sequence[int], *, name: str) -> tuple[int, ...]:
-    dims = []
-    for d in value:
+def _dims(value: Sequence[int], *, what: str) -> tuple[int, ...]:
+    """A non-empty tuple of positive Python ints (bools and floats rejected)."""
+
+    def whole(d: Any) -> int | None:
         if isinstance(d, bool):
-            raise ValueError(f"{name} must contain positive integer dimensions")
+            return None
         try:
-            d = operator.index(d)
-        except TypeError as error:
-            raise ValueError(f"{name} must contain positive integer dimensions") from error
-        if d <= 0:
-            raise ValueError(f"{name} must contain positive integer dimensions")
-        dims.append(d)
-    if not dims:
-        raise ValueError(f"{name} must contain positive integer dimensions")
-    return tuple(dims)
+            return operator.index(d)
+        except TypeError:
+            return None
+
+    dims = tuple(whole(d) for d in value)
+    if not dims or any(d is None or d < 1 for d in dims):
+        raise ValueError(f"{what} {tuple(value)!r}: dimensions have to be whole numbers >= 1")
+    return dims  # type: ignore[return-value]
+
+
+def _covers(bigger: tuple[int, ...], smaller: tuple[int, ...]) -> bool:
+    return all(b >= s for b, s in zip(bigger, smaller))
 
 
 def select_static_shape_bucket(required_shape: Sequence[int],
@@ -58,20 +62,30 @@ def select_static_shape_bucket(required_shape: Sequence[int],
     this raises instead of guessing.
     """
 
-    required = _shape(required_shape, name="required_shape")
-    buckets = tuple(dict.fromkeys(_shape(s, name="static shape buckets") for s in admitted_shapes))
-    if not buckets:
-        raise ValueError("at least one static shape bucket is required")
-    if any(len(b) != len(required) for b in buckets):
-        raise ValueError("static shape buckets must match required_shape rank")
-    fits = [b for b in buckets if all(r <= a for r, a in zip(required, b))]
-    if not fits:
-        raise ValueError(f"required shape {required!r} exceeds admitted buckets {buckets!r}")
-    minimal = [b for b in fits if not any(o != b and all(x <= y for x, y in zip(o, b)) for o in fits)]
-    if len(minimal) != 1:
-        raise ValueError(f"required shape {required!r} has incomparable admitted buckets {tuple(minimal)!r}; "
-                         "the model processor must choose explicitly")
+    need = _dims(required_shape, what="required shape")
+    menu = list(dict.fromkeys(_dims(s, what="admitted shape") for s in admitted_shapes))
+    if not menu or {len(s) for s in menu} != {len(need)}:
+        raise ValueError(f"admitted shapes {menu} have to be a non-empty list of rank-{len(need)} shapes")
+    covering = [s for s in menu if _covers(s, need)]
+    if not covering:
+        raise ValueError(f"required shape {need} exceeds every admitted shape {menu}")
+    # a covering shape is minimal when no other covering shape fits inside it
+    minimal = [s for s in covering if not any(o != s and _covers(s, o) for o in covering)]
+    if len(minimal) > 1:
+        raise ValueError(f"required shape {need} fits incomparable minimal shapes {minimal}; the model's "
+                         "processor has to pick one itself")
     return minimal[0]
+
+
+def _frozen_json(values: Mapping[str, Any], *, what: str) -> MappingProxyType:
+    """A read-only copy of ``values`` after checking it serialises to JSON."""
+
+    copy = dict(values)
+    try:
+        json.dumps(copy, sort_keys=True)
+    except (TypeError, ValueError) as error:
+        raise TypeError(f"{what} has to be JSON data: {error}") from error
+    return MappingProxyType(copy)
 
 
 @dataclass(frozen=True)
@@ -83,13 +97,8 @@ class Processor:
 
     def __post_init__(self) -> None:
         if not callable(self.process):
-            raise TypeError("processor process must be callable")
-        contract = dict(self.contract)
-        try:
-            json.dumps(contract, sort_keys=True)
-        except (TypeError, ValueError) as error:
-            raise TypeError("processor contract must be JSON serializable") from error
-        object.__setattr__(self, "contract", MappingProxyType(contract))
+            raise TypeError(f"Processor.process is a {type(self.process).__name__}, not a function")
+        object.__setattr__(self, "contract", _frozen_json(self.contract, what="Processor.contract"))
 
     def data_contract(self) -> dict[str, Any]:
         return dict(self.contract)
@@ -103,29 +112,37 @@ class Processor:
 
 
 def _callable_contract(value: Callable[..., Any]) -> dict[str, str]:
-    module = getattr(value, "__module__", type(value).__module__)
-    qual = getattr(value, "__qualname__", type(value).__qualname__)
-    identity = f"{module}.{qual}"
-    target = value if inspect.isfunction(value) or inspect.isclass(value) or inspect.ismethod(value) else type(value)
+    """Identity of a callable plus a digest of the code that defines it.
+
+    The digest covers the whole defining module file when there is one (so a
+    change anywhere in it changes the data contract), else the callable's own
+    source, else nothing beyond the dotted name.
+    """
+
+    owner = value if (inspect.isfunction(value) or inspect.isclass(value) or inspect.ismethod(value)) \
+        else type(value)
+    name = f"{getattr(value, '__module__', owner.__module__)}.{getattr(value, '__qualname__', owner.__qualname__)}"
+    record = {"callable": name}
     try:
-        path = inspect.getsourcefile(target)
+        source_file = inspect.getsourcefile(owner)
     except TypeError:
-        path = None
-    if path is not None and Path(path).is_file():
-        return {"callable": identity, "module_file_sha256": hashlib.sha256(Path(path).read_bytes()).hexdigest()}
+        source_file = None
+    if source_file and Path(source_file).is_file():
+        record["module_file_sha256"] = hashlib.sha256(Path(source_file).read_bytes()).hexdigest()
+        return record
     try:
-        source = inspect.getsource(target).encode()
+        record["callable_source_sha256"] = hashlib.sha256(inspect.getsource(owner).encode()).hexdigest()
     except (OSError, TypeError):
-        return {"callable": identity}
-    return {"callable": identity, "callable_source_sha256": hashlib.sha256(source).hexdigest()}
+        pass
+    return record
 
 
 def _as_artifact(value: Any, modality: Modality) -> Artifact:
-    if isinstance(value, Artifact):
-        if value.modality != modality:
-            raise TypeError(f"{modality} processors cannot consume {value.modality} artifacts")
+    if not isinstance(value, Artifact):
+        return Artifact.inline(modality, value)
+    if value.modality == modality:
         return value
-    return Artifact.inline(modality, value)
+    raise TypeError(f"a {modality} processor was given a {value.modality} artifact")
 
 
 def make_media_processor(*, modality: Modality | str, admitted_shapes: Sequence[Sequence[int]],
@@ -141,38 +158,37 @@ def make_media_processor(*, modality: Modality | str, admitted_shapes: Sequence[
     """
 
     modality = Modality(modality)
-    if not (callable(probe) and callable(prepare) and callable(batch_builder)):
-        raise TypeError("media probe, prepare and batch_builder must be callable")
-    config = dict(configuration)
-    try:
-        json.dumps(config, sort_keys=True)
-    except (TypeError, ValueError) as error:
-        raise TypeError("media processor configuration must be JSON serializable") from error
-    shapes = tuple(dict.fromkeys(_shape(s, name="admitted media shapes") for s in admitted_shapes))
-    if not shapes:
-        raise ValueError("at least one admitted media shape is required")
-    rank = len(shapes[0])
-    if any(len(s) != rank for s in shapes):
-        raise ValueError("admitted media shapes must have one consistent rank")
+    not_callable = [n for n, f in (("probe", probe), ("prepare", prepare), ("batch_builder", batch_builder))
+                    if not callable(f)]
+    if not_callable:
+        raise TypeError(f"media processor: {', '.join(not_callable)} not callable")
+    config = dict(_frozen_json(configuration, what="media processor configuration"))
+    shapes = tuple(dict.fromkeys(_dims(s, what="admitted media shape") for s in admitted_shapes))
+    ranks = {len(s) for s in shapes}
+    if len(ranks) != 1:
+        raise ValueError(f"admitted media shapes {list(shapes)} need one common, non-zero rank")
+    rank = ranks.pop()
 
     def process(artifacts: Sequence[Any], *, route: Route, seed: int | None) -> Any:
-        if not artifacts:
-            raise ValueError("media processor batches must be non-empty")
+        if len(artifacts) == 0:
+            raise ValueError("a media batch needs at least one artifact")
         items = [_as_artifact(a, modality) for a in artifacts]
-        needs = [_shape(probe(a, route=route), name=f"{modality} shape requirement") for a in items]
-        if any(len(n) != rank for n in needs):
-            raise ValueError(f"{modality} shape requirements must have rank {rank}")
+        needs = [_dims(probe(a, route=route), what=f"{modality} probe result") for a in items]
+        if {len(n) for n in needs} != {rank}:
+            raise ValueError(f"{modality} probe results have to be rank {rank}, got {needs}")
         bucket = select_static_shape_bucket(tuple(max(v) for v in zip(*needs)), shapes)
         seeds = [None] * len(items) if seed is None else np.random.SeedSequence(seed).spawn(len(items))
         rows = []
         for item, s in zip(items, seeds):
             prepared = prepare(item, bucket=bucket, route=route, rng=None if s is None else np.random.default_rng(s))
-            if not isinstance(prepared, Mapping) or not prepared:
-                raise TypeError("media prepare must return a non-empty mapping")
+            if not (isinstance(prepared, Mapping) and prepared):
+                raise TypeError(f"prepare() returned {type(prepared).__name__}; a non-empty dict of arrays "
+                                "was expected")
             rows.append({k: np.asarray(v) for k, v in prepared.items()})
         names = tuple(rows[0])
-        if any(tuple(r) != names for r in rows[1:]):
-            raise ValueError("media prepare fields must be identical for every row")
+        odd = [i for i, r in enumerate(rows) if tuple(r) != names]
+        if odd:
+            raise ValueError(f"prepare() returned other fields for rows {odd} than {list(names)}")
         arrays = {}
         for name in names:
             if len({r[name].shape for r in rows}) != 1:
@@ -193,8 +209,9 @@ def make_media_processor(*, modality: Modality | str, admitted_shapes: Sequence[
 
 def _media_with_rank(modality: Modality, rank: int, what: str):
     def build(*, admitted_shapes, probe, prepare, batch_builder, configuration) -> Processor:
-        if any(len(tuple(s)) != rank for s in admitted_shapes):
-            raise ValueError(f"{modality} admitted shapes must be {what}")
+        wrong = [tuple(s) for s in admitted_shapes if len(tuple(s)) != rank]
+        if wrong:
+            raise ValueError(f"{modality} shapes are {what}; got {wrong}")
         return make_media_processor(modality=modality, admitted_shapes=admitted_shapes, probe=probe,
                                     prepare=prepare, batch_builder=batch_builder, configuration=configuration)
 
@@ -206,6 +223,33 @@ def _media_with_rank(modality: Modality, rank: int, what: str):
 make_image_processor = _media_with_rank(Modality.IMAGE, 2, "(height, width)")
 make_audio_processor = _media_with_rank(Modality.AUDIO, 1, "(samples,)")
 make_video_processor = _media_with_rank(Modality.VIDEO, 3, "(frames, height, width)")
+
+
+_ROUTE_PROMPTS = {Route.QUERY: ("query",), Route.DOCUMENT: ("document", "passage", "corpus")}
+
+
+def _length_buckets(longest: int | None, buckets: Sequence[int] | None) -> tuple[int, ...]:
+    """Sorted distinct padding lengths; a single bucket of ``longest`` when none are given."""
+
+    if buckets is None:
+        if longest is None:
+            raise ValueError("give max_sequence_length, sequence_length_buckets or both")
+        buckets = (longest,)
+    picked = tuple(buckets)
+    if not picked or not all(type(n) is int and n > 0 for n in picked):
+        raise ValueError(f"sequence_length_buckets {picked!r}: lengths have to be ints >= 1")
+    ordered = tuple(sorted(set(picked)))
+    if longest is not None and ordered[-1] > longest:
+        raise ValueError(f"bucket {ordered[-1]} is longer than max_sequence_length {longest}")
+    return ordered
+
+
+def _text_of(item: Any) -> str:
+    if isinstance(item, str):
+        return item
+    if isinstance(item, Artifact) and item.modality == Modality.TEXT and isinstance(item.data, str):
+        return item.data
+    raise TypeError(f"text processor input {item!r} is neither a string nor an inline text artifact")
 
 
 def make_text_processor(*, tokenizer: Any, batch_builder: Callable[..., Any], max_sequence_length: int | None = None,
@@ -220,51 +264,39 @@ def make_text_processor(*, tokenizer: Any, batch_builder: Callable[..., Any], ma
     tokens are masked out of pooling through ``pooling_batch_builder``.
     """
 
-    if sequence_length_buckets is None:
-        if max_sequence_length is None:
-            raise ValueError("max_sequence_length or sequence_length_buckets is required")
-        sequence_length_buckets = (max_sequence_length,)
-    lengths = tuple(sequence_length_buckets)
-    if not lengths or any(not isinstance(n, int) or isinstance(n, bool) or n <= 0 for n in lengths):
-        raise ValueError("sequence_length_buckets must be positive integers")
-    lengths = tuple(sorted(set(lengths)))
-    if max_sequence_length is not None and lengths[-1] > max_sequence_length:
-        raise ValueError("sequence length buckets cannot exceed max_sequence_length")
+    lengths = _length_buckets(max_sequence_length, sequence_length_buckets)
     prompt_values = dict(prompts or {})
     if default_prompt_name is not None and default_prompt_name not in prompt_values:
-        raise ValueError("default_prompt_name does not name a configured prompt")
+        raise ValueError(f"default prompt {default_prompt_name!r} is none of {sorted(prompt_values)}")
     if not include_prompt and pooling_batch_builder is None:
-        raise ValueError("prompt exclusion requires pooling_batch_builder")
+        raise ValueError("include_prompt=False masks prompt tokens through pooling_batch_builder; pass one")
     maximum = lengths[-1]
 
     def route_prompt(route: Route, prompt_name: str | None, prompt: str | None) -> str:
-        if prompt_name is not None and prompt is not None:
-            raise ValueError("specify prompt_name or prompt, not both")
         if prompt is not None:
+            if prompt_name is not None:
+                raise ValueError("pass a prompt text or a prompt name, not both")
             return prompt
         if prompt_name is not None:
             if prompt_name not in prompt_values:
-                raise KeyError(f"unknown prompt {prompt_name!r}")
+                raise KeyError(f"no prompt named {prompt_name!r} (have {sorted(prompt_values)})")
             return prompt_values[prompt_name]
-        if route is Route.QUERY:
-            names = ("query",)
-        elif route is Route.DOCUMENT:
-            names = ("document", "passage", "corpus")
-        else:
-            names = () if default_prompt_name is None else (default_prompt_name,)
-        return next((prompt_values[n] for n in names if n in prompt_values), "")
+        candidates = _ROUTE_PROMPTS.get(route, ())
+        if route is Route.GENERIC and default_prompt_name is not None:
+            candidates = (default_prompt_name,)
+        return next((prompt_values[n] for n in candidates if n in prompt_values), "")
 
     def pad_id() -> int:
         value = getattr(tokenizer, "pad_token_id", None)
         if value is None:
             value = getattr(tokenizer, "pad_id", 0)
         if value is None:
-            raise ValueError("text tokenizer must define a pad token")
+            raise ValueError(f"{type(tokenizer).__name__} has no pad token; set pad_token_id")
         return int(value)
 
     def tokenize(texts: Sequence[str]) -> dict[str, np.ndarray]:
-        if not texts:
-            raise ValueError("processor batches must be non-empty")
+        if len(texts) == 0:
+            raise ValueError("a text batch needs at least one text")
         encoded = tokenizer(list(texts), padding=True, truncation=True, max_length=maximum, return_tensors="np")
         if not isinstance(encoded, Mapping):
             encoded = dict(encoded)
@@ -272,8 +304,8 @@ def make_text_processor(*, tokenizer: Any, batch_builder: Callable[..., Any], ma
         if "input_ids" not in arrays:
             raise KeyError("tokenizer output is missing 'input_ids'")
         ids = arrays["input_ids"]
-        if ids.ndim != 2 or ids.shape[0] != len(texts):
-            raise ValueError("tokenizer input_ids must have shape [batch, sequence]")
+        if ids.shape[:1] != (len(texts),) or ids.ndim != 2:
+            raise ValueError(f"tokenizer returned input_ids of shape {ids.shape} for {len(texts)} texts")
         bucket = select_static_shape_bucket((ids.shape[1],), tuple((n,) for n in lengths))[0]
         out = {}
         for name, value in arrays.items():
@@ -300,16 +332,7 @@ def make_text_processor(*, tokenizer: Any, batch_builder: Callable[..., Any], ma
     def process(artifacts: Sequence[str | Artifact], *, route: Route, seed: int | None,
                 prompt_name: str | None = None, prompt: str | None = None) -> Any:
         del seed
-        texts = []
-        for a in artifacts:
-            if isinstance(a, Artifact):
-                if a.modality != Modality.TEXT or not isinstance(a.data, str):
-                    raise TypeError("text processors require inline text artifacts")
-                texts.append(a.data)
-            elif isinstance(a, str):
-                texts.append(a)
-            else:
-                raise TypeError("text processors require strings or artifacts")
+        texts = [_text_of(a) for a in artifacts]
         prefix = route_prompt(route, prompt_name, prompt)
         enc = tokenize([prefix + t for t in texts])
         if "attention_mask" not in enc:

@@ -31,14 +31,11 @@ class SentencePooling(nn.Module):
 
     def __init__(self, input_dimension: int, modes: tuple[str, ...] = ("mean",), include_prompt: bool = True) -> None:
         super().__init__()
-        if input_dimension <= 0:
-            raise ValueError("pooling input_dimension must be positive")
         modes = (modes,) if isinstance(modes, str) else tuple(modes)
-        if not modes:
-            raise ValueError("pooling requires at least one mode")
-        bad = tuple(m for m in modes if m not in POOLING_MODES)
-        if bad:
-            raise ValueError(f"unsupported pooling modes: {bad}")
+        unknown = [m for m in modes if m not in POOLING_MODES]
+        if input_dimension < 1 or not modes or unknown:
+            raise ValueError(f"SentencePooling({input_dimension}, {modes}): width >= 1 and modes from "
+                             f"{sorted(POOLING_MODES)} required")
         self.input_dimension = input_dimension
         self.modes = modes
         self.include_prompt = include_prompt
@@ -48,12 +45,10 @@ class SentencePooling(nn.Module):
         return self.input_dimension * len(self.modes)
 
     def forward(self, hidden: torch.Tensor, attention_mask: torch.Tensor) -> torch.Tensor:
-        if hidden.ndim != 3:
-            raise ValueError("token embeddings must have shape [batch, sequence, hidden]")
-        if tuple(attention_mask.shape) != tuple(hidden.shape[:2]):
-            raise ValueError("attention mask must align with token embeddings")
-        if hidden.shape[2] != self.input_dimension:
-            raise ValueError(f"pooling expected hidden dimension {self.input_dimension}; received {hidden.shape[2]}")
+        expected = (*attention_mask.shape, self.input_dimension)
+        if tuple(hidden.shape) != expected:
+            raise ValueError(f"pooling got token states {tuple(hidden.shape)} for a mask of "
+                             f"{tuple(attention_mask.shape)}; expected {expected}")
         valid = attention_mask.to(hidden.device).bool()
         mask = valid[..., None].to(hidden.dtype)
         b, s, _ = hidden.shape
@@ -90,7 +85,7 @@ class SentenceDense(nn.Module):
     def __init__(self, weight: torch.Tensor, bias: torch.Tensor | None = None, activation: str = "tanh") -> None:
         super().__init__()
         if activation not in DENSE_ACTIVATIONS:
-            raise ValueError(f"unsupported dense activation: {activation!r}")
+            raise ValueError(f"Dense activation {activation!r} is not implemented")
         self.weight = nn.Parameter(weight.detach().clone().float())
         self.bias = None if bias is None else nn.Parameter(bias.detach().clone().float())
         self.activation = activation
@@ -156,7 +151,7 @@ class SentenceEncoder(nn.Module):
         for module in postprocessors:
             out = getattr(module, "output_dimension", out)
         if truncate_dimension is not None and not 0 < truncate_dimension <= out:
-            raise ValueError("truncate_dimension must index the final embedding dimension")
+            raise ValueError("truncate_dimension is larger than the embedding or below 1")
         self.truncate_dimension = truncate_dimension
         if metadata is None:
             base = backbone.metadata
@@ -180,7 +175,7 @@ class SentenceEncoder(nn.Module):
     def make_batch(self, *, input_ids, attention_mask, token_type_ids=None):
         builder = getattr(self.backbone, "make_batch", None)
         if not callable(builder):
-            raise TypeError("sentence backbones must implement make_batch")
+            raise TypeError(f"{type(self.backbone).__name__} has no make_batch(); it cannot build token batches")
         return builder(input_ids=input_ids, attention_mask=attention_mask, token_type_ids=token_type_ids)
 
     @staticmethod
@@ -189,7 +184,7 @@ class SentenceEncoder(nn.Module):
             return inputs.backbone_inputs, inputs.pooling_mask
         mask = getattr(inputs, "attention_mask", None)
         if mask is None:
-            raise TypeError("sentence inputs must expose attention_mask")
+            raise TypeError(f"{type(inputs).__name__} has no attention_mask to pool with")
         return inputs, mask
 
     def _post(self, value: torch.Tensor) -> torch.Tensor:
@@ -203,7 +198,7 @@ class SentenceEncoder(nn.Module):
         del route
         hidden_states = getattr(self.backbone, "hidden_states", None)
         if not callable(hidden_states):
-            raise TypeError("sentence backbones must implement hidden_states")
+            raise TypeError(f"{type(self.backbone).__name__} has no hidden_states(); nothing to pool")
         backbone_inputs, mask = self._split(inputs)
         return self._post(self.pooling(hidden_states(backbone_inputs, generator=generator), mask))
 
@@ -211,7 +206,7 @@ class SentenceEncoder(nn.Module):
         del route
         layer_states = getattr(self.backbone, "hidden_states_by_layer", None)
         if not callable(layer_states):
-            raise TypeError("sentence backbone does not expose layerwise hidden states")
+            raise TypeError(f"{type(self.backbone).__name__} has no hidden_states_by_layer()")
         backbone_inputs, mask = self._split(inputs)
         states = layer_states(backbone_inputs, generator=generator)
         return torch.stack([self._post(self.pooling(h, mask)) for h in states])

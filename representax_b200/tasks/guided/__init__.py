@@ -51,9 +51,9 @@ class GISTBatch:
             self.valid = torch.ones(rows, dtype=torch.bool, device=self.guide_anchor.device)
         guides = (self.guide_anchor, self.guide_positive, *self.guide_negatives)
         if any(g.ndim != 2 or not g.is_floating_point() or g.shape[0] != rows for g in guides):
-            raise TypeError("GIST guide embeddings must be aligned floating matrices")
+            raise TypeError("GIST guide embeddings have to be float matrices with one row per batch row")
         if len(self.negatives) != len(self.guide_negatives):
-            raise ValueError("every GIST negative requires matching guide embeddings")
+            raise ValueError(f"{len(self.negatives)} negative columns but {len(self.guide_negatives)} guide columns for them")
         for payload in (self.anchor, self.positive, *self.negatives):
             if leading_rows(payload) != rows:
                 raise ValueError("GIST payloads must contain one row per batch row")
@@ -72,6 +72,18 @@ class GISTLossTerms(NamedTuple):
     masked_candidates: torch.Tensor
 
 
+def _check_gist_options(temperature: float, margin_strategy: str, margin: float) -> None:
+    wrong = []
+    if not (math.isfinite(temperature) and temperature > 0):
+        wrong.append(f"temperature {temperature} (needs a finite value > 0)")
+    if margin_strategy not in ("absolute", "relative"):
+        wrong.append(f"margin_strategy {margin_strategy!r} (absolute or relative)")
+    if not (math.isfinite(margin) and margin >= 0):
+        wrong.append(f"margin {margin} (needs a finite value >= 0)")
+    if wrong:
+        raise ValueError("GIST: bad " + "; ".join(wrong))
+
+
 def _n(x):
     x = x.float()
     return x / torch.clamp(torch.linalg.vector_norm(x, dim=-1, keepdim=True), min=1e-12)
@@ -79,12 +91,10 @@ def _n(x):
 
 def gist_loss_terms(embeddings, guide_embeddings, *, valid=None, temperature=0.01, margin_strategy="absolute",
                     margin=0.0, contrast_anchors=True, contrast_positives=True, row_chunk_size=None) -> GISTLossTerms:
-    if len(embeddings) < 2 or len(embeddings) != len(guide_embeddings):
-        raise ValueError("GIST requires aligned anchor, positive, and guide columns")
-    if not math.isfinite(temperature) or temperature <= 0:
-        raise ValueError("GIST temperature must be finite and positive")
-    if margin_strategy not in {"absolute", "relative"}:
-        raise ValueError("GIST margin_strategy must be 'absolute' or 'relative'")
+    if not 2 <= len(embeddings) == len(guide_embeddings):
+        raise ValueError(f"GIST takes >= 2 embedding columns (anchor, positive, ...) with one guide column each; "
+                         f"got {len(embeddings)} and {len(guide_embeddings)}")
+    _check_gist_options(temperature, margin_strategy, 0.0)
     emb = [_n(e) for e in embeddings]
     guide = [_n(g) for g in guide_embeddings]
     b = emb[0].shape[0]
@@ -132,12 +142,7 @@ class GISTTask:
     contrast_positives: bool = True
 
     def __post_init__(self) -> None:
-        if not math.isfinite(self.temperature) or self.temperature <= 0:
-            raise ValueError("GIST temperature must be finite and positive")
-        if self.margin_strategy not in {"absolute", "relative"}:
-            raise ValueError("GIST margin_strategy must be 'absolute' or 'relative'")
-        if not math.isfinite(self.margin) or self.margin < 0:
-            raise ValueError("GIST margin must be finite and non-negative")
+        _check_gist_options(self.temperature, self.margin_strategy, self.margin)
 
     def representations(self, model, batch: GISTBatch, *, generator=None, encode_fn=encode):
         anchor = encode_fn(model, batch.anchor, route=Route.QUERY, generator=generator)

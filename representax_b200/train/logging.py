@@ -12,13 +12,16 @@ resume so the logs match the restored state exactly.
 
 from __future__ import annotations
 
+import contextlib
 import datetime as _dt
 import json
+import math
 import os
 import queue
+import tempfile
 import threading
 from collections.abc import Mapping, Sequence
-from dataclasses import dataclass, field
+from dataclasses import asdict, dataclass, field, fields
 from pathlib import Path
 from typing import Any, Protocol
 
@@ -27,6 +30,7 @@ import torch
 RUN_SCHEMA = "representax-run-v1"
 EVENT_SCHEMA = "representax-event-v1"
 METRICS_SCHEMA = "representax-metrics-v1"
+_NAMESPACES = frozenset({"train", "valid", "perf"})
 
 
 def _timestamp() -> str:
@@ -34,28 +38,74 @@ def _timestamp() -> str:
 
 
 def _json_value(value: Any) -> Any:
+    """Host JSON form of a metric value: tensors read out, non-finite floats as strings."""
+
     if isinstance(value, torch.Tensor):
-        value = value.detach()
-        if value.numel() == 1:
-            return value.item()
-        return value.cpu().tolist()
+        host = value.detach().cpu()
+        return host.item() if host.numel() == 1 else host.tolist()
     if isinstance(value, Mapping):
-        return {str(k): _json_value(v) for k, v in value.items()}
+        return {str(key): _json_value(item) for key, item in value.items()}
     if isinstance(value, (list, tuple)):
-        return [_json_value(v) for v in value]
-    if isinstance(value, float) and (value != value or value in (float("inf"), float("-inf"))):
-        return str(value)
+        return list(map(_json_value, value))
+    if isinstance(value, float) and not math.isfinite(value):
+        return repr(value)  # 'nan', 'inf', '-inf'
     return value
 
 
 def _atomic_write_json(path: Path, document: Mapping[str, Any]) -> None:
-    tmp = path.with_name(path.name + ".tmp")
-    with open(tmp, "w", encoding="utf-8") as handle:
-        json.dump(document, handle, indent=2, sort_keys=True, default=str)
-        handle.write("\n")
-        handle.flush()
+    """Replace ``path`` by a fully written, fsynced JSON file (readers never see half a file)."""
+
+    fd, scratch = tempfile.mkstemp(prefix=f".{path.name}.", dir=path.parent)
+    try:
+        with os.fdopen(fd, "w", encoding="utf-8") as handle:
+            handle.write(json.dumps(document, indent=2, sort_keys=True, default=str) + "\n")
+            handle.flush()
+            os.fsync(handle.fileno())
+        os.replace(scratch, path)
+    except BaseException:
+        with contextlib.suppress(FileNotFoundError):
+            os.unlink(scratch)
+        raise
+
+
+@dataclass(frozen=True)
+class LogCursor:
+    """Where a checkpoint's view of the run logs ends."""
+
+    events_bytes: int
+    metrics_bytes: int
+    optimizer_step: int
+    sequence: int
+
+    @classmethod
+    def parse(cls, values: Mapping[str, int]) -> "LogCursor":
+        names = [f.name for f in fields(cls)]
+        if sorted(values) != sorted(names):
+            raise ValueError(f"log cursor has keys {sorted(values)}; a cursor has exactly {sorted(names)}")
+        parsed = cls(**{name: int(values[name]) for name in names})
+        negative = [name for name in names if getattr(parsed, name) < 0]
+        if negative:
+            raise ValueError(f"log cursor fields {negative} are negative")
+        return parsed
+
+
+def _cut_log(path: Path, length: int) -> None:
+    """Drop everything after byte ``length`` of an append-only log (resume to a checkpoint)."""
+
+    try:
+        size = path.stat().st_size
+    except FileNotFoundError:
+        raise FileNotFoundError(f"cannot resume: the run log {path} is gone") from None
+    if length > size:
+        raise ValueError(f"cannot resume: checkpoint expects {length} bytes of {path.name}, the file has {size}")
+    with open(path, "r+b") as handle:
+        handle.truncate(length)
         os.fsync(handle.fileno())
-    os.replace(tmp, path)
+
+
+_RESUME_MUST_MATCH = ("scientific", "scientific_fingerprint", "data_contract", "data_fingerprint")
+_DROPPED_ON_RESUME = frozenset({"checkpoint", "completed_iterations", "config", "error", "error_type", "execution",
+                                "finished_at", "optimizer_steps", "runtime", "scientific"})
 
 
 @dataclass(frozen=True)
@@ -89,8 +139,8 @@ class RunLogger:
     def __init__(self, run_directory: str | Path, *, manifest: Mapping[str, Any],
                  reporters: Sequence[Reporter] = (), resume_cursor: Mapping[str, int] | None = None,
                  queue_size: int = 16, initial_optimizer_step: int = 0, console: bool = False) -> None:
-        if queue_size <= 0:
-            raise ValueError("reporter queue_size must be positive")
+        if not queue_size >= 1:
+            raise ValueError(f"queue_size {queue_size} leaves no room for a single report")
         self.run_directory = Path(run_directory).expanduser().resolve()
         self._events_path = self.run_directory / "events.jsonl"
         self._metrics_path = self.run_directory / "metrics.jsonl"
@@ -115,47 +165,30 @@ class RunLogger:
 
     # ------------------------------------------------------------------ resume
     def _resume(self, manifest: Mapping[str, Any], cursor: Mapping[str, int]) -> dict[str, Any]:
-        run_path = self.run_directory / "run.json"
-        if not run_path.is_file():
-            raise FileNotFoundError(f"run manifest is missing: {run_path}")
-        previous = json.loads(run_path.read_text())
-        if previous.get("schema_version") != RUN_SCHEMA or previous.get("kind") != "train":
-            raise ValueError(f"run manifest is incompatible: {run_path}")
-        normalized = _json_value(manifest)
-        for name in ("scientific", "scientific_fingerprint", "data_contract", "data_fingerprint"):
-            if previous.get(name) != normalized.get(name):
-                raise ValueError(f"resumed run {name} differs")
-        required = {"events_bytes", "metrics_bytes", "optimizer_step", "sequence"}
-        if set(cursor) != required:
-            raise ValueError(f"logging cursor keys differ; expected={sorted(required)}, actual={sorted(cursor)}")
-        pos = {k: int(v) for k, v in cursor.items()}
-        if any(v < 0 for v in pos.values()):
-            raise ValueError("logging cursor values must be non-negative")
-        if pos["optimizer_step"] != self._optimizer_step:
-            raise ValueError("logging cursor optimizer_step differs from restored training state")
-        self._truncate(self._events_path, pos["events_bytes"])
-        self._truncate(self._metrics_path, pos["metrics_bytes"])
+        try:
+            previous = json.loads((self.run_directory / "run.json").read_text())
+        except FileNotFoundError:
+            raise FileNotFoundError(f"cannot resume: {self.run_directory} has no run.json") from None
+        if (previous.get("schema_version"), previous.get("kind")) != (RUN_SCHEMA, "train"):
+            raise ValueError(f"cannot resume: {self.run_directory}/run.json is not a {RUN_SCHEMA} training run")
+        incoming = _json_value(manifest)
+        changed = [key for key in _RESUME_MUST_MATCH if previous.get(key) != incoming.get(key)]
+        if changed:
+            raise ValueError(f"cannot resume: the job changed {changed} since the run started")
+        position = LogCursor.parse(cursor)
+        if position.optimizer_step != self._optimizer_step:
+            raise ValueError(f"cannot resume: logs end at optimizer step {position.optimizer_step} but the "
+                             f"restored state is at step {self._optimizer_step}")
+        _cut_log(self._events_path, position.events_bytes)
+        _cut_log(self._metrics_path, position.metrics_bytes)
         self._events = open(self._events_path, "a", encoding="utf-8", buffering=1)
         self._metrics = open(self._metrics_path, "a", encoding="utf-8", buffering=1)
-        self._sequence = pos["sequence"]
-        terminal = {"checkpoint", "completed_iterations", "config", "error", "error_type", "execution",
-                    "finished_at", "optimizer_steps", "runtime", "scientific"}
-        active = {k: v for k, v in previous.items() if k not in terminal}
-        return {**active, "config": normalized.get("config"), "execution": normalized.get("execution"),
-                "scientific": normalized.get("scientific"), "status": "running", "resumed_at": _timestamp(),
-                "resume_count": int(previous.get("resume_count", 0)) + 1}
-
-    @staticmethod
-    def _truncate(path: Path, position: int) -> None:
-        if not path.is_file():
-            raise FileNotFoundError(f"append-only run log is missing: {path}")
-        size = path.stat().st_size
-        if position > size:
-            raise ValueError(f"log cursor {position} is beyond the end of {path} ({size} bytes)")
-        with open(path, "r+b") as handle:
-            handle.truncate(position)
-            handle.flush()
-            os.fsync(handle.fileno())
+        self._sequence = position.sequence
+        kept = {key: value for key, value in previous.items() if key not in _DROPPED_ON_RESUME}
+        kept.update(config=incoming.get("config"), execution=incoming.get("execution"),
+                    scientific=incoming.get("scientific"), status="running", resumed_at=_timestamp(),
+                    resume_count=int(previous.get("resume_count", 0)) + 1)
+        return kept
 
     # ------------------------------------------------------------------ worker
     def _run(self) -> None:
@@ -196,14 +229,14 @@ class RunLogger:
 
     def _put(self, item: _Item) -> _Item:
         if self._closed:
-            raise RuntimeError("run logger is closed")
+            raise RuntimeError("RunLogger.close() was called; nothing more can be logged")
         self.raise_if_failed()
         self._queue.put(item)
         return item
 
     def raise_if_failed(self) -> None:
         if self._error is not None:
-            raise RuntimeError(f"run logger worker failed: {self._error}") from self._error
+            raise RuntimeError(f"the log writer thread stopped: {self._error!r}") from self._error
 
     # ------------------------------------------------------------------ API
     def event(self, name: str, **fields: Any) -> None:
@@ -212,8 +245,8 @@ class RunLogger:
 
     def metrics(self, namespace: str, iteration: int, values: Mapping[str, Any], *,
                 optimizer_step: Any = None) -> None:
-        if namespace not in {"train", "valid", "perf"}:
-            raise ValueError("metric namespace must be train, valid or perf")
+        if namespace not in _NAMESPACES:
+            raise ValueError(f"metric namespace {namespace!r} is not one of {sorted(_NAMESPACES)}")
         self._put(_Item("metrics", (namespace, iteration,
                                     self._optimizer_step if optimizer_step is None else optimizer_step,
                                     dict(values))))
@@ -227,9 +260,10 @@ class RunLogger:
         item = self._put(_Item("flush"))
         item.done.wait()
         self.raise_if_failed()
-        return {"events_bytes": self._events_path.stat().st_size,
-                "metrics_bytes": self._metrics_path.stat().st_size,
-                "optimizer_step": int(self._optimizer_step), "sequence": int(self._sequence)}
+        position = LogCursor(events_bytes=self._events_path.stat().st_size,
+                             metrics_bytes=self._metrics_path.stat().st_size,
+                             optimizer_step=int(self._optimizer_step), sequence=int(self._sequence))
+        return asdict(position)
 
     def close(self, *, status: str = "completed", **fields: Any) -> None:
         if self._closed:
