@@ -111,7 +111,7 @@ def _modernvbert(args, rng_for_rank):
             "documents": "one 512x512 N(0,1) image (64 image tokens) per document",
             "loss": "cached MNR (GradCache), scale 20", "precision": "fp8 linear layers (per-tensor scaled E4M3 / "
             "E5M2 gradients), bf16 elsewhere, fp32 master", "reference_parallelism": "FSDP over 8 GPUs"}
-    return model, task, GradCache(query_chunk_size=mini), FP8_MIXED_POLICY, batch, per_rank, info
+    return model, task, GradCache(query_chunk_size=mini, retain_bytes="auto"), FP8_MIXED_POLICY, batch, per_rank, info
 
 
 def _qwen3vl(args, rng_for_rank):
@@ -164,7 +164,7 @@ def _qwen3vl(args, rng_for_rank):
             "adapters": "packed INT4 base weights + LoRA r16 (alpha 32) on q/k/v/o/gate/up/down",
             "loss": "cached MNR (GradCache), scale 20, last-token pooling",
             "reference_parallelism": "TP=2 x FSDP=4 on 8 GPUs"}
-    return model, task, GradCache(query_chunk_size=mini), BF16_MIXED_POLICY, batch, per_rank, info
+    return model, task, GradCache(query_chunk_size=mini, retain_bytes="auto"), BF16_MIXED_POLICY, batch, per_rank, info
 
 
 BUILDERS = {"mpnet": _mpnet, "modernvbert": _modernvbert, "qwen3vl": _qwen3vl}

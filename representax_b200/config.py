@@ -430,8 +430,9 @@ class B200ExecutionConfig(FrozenConfig):
     deterministic: bool = True
     # GradCache: device bytes that first-pass chunk graphs may keep so their
     # replay forward is skipped (exact same gradient). None (the default) and 0
-    # both mean: replay every chunk, the memory bound GradCache is chosen for.
-    grad_cache_retain_bytes: NonNegativeInt | None = None
+    # both mean: replay every chunk, the memory bound GradCache is chosen for;
+    # "auto" keeps as many as the free HBM allows.
+    grad_cache_retain_bytes: NonNegativeInt | Literal["auto"] | None = None
 
 
 class TrainingConfig(FrozenConfig):

@@ -91,4 +91,45 @@ def barrier(ctx: DistContext) -> None:
         dist.barrier()
 
 
-__all__ = ["DistContext", "LOCAL", "all_reduce_sum_", "barrier", "gather_rows", "init_from_env"]
+class StoreBarrier:
+    """Host barrier over the rendezvous key-value store, usable from any thread.
+
+    Collectives of a process group must be issued in the same order by every
+    rank from one thread; background work (checkpoint writers) instead meets
+    here: each ``wait(name)`` increments a counter under a key unique to that
+    name and call count and polls it until all ``world_size`` ranks arrived.
+    A rank that never arrives makes the others raise :class:`TimeoutError`
+    after ``timeout_s`` (the process keeps running; the caller decides).
+    """
+
+    def __init__(self, store, rank: int, world_size: int, *, prefix: str = "rx-barrier",
+                 timeout_s: float = 300.0, poll_s: float = 0.005) -> None:
+        self.store, self.rank, self.world_size = store, rank, world_size
+        self.prefix, self.timeout_s, self.poll_s = prefix, timeout_s, poll_s
+        self._calls: dict[str, int] = {}
+
+    @classmethod
+    def from_default_group(cls, ctx: DistContext, **kwargs) -> "StoreBarrier | None":
+        if not ctx.enabled:
+            return None
+        from torch.distributed import distributed_c10d
+
+        return cls(distributed_c10d._get_default_store(), ctx.rank, ctx.world_size, **kwargs)
+
+    def wait(self, name: str) -> None:
+        import time
+
+        generation = self._calls.get(name, 0)
+        self._calls[name] = generation + 1
+        key = f"{self.prefix}/{name}/{generation}"
+        arrived = self.store.add(key, 1)
+        deadline = time.monotonic() + self.timeout_s
+        while arrived < self.world_size:
+            if time.monotonic() > deadline:
+                raise TimeoutError(f"barrier {name!r}: {arrived} of {self.world_size} ranks arrived within "
+                                   f"{self.timeout_s:.0f}s (rank {self.rank} waiting)")
+            time.sleep(self.poll_s)
+            arrived = self.store.add(key, 0)
+
+
+__all__ = ["DistContext", "LOCAL", "StoreBarrier", "all_reduce_sum_", "barrier", "gather_rows", "init_from_env"]

@@ -11,8 +11,17 @@ Storage differs by design: instead of Orbax, each checkpoint directory holds
 ``state.safetensors`` (fp32 master parameters by name, both AdamW moments,
 the optimizer scalars) written by a background thread from a pinned host
 snapshot taken on a side CUDA stream, plus ``progress.json`` (iteration,
-optimizer step, data cursor, logging cursor, rng seed). Under FSDP every rank
-writes its own ``state.rank{r}.safetensors`` shard and rank 0 the manifest.
+optimizer step, data cursor, logging cursor, rng seed).
+
+With several ranks every rank writes its own ``state.rank{r}.safetensors``
+(its optimizer shard plus the parameters it holds) into a staging directory;
+ranks meet at host barriers (``StoreBarrier``, safe from the writer thread)
+before writing, after writing and after publication. Only rank 0 clears a
+stale staging directory (before the first barrier), hashes every shard,
+writes ``progress.json`` / ``checkpoint.json`` / the marker and renames the
+staging directory into place; nobody removes a directory another rank may
+still be writing. Restore checks that the checkpoint was written by the same
+number of ranks and reads the calling rank's shard.
 """
 
 from __future__ import annotations
@@ -150,7 +159,9 @@ class CheckpointManager:
 
     def __init__(self, root: str | Path, *, keep: int = 3, keep_best: int = 1, asynchronous: bool = True,
                  scientific: str = "", data: str = "", rank: int = 0, world_size: int = 1,
-                 metric_mode: str = "min") -> None:
+                 metric_mode: str = "min", barrier=None) -> None:
+        if world_size > 1 and barrier is None:
+            raise ValueError("a multi-rank CheckpointManager needs a host barrier (StoreBarrier)")
         self.root = Path(root)
         self.keep = keep
         self.keep_best = keep_best
@@ -160,6 +171,7 @@ class CheckpointManager:
         self.rank = rank
         self.world_size = world_size
         self.metric_mode = metric_mode
+        self.barrier = barrier
         self._thread: threading.Thread | None = None
         self._error: BaseException | None = None
         self.events: list[dict[str, Any]] = []
@@ -205,15 +217,32 @@ class CheckpointManager:
             work()
             self.wait()
 
+    def _meet(self, name: str, iteration: int) -> None:
+        if self.barrier is not None:
+            self.barrier.wait(f"checkpoint-{iteration}-{name}")
+
     def _write(self, iteration: int, snapshot: dict[str, torch.Tensor], progress: dict, metric, best) -> None:
-        self.root.mkdir(parents=True, exist_ok=True)
-        directory = self._dir(iteration)
-        if self.rank == 0 and directory.exists():
-            shutil.rmtree(directory)
-        directory.mkdir(parents=True, exist_ok=True)
-        save_file(snapshot, str(directory / self._state_name()))
-        if self.rank != 0:
-            return
+        final = self._dir(iteration)
+        staging = self.root / f".{final.name}.staging"
+        if self.rank == 0:
+            self.root.mkdir(parents=True, exist_ok=True)
+            if staging.exists():  # left by an interrupted save; nobody writes it before "begin"
+                shutil.rmtree(staging)
+            staging.mkdir(parents=True)
+        self._meet("begin", iteration)
+        save_file(snapshot, str(staging / self._state_name()))
+        self._meet("written", iteration)
+        if self.rank == 0:
+            self._publish(iteration, staging, final, progress, metric, best)
+        self._meet("published", iteration)
+
+    def _publish(self, iteration: int, staging: Path, final: Path, progress: dict, metric, best) -> None:
+        directory = staging
+        shards = sorted(p.name for p in directory.glob("*.safetensors"))
+        expected = [STATE_FILE] if self.world_size == 1 else sorted(
+            f"state.rank{r}.safetensors" for r in range(self.world_size))
+        if shards != expected:
+            raise CheckpointWriteError(f"staging {directory} holds {shards}, expected {expected}")
         _atomic_write_json(directory / PROGRESS_FILE, progress)
         files = {p.name: _sha256_file(p) for p in sorted(directory.iterdir())
                  if p.name.endswith(".safetensors") or p.name == PROGRESS_FILE}
@@ -230,11 +259,15 @@ class CheckpointManager:
         _atomic_write_json(directory / CHECKPOINT_MANIFEST, manifest)
         _atomic_write_text(directory / COMPLETE_MARKER, manifest["checkpoint_fingerprint"] + "\n")
         _fsync_dir(directory)
+        if final.exists():  # same iteration saved again (e.g. final == periodic)
+            shutil.rmtree(final)
+        os.replace(directory, final)
+        _fsync_dir(self.root)
         _atomic_write_json(self.root / LATEST_POINTER, {"schema_version": LATEST_SCHEMA, "iteration": iteration,
-                                                        "path": directory.name})
+                                                        "path": final.name})
         if best:
             _atomic_write_json(self.root / BEST_POINTER, {"schema_version": BEST_SCHEMA, "iteration": iteration,
-                                                          "path": directory.name, "metric": metric})
+                                                          "path": final.name, "metric": metric})
         _fsync_dir(self.root)
         self._retain()
 
@@ -277,6 +310,10 @@ class CheckpointManager:
 
     def restore(self, record: CheckpointRecord, device: torch.device | str = "cpu") -> tuple[dict, dict]:
         self.wait()
+        written_by = json.loads((record.path / CHECKPOINT_MANIFEST).read_text()).get("world_size", 1)
+        if written_by != self.world_size:
+            raise IncompleteCheckpointError(f"{record.path} holds {written_by} rank shard(s); this run has "
+                                            f"{self.world_size} ranks")
         tensors = load_file(str(record.path / self._state_name()), device=str(device))
         progress = json.loads((record.path / PROGRESS_FILE).read_text())
         return tensors, progress

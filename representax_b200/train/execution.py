@@ -14,11 +14,12 @@ autograd and back-propagated with its slice of the representation gradient.
 Replay draws the same random streams as the first pass, so the update equals
 the direct one.
 
-On a GPU with memory to spare, the first pass keeps the autograd graph of as
-many chunks as fit in ``retain_bytes`` (by default the free HBM minus a
-reserve for replaying the others): those chunks are back-propagated straight
-from their first-pass graph instead of being re-encoded. The gradient is the
-same; only the recomputation is skipped.
+Optionally (``retain_bytes``, off by default so GradCache keeps its memory
+bound), the first pass keeps the autograd graph of as many chunks as fit in
+that many bytes (``"auto"``: the free HBM minus a reserve for replaying the
+others): those chunks are back-propagated straight from their first-pass
+graph instead of being re-encoded. The gradient is the same; only the
+recomputation is skipped.
 """
 
 from __future__ import annotations
@@ -123,7 +124,10 @@ class RetainBudget:
 
     RESERVE = 12 * 2 ** 30
 
-    def __init__(self, limit: int | None, device: torch.device | None) -> None:
+    def __init__(self, limit: int | str | None, device: torch.device | None) -> None:
+        if limit is not None and limit != "auto" and not (isinstance(limit, int) and limit >= 0):
+            raise ValueError(f"retain_bytes is a byte count >= 0, 'auto' or None, not {limit!r}")
+        limit = None if limit == "auto" else (limit or 0)
         self.enabled = device is not None and device.type == "cuda" and limit != 0
         self.device = device
         if self.enabled and limit is None:
@@ -200,7 +204,9 @@ class GradCache:
     document_chunk_size: int | None = None
     loss_row_chunk_size: int | None = None
     fused: bool = True
-    retain_bytes: int | None = None
+    # Bytes of first-pass chunk graphs that may stay resident: 0/None = replay
+    # every chunk (the GradCache memory bound), "auto" = free HBM minus a reserve.
+    retain_bytes: int | str | None = 0
     stats: dict = field(default_factory=dict, compare=False, repr=False)
 
     def __post_init__(self) -> None:

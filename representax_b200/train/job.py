@@ -20,7 +20,7 @@ from typing import Any
 import torch
 
 from representax_b200.config import JobConfig
-from representax_b200.parallel.dist import LOCAL, DistContext
+from representax_b200.parallel.dist import LOCAL, DistContext, StoreBarrier
 from representax_b200.precision import resolve_precision_policy
 
 from .checkpoint import CheckpointManager, scientific_fingerprint
@@ -219,8 +219,9 @@ def run_job(job: JobConfig, run_directory: str | Path, *, resume: bool = False, 
     if job.checkpointing is not None:
         checkpoints = CheckpointManager(run_directory / "checkpoints", keep=job.checkpointing.keep,
                                         asynchronous=job.checkpointing.asynchronous, scientific=sci, data=data_fp,
-                                        rank=dist.rank, world_size=1,
-                                        metric_mode=job.evaluation.primary_metric_mode if job.evaluation else "min")
+                                        rank=dist.rank, world_size=dist.world_size,
+                                        metric_mode=job.evaluation.primary_metric_mode if job.evaluation else "min",
+                                        barrier=StoreBarrier.from_default_group(dist))
         if resume:
             record = checkpoints.latest()
             if record is not None:

@@ -17,8 +17,22 @@ class StepMetrics:
     learning_rate: float
     optimizer_step: torch.Tensor
     metrics: dict[str, torch.Tensor] = field(default_factory=dict)
+    # Copy of the device status word taken right after the step's kernels were
+    # queued (CUDA only). Reading it here, one step late like the other
+    # scalars, surfaces a bounded device wait that ran out without a per-step
+    # synchronisation.
+    device_status: torch.Tensor | None = None
 
     def to_host(self) -> dict[str, float]:
+        if self.device_status is not None:
+            code = int(self.device_status[0])
+            if code != 0:
+                from representax_b200.ops._ext import STATUS_MESSAGES, KernelTimeoutError, status
+
+                if self.device_status.is_cuda:
+                    status(self.device_status.device).zero_()  # the live word; this copy stays as read
+                raise KernelTimeoutError(f"a kernel of this training step reported: "
+                                         f"{STATUS_MESSAGES.get(code, f'status {code}')}")
         out = {
             "loss": float(self.loss),
             "gradient_norm": float(self.gradient_norm),

@@ -189,9 +189,14 @@ class TrainStep:
         loss, metrics = self._loss_and_grads(batch, iteration)
         self._apply_update(loss, metrics, lr)
         s = self.state.scalars
+        device_status = None
+        if self._native:
+            from representax_b200.ops._ext import status
+
+            device_status = status(self.state.store.device)[:1].clone()
         return StepMetrics(loss=loss.detach(), gradient_norm=s[3].clone(), finite=s[1].clone() > 0,
                            learning_rate=lr, optimizer_step=s[2].clone(),
-                           metrics={k: v.detach() for k, v in metrics.items()})
+                           metrics={k: v.detach() for k, v in metrics.items()}, device_status=device_status)
 
 
 def build_train_step(state: TrainState, task: Any, **kwargs) -> TrainStep:
