@@ -170,6 +170,57 @@ def bench_norm(timer, hbm, flops_peak, tag, report):
             f"frac_of_{tag}_hbm": by / t / hbm})
 
 
+def bench_mnr(timer, hbm, flops_peak, tag, report):
+    """MNR similarity products (config 2: 4096 pairs, width 768).
+
+    ``scores`` is the fused staging + tcgen05 scoring kernel; with ``owners`` > 1
+    the candidate rows sit in that many separate buffers (a per-rank slice of
+    an N-GPU run emulated on one GPU: staging, readiness counters and the
+    owner-rotated tile order, but local instead of NVLink traffic). FLOPs are
+    counted as 2 M N K (the split-bf16 scheme issues three MMAs per product).
+    """
+
+    from representax_b200.ops._ext import ext
+    from representax_b200.ops.mnr import split_bf16, tc_gemm, tc_scores
+
+    C = ext()
+    width = 768
+    for rows, owners, cand_rows in ((4096, 1, 4096), (512, 8, 512)):
+        q = torch.nn.functional.normalize(torch.randn(rows, width, device="cuda"), dim=1)
+        cands = [torch.nn.functional.normalize(torch.randn(cand_rows, width, device="cuda"), dim=1)
+                 for _ in range(owners)]
+        ptrs = [c.data_ptr() for c in cands]
+        n = owners * cand_rows
+        t = timer(lambda: tc_scores(q, ptrs, cand_rows, 0))
+        flops = 2 * rows * n * width
+        report({"kernel": "mnr_scores_tc", "M": rows, "N": n, "K": width, "owners": owners, "ms": t * 1e3,
+                "tflops": flops / t / 1e12, f"frac_of_{tag}_bf16": flops / t / flops_peak})
+        scores, qs, ds = tc_scores(q, ptrs, cand_rows, 0)
+        g = torch.randn(rows, n, device="cuda") * 1e-3
+        gs = split_bf16(g)
+        dq = torch.empty(rows, width, device="cuda")
+        dd = torch.empty(n, width, device="cuda")
+        t = timer(lambda: tc_gemm(gs, False, ds, True, rows, width, n, out=dq))
+        report({"kernel": "mnr_dq_tc", "M": rows, "N": width, "K": n, "ms": t * 1e3,
+                "tflops": flops / t / 1e12, f"frac_of_{tag}_bf16": flops / t / flops_peak})
+        t = timer(lambda: tc_gemm(gs, True, qs, True, n, width, rows, out=dd))
+        report({"kernel": "mnr_dd_tc", "M": n, "N": width, "K": rows, "ms": t * 1e3,
+                "tflops": flops / t / 1e12, f"frac_of_{tag}_bf16": flops / t / flops_peak})
+        t = timer(lambda: split_bf16(g))
+        by = g.numel() * 8
+        report({"kernel": "mnr_split", "elements": g.numel(), "ms": t * 1e3, "gbs": by / t / 1e9,
+                f"frac_of_{tag}_hbm": by / t / hbm})
+        if owners == 1:  # the fp32 CUDA-core GEMM it replaces
+            out = torch.empty(rows, n, device="cuda")
+            cat = torch.cat(cands)
+            t = timer(lambda: C.sgemm(q, False, cat, False, out, 1.0, False))
+            report({"kernel": "mnr_scores_simt_fp32", "M": rows, "N": n, "K": width, "ms": t * 1e3,
+                    "tflops": flops / t / 1e12})
+            ref = q.double() @ cat.double().T
+            report({"check": "mnr_scores_tc_max_abs_err_vs_fp64",
+                    "value": (scores.double() - ref).abs().max().item()})
+
+
 def main(argv=None):
     parser = argparse.ArgumentParser()
     parser.add_argument("--only", default="gemm,attention,norm")
@@ -193,6 +244,8 @@ def main(argv=None):
         bench_attention(timer, hbm, flops_peak, tag, report)
     if "norm" in selected:
         bench_norm(timer, hbm, flops_peak, tag, report)
+    if "mnr" in selected:
+        bench_mnr(timer, hbm, flops_peak, tag, report)
     from representax_b200.ops._ext import check_status
 
     torch.cuda.synchronize()

@@ -85,6 +85,14 @@ void peer_sgemm(const at::Tensor& A, bool a_mn, const at::Tensor& b_ptrs, int64_
                 bool b_seg_k, int64_t M, int64_t N, int64_t K, at::Tensor& C, const c10::optional<at::Tensor>& c_ptrs,
                 int64_t seg_c, int64_t c_slot, double alpha, bool accumulate);
 void slot_reduce(const at::Tensor& slots, int64_t world, at::Tensor& out, bool accumulate);
+void mnr_split(const at::Tensor& src, at::Tensor& hi, at::Tensor& lo);
+void mnr_tc_scores(const at::Tensor& rows, const std::vector<int64_t>& src_ptrs, int64_t src_rows, int64_t rank,
+                   at::Tensor& a_hi, at::Tensor& a_lo, at::Tensor& b_hi, at::Tensor& b_lo, at::Tensor& ready,
+                   at::Tensor& scores, double alpha, const at::Tensor& status);
+void mnr_tc_gemm(const at::Tensor& a_hi, const at::Tensor& a_lo, bool a_mn, const at::Tensor& b_hi,
+                 const at::Tensor& b_lo, bool b_mn, int64_t M, int64_t N, int64_t K,
+                 const c10::optional<at::Tensor>& out, const std::vector<int64_t>& route_ptrs, int64_t route_seg,
+                 int64_t route_off, int64_t ldc, double alpha, bool accumulate, const at::Tensor& status);
 void sharded_grad_reduce(const at::Tensor& grad_ptrs, int64_t world, int64_t off, int64_t n, at::Tensor& shard,
                          at::Tensor& norm_sq);
 void sharded_adamw(const at::Tensor& shard_grad, int64_t off, int64_t n, const at::Tensor& master_ptrs,
@@ -135,6 +143,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("signal_barrier", &rx::signal_barrier);
   m.def("peer_sgemm", &rx::peer_sgemm);
   m.def("slot_reduce", &rx::slot_reduce);
+  m.def("mnr_split", &rx::mnr_split, "fp32 -> (hi, lo) bf16 split");
+  m.def("mnr_tc_scores", &rx::mnr_tc_scores, "tcgen05 MNR scores with the candidate all-gather fused in");
+  m.def("mnr_tc_gemm", &rx::mnr_tc_gemm, "tcgen05 split-bf16 GEMM, local or row-routed (peer) output");
   m.def("sharded_grad_reduce", &rx::sharded_grad_reduce);
   m.def("sharded_adamw", &rx::sharded_adamw);
   m.def("int4_dequantize", &rx::int4_dequantize);

@@ -142,30 +142,38 @@ def read_local_artifact(artifact: Artifact) -> bytes:
 
 
 def read_http_artifact(artifact: Artifact) -> bytes:
-    """HTTP(S) read with a Range header and an If-Match ETag pin."""
+    """HTTP(S) read of a pinned object (``If-Match`` ETag), or of an exact byte range.
+
+    A byte range must come back as a 206 with the matching ``Content-Range``;
+    a server that ignores the range is refused rather than downloading the
+    whole object. Archive members are not read over HTTP (that would fetch the
+    whole archive); register a reader for an indexed archive format instead.
+    """
 
     import urllib.request
 
     if artifact.etag is None:
-        raise ValueError("remote artifacts must pin an etag")
+        raise ValueError(f"{artifact.uri}: remote artifacts pin the object with an etag")
+    if artifact.archive_member is not None:
+        raise ValueError(f"{artifact.uri}: reading archive member {artifact.archive_member!r} over HTTP would "
+                         "download the whole archive; register an indexed reader for this scheme")
     request = urllib.request.Request(artifact.uri, headers={"If-Match": artifact.etag})
-    if artifact.byte_range is not None and artifact.archive_member is None:
+    if artifact.byte_range is not None:
         start, stop = artifact.byte_range
         request.add_header("Range", f"bytes={start}-{stop - 1}")
     with urllib.request.urlopen(request) as response:  # noqa: S310 - explicit user URI
-        etag = response.headers.get("ETag")
-        if etag is not None and etag.strip('"') != artifact.etag.strip('"'):
-            raise ValueError("remote object changed: ETag mismatch")
+        seen = response.headers.get("ETag")
+        if seen is None or seen.strip('"') != artifact.etag.strip('"'):
+            raise ValueError(f"{artifact.uri}: server ETag {seen!r} is not the pinned {artifact.etag!r}")
+        if artifact.byte_range is not None:
+            start, stop = artifact.byte_range
+            got_range = response.headers.get("Content-Range") or ""
+            if getattr(response, "status", None) != 206 or not got_range.startswith(f"bytes {start}-{stop - 1}/"):
+                raise OSError(f"{artifact.uri}: asked for bytes {start}-{stop - 1}, server answered status "
+                              f"{getattr(response, 'status', None)} with Content-Range {got_range!r}")
         data = response.read()
-    if artifact.archive_member is not None:
-        buffer = io.BytesIO(data)
-        if zipfile.is_zipfile(buffer):
-            data = zipfile.ZipFile(buffer).read(artifact.archive_member)
-        else:
-            buffer.seek(0)
-            with tarfile.open(fileobj=buffer) as archive:
-                data = archive.extractfile(artifact.archive_member).read()
-        data = _span(data, artifact.byte_range)
+    if artifact.byte_range is not None and len(data) != artifact.byte_range[1] - artifact.byte_range[0]:
+        raise EOFError(f"{artifact.uri}: byte range {artifact.byte_range} returned {len(data)} bytes")
     return data
 
 

@@ -8,9 +8,10 @@ src/representax/tasks/retrieval/mnr.py:123-379:
     loss = mean of row_loss over active rows (valid, with positive weight)
 
 (symmetric mode averages it with the transposed direction). On CUDA the
-similarity matrices and both gradient products run in the fp32 tiled GEMM of
-``csrc/mnr.cu`` and the masked log-sum-exp / cross-entropy / logit gradient in
-one row kernel; elsewhere the same formula runs in PyTorch.
+similarity matrices and both gradient products run on the tcgen05 tensor cores
+(``csrc/mnr_tc.cu``: split-bf16 operands, fp32 accumulation) and the masked
+log-sum-exp / cross-entropy / logit gradient in one row kernel
+(``csrc/mnr.cu``); elsewhere the same formula runs in PyTorch.
 """
 
 from __future__ import annotations
@@ -61,6 +62,82 @@ def _active_count(weights, row_valid, cand_valid):
     return (row_valid & (w.sum(1) > 0)).sum().clamp(min=1).to(torch.float32)
 
 
+# --------------------------------------------------------------------------- tensor-core path
+# The similarity products run on tcgen05 with every fp32 operand split into a
+# bf16 (hi, lo) pair (three MMAs per K step, ~1e-5 agreement with fp32). The
+# operands' row counts are padded to multiples of 8 (16-byte TMA strides);
+# padded candidates are invalid (masked out of the log-sum-exp, zero gradient).
+
+_READY: dict[int, torch.Tensor] = {}
+
+
+def _ready(device: torch.device) -> torch.Tensor:
+    buf = _READY.get(device.index)
+    if buf is None:
+        buf = torch.zeros(32, dtype=torch.int32, device=device)
+        _READY[device.index] = buf
+    return buf
+
+
+def _status(device: torch.device) -> torch.Tensor:
+    from ._ext import status
+
+    return status(device)
+
+
+def split_bf16(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """fp32 ``x`` -> (hi, lo) bf16 with hi = bf16(x), lo = bf16(x - hi)."""
+
+    x = x.contiguous()
+    hi = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
+    lo = torch.empty_like(hi)
+    ext().mnr_split(x, hi, lo)
+    return hi, lo
+
+
+def tc_scores(rows: torch.Tensor, cand_ptrs: list[int], cand_rows: int, rank: int):
+    """``rows . candidates^T`` where rank r's candidates start at ``cand_ptrs[r]``.
+
+    Returns the fp32 scores and the split operands (rows, all candidates) that
+    the kernel staged on this GPU, for the gradient products.
+    """
+
+    m, k = rows.shape
+    n = len(cand_ptrs) * cand_rows
+    dev = rows.device
+    a = (torch.empty(m, k, dtype=torch.bfloat16, device=dev), torch.empty(m, k, dtype=torch.bfloat16, device=dev))
+    b = (torch.empty(n, k, dtype=torch.bfloat16, device=dev), torch.empty(n, k, dtype=torch.bfloat16, device=dev))
+    scores = torch.empty(m, n, dtype=torch.float32, device=dev)
+    ext().mnr_tc_scores(rows.contiguous(), [int(p) for p in cand_ptrs], cand_rows, rank, a[0], a[1], b[0], b[1],
+                        _ready(dev), scores, 1.0, _status(dev))
+    return scores, a, b
+
+
+def tc_gemm(a, a_mn: bool, b, b_mn: bool, m: int, n: int, k: int, *, out: torch.Tensor | None = None,
+            route: list[int] | None = None, route_rows: int = 1, route_offset: int = 0, ldc: int | None = None,
+            accumulate: bool = False) -> None:
+    """``out (+)= A . B^T`` on split operands (A [m, k] or [k, m], B [n, k] or [k, n]).
+
+    With ``route`` the output rows go to other ranks' memory: row i lands at
+    ``route[i // route_rows] + route_offset + (i % route_rows) * ldc`` (fp32).
+    """
+
+    dev = a[0].device
+    ext().mnr_tc_gemm(a[0], a[1], a_mn, b[0], b[1], b_mn, m, n, k, out, [int(p) for p in (route or [])],
+                      route_rows, route_offset, ldc if ldc is not None else n, 1.0, accumulate, _status(dev))
+
+
+def _pad_rows(x: torch.Tensor, rows: int, value=0) -> torch.Tensor:
+    if x.shape[0] == rows:
+        return x.contiguous()
+    pad = torch.full((rows - x.shape[0], *x.shape[1:]), value, dtype=x.dtype, device=x.device)
+    return torch.cat([x, pad]).contiguous()
+
+
+def _up8(n: int) -> int:
+    return (n + 7) // 8 * 8
+
+
 class _NativeMNR(torch.autograd.Function):
     """Normalised embeddings in, (loss, forward, reverse) out."""
 
@@ -69,49 +146,56 @@ class _NativeMNR(torch.autograd.Function):
         C = ext()
         dev = qn.device
         half = 0.5 if symmetric else 1.0
-        qn = qn.contiguous()
-        dn = dn.contiguous()
-        weights = weights.to(torch.float32).contiguous()
+        lq, ld = qn.shape[0], dn.shape[0]
+        pq, pd = _up8(lq), _up8(ld)
+        qp, dp = _pad_rows(qn.float(), pq), _pad_rows(dn.float(), pd)
+        qv, dv = _pad_rows(q_valid.bool(), pq, False), _pad_rows(d_valid.bool(), pd, False)
+        w = torch.zeros(pq, pd, dtype=torch.float32, device=dev)
+        w[:lq, :ld] = weights.to(torch.float32)
 
-        def direction(rows, cands, w, rv, cv):
-            cos = torch.empty(rows.shape[0], cands.shape[0], device=dev, dtype=torch.float32)
-            C.sgemm(rows, False, cands, False, cos, 1.0, False)
-            n_active = _active_count(w, rv, cv)
+        def direction(scores, w_dir, rv, cv):
+            n_active = _active_count(w_dir, rv, cv)
             coef = (half / n_active).reshape(1)
-            grad = torch.empty_like(cos)
-            row_loss = torch.empty(rows.shape[0], device=dev)
-            row_active = torch.empty(rows.shape[0], device=dev)
-            C.mnr_rows(cos, w, rv, cv, grad, row_loss, row_active, float(scale), coef)
-            loss = (row_loss * row_active).sum() / n_active
-            return loss, grad
+            grad = torch.empty_like(scores)
+            row_loss = torch.empty(scores.shape[0], device=dev)
+            row_active = torch.empty(scores.shape[0], device=dev)
+            C.mnr_rows(scores, w_dir, rv, cv, grad, row_loss, row_active, float(scale), coef)
+            return (row_loss * row_active).sum() / n_active, grad
 
-        forward_loss, grad_f = direction(qn, dn, weights, q_valid, d_valid)
+        scores_f, q_split, d_split = tc_scores(qp, [dp.data_ptr()], pd, 0)
+        forward_loss, grad_f = direction(scores_f, w, qv, dv)
+        del scores_f
         if symmetric:
-            reverse_loss, grad_r = direction(dn, qn, weights.T.contiguous(), d_valid, q_valid)
+            scores_r, _, _ = tc_scores(dp, [qp.data_ptr()], pq, 0)
+            reverse_loss, grad_r = direction(scores_r, w.T.contiguous(), dv, qv)
+            del scores_r
             loss = (forward_loss + reverse_loss) / 2.0
         else:
             reverse_loss = torch.zeros((), device=dev)
-            grad_r = None
+            grad_r = torch.empty(0, device=dev)
             loss = forward_loss.clone()
-        ctx.save_for_backward(qn, dn, grad_f, grad_r if grad_r is not None else torch.empty(0, device=dev))
-        ctx.symmetric = symmetric
+        ctx.save_for_backward(grad_f, grad_r, *q_split, *d_split)
+        ctx.meta = (symmetric, lq, ld, pq, pd, qn.shape[1])
         ctx.mark_non_differentiable(forward_loss, reverse_loss)
         return loss, forward_loss, reverse_loss
 
     @staticmethod
     def backward(ctx, grad_loss, _gf, _gr):
-        C = ext()
-        qn, dn, grad_f, grad_r = ctx.saved_tensors
-        dq = torch.empty_like(qn)
-        dd = torch.empty_like(dn)
-        # dq = G_f dn ; dd = G_f^T qn  (+ reverse direction terms)
-        C.sgemm(grad_f, False, dn, True, dq, 1.0, False)
-        C.sgemm(grad_f, True, qn, True, dd, 1.0, False)
-        if ctx.symmetric:
-            C.sgemm(grad_r, False, qn, True, dd, 1.0, True)
-            C.sgemm(grad_r, True, dn, True, dq, 1.0, True)
-        dq = dq * grad_loss
-        dd = dd * grad_loss
+        grad_f, grad_r, q_hi, q_lo, d_hi, d_lo = ctx.saved_tensors
+        symmetric, lq, ld, pq, pd, width = ctx.meta
+        qs, ds = (q_hi, q_lo), (d_hi, d_lo)
+        dev = grad_f.device
+        dq = torch.empty(pq, width, dtype=torch.float32, device=dev)
+        dd = torch.empty(pd, width, dtype=torch.float32, device=dev)
+        gf = split_bf16(grad_f)
+        tc_gemm(gf, False, ds, True, pq, width, pd, out=dq)  # dq = G_f . D
+        tc_gemm(gf, True, qs, True, pd, width, pq, out=dd)   # dd = G_f^T . Q
+        if symmetric:
+            gr = split_bf16(grad_r)
+            tc_gemm(gr, False, qs, True, pd, width, pq, out=dd, accumulate=True)  # dd += G_r . Q
+            tc_gemm(gr, True, ds, True, pq, width, pd, out=dq, accumulate=True)   # dq += G_r^T . D
+        dq = dq[:lq] * grad_loss
+        dd = dd[:ld] * grad_loss
         return dq, dd, None, None, None, None, None
 
 
@@ -125,4 +209,4 @@ def mnr_loss(q, d, weights, q_valid, d_valid, *, scale: float = 20.0, symmetric:
     return loss, forward, reverse
 
 
-__all__ = ["mnr_loss", "mnr_terms_reference", "normalize"]
+__all__ = ["mnr_loss", "mnr_terms_reference", "normalize", "split_bf16", "tc_gemm", "tc_scores"]

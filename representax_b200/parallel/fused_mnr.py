@@ -5,12 +5,14 @@ order; Ld > Lq with hard negatives). Instead of all-gathering the embeddings, co
 [N*L, N*L] objective on every rank and slicing the gradient, every rank:
 
   forward   writes its normalised rows into its peer buffers, barriers, and
-            computes its own L score rows against all N*L candidates with a
-            GEMM whose candidate tiles are loaded directly from the owning
-            ranks' buffers (fused all-gather), then the masked LSE /
-            cross-entropy / logit-gradient row kernel.
-  backward  dQ_local = G D_all reads peers again; the candidate-side product
-            G^T Q_local is written by the GEMM straight into each owner's slot
+            computes its own L score rows against all N*L candidates in one
+            tcgen05 kernel whose stager warps pull the owners' rows over
+            NVLink into local split-bf16 operands while the tensor cores
+            multiply the blocks already staged (fused all-gather), then the
+            masked LSE / cross-entropy / logit-gradient row kernel.
+  backward  dQ_local = G D_all reuses the candidates staged in the forward
+            (no second transfer); the candidate-side product G^T Q_local is
+            written by the tcgen05 epilogue straight into each owner's slot
             buffer (slot = this rank), and after a device barrier every owner
             sums its N slots in rank order (fused, deterministic
             reduce-scatter). Symmetric mode runs the transposed direction the
@@ -34,6 +36,7 @@ import torch
 import torch.distributed as dist
 
 from representax_b200.ops._ext import ext
+from representax_b200.ops.mnr import split_bf16, tc_gemm, tc_scores
 
 from .dist import DistContext, gather_rows
 from .peer import PeerGroup, peer_group
@@ -76,11 +79,20 @@ class ShardedRetrievalBatch:
         return cls(ctx, w.contiguous(), reverse, batch.query_valid.bool(), batch.document_valid.bool(), qv_all, dv_all)
 
 
-def _active(weights, row_valid, col_valid, ctx):
+def _local_active(weights, row_valid, col_valid):
     w = weights * col_valid[None, :].to(weights.dtype)
-    count = (row_valid & (w.sum(1) > 0)).sum().to(torch.float32).reshape(1)
-    dist.all_reduce(count)
-    return torch.clamp(count, min=1.0)
+    return (row_valid & (w.sum(1) > 0)).sum().to(torch.float32).reshape(1)
+
+
+def _active_counts(sb: "ShardedRetrievalBatch", symmetric: bool):
+    """Global active-row counts of both directions in one 8-byte all-reduce."""
+
+    f = _local_active(sb.forward_weights, sb.query_valid, sb.document_valid_all)
+    r = _local_active(sb.reverse_weights, sb.document_valid, sb.query_valid_all) if symmetric else f
+    counts = torch.cat([f, r])
+    dist.all_reduce(counts)
+    counts = torch.clamp(counts, min=1.0)
+    return counts[0:1], counts[1:2]
 
 
 class _ShardedMNR(torch.autograd.Function):
@@ -90,6 +102,9 @@ class _ShardedMNR(torch.autograd.Function):
         C = ext()
         Lq, D = qn.shape
         Ld = dn.shape[0]
+        if Lq % 8 or Ld % 8:
+            raise ValueError(f"fused cross-rank MNR needs per-rank query and document counts divisible by 8 "
+                             f"(got {Lq} and {Ld})")
         world, rank = group.world, group.rank
         dev = qn.device
         half = 0.5 if symmetric else 1.0
@@ -103,48 +118,50 @@ class _ShardedMNR(torch.autograd.Function):
         group.barrier()  # every rank's rows are published
 
         def direction(rows, cands_buf, n_cands, weights, row_valid, col_valid, n_active):
-            n_rows = rows.shape[0]
-            scores = torch.empty(n_rows, world * n_cands, device=dev, dtype=torch.float32)
-            C.peer_sgemm(rows, False, cands_buf.ptrs, n_cands, D, False, False, n_rows, world * n_cands, D, scores,
-                         None, 1, 0, 1.0, False)
+            # scores against every rank's candidates; the kernel pulls the peers'
+            # rows over NVLink into local split operands while it multiplies
+            scores, own, cands = tc_scores(rows, cands_buf.peer_ptrs, n_cands, rank)
             grad = torch.empty_like(scores)
-            row_loss = torch.empty(n_rows, device=dev)
-            row_active = torch.empty(n_rows, device=dev)
+            row_loss = torch.empty(rows.shape[0], device=dev)
+            row_active = torch.empty(rows.shape[0], device=dev)
             coef = (half / n_active).reshape(1)
             C.mnr_rows(scores, weights, row_valid, col_valid, grad, row_loss, row_active, float(scale), coef)
-            return (row_loss * row_active).sum() / n_active.reshape(()), grad
+            return (row_loss * row_active).sum() / n_active.reshape(()), grad, own, cands
 
-        fwd_local, g_f = direction(qn, dbuf, Ld, sb.forward_weights, sb.query_valid, sb.document_valid_all, n_f)
+        fwd_local, g_f, q_own, d_all = direction(qn, dbuf, Ld, sb.forward_weights, sb.query_valid,
+                                                 sb.document_valid_all, n_f)
         if symmetric:
-            rev_local, g_r = direction(dn, qbuf, Lq, sb.reverse_weights, sb.document_valid, sb.query_valid_all,
-                                       n_r)
+            rev_local, g_r, d_own, q_all = direction(dn, qbuf, Lq, sb.reverse_weights, sb.document_valid,
+                                                     sb.query_valid_all, n_r)
         else:
-            rev_local, g_r = torch.zeros((), device=dev), torch.empty(0, device=dev)
-        ctx_.save_for_backward(qn, dn, g_f, g_r)
-        ctx_.meta = (group, symmetric, Lq, Ld, D, qbuf, dbuf, qslots, dslots)
+            rev_local = torch.zeros((), device=dev)
+            empty = torch.empty(0, device=dev)
+            g_r, d_own, q_all = empty, (empty, empty), (empty, empty)
+        ctx_.save_for_backward(g_f, g_r, *q_own, *d_all, *d_own, *q_all)
+        ctx_.meta = (group, symmetric, Lq, Ld, D, qslots, dslots)
         return fwd_local, rev_local
 
     @staticmethod
     def backward(ctx_, grad_fwd, grad_rev):
         C = ext()
-        qn, dn, g_f, g_r = ctx_.saved_tensors
-        group, symmetric, Lq, Ld, D, qbuf, dbuf, qslots, dslots = ctx_.meta
+        g_f, g_r, q_hi, q_lo, da_hi, da_lo, d_hi, d_lo, qa_hi, qa_lo = ctx_.saved_tensors
+        group, symmetric, Lq, Ld, D, qslots, dslots = ctx_.meta
         world, rank = group.world, group.rank
         half = 0.5 if symmetric else 1.0
         # g_* hold d(loss)/d(score) for loss = half * (fwd + rev); rescale by the upstream gradients.
-        g_f = g_f * (grad_fwd / half)
-        dq = torch.empty_like(qn)
-        C.peer_sgemm(g_f, False, dbuf.ptrs, Ld, D, True, True, Lq, D, world * Ld, dq, None, 1, 0, 1.0, False)
-        local_q = torch.tensor([qn.data_ptr()], dtype=torch.int64, device=qn.device)
-        C.peer_sgemm(g_f, True, local_q, D, D, True, False, world * Ld, D, Lq, dq, dslots.ptrs, Ld, rank, 1.0,
-                     False)
-        dd = torch.zeros_like(dn)
+        gf = split_bf16(g_f * (grad_fwd / half))
+        dq = torch.empty(Lq, D, dtype=torch.float32, device=g_f.device)
+        # dQ = G_f . D_all from the candidates staged on this GPU in the forward (no NVLink)
+        tc_gemm(gf, False, (da_hi, da_lo), True, Lq, D, world * Ld, out=dq)
+        # G_f^T . Q: candidate-gradient rows of owner r go straight into slot `rank` of r's buffer
+        tc_gemm(gf, True, (q_hi, q_lo), True, world * Ld, D, Lq, route=dslots.peer_ptrs, route_rows=Ld,
+                route_offset=rank * Ld * D, ldc=D)
+        dd = torch.zeros(Ld, D, dtype=torch.float32, device=g_f.device)
         if symmetric:
-            g_r = g_r * (grad_rev / half)
-            C.peer_sgemm(g_r, False, qbuf.ptrs, Lq, D, True, True, Ld, D, world * Lq, dd, None, 1, 0, 1.0, False)
-            local_d = torch.tensor([dn.data_ptr()], dtype=torch.int64, device=dn.device)
-            C.peer_sgemm(g_r, True, local_d, D, D, True, False, world * Lq, D, Ld, dd, qslots.ptrs, Lq, rank, 1.0,
-                         False)
+            gr = split_bf16(g_r * (grad_rev / half))
+            tc_gemm(gr, False, (qa_hi, qa_lo), True, Ld, D, world * Lq, out=dd)
+            tc_gemm(gr, True, (d_hi, d_lo), True, world * Lq, D, Ld, route=qslots.peer_ptrs, route_rows=Lq,
+                    route_offset=rank * Lq * D, ldc=D)
         group.barrier()  # every rank's slot contributions have landed
         C.slot_reduce(dslots.tensor, world, dd, True)
         if symmetric:
@@ -160,8 +177,7 @@ def sharded_mnr_loss(q: torch.Tensor, d: torch.Tensor, sb: ShardedRetrievalBatch
 
     group = peer_group(sb.ctx, q.device)
     qn, dn = normalize(q).contiguous(), normalize(d).contiguous()
-    n_f = _active(sb.forward_weights, sb.query_valid, sb.document_valid_all, sb.ctx)
-    n_r = _active(sb.reverse_weights, sb.document_valid, sb.query_valid_all, sb.ctx) if symmetric else n_f
+    n_f, n_r = _active_counts(sb, symmetric)
     fwd_local, rev_local = _ShardedMNR.apply(qn, dn, sb, scale, symmetric, group, n_f, n_r)
     values = torch.stack([fwd_local.detach(), rev_local.detach()])
     dist.all_reduce(values)

@@ -359,6 +359,8 @@ def training_tensors(state) -> dict[str, torch.Tensor]:
             out[f"optimizer/exp_avg/{name}"] = view
         for name, view in store.named_views("exp_avg_sq"):
             out[f"optimizer/exp_avg_sq/{name}"] = view
+    for name, buf in getattr(state, "optimizer_state", {}).items():
+        out[f"optimizer/flat/{name}"] = buf
     out["optimizer/scalars"] = state.scalars
     return {k: v.contiguous() for k, v in out.items()}
 
@@ -383,6 +385,10 @@ def load_training_tensors(state, tensors: Mapping[str, torch.Tensor]) -> None:
                     raise IncompleteCheckpointError(f"checkpoint lacks {key}")
                 view.copy_(tensors[key].to(view.device))
         state.scalars.copy_(tensors["optimizer/scalars"].to(state.scalars.device))
+        flat = {k[len("optimizer/flat/"):]: v for k, v in tensors.items() if k.startswith("optimizer/flat/")}
+        if flat:
+            state.optimizer_state.clear()
+            state.optimizer_state.update({k: v.to(store.device).clone() for k, v in flat.items()})
     store.refresh_compute()
 
 

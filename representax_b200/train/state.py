@@ -51,6 +51,8 @@ class TrainState:
     model: torch.nn.Module
     store: object
     scalars: torch.Tensor  # [8] fp32: clip coef, finite, step, norm, skipped
+    # flat buffers of an optimizer other than the fused AdamW (e.g. SGD momentum)
+    optimizer_state: dict = field(default_factory=dict)
 
     @property
     def step(self) -> int:

@@ -23,7 +23,7 @@ from representax_b200.tasks._batch import leading_rows, slice_rows
 
 from .execution import Direct
 from .flat import FlatParameterStore
-from .optimizer import AdamW
+from .optimizer import AdamW, is_flat_optimizer
 from .rng import StreamFactory
 from .state import StepMetrics, TrainState
 
@@ -115,6 +115,9 @@ class TrainStep:
         gate = loss.detach().reshape(1).to(torch.float32)
         for v in metrics.values():
             gate = gate + 0.0 * v.detach().reshape(-1)[:1].to(gate.device, torch.float32)
+        if not isinstance(opt, AdamW):
+            self._flat_update(opt, gate, max_norm, lr)
+            return
         if self._native and store.sharded:
             self._sharded_update(gate, max_norm, lr)
             return
@@ -147,6 +150,34 @@ class TrainStep:
             vhat = store.exp_avg_sq / (1 - opt.b2 ** step)
             update = mhat / (vhat.sqrt() + opt.eps) + opt.weight_decay * store.master
             store.master.add_(update, alpha=-lr)
+            store.refresh_compute()
+
+    def _flat_update(self, opt, gate: torch.Tensor, max_norm: float, lr: float) -> None:
+        """Norm, clip and finite gate as for AdamW, then ``opt.update`` on the flat fp32 buffers.
+
+        Used for optimizers built from other dotted targets (SGD, Lion, user
+        classes); it reads the finite flag on the host once per step.
+        """
+
+        store: FlatParameterStore = self.state.store
+        if store.sharded:
+            raise ValueError("the sharded optimizer layout runs the fused AdamW only; use sharded_optimizer=False "
+                             f"for {type(opt).__name__}")
+        if not is_flat_optimizer(opt):
+            raise TypeError(f"{type(opt).__name__} is not a flat optimizer (lr / init_state / update)")
+        s = self.state.scalars
+        with torch.no_grad():
+            norm = torch.linalg.vector_norm(store.grad.double()).float()
+            finite = bool(torch.isfinite(norm)) and bool(torch.isfinite(gate).all())
+            coef = min(1.0, max_norm / (float(norm) + 1e-6)) if (max_norm > 0 and finite) else 1.0
+            s[0], s[1], s[3] = coef, 1.0 if finite else 0.0, norm
+            if not finite:
+                s[4] += 1
+                return
+            s[2] += 1
+            if not self.state.optimizer_state:
+                self.state.optimizer_state.update(opt.init_state(store.master))
+            opt.update(store.master, store.grad * coef, self.state.optimizer_state, lr, int(s[2].item()))
             store.refresh_compute()
 
     def _sharded_update(self, gate: torch.Tensor, max_norm: float, lr: float) -> None:

@@ -64,3 +64,107 @@ def test_nonfinite_step_keeps_state():
     after = state.store.master.clone()
     after[slot.offset] = before[slot.offset]
     assert torch.equal(after, before)
+
+
+class _HalvingOptimizer:
+    """A user optimizer reached through a dotted target: master -= lr * g / 2."""
+
+    def __init__(self, learning_rate=0.1):
+        self.learning_rate = learning_rate
+
+    def lr(self, step):
+        return self.learning_rate
+
+    def init_state(self, master):
+        return {"calls": torch.zeros(1)}
+
+    def update(self, master, grad, state, lr, step):
+        state["calls"] += 1
+        master.add_(grad, alpha=-lr / 2)
+
+
+def test_optimizers_from_dotted_targets():
+    from representax_b200.config import ComponentConfig, OptimizationConfig
+    from representax_b200.train.optimizer import SGD, AdamW, Lion, build_optimizer
+
+    def build(target, schedule=None, **params):
+        return build_optimizer(OptimizationConfig(optimizer=ComponentConfig(target=target, parameters=params),
+                                                  schedule=schedule))
+
+    assert isinstance(build("optax.adamw", learning_rate=1e-3), AdamW)
+    assert build("optax.adam").weight_decay == 0.0
+    assert isinstance(build("optax.sgd", learning_rate=0.1, momentum=0.9), SGD)
+    assert isinstance(build("optax.lion"), Lion)
+    custom = build("tests.test_train_cpu._HalvingOptimizer", learning_rate=0.2)
+    assert type(custom).__name__ == "_HalvingOptimizer" and custom.learning_rate == 0.2
+    sched = build("optax.sgd", ComponentConfig(target="optax.linear_schedule",
+                                               parameters={"init_value": 1.0, "end_value": 0.0,
+                                                           "transition_steps": 4}))
+    assert sched.lr(2) == 0.5
+    with pytest.raises(ValueError, match="both"):
+        build("optax.sgd", ComponentConfig(target="optax.constant_schedule", parameters={"value": 1.0}),
+              learning_rate=0.1)
+    with pytest.raises(TypeError, match="init_state"):
+        build("collections.OrderedDict")
+    with pytest.raises(ImportError):
+        build("no_such_module.factory")
+
+
+@pytest.mark.parametrize("name", ["sgd", "lion", "custom"])
+def test_flat_optimizers_update_rules(name):
+    from representax_b200.train.optimizer import SGD, Lion
+
+    torch.manual_seed(0)
+    master = torch.randn(10, dtype=torch.float64)
+    grads = [torch.randn(10, dtype=torch.float64) for _ in range(3)]
+    if name == "sgd":
+        opt = SGD(learning_rate=0.1, momentum=0.9, nesterov=True, weight_decay=0.01)
+    elif name == "lion":
+        opt = Lion(learning_rate=0.01, b1=0.9, b2=0.99, weight_decay=0.1)
+    else:
+        opt = _HalvingOptimizer(0.2)
+    state = opt.init_state(master)
+    got = master.clone()
+    for step, g in enumerate(grads, start=1):
+        opt.update(got, g, state, opt.lr(step), step)
+    want, m = master.clone(), torch.zeros(10, dtype=torch.float64)
+    for g in grads:
+        if name == "sgd":
+            g = g + 0.01 * want
+            m = 0.9 * m + g
+            want = want - 0.1 * (g + 0.9 * m)
+        elif name == "lion":
+            c = torch.sign(0.9 * m + 0.1 * g)
+            want = want - 0.01 * (c + 0.1 * want)
+            m = 0.99 * m + 0.01 * g
+        else:
+            want = want - 0.1 * g
+    assert torch.allclose(got, want, atol=1e-12)
+
+
+def test_train_step_with_sgd_checkpoints_its_state(tmp_path):
+    from representax_b200.models.bert import BertConfig, BertEncoder
+    from representax_b200.precision import FP32_POLICY
+    from representax_b200.tasks.retrieval import MNRTask
+    from representax_b200.train.checkpoint import load_training_tensors, training_tensors
+    from representax_b200.train.optimizer import SGD
+    from representax_b200.train.step import TrainStep, init_train_state
+    from representax_b200.data.synthetic import retrieval_pairs
+
+    import numpy as np
+
+    cfg = BertConfig(vocab_size=500, hidden_size=32, intermediate_size=64, num_hidden_layers=1,
+                     num_attention_heads=4, max_position_embeddings=64, hidden_dropout_probability=0.0,
+                     attention_dropout_probability=0.0)
+    state = init_train_state(BertEncoder(cfg, seed=0), device="cpu", precision=FP32_POLICY)
+    step = TrainStep(state, MNRTask(scale=20.0), optimizer=SGD(learning_rate=0.5, momentum=0.9),
+                     precision=FP32_POLICY)
+    batch = retrieval_pairs(np.random.default_rng(0), 4, 16, vocab=500, low=10, min_len=4)
+    before = state.store.master.clone()
+    m = step(batch, 0)
+    assert int(m.optimizer_step) == 1 and not torch.equal(before, state.store.master)
+    tensors = training_tensors(state)
+    assert "optimizer/flat/trace" in tensors
+    state.optimizer_state["trace"].zero_()
+    load_training_tensors(state, tensors)
+    assert torch.equal(state.optimizer_state["trace"], tensors["optimizer/flat/trace"])
