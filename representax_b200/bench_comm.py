@@ -125,9 +125,78 @@ def bench_mnr(rows: int, width: int, report) -> None:
     check_status(dev)
 
 
+def bench_fsdp(report) -> None:
+    """First-use GEMMs of FSDP-sharded BERT-base weights on one GradCache chunk (18432 tokens).
+
+    ``fsdp_gather_gemm_fused``: the weight's flat segments sit in their owners'
+    IPC buffers; one tcgen05 launch copies the remote rows into this GPU's cache
+    (epilogue warps, peer loads) while the producer starts tiles whose rows are
+    in place. ``fsdp_gather_gemm_nccl``: NCCL all_gather of the bf16 weight, then
+    the plain GEMM. ``gemm_local``: the GEMM alone on a local weight.
+    """
+
+    from representax_b200.ops import gemm as G
+    from representax_b200.ops._ext import check_status, ext, status
+    from representax_b200.parallel.dist import DistContext
+    from representax_b200.parallel.peer import peer_group
+
+    world, rank = dist.get_world_size(), dist.get_rank()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    group = peer_group(DistContext(rank=rank, world_size=world, local_rank=dev.index), dev)
+    peak = _peak_flops()
+    rows = 18432
+    ready = torch.zeros(8192, dtype=torch.int32, device=dev)
+    for name, n, k in (("qkv", 2304, 768), ("ffn_in", 3072, 768), ("ffn_out", 768, 3072)):
+        numel = n * k
+        seg = -(-numel // world)
+        seg = (seg + 63) // 64 * 64
+        owner = group.cached(("bench_fsdp", name), seg, torch.bfloat16)
+        g = torch.Generator(device="cpu").manual_seed(11)
+        full = (torch.randn(world * seg, generator=g) * 0.02).to(torch.bfloat16).to(dev)
+        owner.tensor.copy_(full[rank * seg:(rank + 1) * seg])
+        group.barrier()
+        cache = torch.empty(world * seg, dtype=torch.bfloat16, device=dev)
+        w = cache[:numel].view(n, k)
+        x = (torch.randn(rows, k, device=dev) * 0.5).to(torch.bfloat16)
+        bias = torch.zeros(n, dtype=torch.bfloat16, device=dev)
+        out = torch.empty(rows, n, dtype=torch.bfloat16, device=dev)
+        st = status(dev)
+        flops = 2 * rows * n * k
+        remote = (world - 1) * seg * 2
+
+        def fused():
+            ext().gemm_gather(x, w, out, G.EPI_BIAS, G.OUT_BF16, 1.0, bias, None, None, st, 0, 0, 0.0,
+                              owner.peer_ptrs, seg, 0, ready, 0)
+
+        t = _time(fused)
+        bound = max(flops / peak, remote / (NVLINK_GBS * 1e9))
+        report({"case": f"fsdp_gather_gemm_fused_{name}", "world": world, "M": rows, "N": n, "K": k,
+                "ms": t * 1e3, "tflops": flops / t / 1e12, "nvlink_bytes_in": remote, "roofline_ms": bound * 1e3,
+                "frac_of_roofline": bound / t})
+        assert torch.equal(w, full[:numel].view(n, k))
+        gathered = torch.empty(world * seg, dtype=torch.bfloat16, device=dev)
+        wg = gathered[:numel].view(n, k)
+
+        def nccl():
+            dist.all_gather_into_tensor(gathered, owner.tensor[:seg])
+            G.gemm(x, wg, out, epi=G.EPI_BIAS, bias=bias)
+
+        t = _time(nccl)
+        report({"case": f"fsdp_gather_gemm_nccl_{name}", "world": world, "M": rows, "N": n, "K": k,
+                "ms": t * 1e3, "tflops": flops / t / 1e12, "roofline_ms": bound * 1e3, "frac_of_roofline": bound / t})
+        t = _time(lambda: G.gemm(x, wg, out, epi=G.EPI_BIAS, bias=bias, variant=1))
+        report({"case": f"gemm_local_single_cta_{name}", "world": world, "M": rows, "N": n, "K": k,
+                "ms": t * 1e3, "tflops": flops / t / 1e12, "frac_of_peak": flops / t / peak})
+        t = _time(lambda: G.gemm(x, wg, out, epi=G.EPI_BIAS, bias=bias))
+        report({"case": f"gemm_local_pair_{name}", "world": world, "M": rows, "N": n, "K": k,
+                "ms": t * 1e3, "tflops": flops / t / 1e12, "frac_of_peak": flops / t / peak})
+    torch.cuda.synchronize()
+    check_status(dev)
+
+
 def main(argv=None) -> None:
     parser = argparse.ArgumentParser()
-    parser.add_argument("--only", default="mnr")
+    parser.add_argument("--only", default="mnr,fsdp")
     parser.add_argument("--rows", type=int, default=None, help="rows per rank (default 4096 / world)")
     parser.add_argument("--width", type=int, default=768)
     parser.add_argument("--out", default=None)
@@ -147,6 +216,8 @@ def main(argv=None) -> None:
 
     if "mnr" in args.only.split(","):
         bench_mnr(args.rows or 4096 // world, args.width, report)
+    if "fsdp" in args.only.split(","):
+        bench_fsdp(report)
     if args.out and dist.get_rank() == 0:
         with open(args.out, "a") as handle:
             for row in lines:

@@ -26,10 +26,11 @@ named shape, with random-init weights and synthetic inputs:
   text prompt; last-token pooling; cached MNR with global batch 1024 and
   mini-batch 16.
 
-Multi-GPU runs are data parallel (one process per GPU, NCCL, cross-rank
-in-batch negatives through the fused peer-memory MNR kernels, sharded
-optimizer state); the reference's FSDP / TP layouts are recorded beside the
-number. Timing follows ``bench.py``: W untimed warm-up steps, then K steps
+Multi-GPU runs are one process per GPU with cross-rank in-batch negatives
+through the fused peer-memory MNR kernels; ``mpnet`` and ``modernvbert`` run
+their named FSDP layout by default (``--layout``), ``qwen3vl`` runs data
+parallel with a sharded optimizer (its TP x FSDP layout is not built); the
+layout is recorded beside the number. Timing follows ``bench.py``: W untimed warm-up steps, then K steps
 bracketed by a barrier and ``torch.cuda.synchronize()``, CUDA events on the
 launching stream, maximum over ranks; rank 0 prints one JSON line.
 
@@ -179,6 +180,11 @@ def main(argv=None) -> None:
                         help="override the per-rank triplets (mpnet) or global batch (others)")
     parser.add_argument("--dropout", type=float, default=0.1, help="mpnet hidden / attention dropout")
     parser.add_argument("--out", default=None, help="append the JSON line to this file (rank 0)")
+    parser.add_argument("--layout", choices=["auto", "dp", "fsdp"], default="auto",
+                        help="N > 1: dp = replicated weights + sharded optimizer; fsdp = master weights, moments and "
+                             "bf16 owner copies sharded, weights gathered at first use (fused into the forward "
+                             "GEMMs); auto = the configuration's named layout (FSDP for mpnet / modernvbert, dp for "
+                             "qwen3vl, whose TP x FSDP layout is not built)")
     args = parser.parse_args(argv)
 
     import sys
@@ -199,7 +205,10 @@ def main(argv=None) -> None:
     device = torch.device("cuda", ctx.local_rank)
     torch.cuda.set_device(device)
     model, task, execution, policy, make_batch, rows, info = BUILDERS[args.config](args, None)
-    state = init_train_state(model, device=device, precision=policy, dist=ctx, sharded_optimizer=world > 1)
+    layout = args.layout if args.layout != "auto" else ("dp" if args.config == "qwen3vl" else "fsdp")
+    fsdp = layout == "fsdp" and world > 1
+    state = init_train_state(model, device=device, precision=policy, dist=ctx, sharded_optimizer=world > 1,
+                             fsdp=fsdp)
     step = TrainStep(state, task, optimizer=AdamW(learning_rate=2e-5, weight_decay=0.01), precision=policy,
                      execution=execution, max_gradient_norm=1.0, dist=ctx,
                      stochastic=args.config == "mpnet" and args.dropout > 0)
@@ -245,8 +254,10 @@ def main(argv=None) -> None:
                "value": global_rows * args.steps / elapsed, "unit": f"{info['unit_rows']}/s", "n_gpus": world,
                "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * elapsed / args.steps,
                "higher_is_better": True, "dtype": "bf16", "data": "synthetic inputs; random-init weights",
-               "config": dict(info, name=args.config, parallelism=f"dp{world}"
-                              + ("" if world == 1 else " (sharded optimizer, cross-rank negatives)")),
+               "config": dict(info, name=args.config,
+                              parallelism=(f"fsdp{world} (sharded master / moments / bf16 owner copy, fused "
+                                           "gather-GEMM, cross-rank negatives)") if fsdp else
+                              (f"dp{world}" + ("" if world == 1 else " (sharded optimizer, cross-rank negatives)"))),
                "clocks": clocks, "gpu_launches": counter.launches, "final_loss": float(metrics.loss),
                "peak_memory_gb": torch.cuda.max_memory_allocated(device) / 2**30, "impl": "ours"}
         line = json.dumps(out)

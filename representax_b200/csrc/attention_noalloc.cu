@@ -17,19 +17,28 @@ static __device__ __align__(256) unsigned char g_scratch[RX_NOALLOC_SCRATCH_BYTE
 constexpr int kMaxDevices = 64;
 std::mutex g_setup_lock;
 void* g_scratch_ptr[kMaxDevices] = {nullptr};
+// The CUDA error behind the calling thread's last RX_NOALLOC_CUDA_ERROR.
+thread_local cudaError_t g_last_error = cudaSuccess;
+
+int cuda_failed(cudaError_t e) {
+  g_last_error = e;
+  return RX_NOALLOC_CUDA_ERROR;
+}
 
 // Device address of g_scratch on the current device. In host code the name
 // g_scratch is only a host-side stand-in, so the address must be looked up
 // (once per device, with that device current) before a kernel may use it.
 int scratch_address(void** out) {
   int device = 0;
-  if (cudaGetDevice(&device) != cudaSuccess) return RX_NOALLOC_CUDA_ERROR;
+  const cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess) return cuda_failed(e);
   if (device < 0 || device >= kMaxDevices) return RX_NOALLOC_BAD_ARGUMENT;
   std::lock_guard<std::mutex> guard(g_setup_lock);
   if (g_scratch_ptr[device] == nullptr) {
     void* ptr = nullptr;
-    if (cudaGetSymbolAddress(&ptr, g_scratch) != cudaSuccess || ptr == nullptr)
-      return RX_NOALLOC_CUDA_ERROR;
+    const cudaError_t s = cudaGetSymbolAddress(&ptr, g_scratch);
+    if (s != cudaSuccess) return cuda_failed(s);
+    if (ptr == nullptr) return cuda_failed(cudaErrorInvalidSymbol);
     g_scratch_ptr[device] = ptr;
   }
   *out = g_scratch_ptr[device];
@@ -72,6 +81,13 @@ extern "C" int rx_attention_backward_noalloc(
   const uint64_t dvec_bytes = static_cast<uint64_t>(heads) * total_tokens * sizeof(float);
   if (dvec_offset + dvec_bytes > RX_NOALLOC_SCRATCH_BYTES) return RX_NOALLOC_TOO_LARGE;
 
+  // The scratch address is the current device's; the stream must run there too.
+  int current = 0, stream_device = 0;
+  cudaError_t e = cudaGetDevice(&current);
+  if (e != cudaSuccess) return cuda_failed(e);
+  e = cudaStreamGetDevice(stream, &stream_device);
+  if (e != cudaSuccess) return cuda_failed(e);
+  if (stream_device != current) return RX_NOALLOC_BAD_ARGUMENT;
   void* base = nullptr;
   const int setup = scratch_address(&base);
   if (setup != RX_NOALLOC_OK) return setup;
@@ -106,30 +122,51 @@ extern "C" int rx_attention_backward_noalloc(
 
   // The previous call's contents are still in the array: clear the
   // accumulator (dvec is fully overwritten by its kernel).
-  if (cudaMemsetAsync(dq_acc, 0, acc_bytes, stream) != cudaSuccess) return RX_NOALLOC_CUDA_ERROR;
+  // Every launch goes through cudaLaunchKernel, whose return value is that
+  // launch's own status: errors left by unrelated earlier work are neither
+  // reported as this call's nor cleared.
+  e = cudaMemsetAsync(dq_acc, 0, acc_bytes, stream);
+  if (e != cudaSuccess) return cuda_failed(e);
   {
     const int64_t threads = 256;
     const int64_t warps = static_cast<int64_t>(total_tokens) * heads;
-    attn_dvec_kernel<<<static_cast<unsigned>((warps * 32 + threads - 1) / threads), threads, 0, stream>>>(
-        static_cast<const __nv_bfloat16*>(o), ld_o, p.dO, ld_do, dvec, total_tokens, heads, 64);
+    const __nv_bfloat16* o_arg = static_cast<const __nv_bfloat16*>(o);
+    const __nv_bfloat16* do_arg = p.dO;
+    int t_arg = total_tokens, h_arg = heads, d_arg = 64;
+    void* args[] = {&o_arg, &ld_o, &do_arg, &ld_do, &dvec, &t_arg, &h_arg, &d_arg};
+    e = cudaLaunchKernel(reinterpret_cast<const void*>(&attn_dvec_kernel),
+                         dim3(static_cast<unsigned>((warps * 32 + threads - 1) / threads)), dim3(threads), args, 0,
+                         stream);
+    if (e != cudaSuccess) return cuda_failed(e);
   }
-  dim3 grid((max_len + BN - 1) / BN, heads, batch);
-  attn_bwd_kernel<64, false><<<grid, kThreads, bwd_smem_bytes<64>(), stream>>>(p);
+  {
+    void* args[] = {&p};
+    e = cudaLaunchKernel(reinterpret_cast<const void*>(&attn_bwd_kernel<64, false>),
+                         dim3((max_len + BN - 1) / BN, heads, batch), dim3(kThreads), args, bwd_smem_bytes<64>(),
+                         stream);
+    if (e != cudaSuccess) return cuda_failed(e);
+  }
   {
     const int64_t n4 = static_cast<int64_t>(total_tokens) * static_cast<int64_t>(width) / 4;
-    attn_dq_convert_kernel<<<static_cast<unsigned>((n4 + 255) / 256), 256, 0, stream>>>(
-        dq_acc, static_cast<__nv_bfloat16*>(dq), ld_dq, total_tokens, static_cast<int>(width));
+    __nv_bfloat16* dq_arg = static_cast<__nv_bfloat16*>(dq);
+    int t_arg = total_tokens, w_arg = static_cast<int>(width);
+    void* args[] = {&dq_acc, &dq_arg, &ld_dq, &t_arg, &w_arg};
+    e = cudaLaunchKernel(reinterpret_cast<const void*>(&attn_dq_convert_kernel),
+                         dim3(static_cast<unsigned>((n4 + 255) / 256)), dim3(256), args, 0, stream);
+    if (e != cudaSuccess) return cuda_failed(e);
   }
-  if (cudaGetLastError() != cudaSuccess) return RX_NOALLOC_CUDA_ERROR;
   return RX_NOALLOC_OK;
 }
+
+extern "C" int rx_noalloc_last_cuda_error(void) { return static_cast<int>(g_last_error); }
 
 extern "C" const char* rx_noalloc_error_string(int code) {
   switch (code) {
     case RX_NOALLOC_OK: return "ok";
     case RX_NOALLOC_TOO_LARGE:
       return "problem needs more scratch than the library's static array holds (32 MiB)";
-    case RX_NOALLOC_BAD_ARGUMENT: return "null pointer, negative size, or misaligned tensor";
+    case RX_NOALLOC_BAD_ARGUMENT:
+      return "null pointer, negative size, misaligned tensor, or a stream of another device";
     case RX_NOALLOC_CUDA_ERROR: return "a CUDA call failed";
     default: return "unknown code";
   }

@@ -50,7 +50,11 @@ namespace tc {
 
 constexpr int kThreads = 128;
 constexpr int FQ = 128;   // forward: queries per CTA (one per TMEM lane)
-constexpr int FK = 128;   // forward: keys per block
+// forward: keys per block, FK_FOR<D>: 64 for head dim 64 (TMEM S + O = 128
+// columns, 48 KB of shared memory, 64 score registers per thread: four CTAs
+// per SM), 128 for head dim 128
+template <int D>
+constexpr int FK_FOR = D == 64 ? 64 : 128;
 constexpr int BKT = 128;  // backward: keys per CTA
 constexpr int BQB = 64;   // backward: queries per block
 constexpr uint32_t kSub128 = 128 * 128;  // [128 rows][64 bf16] swizzled sub-tile
@@ -58,18 +62,21 @@ constexpr uint32_t kSub64 = 64 * 128;    // [64 rows][64 bf16]
 constexpr float kLog2e = 1.4426950408889634f;
 
 // Barrier slots (uint64) after the tiles.
-enum Bar : int { kBarQ = 0, kBarK, kBarV, kBarS, kBarO, kBarDrain, kNumBars };
+enum Bar : int { kBarQ = 0, kBarK, kBarV, kBarS, kBarO, kBarDrain, kBarQ1, kNumBars };
 
 template <int D>
 struct FwdLayout {
   static constexpr int DS = D / 64;
+  static constexpr int FK = FK_FOR<D>;
+  static constexpr uint32_t KSUB = FK * 128;  // [FK keys][64 bf16] swizzled sub-tile
   static constexpr uint32_t Q = 0;
   static constexpr uint32_t K = Q + DS * kSub128;
-  static constexpr uint32_t V = K + DS * kSub128;
-  static constexpr uint32_t P = V + DS * kSub128;  // [128 q][128 keys] as two sub-tiles
-  static constexpr uint32_t BARS = P + 2 * kSub128;
+  static constexpr uint32_t V = K + DS * KSUB;
+  static constexpr uint32_t P = V + DS * KSUB;  // [128 q][FK keys] as FK / 64 sub-tiles
+  static constexpr uint32_t BARS = P + (FK / 64) * kSub128;
   static constexpr uint32_t BYTES = BARS + kNumBars * 8 + 16 + 1024;  // + TMEM slot + alignment slack
-  static constexpr uint32_t TMEM_COLS = 256;  // S: [0, 128), O: [128, 128 + D)
+  static constexpr uint32_t TMEM_COLS = FK + D <= 128 ? 128 : 256;  // S: [0, FK), O: [FK, FK + D)
+  static constexpr int CTAS_PER_SM = D == 64 ? 4 : 1;
 };
 
 template <int D>
@@ -77,9 +84,11 @@ struct BwdLayout {
   static constexpr int DS = D / 64;
   static constexpr uint32_t K = 0;
   static constexpr uint32_t V = K + DS * kSub128;
+  // Q and dO of query block `it` live in buffer it & 1 (loaded one block ahead)
   static constexpr uint32_t Q = V + DS * kSub128;
   static constexpr uint32_t DO = Q + DS * kSub64;
-  static constexpr uint32_t DST = DO + DS * kSub64;  // dS^T [128 keys][64 q]
+  static constexpr uint32_t QD_STRIDE = 2 * DS * kSub64;  // buffer 1 = buffer 0 + QD_STRIDE
+  static constexpr uint32_t DST = Q + 2 * QD_STRIDE;  // dS^T [128 keys][64 q]
   static constexpr uint32_t PT = DST + kSub128;      // P^T  [128 keys][64 q]; must follow DST
   static constexpr uint32_t LSE = PT + kSub128;      // 64 floats
   static constexpr uint32_t DVEC = LSE + 256;        // 64 floats
@@ -229,11 +238,13 @@ __device__ __forceinline__ uint64_t bwd_keep_bits(const DropoutSite& site, uint3
 
 // ===================================================================== forward
 template <int D>
-__global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
+__global__ void __launch_bounds__(kThreads, FwdLayout<D>::CTAS_PER_SM)
     attn_tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const Params p) {
   using L = FwdLayout<D>;
   constexpr int DS = L::DS;
+  constexpr int FK = L::FK;
+  constexpr int NC = FK / 32;  // 32-column TMEM chunks of a score block
   const int h = blockIdx.y, b = blockIdx.z;
   const int start = p.cu_seqlens[b];
   const int len = p.cu_seqlens[b + 1] - start;
@@ -266,10 +277,10 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
     fence_mbarrier_init();
     mbar_arrive_expect_tx(&bars[kBarQ], DS * kSub128);
     for (int s = 0; s < DS; ++s) tma_load_2d(base + L::Q + s * kSub128, &tmQ, &bars[kBarQ], h * D + 64 * s, start + q_lo);
-    mbar_arrive_expect_tx(&bars[kBarK], DS * kSub128);
-    for (int s = 0; s < DS; ++s) tma_load_2d(base + L::K + s * kSub128, &tmK, &bars[kBarK], kvh * D + 64 * s, start + k_lo);
-    mbar_arrive_expect_tx(&bars[kBarV], DS * kSub128);
-    for (int s = 0; s < DS; ++s) tma_load_2d(base + L::V + s * kSub128, &tmV, &bars[kBarV], kvh * D + 64 * s, start + k_lo);
+    mbar_arrive_expect_tx(&bars[kBarK], DS * L::KSUB);
+    for (int s = 0; s < DS; ++s) tma_load_2d(base + L::K + s * L::KSUB, &tmK, &bars[kBarK], kvh * D + 64 * s, start + k_lo);
+    mbar_arrive_expect_tx(&bars[kBarV], DS * L::KSUB);
+    for (int s = 0; s < DS; ++s) tma_load_2d(base + L::V + s * L::KSUB, &tmV, &bars[kBarV], kvh * D + 64 * s, start + k_lo);
     k_issued = v_issued = 1;
   }
   if (warp == 0) {
@@ -280,7 +291,7 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem, tO = tmem + 128;
+  const uint32_t tS = tmem, tO = tmem + FK;
   const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
   const int row = warp * 32 + lane;
   const int i = q_lo + row;  // this thread's query (sequence-relative)
@@ -325,8 +336,9 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
         const uint32_t idesc_s = idesc_bf16_f32(128, n16, false, false);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * kSub128 + (kk & 3) * 32;
-          umma_f16_ss(tS, smem_desc_sw128(sQ + off, 16, 1024), smem_desc_sw128(sK + off, 16, 1024), idesc_s,
+          const uint32_t off_q = (kk >> 2) * kSub128 + (kk & 3) * 32;
+          const uint32_t off_k = (kk >> 2) * L::KSUB + (kk & 3) * 32;
+          umma_f16_ss(tS, smem_desc_sw128(sQ + off_q, 16, 1024), smem_desc_sw128(sK + off_k, 16, 1024), idesc_s,
                       kk > 0 ? 1u : 0u);
         }
         umma_commit(&bars[kBarS]);
@@ -343,9 +355,9 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
       if (!ok0) report_status(p.status, kStatusTimeoutMma);
       // The S MMA has retired, so the K buffer is free for the next block.
       if (ok0 && j + 1 < nblk) {
-        mbar_arrive_expect_tx(&bars[kBarK], DS * kSub128);
+        mbar_arrive_expect_tx(&bars[kBarK], DS * L::KSUB);
         for (int s = 0; s < DS; ++s)
-          tma_load_2d(base + L::K + s * kSub128, &tmK, &bars[kBarK], kvh * D + 64 * s, start + k0 + FK);
+          tma_load_2d(base + L::K + s * L::KSUB, &tmK, &bars[kBarK], kvh * D + 64 * s, start + k0 + FK);
         ++k_issued;
       }
     }
@@ -357,16 +369,16 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
 
     __syncwarp();
     if (warp_live) {
-      uint32_t r[4][32];
+      uint32_t r[NC][32];
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
+      for (int c = 0; c < NC; ++c)
         if (c < nch) tmem_ld_32x32b_x32(tS + lane_off + c * 32, r[c]);
       tmem_ld_wait();
       const int clo = vis_lo - k0, chi = vis_hi - k0;  // visible columns of this block
       float mx = -INFINITY;
       if (lut_h == nullptr) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < NC; ++c) {
           if (c < nch) {
 #pragma unroll
             for (int e = 0; e < 32; ++e) {
@@ -380,7 +392,7 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
       } else {
         const float* lut_row = lut_h + (k0 - i);  // bias of column c at lut_row[c]
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < NC; ++c) {
           if (c < nch) {
 #pragma unroll
             for (int e = 0; e < 32; ++e) {
@@ -471,7 +483,7 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
         ++v_waited;
         for (int kk = 0; kk < n16 / 16; ++kk) {
           const uint32_t a_off = (kk >> 2) * kSub128 + (kk & 3) * 32;
-          umma_f16_ss(tO, smem_desc_sw128(sP + a_off, 16, 1024), smem_desc_sw128(sV + kk * 2048, kSub128, 1024),
+          umma_f16_ss(tO, smem_desc_sw128(sP + a_off, 16, 1024), smem_desc_sw128(sV + kk * 2048, L::KSUB, 1024),
                       IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(&bars[kBarO]);
@@ -480,9 +492,9 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
       if (!ok0) report_status(p.status, kStatusTimeoutMma);
       // P V has retired: V (and P) are free.
       if (ok0 && j + 1 < nblk) {
-        mbar_arrive_expect_tx(&bars[kBarV], DS * kSub128);
+        mbar_arrive_expect_tx(&bars[kBarV], DS * L::KSUB);
         for (int s = 0; s < DS; ++s)
-          tma_load_2d(base + L::V + s * kSub128, &tmV, &bars[kBarV], kvh * D + 64 * s, start + k0 + FK);
+          tma_load_2d(base + L::V + s * L::KSUB, &tmV, &bars[kBarV], kvh * D + 64 * s, start + k0 + FK);
         ++v_issued;
       }
     }
@@ -567,18 +579,22 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
   float* s_dvs = reinterpret_cast<float*>(base + L::DVEC);   // Dvec * scale
   float* s_diag = p.drel != nullptr ? reinterpret_cast<float*>(base + L::DIAG) : nullptr;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const uint32_t sK = smem_u32(base + L::K), sV = smem_u32(base + L::V), sQ = smem_u32(base + L::Q),
-                 sDO = smem_u32(base + L::DO), sDST = smem_u32(base + L::DST), sPT = smem_u32(base + L::PT);
+  const uint32_t sK = smem_u32(base + L::K), sV = smem_u32(base + L::V), sQ0 = smem_u32(base + L::Q),
+                 sDO0 = smem_u32(base + L::DO), sDST = smem_u32(base + L::DST), sPT = smem_u32(base + L::PT);
 
-  int kv_waited = 0, qd_issued = 0, qd_waited = 0;
+  int kv_waited = 0;
+  int qd_issued[2] = {0, 0}, qd_waited[2] = {0, 0};  // per Q/dO buffer
   auto issue_qd = [&](int it) {
     const int hq = kvh * p.heads_per_kv + it / nqb;
     const int q0 = q_first + (it % nqb) * BQB;
-    mbar_arrive_expect_tx(&bars[kBarQ], 2 * DS * kSub64);
+    const int buf = it & 1;
+    uint64_t* bar = &bars[buf ? kBarQ1 : kBarQ];
+    mbar_arrive_expect_tx(bar, 2 * DS * kSub64);
     for (int s = 0; s < DS; ++s) {
-      tma_load_2d(base + L::Q + s * kSub64, &tmQ, &bars[kBarQ], hq * D + 64 * s, start + q0);
-      tma_load_2d(base + L::DO + s * kSub64, &tmDO, &bars[kBarQ], hq * D + 64 * s, start + q0);
+      tma_load_2d(base + L::Q + buf * L::QD_STRIDE + s * kSub64, &tmQ, bar, hq * D + 64 * s, start + q0);
+      tma_load_2d(base + L::DO + buf * L::QD_STRIDE + s * kSub64, &tmDO, bar, hq * D + 64 * s, start + q0);
     }
+    ++qd_issued[buf];
   };
   if (s_diag != nullptr)
     for (int t = tid; t < BKT + BQB; t += kThreads) s_diag[t] = 0.f;
@@ -592,7 +608,7 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
         tma_load_2d(base + L::V + s * kSub128, &tmV, &bars[kBarK], kvh * D + 64 * s, start + kt0);
       }
       issue_qd(0);
-      qd_issued = 1;
+      if (total_it > 1) issue_qd(1);
     }
   }
   if (warp == 0) {
@@ -627,6 +643,8 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
     const int hq = kvh * p.heads_per_kv + it / nqb;
     const int q0 = q_first + (it % nqb) * BQB;
     const uint32_t ph = static_cast<uint32_t>(it & 1);
+    const int buf = it & 1;
+    const uint32_t sQ = sQ0 + buf * L::QD_STRIDE, sDO = sDO0 + buf * L::QD_STRIDE;
     const int nq16 = (min(BQB, q_end - q0) + 15) & ~15;  // query columns in use
     if (tid < BQB) {
       const int q = q0 + tid;
@@ -641,8 +659,8 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
         kv_waited = ok0 ? 1 : 0;
       }
       if (ok0) {
-        ok0 = mbar_wait(&bars[kBarQ], static_cast<uint32_t>(qd_waited & 1), p.timeout_ns);
-        if (ok0) ++qd_waited;
+        ok0 = mbar_wait(&bars[buf ? kBarQ1 : kBarQ], static_cast<uint32_t>(qd_waited[buf] & 1), p.timeout_ns);
+        if (ok0) ++qd_waited[buf];
       }
       if (ok0) {
         tc_fence_after();
@@ -786,11 +804,9 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
       umma_commit(&bars[kBarO]);
       ok0 = mbar_wait(&bars[kBarO], ph, p.timeout_ns);
       if (!ok0) report_status(p.status, kStatusTimeoutMma);
-      // Q and dO are free: fetch the next block while this one's dQ drains.
-      if (ok0 && it + 1 < total_it) {
-        issue_qd(it + 1);
-        ++qd_issued;
-      }
+      // This block's Q and dO buffer is free: fetch block it + 2 into it (block
+      // it + 1 was fetched one iteration ago and is landing in the other buffer).
+      if (ok0 && it + 2 < total_it) issue_qd(it + 2);
     }
     if (__syncthreads_or(!ok0)) {
       ok = false;
@@ -853,7 +869,8 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
 
   if (!ok && tid == 0) {
     if (total_it > 0 && kv_waited == 0) drain_phase(&bars[kBarK], 1, 0, p);
-    drain_phase(&bars[kBarQ], qd_issued, qd_waited, p);
+    drain_phase(&bars[kBarQ], qd_issued[0], qd_waited[0], p);
+    drain_phase(&bars[kBarQ1], qd_issued[1], qd_waited[1], p);
     if (mma_issued) {
       umma_commit(&bars[kBarDrain]);
       if (!mbar_wait(&bars[kBarDrain], 0, p.timeout_ns)) report_status(p.status, kStatusTimeoutDrain);
@@ -894,8 +911,9 @@ void tc_forward(Params p, int d, int64_t max_len, cudaStream_t st, int device) {
   const int64_t T = p.total_tokens;
   const int kv_heads = p.heads / p.heads_per_kv;
   const CUtensorMap tq = make_tmap_2d_bf16(p.q, T, static_cast<int64_t>(p.heads) * d, p.ldq, 64, tc::FQ);
-  const CUtensorMap tk = make_tmap_2d_bf16(p.k, T, static_cast<int64_t>(kv_heads) * d, p.ldk, 64, tc::FK);
-  const CUtensorMap tv = make_tmap_2d_bf16(p.v, T, static_cast<int64_t>(kv_heads) * d, p.ldv, 64, tc::FK);
+  const int fk = d == 64 ? tc::FK_FOR<64> : tc::FK_FOR<128>;
+  const CUtensorMap tk = make_tmap_2d_bf16(p.k, T, static_cast<int64_t>(kv_heads) * d, p.ldk, 64, fk);
+  const CUtensorMap tv = make_tmap_2d_bf16(p.v, T, static_cast<int64_t>(kv_heads) * d, p.ldv, 64, fk);
   dim3 grid(static_cast<unsigned>((max_len + tc::FQ - 1) / tc::FQ), p.heads, p.batch);
   if (d == 64) {
     static bool done[64] = {false};

@@ -86,6 +86,13 @@ void peer_sgemm(const at::Tensor& A, bool a_mn, const at::Tensor& b_ptrs, int64_
                 int64_t seg_c, int64_t c_slot, double alpha, bool accumulate);
 void slot_reduce(const at::Tensor& slots, int64_t world, at::Tensor& out, bool accumulate);
 void mnr_split(const at::Tensor& src, at::Tensor& hi, at::Tensor& lo);
+void gemm_gather(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, int64_t epi, int64_t out_mode,
+                 double alpha, const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& aux_out,
+                 const c10::optional<at::Tensor>& residual, const at::Tensor& status, int64_t drop_seed,
+                 int64_t drop_stream, double drop_p, const std::vector<int64_t>& shard_ptrs, int64_t shard_numel,
+                 int64_t flat_offset, const at::Tensor& ready, int64_t variant);
+void gather_ranges(const std::vector<int64_t>& shard_ptrs, int64_t shard_numel, const at::Tensor& ranges,
+                   at::Tensor& dst);
 void mnr_tc_scores(const at::Tensor& rows, const std::vector<int64_t>& src_ptrs, int64_t src_rows, int64_t rank,
                    at::Tensor& a_hi, at::Tensor& a_lo, at::Tensor& b_hi, at::Tensor& b_lo, at::Tensor& ready,
                    at::Tensor& scores, double alpha, const at::Tensor& status);
@@ -98,7 +105,7 @@ void sharded_grad_reduce(const at::Tensor& grad_ptrs, int64_t world, int64_t off
 void sharded_adamw(const at::Tensor& shard_grad, int64_t off, int64_t n, const at::Tensor& master_ptrs,
                    const c10::optional<at::Tensor>& copy_ptrs, int64_t world, int64_t rank, at::Tensor& exp_avg,
                    at::Tensor& exp_avg_sq, const at::Tensor& scalars, double lr, double b1, double b2, double eps,
-                   double wd);
+                   double wd, int64_t dst_offset);
 }  // namespace rx
 
 namespace rx {
@@ -144,6 +151,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("peer_sgemm", &rx::peer_sgemm);
   m.def("slot_reduce", &rx::slot_reduce);
   m.def("mnr_split", &rx::mnr_split, "fp32 -> (hi, lo) bf16 split");
+  m.def("gemm_gather", &rx::gemm_gather, "forward tcgen05 GEMM with the FSDP weight gather fused in");
+  m.def("gather_ranges", &rx::gather_ranges, "copy flat [lo, hi) ranges of a sharded bf16 buffer into a full copy");
   m.def("mnr_tc_scores", &rx::mnr_tc_scores, "tcgen05 MNR scores with the candidate all-gather fused in");
   m.def("mnr_tc_gemm", &rx::mnr_tc_gemm, "tcgen05 split-bf16 GEMM, local or row-routed (peer) output");
   m.def("sharded_grad_reduce", &rx::sharded_grad_reduce);

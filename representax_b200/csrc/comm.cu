@@ -22,6 +22,7 @@
 // embeddings (src/representax/tasks/retrieval/mnr.py:140-148) and gradient
 // reduction (src/representax/train/sharding.py:441-492) that XLA inserts.
 #include <cstring>
+#include <vector>
 
 #include "common.h"
 #include "sm100.cuh"
@@ -205,12 +206,14 @@ __global__ void rs_grad_kernel(const int64_t* __restrict__ grad_ptrs, int world,
 // Phase 2: clipped AdamW on the owned shard; the new fp32 master and bf16
 // compute values are stored into every rank's buffers (fused all-gather).
 // master_ptrs[r] / copy_ptrs[r]: rank r's flat master / compute buffers;
-// m / v hold only this rank's shard (indexed from 0).
+// m / v hold only this rank's shard (indexed from 0). With FSDP (world = 1,
+// the rank's own shard buffers, dst_off = off) nothing is pushed: the master
+// and compute values stay in the owner's shard, which peers gather at use.
 __global__ void adamw_shard_kernel(const float* __restrict__ shard_grad, int64_t off, int64_t n,
                                    const int64_t* __restrict__ master_ptrs, const int64_t* __restrict__ copy_ptrs,
                                    int world, int me, float* __restrict__ m, float* __restrict__ v,
                                    const float* __restrict__ scalars, float lr, float b1, float b2, float eps,
-                                   float wd) {
+                                   float wd, int64_t dst_off) {
   if (scalars[1] == 0.f) return;  // non-finite step: nothing changes anywhere
   const float coef = scalars[0];
   const float step = scalars[2];
@@ -219,7 +222,7 @@ __global__ void adamw_shard_kernel(const float* __restrict__ shard_grad, int64_t
   const float* local = reinterpret_cast<const float*>(master_ptrs[me]);
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
-    const int64_t gi = off + i;
+    const int64_t gi = off + i - dst_off;
     const float g = shard_grad[i] * coef;
     const float mi = b1 * m[i] + (1.f - b1) * g;
     const float vi = b2 * v[i] + (1.f - b2) * g * g;
@@ -232,6 +235,26 @@ __global__ void adamw_shard_kernel(const float* __restrict__ shard_grad, int64_t
       reinterpret_cast<float*>(master_ptrs[r])[gi] = np;
       if (copy_ptrs != nullptr) reinterpret_cast<__nv_bfloat16*>(copy_ptrs[r])[gi] = nb;
     }
+  }
+}
+
+// FSDP: copy flat element ranges [lo, hi) of a buffer sharded over ranks
+// (rank r holds [r * seg, (r + 1) * seg) at src[r]) into this GPU's full copy,
+// 16 bytes (8 bf16) at a time from whichever rank owns each piece.
+struct ShardSources {
+  int64_t ptr[16];
+};
+
+__global__ void gather_ranges_kernel(ShardSources src, int64_t seg, const int64_t* __restrict__ ranges,
+                                     __nv_bfloat16* __restrict__ dst) {
+  const int64_t lo = ranges[2 * blockIdx.y], hi = ranges[2 * blockIdx.y + 1];
+  const int64_t pieces = (hi - lo) >> 3;
+  for (int64_t q = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; q < pieces;
+       q += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t e = lo + (q << 3);
+    const int64_t owner = e / seg;
+    *reinterpret_cast<uint4*>(dst + e) =
+        *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(src.ptr[owner]) + (e - owner * seg));
   }
 }
 
@@ -353,7 +376,7 @@ void sharded_grad_reduce(const at::Tensor& grad_ptrs, int64_t world, int64_t off
 void sharded_adamw(const at::Tensor& shard_grad, int64_t off, int64_t n, const at::Tensor& master_ptrs,
                    const c10::optional<at::Tensor>& copy_ptrs, int64_t world, int64_t rank, at::Tensor& exp_avg,
                    at::Tensor& exp_avg_sq, const at::Tensor& scalars, double lr, double b1, double b2, double eps,
-                   double wd) {
+                   double wd, int64_t dst_offset) {
   if (n == 0) return;
   c10::cuda::CUDAGuard guard(shard_grad.get_device());
   const int sms = num_sms(shard_grad.get_device());
@@ -362,7 +385,28 @@ void sharded_adamw(const at::Tensor& shard_grad, int64_t off, int64_t n, const a
       shard_grad.data_ptr<float>(), off, n, master_ptrs.data_ptr<int64_t>(),
       copy_ptrs.has_value() ? copy_ptrs->data_ptr<int64_t>() : nullptr, static_cast<int>(world),
       static_cast<int>(rank), exp_avg.data_ptr<float>(), exp_avg_sq.data_ptr<float>(), scalars.data_ptr<float>(), static_cast<float>(lr),
-      static_cast<float>(b1), static_cast<float>(b2), static_cast<float>(eps), static_cast<float>(wd));
+      static_cast<float>(b1), static_cast<float>(b2), static_cast<float>(eps), static_cast<float>(wd), dst_offset);
+  RX_CUDA_CHECK(cudaGetLastError());
+}
+
+void gather_ranges(const std::vector<int64_t>& shard_ptrs, int64_t shard_numel, const at::Tensor& ranges,
+                   at::Tensor& dst) {
+  check_bf16(dst, "dst");
+  RX_CHECK(ranges.is_cuda() && ranges.scalar_type() == at::kLong && ranges.dim() == 2 && ranges.size(1) == 2,
+           "ranges must be CUDA int64 [n, 2]");
+  RX_CHECK(!shard_ptrs.empty() && shard_ptrs.size() <= 16, "1..16 shards");
+  RX_CHECK(shard_numel % 8 == 0 && dst.numel() >= static_cast<int64_t>(shard_ptrs.size()) * shard_numel,
+           "shards must be 8-element multiples and dst must cover them");
+  if (ranges.size(0) == 0) return;
+  comm::ShardSources src{};
+  for (size_t r = 0; r < shard_ptrs.size(); ++r) {
+    RX_CHECK(shard_ptrs[r] % 16 == 0, "shard pointers must be 16-byte aligned");
+    src.ptr[r] = shard_ptrs[r];
+  }
+  c10::cuda::CUDAGuard guard(dst.get_device());
+  dim3 grid(64, static_cast<unsigned>(ranges.size(0)));
+  comm::gather_ranges_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream().stream()>>>(
+      src, shard_numel, ranges.data_ptr<int64_t>(), reinterpret_cast<__nv_bfloat16*>(dst.data_ptr()));
   RX_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -3,6 +3,7 @@
 #include "gemm_kernel.cuh"
 
 #include <algorithm>
+#include <vector>
 
 namespace rx {
 void colsum_accumulate(const at::Tensor& x, at::Tensor& out);
@@ -11,13 +12,21 @@ void colsum_accumulate(const at::Tensor& x, at::Tensor& out);
 // (a_mn true); B is [N, K] (b_mn false) or [K, N] (b_mn true); C is [M, N].
 // `split_k` > 1 is allowed only with the atomic fp32 output mode; 0 picks a
 // split automatically when the output has too few tiles to fill the GPU.
-void gemm_tcgen05(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_mn, bool b_mn,
-                  int64_t epi, int64_t out_mode, double alpha,
-                  const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& aux_in,
-                  const c10::optional<at::Tensor>& aux_out,
-                  const c10::optional<at::Tensor>& residual, const at::Tensor& status,
-                  int64_t split_k, int64_t variant, int64_t drop_seed, int64_t drop_stream, double drop_p,
-                  const c10::optional<at::Tensor>& colsum) {
+namespace {
+
+struct GatherArgs {
+  const std::vector<int64_t>* src;
+  int64_t seg, off;
+  at::Tensor ready;
+};
+
+void gemm_impl(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_mn, bool b_mn,
+               int64_t epi, int64_t out_mode, double alpha,
+               const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& aux_in,
+               const c10::optional<at::Tensor>& aux_out,
+               const c10::optional<at::Tensor>& residual, const at::Tensor& status,
+               int64_t split_k, int64_t variant, int64_t drop_seed, int64_t drop_stream, double drop_p,
+               const c10::optional<at::Tensor>& colsum, const GatherArgs* gather) {
   using namespace gemm;
   check_bf16(A, "A");
   check_bf16(B, "B");
@@ -88,8 +97,31 @@ void gemm_tcgen05(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool 
     p.drop = make_dropout_site(drop_seed, drop_stream, drop_p);
   }
   // variant: 1 = one CTA per 128x256 tile, 2 = CTA pair per 256x256 tile,
-  // 0 = pair whenever there are at least 256 rows.
+  // 0 = pair whenever there are at least 256 rows (with or without a fused gather).
   const bool pair = variant == 2 || (variant == 0 && M >= 256);
+  if (gather != nullptr) {
+    RX_CHECK(!a_mn && !b_mn, "the fused weight gather is a forward (K-major) GEMM");
+    const int64_t world = static_cast<int64_t>(gather->src->size());
+    RX_CHECK(world >= 1 && world <= kMaxGatherRanks, "gather: 1..", kMaxGatherRanks, " owners");
+    RX_CHECK(B.is_contiguous() && K % 8 == 0 && gather->off % 8 == 0 && gather->seg % 8 == 0,
+             "gather: contiguous [N, K] weight, K and flat offsets multiples of 8 elements");
+    RX_CHECK(gather->off + N * K <= world * gather->seg, "gather: weight range beyond the shards");
+    const int64_t chunks = (N + kGatherRows - 1) / kGatherRows;
+    RX_CHECK(gather->ready.is_cuda() && gather->ready.scalar_type() == at::kInt && gather->ready.numel() >= chunks,
+             "gather: ready must be CUDA int32 with one entry per ", kGatherRows, " weight rows");
+    for (int64_t r = 0; r < world; ++r) {
+      RX_CHECK(gather->src->at(r) % 16 == 0, "gather: shard pointers must be 16-byte aligned");
+      p.g_src[r] = gather->src->at(r);
+    }
+    p.gather = 1;
+    p.g_world = static_cast<int>(world);
+    p.g_seg = gather->seg;
+    p.g_off = gather->off;
+    p.g_dst = reinterpret_cast<__nv_bfloat16*>(B.data_ptr());
+    p.g_ready = gather->ready.data_ptr<int>();
+    RX_CUDA_CHECK(cudaMemsetAsync(p.g_ready, 0, sizeof(int) * chunks,
+                                  at::cuda::getCurrentCUDAStream(C.get_device()).stream()));
+  }
   bool colsum_after = false;
   if (epi & EPI_COLSUM) {
     RX_CHECK(colsum.has_value() && colsum->numel() == N, "the column-sum epilogue needs an fp32 [N] accumulator");
@@ -153,6 +185,33 @@ void gemm_tcgen05(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool 
     at::Tensor out = *colsum;
     colsum_accumulate(C, out);
   }
+}
+
+}  // namespace
+
+void gemm_tcgen05(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_mn, bool b_mn,
+                  int64_t epi, int64_t out_mode, double alpha,
+                  const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& aux_in,
+                  const c10::optional<at::Tensor>& aux_out,
+                  const c10::optional<at::Tensor>& residual, const at::Tensor& status,
+                  int64_t split_k, int64_t variant, int64_t drop_seed, int64_t drop_stream, double drop_p,
+                  const c10::optional<at::Tensor>& colsum) {
+  gemm_impl(A, B, C, a_mn, b_mn, epi, out_mode, alpha, bias, aux_in, aux_out, residual, status, split_k, variant,
+            drop_seed, drop_stream, drop_p, colsum, nullptr);
+}
+
+// Forward GEMM whose weight B is first assembled (inside the kernel) from its
+// owners' shards: `B` is this GPU's full-copy view of the weight, `shard_ptrs`
+// the bf16 shard base of every rank, `shard_numel` the flat elements per
+// shard and `flat_offset` the weight's first flat element.
+void gemm_gather(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, int64_t epi, int64_t out_mode,
+                 double alpha, const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& aux_out,
+                 const c10::optional<at::Tensor>& residual, const at::Tensor& status, int64_t drop_seed,
+                 int64_t drop_stream, double drop_p, const std::vector<int64_t>& shard_ptrs, int64_t shard_numel,
+                 int64_t flat_offset, const at::Tensor& ready, int64_t variant) {
+  GatherArgs g{&shard_ptrs, shard_numel, flat_offset, ready};
+  gemm_impl(A, B, C, false, false, epi, out_mode, alpha, bias, c10::nullopt, aux_out, residual, status, 0, variant,
+            drop_seed, drop_stream, drop_p, c10::nullopt, &g);
 }
 
 }  // namespace rx

@@ -35,6 +35,8 @@ namespace gemm {
 constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int kEpilogueWarps = 8;  // two per TMEM lane quadrant, each owning half the columns
+constexpr int kMaxGatherRanks = 16;
+constexpr int kGatherRows = 32;  // rows per gather chunk (one readiness flag each)
 constexpr int kThreads = 64 + 32 * kEpilogueWarps;
 
 // EPI_DROP: inverted dropout of the (biased) value before the residual add;
@@ -64,6 +66,19 @@ struct Params {
   float* colsum;
   int* status;
   uint64_t timeout_ns;
+  // Fused FSDP gather (forward, single-CTA kernel only). The B operand is a
+  // weight whose flat elements [g_off, g_off + N * K) are spread over the
+  // ranks' shards (rank r holds flat [r * g_seg, (r + 1) * g_seg) at
+  // g_src[r], bf16). The epilogue warps first copy 32-row chunks of it into
+  // g_dst (this GPU's full copy, which B's tensor map reads) by plain loads
+  // from the owners, raising g_ready[chunk]; the producer waits for a tile's
+  // chunks before loading it.
+  int gather;
+  int g_world;
+  int64_t g_seg, g_off;
+  int64_t g_src[kMaxGatherRanks];
+  __nv_bfloat16* g_dst;
+  int* g_ready;
 };
 
 // Operand kinds: 0 = bf16 x bf16 (kind::f16); 1.. = 8-bit floats
@@ -317,6 +332,64 @@ __device__ __forceinline__ void decode_unit(const Params& p, int u, int& m0, int
   kb1 = min(p.kb_total, kb0 + p.kb_per_split);
 }
 
+__device__ __forceinline__ int ld_acquire_gpu_s32(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Copy gather chunks c = first, first + step, ... of the weight into p.g_dst.
+// Runs on the epilogue warps (256 threads, named barrier 1); every 16-byte
+// piece comes from the rank owning that flat position (runs split at shard
+// boundaries; slots and shards are 64-element aligned, rows 8-element aligned).
+__device__ __forceinline__ void gather_weight_chunks(const Params& p, int first, int step, int tid) {
+  const int64_t row_elems = p.K;
+  const int chunks = (p.N + kGatherRows - 1) / kGatherRows;
+  for (int c = first; c < chunks; c += step) {
+    const int64_t e0 = p.g_off + static_cast<int64_t>(c) * kGatherRows * row_elems;
+    const int64_t e1 = p.g_off + static_cast<int64_t>(min(p.N, (c + 1) * kGatherRows)) * row_elems;
+    const int64_t pieces = (e1 - e0) >> 3;  // 8 bf16 per 16-byte piece
+    for (int64_t base = 0; base < pieces; base += 256 * 8) {
+      uint4 v[8];
+      int64_t at[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int64_t q = base + u * 256 + tid;
+        at[u] = -1;
+        if (q < pieces) {
+          const int64_t e = e0 + (q << 3);
+          const int owner = static_cast<int>(e / p.g_seg);
+          at[u] = e;
+          v[u] = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(p.g_src[owner]) +
+                                                 (e - owner * p.g_seg));
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (at[u] >= 0) *reinterpret_cast<uint4*>(p.g_dst + (at[u] - p.g_off)) = v[u];
+    }
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    __threadfence();
+    asm volatile("bar.sync 1, %0;" ::"n"(32 * kEpilogueWarps) : "memory");
+    if (tid == 0) asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(p.g_ready + c) : "memory");
+  }
+}
+
+// Producer side: all chunks holding rows [n0, n0 + bn) of the weight are in place.
+__device__ __forceinline__ bool gather_rows_ready(const Params& p, int n0, int bn) {
+  const int c1 = (min(p.N, n0 + bn) + kGatherRows - 1) / kGatherRows;
+  for (int c = n0 / kGatherRows; c < c1; ++c) {
+    if (ld_acquire_gpu_s32(p.g_ready + c) > 0) continue;
+    const uint64_t start = globaltimer_ns();
+    while (ld_acquire_gpu_s32(p.g_ready + c) <= 0) {
+      if (globaltimer_ns() - start > p.timeout_ns) return false;
+      __nanosleep(128);
+    }
+  }
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  return true;
+}
+
 template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, int OUT, int KIND = kKindBf16>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -383,6 +456,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         int m0, n_t, kb0, kb1;
         decode_unit(p, u, m0, n_t, kb0, kb1);
         const int n0 = n_t * BN;
+        if (p.gather && !gather_rows_ready(p, n0, BN)) {
+          report_status(p.status, kStatusTimeoutPeer);
+          *abort_flag = 1;
+          ok = false;
+          break;
+        }
         for (int kb = kb0; kb < kb1; ++kb) {
           if (*abort_flag) { ok = false; break; }
           if (!mbar_wait(&empty[stage], phase ^ 1, p.timeout_ns)) {
@@ -487,6 +566,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
+    // (with a fused gather, the epilogue warps first assemble this CTA's share
+    // of the weight; they have no tile to store before the first MMAs finish)
+    if (p.gather) gather_weight_chunks(p, blockIdx.x, gridDim.x, threadIdx.x - 64);
     const int quad = warp & 3;  // TMEM lanes this warp may access: [32*quad, 32*quad+32)
     const int row_local = quad * 32 + lane;
     constexpr int kChunksPerWarp = BN / 32 / (kEpilogueWarps / 4);
@@ -546,6 +628,21 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int g
     RX_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem)));
     if (device >= 0 && device < 64) configured[device] = true;
+  }
+  if (p.gather) {
+    // CTAs wait for chunks that other CTAs of the grid copy: guarantee co-residency.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    RX_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, p));
+    return;
   }
   kern<<<grid, kThreads, smem, stream>>>(ta, tb, p);
   RX_CUDA_CHECK(cudaGetLastError());
@@ -660,6 +757,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         decode(u, m0, n0, kb0, kb1);
         const int my_m = m0 + static_cast<int>(rank) * BM;
         const int my_n = n0 + static_cast<int>(rank) * HALF_N;
+        if (p.gather && !gather_rows_ready(p, my_n, HALF_N)) {
+          report_status(p.status, kStatusTimeoutPeer);
+          *abort_flag = 1;
+          ok = false;
+          break;
+        }
         for (int kb = kb0; kb < kb1; ++kb) {
           if (*abort_flag) { ok = false; break; }
           if (!mbar_wait(&empty[stage], phase ^ 1, p.timeout_ns)) {
@@ -759,6 +862,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue (both CTAs)
+    // (a fused FSDP gather first: see the single-CTA kernel)
+    if (p.gather) gather_weight_chunks(p, blockIdx.x, gridDim.x, threadIdx.x - 64);
     const int quad = warp & 3;
     const int row_local = quad * 32 + lane;
     constexpr int kChunksPerWarp = BN / 32 / (kEpilogueWarps / 4);
@@ -877,13 +982,16 @@ void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, 
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  // a fused gather makes CTAs wait for chunks copied by other CTAs: co-resident grid
+  attr[1].id = cudaLaunchAttributeCooperative;
+  attr[1].val.cooperative = p.gather ? 1 : 0;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = p.gather ? 2 : 1;
   RX_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, tc, taux, p));
 }
 

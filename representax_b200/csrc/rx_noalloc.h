@@ -20,6 +20,9 @@
  *     race on the array and produce wrong gradients: order them.
  *   - The first call on each device looks up the array's device address with
  *     that device current; make that first call before any stream capture.
+ *   - The array used is the current device's, so `stream` has to belong to
+ *     the current device; a stream of another device is rejected with
+ *     RX_NOALLOC_BAD_ARGUMENT.
  *   - Head dimension 64, heads == key/value heads, bf16 tensors, packed
  *     sequences delimited by cu_seqlens (int32, on the device).
  */
@@ -38,8 +41,8 @@ extern "C" {
 enum {
   RX_NOALLOC_OK = 0,
   RX_NOALLOC_TOO_LARGE = 1,    /* the problem needs more scratch than the array holds */
-  RX_NOALLOC_BAD_ARGUMENT = 2, /* null pointer, bad size, or misaligned tensor */
-  RX_NOALLOC_CUDA_ERROR = 3    /* a CUDA call failed; see cudaGetLastError() */
+  RX_NOALLOC_BAD_ARGUMENT = 2, /* null pointer, bad size, misaligned tensor, or stream of another device */
+  RX_NOALLOC_CUDA_ERROR = 3    /* a CUDA call failed; rx_noalloc_last_cuda_error() gives its cudaError_t */
 };
 
 /* dQ, dK, dV of packed multi-head attention given dO, the forward inputs q/k/v,
@@ -56,6 +59,11 @@ int rx_attention_backward_noalloc(const void* dO, int64_t ld_do, const void* q, 
 
 /* Human-readable text of a return code. */
 const char* rx_noalloc_error_string(int code);
+
+/* The cudaError_t (as int) of the calling thread's last RX_NOALLOC_CUDA_ERROR.
+ * The entry point never calls cudaGetLastError, so errors of other work stay
+ * where they were. */
+int rx_noalloc_last_cuda_error(void);
 
 #ifdef __cplusplus
 }

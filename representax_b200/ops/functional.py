@@ -38,7 +38,18 @@ class Packed:
         return self.cu_seqlens.numel() - 1
 
 
-def compute_view(param: torch.Tensor) -> torch.Tensor:
+def compute_view(param: torch.Tensor, *, fused_gather: bool = False) -> torch.Tensor:
+    """The bf16 compute copy of a parameter.
+
+    Under FSDP the copy is this GPU's cache of the sharded weights: it is
+    gathered here on first use in a parameter version, or, with
+    ``fused_gather`` (the caller feeds it straight to a forward GEMM), by that
+    GEMM's kernel itself.
+    """
+
+    state = getattr(param, "fsdp_state", None)
+    if state is not None:
+        return state.view(param, fused=fused_gather)
     copy = getattr(param, "compute", None)
     if copy is not None:
         return copy
@@ -107,8 +118,8 @@ class AttentionBlockFn(torch.autograd.Function):
         C = ext()
         T, H = x.shape
         head_dim = 64
-        wq, bq = compute_view(w_qkv), compute_view(b_qkv)
-        wo, bo = compute_view(w_o), compute_view(b_o)
+        wq, bq = compute_view(w_qkv, fused_gather=True), compute_view(b_qkv)
+        wo, bo = compute_view(w_o, fused_gather=True), compute_view(b_o)
         qkv = G.linear_forward(x, wq, bq)
         qd, kd = heads * head_dim, kv_heads * head_dim
         q, k, v = qkv[:, :qd], qkv[:, qd:qd + kd], qkv[:, qd + kd:]
@@ -178,8 +189,8 @@ class MlpBlockFn(torch.autograd.Function):
         T = x.shape[0]
         inter = w1.shape[0]
         z = torch.empty(T, inter, dtype=torch.bfloat16, device=x.device)
-        g = G.linear_forward(x, compute_view(w1), compute_view(b1), gelu_preact=z)
-        s = G.linear_forward(g, compute_view(w2), compute_view(b2), residual=x,
+        g = G.linear_forward(x, compute_view(w1, fused_gather=True), compute_view(b1), gelu_preact=z)
+        s = G.linear_forward(g, compute_view(w2, fused_gather=True), compute_view(b2), residual=x,
                              dropout=None if dropout is None else dropout.hidden_args(2))
         ctx.save_for_backward(x, z, g, w1, b1, w2, b2)
         ctx.out_bias_grad_fused = out_bias_grad_fused

@@ -10,6 +10,8 @@ from __future__ import annotations
 
 import torch
 
+from representax_b200.parallel.fsdp import take_pending
+
 from ._ext import ext, status
 
 EPI_NONE = 0
@@ -57,6 +59,16 @@ def gemm(
         epi |= EPI_DROP
     if colsum is not None:
         epi |= EPI_COLSUM
+    pending = take_pending(b)
+    if pending is not None:  # an FSDP weight whose first use in this version is this GEMM
+        state, slot = pending
+        if not a_mn and not b_mn and colsum is None and aux_in is None and out_mode in (OUT_BF16, OUT_F32):
+            shards, shard_numel, offset, ready = state.gemm_gather_args(slot)
+            ext().gemm_gather(a, b, out, epi, out_mode, alpha, bias, aux_out, residual, status(out.device), seed,
+                              stream, p, shards, shard_numel, offset, ready,
+                              GEMM_VARIANT if variant is None else variant)
+            return out
+        state._gather_slot(slot)
     ext().gemm(
         a, b, out, a_mn, b_mn, epi, out_mode, alpha, bias, aux_in, aux_out, residual,
         status(out.device), split_k, GEMM_VARIANT if variant is None else variant, seed, stream, p, colsum,

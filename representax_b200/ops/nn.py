@@ -73,7 +73,8 @@ class Segments:
 class _LinearFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, w, b, residual):
-        y = G.linear_forward(x, compute_view(w), None if b is None else compute_view(b), residual=residual)
+        y = G.linear_forward(x, compute_view(w, fused_gather=True), None if b is None else compute_view(b),
+                             residual=residual)
         ctx.save_for_backward(x, w, b if b is not None else torch.empty(0, device=x.device))
         ctx.has_b, ctx.has_res = b is not None, residual is not None
         return y

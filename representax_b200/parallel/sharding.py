@@ -114,6 +114,20 @@ class ShardingPlan:
         return self.kind != "ddp" and self.world_size > 1
 
     @property
+    def shards_parameters(self) -> bool:
+        """Whether execution shards the parameters themselves (FSDP layout).
+
+        FSDP always does; custom rules do when any rule shards a parameter.
+        Execution shards the flat parameter vector in equal per-rank segments
+        (``representax_b200.parallel.fsdp``), so the specs decide whether the
+        layout is sharded, not which axis a tensor is cut along.
+        """
+
+        if self.world_size <= 1:
+            return False
+        return self.kind == "fsdp" or (self.kind == "custom" and self.has_sharded_parameters)
+
+    @property
     def has_sharded_parameters(self) -> bool:
         return any(any(a is not None for a in spec) for spec in self.parameter_specs.values())
 
@@ -132,6 +146,7 @@ class ShardingPlan:
     def describe(self) -> dict[str, Any]:
         return {"kind": self.kind, "world_size": self.world_size, "data_axis": self.data_axis,
                 "parameter_axis": self.parameter_axis, "sharded_optimizer": self.sharded_optimizer,
+                "shards_parameters": self.shards_parameters,
                 "sharded_parameter_specs": sum(1 for s in self.parameter_specs.values() if any(s))}
 
 

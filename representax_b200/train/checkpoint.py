@@ -347,6 +347,15 @@ def training_tensors(state) -> dict[str, torch.Tensor]:
 
     store = state.store
     out: dict[str, torch.Tensor] = {}
+    if getattr(store, "fsdp", None) is not None:
+        # FSDP: each rank's file holds its own segment of the master weights and moments
+        out["model/master_segment"] = store.master
+        if store.exp_avg is not None:
+            out["optimizer/exp_avg_shard"] = store.exp_avg
+            out["optimizer/exp_avg_sq_shard"] = store.exp_avg_sq
+        out["optimizer/shard"] = torch.tensor([store.shard_offset, store.shard_numel, store.group.world])
+        out["optimizer/scalars"] = state.scalars
+        return {k: v.contiguous() for k, v in out.items()}
     for name, view in store.named_views("master"):
         out[f"model/{name}"] = view
     if store.exp_avg is not None and getattr(store, "sharded", False):
@@ -368,6 +377,19 @@ def training_tensors(state) -> dict[str, torch.Tensor]:
 def load_training_tensors(state, tensors: Mapping[str, torch.Tensor]) -> None:
     store = state.store
     sharded = getattr(store, "sharded", False)
+    if getattr(store, "fsdp", None) is not None:
+        meta = tensors.get("optimizer/shard")
+        if (meta is None or "model/master_segment" not in tensors
+                or tuple(int(v) for v in meta) != (store.shard_offset, store.shard_numel, store.group.world)):
+            raise IncompleteCheckpointError("checkpoint segments do not match this run's FSDP layout")
+        with torch.no_grad():
+            store.master.copy_(tensors["model/master_segment"].to(store.device))
+            if store.exp_avg is not None:
+                store.exp_avg.copy_(tensors["optimizer/exp_avg_shard"].to(store.device))
+                store.exp_avg_sq.copy_(tensors["optimizer/exp_avg_sq_shard"].to(store.device))
+            state.scalars.copy_(tensors["optimizer/scalars"].to(state.scalars.device))
+        store.refresh_compute()
+        return
     with torch.no_grad():
         if sharded:
             meta = tensors.get("optimizer/shard")

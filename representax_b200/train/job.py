@@ -176,8 +176,10 @@ def build_job_runtime(job: JobConfig, *, device: torch.device | str | None = Non
     from representax_b200.parallel.sharding import plan_from_config
 
     plan = plan_from_config(job.training.sharding, model, dist.world_size)
+    cuda = torch.device(device).type == "cuda"
     state = init_train_state(model, device=device, precision=precision, dist=dist,
-                             sharded_optimizer=plan.sharded_optimizer)
+                             sharded_optimizer=plan.sharded_optimizer,
+                             fsdp=plan.shards_parameters and cuda and precision.compute_dtype != torch.float32)
     optimizer = build_optimizer(job.optimization)
     execution = build_execution(job.training)
     if job.training.global_batch_size % dist.world_size:
@@ -241,6 +243,8 @@ def run_job(job: JobConfig, run_directory: str | Path, *, resume: bool = False, 
             heartbeat_seconds=job.data.data_wait_heartbeat_seconds,
             timeout_seconds=job.data.data_wait_timeout_seconds)
         bundle = None
+        if job.export.enabled and getattr(runtime.state.store, "fsdp", None) is not None:
+            runtime.state.store.unshard()  # collective: every rank takes part
         if job.export.enabled and dist.rank == 0:
             if job.export.selection == "best" and checkpoints is not None and checkpoints.best() is not None:
                 from .checkpoint import load_training_tensors

@@ -29,18 +29,26 @@ from .state import StepMetrics, TrainState
 
 
 def init_train_state(model: torch.nn.Module, *, device, precision: PrecisionPolicy, dist: DistContext = LOCAL,
-                     sharded_optimizer: bool = False) -> TrainState:
+                     sharded_optimizer: bool = False, fsdp: bool = False) -> TrainState:
     """``sharded_optimizer`` (CUDA, world > 1): AdamW moments sharded over the
     ranks, gradients reduce-scattered and parameters all-gathered by peer
-    memory kernels fused with the update (see ``TrainStep``)."""
+    memory kernels fused with the update (see ``TrainStep``).
+
+    ``fsdp`` (CUDA, world > 1, bf16 compute): fp32 master weights, moments and
+    the bf16 owner copy are sharded too; each rank gathers the weights at their
+    first use in a step, the forward GEMMs with the gather fused into the
+    kernel (``representax_b200.parallel.fsdp``)."""
 
     model.to(torch.float32)
     group = None
-    if sharded_optimizer and dist.enabled and torch.device(device).type == "cuda":
+    if (sharded_optimizer or fsdp) and dist.enabled and torch.device(device).type == "cuda":
         from representax_b200.parallel.peer import peer_group
 
         group = peer_group(dist, torch.device(device))
-    store = FlatParameterStore(model, device=device, compute_dtype=precision.compute_dtype, peer_group=group)
+    elif fsdp and dist.enabled:
+        raise ValueError("FSDP runs on CUDA devices (peer memory); use DDP on CPU")
+    store = FlatParameterStore(model, device=device, compute_dtype=precision.compute_dtype, peer_group=group,
+                               fsdp=fsdp and group is not None)
     scalars = torch.zeros(8, dtype=torch.float32, device=store.device)
     return TrainState(model=model, store=store, scalars=scalars)
 
@@ -210,9 +218,15 @@ class TrainStep:
                               self._shard_grad, self._norm_sq)
         tdist.all_reduce(self._norm_sq)
         C.finalize_clip(self._norm_sq, s, gate.contiguous(), max_norm, 1)
-        C.sharded_adamw(self._shard_grad, store.shard_offset, store.shard_numel, store.peer_pointers("master"),
-                        store.peer_pointers("compute") if store.mixed else None, group.world, group.rank,
-                        store.exp_avg, store.exp_avg_sq, s, lr, opt.b1, opt.b2, opt.eps, opt.weight_decay)
+        if store.fsdp is not None:  # update the owned segments only; peers gather them at next use
+            C.sharded_adamw(self._shard_grad, store.shard_offset, store.shard_numel, store.master_ptrs,
+                            store.owner_ptrs, 1, 0, store.exp_avg, store.exp_avg_sq, s, lr, opt.b1, opt.b2, opt.eps,
+                            opt.weight_decay, store.shard_offset)
+            store.fsdp.advance()
+        else:
+            C.sharded_adamw(self._shard_grad, store.shard_offset, store.shard_numel, store.peer_pointers("master"),
+                            store.peer_pointers("compute") if store.mixed else None, group.world, group.rank,
+                            store.exp_avg, store.exp_avg_sq, s, lr, opt.b1, opt.b2, opt.eps, opt.weight_decay, 0)
         group.barrier()
 
     def __call__(self, batch: Any, iteration: int) -> StepMetrics:
