@@ -230,12 +230,29 @@ def main() -> None:
                                          retain_bytes="auto" if args.retain_gb is None else int(args.retain_gb * 2**30)),
                      max_gradient_norm=1.0, dist=ctx, stochastic=args.dropout > 0)
 
-    # Host batches (pinned), distinct per step and per rank; same shapes every step.
-    rng = np.random.default_rng(1234 + ctx.rank)
+    # Host batches (pinned), distinct per step; same shapes every step. Every rank
+    # draws the same global batch and keeps its token-balanced share of the pairs
+    # (equal pair counts, token counts within one pair of each other), so no rank
+    # waits for a rank that drew longer sequences.
+    from representax_b200.data.balance import pair_lengths, token_balanced_shards
+    from representax_b200.models.text_batch import TokenBatch
+    from representax_b200.tasks.retrieval import RetrievalBatch
+
+    rng = np.random.default_rng(1234)
     n_host = 4
     host = []
     for _ in range(n_host):
-        b = retrieval_pairs(rng, local, SEQ, vocab=VOCAB, low=1000, min_len=MIN_LEN, max_len=SEQ)
+        full = retrieval_pairs(rng, args.global_batch, SEQ, vocab=VOCAB, low=1000, min_len=MIN_LEN, max_len=SEQ,
+                               pack=False)
+        mine = torch.from_numpy(token_balanced_shards(
+            pair_lengths(full.query.attention_mask.sum(1).numpy(), full.document.attention_mask.sum(1).numpy()),
+            world)[ctx.rank])
+
+        def rows(tb):
+            return TokenBatch(input_ids=tb.input_ids[mine], attention_mask=tb.attention_mask[mine]).pack()
+
+        b = RetrievalBatch(query=rows(full.query), document=rows(full.document),
+                           positive_mask=torch.eye(local, dtype=torch.bool))
         b = b.map_tensors(lambda t: t.pin_memory())
         host.append(b)
 
@@ -379,6 +396,8 @@ def main() -> None:
                                    if args.optimizer == "sharded" else "NCCL all-reduce + replicated fused AdamW"),
                 "dropout": args.dropout,
                 "padding": "packed (padding tokens are not computed)",
+                "rank_assignment": ("one global batch per step, its pairs dealt to ranks token-balanced "
+                                    "(serpentine over pairs sorted by length)"),
                 "l2": "per-step working set > 126 MB L2; no explicit flush",
             },
             "clocks": clocks,

@@ -183,7 +183,8 @@ class DataLoader:
                  collate: Callable[[list[Any]], Any] | None = None, batch_size: int,
                  drop_remainder: bool = True, num_threads: int = 4, prefetch: int = 4,
                  num_batches: int | None = None, shard: tuple[int, int] = (0, 1),
-                 contract: Mapping[str, Any] | None = None, host_memory_budget_bytes: int | None = None) -> None:
+                 contract: Mapping[str, Any] | None = None, host_memory_budget_bytes: int | None = None,
+                 token_length: Callable[[Any], int] | None = None) -> None:
         if batch_size <= 0:
             raise ValueError("batch_size must be positive")
         self.sources = list(sources)
@@ -199,7 +200,13 @@ class DataLoader:
         if batch_size % self.shard_count:
             raise ValueError("global batch size must divide evenly over data shards")
         self.host_memory_budget_bytes = host_memory_budget_bytes
+        # With several shards and a token_length function, every rank maps the
+        # whole global batch and keeps its token-balanced share of the rows
+        # (representax_b200.data.balance) instead of a contiguous slice.
+        self.token_length = token_length
         self.data_contract = dict(contract or {})
+        if token_length is not None and self.shard_count > 1:
+            self.data_contract.setdefault("rank_assignment", "token_balanced")
         self.data_contract.setdefault("batch_size", batch_size)
         self.data_contract.setdefault("drop_remainder", drop_remainder)
 
@@ -218,11 +225,22 @@ class DataLoader:
     def make_batch(self, index: int):
         started = time.perf_counter()
         local = self.batch_size // self.shard_count
-        base = index * self.batch_size + self.shard_index * local
-        records = []
-        for i in range(base, base + local):
-            source, row = self.sampler[i]
-            records.append(self.mappers[source](self.sources[source][row]))
+        if self.token_length is not None and self.shard_count > 1:
+            from .balance import token_balanced_shards
+
+            start = index * self.batch_size
+            everything = []
+            for i in range(start, start + self.batch_size):
+                source, row = self.sampler[i]
+                everything.append(self.mappers[source](self.sources[source][row]))
+            mine = token_balanced_shards([self.token_length(r) for r in everything], self.shard_count)
+            records = [everything[i] for i in mine[self.shard_index]]
+        else:
+            base = index * self.batch_size + self.shard_index * local
+            records = []
+            for i in range(base, base + local):
+                source, row = self.sampler[i]
+                records.append(self.mappers[source](self.sources[source][row]))
         batch = self.collate(records)
         nbytes = host_nbytes(batch) if not isinstance(batch, list) else 0
         if self.host_memory_budget_bytes is not None:

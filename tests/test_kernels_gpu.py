@@ -362,10 +362,11 @@ def test_attention_tcgen05_is_default(C):
 
 
 @pytest.mark.parametrize("mode", [0, 1, 2])
-def test_pool(C, mode):
+@pytest.mark.parametrize("lens,h", [([3, 1, 50, 128], 768), ([40, 0, 33, 7], 4096), ([300], 2048)])
+def test_pool(C, mode, lens, h):
+    """Slices of 32 packed rows cross sequence boundaries; an empty sequence pools to zero."""
+
     torch.manual_seed(8)
-    lens = [3, 1, 50, 128]
-    h = 768
     total = sum(lens)
     x = _rand(total, h)
     cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), dtype=torch.int32, device=_dev())
@@ -377,7 +378,10 @@ def test_pool(C, mode):
     s = 0
     for n in lens:
         seg = xf[s:s + n]
-        pooled.append(seg.mean(0) if mode == 0 else seg[0] if mode == 1 else seg[-1])
+        if n == 0:
+            pooled.append(torch.zeros(h, device=xf.device))
+        else:
+            pooled.append(seg.mean(0) if mode == 0 else seg[0] if mode == 1 else seg[-1])
         s += n
     ref = torch.nn.functional.normalize(torch.stack(pooled), dim=-1, eps=1e-12)
     _close(out, ref, rtol=1e-3, atol=1e-4, what="pool fwd")
@@ -389,8 +393,9 @@ def test_pool(C, mode):
 
 
 def test_colsum_and_cast(C):
-    for rows, cols in ((1000, 768), (37, 2304), (5000, 3072)):
-        x = _rand(rows, cols)
+    for rows, cols, ld in ((1000, 768, 768), (37, 2304, 2304), (5000, 3072, 3072), (129, 8, 8),
+                           (300, 4096, 4104), (70, 10240, 10240), (18432, 2304, 2304)):
+        x = _rand(rows, ld)[:, :cols]
         out = torch.ones(cols, device=_dev())
         C.colsum_accumulate(x, out)
         _close(out, 1 + x.float().sum(0), rtol=1e-4, atol=2e-3, what=f"colsum {cols}")

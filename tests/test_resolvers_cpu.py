@@ -131,3 +131,30 @@ def test_http_artifact_range_and_etag(monkeypatch):
     member = Artifact(modality="image", uri="https://example.org/a.zip", etag='"e1"', archive_member="x.png")
     with pytest.raises(ValueError, match="archive"):
         read_artifact(member)
+
+
+def test_token_balanced_shards_equalise_work():
+    import numpy as np
+
+    from representax_b200.data.balance import token_balanced_shards
+    from representax_b200.data.loader import DataLoader
+
+    rng = np.random.default_rng(0)
+    lengths = rng.integers(64, 513, size=4096)
+    for world in (2, 4, 8):
+        shards = token_balanced_shards(lengths, world)
+        assert sorted(np.concatenate(shards).tolist()) == list(range(4096))  # a partition
+        assert {len(s) for s in shards} == {4096 // world}
+        sums = [int(lengths[s].sum()) for s in shards]
+        assert max(sums) - min(sums) <= lengths.max()  # within one row's length
+    records = [{"n": int(n)} for n in rng.integers(1, 100, size=64)]
+    seen = []
+    for rank in range(4):
+        loader = DataLoader([records], weights=[1.0], seed=0, batch_size=32, shard=(rank, 4), num_threads=1,
+                            prefetch=1, token_length=lambda r: r["n"])
+        batch, _, _ = loader.make_batch(0)
+        seen.extend(r["n"] for r in batch)
+        assert len(batch) == 8
+        assert loader.data_contract["rank_assignment"] == "token_balanced"
+    whole = DataLoader([records], weights=[1.0], seed=0, batch_size=32, num_threads=1, prefetch=1)
+    assert sorted(seen) == sorted(r["n"] for r in whole.make_batch(0)[0])  # same global batch
