@@ -100,6 +100,9 @@ void mnr_tc_gemm(const at::Tensor& a_hi, const at::Tensor& a_lo, bool a_mn, cons
                  const at::Tensor& b_lo, bool b_mn, int64_t M, int64_t N, int64_t K,
                  const c10::optional<at::Tensor>& out, const std::vector<int64_t>& route_ptrs, int64_t route_seg,
                  int64_t route_off, int64_t ldc, double alpha, bool accumulate, const at::Tensor& status);
+void mnr_tc_argmax(const at::Tensor& a_hi, const at::Tensor& a_lo, const at::Tensor& b_hi, const at::Tensor& b_lo,
+                   at::Tensor& best, const c10::optional<at::Tensor>& valid, int64_t exclude_off,
+                   const at::Tensor& status);
 void sharded_grad_reduce(const at::Tensor& grad_ptrs, int64_t world, int64_t off, int64_t n, at::Tensor& shard,
                          at::Tensor& norm_sq);
 void sharded_adamw(const at::Tensor& shard_grad, int64_t off, int64_t n, const at::Tensor& master_ptrs,
@@ -155,6 +158,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gather_ranges", &rx::gather_ranges, "copy flat [lo, hi) ranges of a sharded bf16 buffer into a full copy");
   m.def("mnr_tc_scores", &rx::mnr_tc_scores, "tcgen05 MNR scores with the candidate all-gather fused in");
   m.def("mnr_tc_gemm", &rx::mnr_tc_gemm, "tcgen05 split-bf16 GEMM, local or row-routed (peer) output");
+  m.def("mnr_tc_argmax", &rx::mnr_tc_argmax, "tcgen05 split-bf16 scores reduced to each row's hardest candidate");
   m.def("sharded_grad_reduce", &rx::sharded_grad_reduce);
   m.def("sharded_adamw", &rx::sharded_adamw);
   m.def("int4_dequantize", &rx::int4_dequantize);

@@ -19,7 +19,10 @@
 //               MMAs (M = 128, N = 128, K = 16, three per K step).
 //   warps 2-5   epilogue: tcgen05.ld, scale, fp32 stores either into a local
 //               matrix (optionally accumulating) or, row block by row block,
-//               into the owning rank's slot buffer by peer stores.
+//               into the owning rank's slot buffer by peer stores; or, for
+//               hardest-negative mining, no stores at all: each row's best
+//               (score, column) over the tile, merged across tiles by one
+//               64-bit atomicMax per row (scores never reach memory).
 //   warps 6-9   stagers (scoring launch only): convert the local rows and
 //               every rank's candidate rows (plain vector loads from the
 //               owner's memory over NVLink) into the split bf16 operand
@@ -73,7 +76,17 @@ struct Params {
   int* ready;  // [world + 1] finished chunks per owner (index world: the local rows)
   int* status;
   uint64_t timeout_ns;
+  // mining: best[m] = max over allowed columns n of key(score) << 32 | ~n
+  unsigned long long* best;
+  const uint8_t* valid;  // [N] allowed candidates (nullptr: all)
+  int64_t exclude_off;   // column m + exclude_off is never a candidate
 };
+
+// Order-preserving map of an fp32 score onto uint32 (larger score, larger key).
+__device__ __forceinline__ uint32_t score_key(float v) {
+  const uint32_t b = __float_as_uint(v);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
 
 __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
   int v;
@@ -353,6 +366,30 @@ __global__ void __launch_bounds__(kThreads, 1)
                   : p.C + static_cast<int64_t>(m) * p.ldc;
       }
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      if (p.best != nullptr) {
+        // hardest-candidate mining: ties go to the smaller column (~n is larger)
+        unsigned long long best = 0ull;
+        const int64_t skip = static_cast<int64_t>(m) + p.exclude_off;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_row + c * 32, r);
+          tmem_ld_wait();
+          const int nb = n0 + c * 32;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int n = nb + i;
+            if (n >= p.N || n == skip || (p.valid != nullptr && p.valid[n] == 0)) continue;
+            const unsigned long long key =
+                (static_cast<unsigned long long>(score_key(__uint_as_float(r[i]))) << 32) | (0xffffffffu - n);
+            best = key > best ? key : best;
+          }
+        }
+        if (m < p.M && best != 0ull) atomicMax(p.best + m, best);
+        tc_fence_before();
+        mbar_arrive(&tempty[acc]);
+        continue;
+      }
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
@@ -617,6 +654,37 @@ void mnr_tc_gemm(const at::Tensor& a_hi, const at::Tensor& a_lo, bool a_mn, cons
   } else {
     mnrtc::launch<true, false, false>(ah, al, bh, bl, p, dev, stream);
   }
+}
+
+// Hardest candidate per row: best[m] = max over n of key(A[m] . B[n]) << 32 | (2^32 - 1 - n),
+// over candidates with valid[n] != 0 (all when `valid` is absent) and
+// n != m + exclude_off. A / B are split [M, K] / [N, K] operands; best is
+// int64 [M], zeroed here (0 = no candidate). The score matrix is never stored.
+void mnr_tc_argmax(const at::Tensor& a_hi, const at::Tensor& a_lo, const at::Tensor& b_hi, const at::Tensor& b_lo,
+                   at::Tensor& best, const c10::optional<at::Tensor>& valid, int64_t exclude_off,
+                   const at::Tensor& status) {
+  RX_CHECK(a_lo.sizes() == a_hi.sizes() && b_lo.sizes() == b_hi.sizes(), "hi / lo shapes differ");
+  RX_CHECK(a_hi.dim() == 2 && b_hi.dim() == 2 && a_hi.size(1) == b_hi.size(1), "A [M, K] and B [N, K] must share K");
+  const int64_t M = a_hi.size(0), N = b_hi.size(0), K = a_hi.size(1);
+  RX_CHECK(N < 0xffffffffll, "too many candidates");
+  RX_CHECK(best.is_cuda() && best.scalar_type() == at::kLong && best.is_contiguous() && best.numel() == M,
+           "best must be a contiguous int64 [M]");
+  c10::cuda::CUDAGuard guard(a_hi.get_device());
+  auto stream = at::cuda::getCurrentCUDAStream().stream();
+  if (M == 0) return;
+  RX_CUDA_CHECK(cudaMemsetAsync(best.data_ptr(), 0, sizeof(int64_t) * M, stream));
+  if (N == 0) return;
+  mnrtc::Params p = base_params(M, N, K, 1.0, status);
+  p.best = reinterpret_cast<unsigned long long*>(best.data_ptr());
+  p.exclude_off = exclude_off;
+  if (valid.has_value()) {
+    RX_CHECK(valid->is_cuda() && (valid->scalar_type() == at::kBool || valid->scalar_type() == at::kByte) &&
+                 valid->is_contiguous() && valid->numel() == N,
+             "valid must be a contiguous bool / uint8 [N]");
+    p.valid = reinterpret_cast<const uint8_t*>(valid->data_ptr());
+  }
+  mnrtc::launch<false, false, false>(operand_map(a_hi, false), operand_map(a_lo, false), operand_map(b_hi, false),
+                                     operand_map(b_lo, false), p, a_hi.get_device(), stream);
 }
 
 }  // namespace rx

@@ -59,20 +59,28 @@ class BatchTelemetry:
 
 
 def host_nbytes(batch: Any) -> int:
-    from representax_b200.tasks._batch import iter_tensors
+    """Bytes of the host arrays in a batch (torch tensors and numpy arrays, found
+    through dicts, sequences and dataclasses such as packed token batches)."""
 
-    total = 0
-    for t in iter_tensors(batch):
-        if t.is_cuda:
-            raise TypeError("host preprocessing emitted a device tensor; let the training loop place batches")
-        total += t.numel() * t.element_size()
-    packed = getattr(batch, "query", None)
-    for part in (getattr(batch, "query", None), getattr(batch, "document", None)):
-        p = getattr(part, "packed", None)
-        if p is not None:
-            total += p.nbytes()
-    del packed
-    return total
+    seen: set[int] = set()
+
+    def walk(x: Any) -> int:
+        if isinstance(x, torch.Tensor):
+            if x.is_cuda:
+                raise TypeError("host preprocessing emitted a device tensor; let the training loop place batches")
+            return x.numel() * x.element_size()
+        if isinstance(x, np.ndarray):
+            return int(x.nbytes)
+        if isinstance(x, dict):
+            return sum(walk(v) for v in x.values())
+        if isinstance(x, (list, tuple)):
+            return sum(walk(v) for v in x)
+        if hasattr(x, "__dataclass_fields__") and id(x) not in seen:
+            seen.add(id(x))
+            return sum(walk(getattr(x, name)) for name in x.__dataclass_fields__ if not name.startswith("_"))
+        return 0
+
+    return walk(batch)
 
 
 class MixtureSampler:
@@ -187,6 +195,16 @@ class DataLoader:
                  token_length: Callable[[Any], int] | None = None) -> None:
         if batch_size <= 0:
             raise ValueError("batch_size must be positive")
+        if num_threads < 0 or prefetch < 0:
+            raise ValueError("num_threads and prefetch must be non-negative")
+        if host_memory_budget_bytes is not None:
+            # the budget covers every model-ready batch the loader can hold at
+            # once: the prefetch queue plus the batch being handed out
+            if host_memory_budget_bytes <= 0:
+                raise ValueError("host_memory_budget_bytes must be positive or None")
+            if host_memory_budget_bytes // (max(prefetch, 1) + 1) == 0:
+                raise ValueError(f"host_memory_budget_bytes={host_memory_budget_bytes} cannot hold "
+                                 f"{max(prefetch, 1) + 1} batch slots")
         self.sources = list(sources)
         self.sampler = MixtureSampler([len(s) for s in self.sources], weights, seed, shuffle)
         self.mappers = list(mappers) if mappers is not None else [identity] * len(self.sources)
@@ -244,7 +262,7 @@ class DataLoader:
         batch = self.collate(records)
         nbytes = host_nbytes(batch) if not isinstance(batch, list) else 0
         if self.host_memory_budget_bytes is not None:
-            slot = self.host_memory_budget_bytes // (self.prefetch + 1)
+            slot = self.host_memory_budget_bytes // (max(self.prefetch, 1) + 1)
             if nbytes > slot:
                 raise MemoryError(f"host batch uses {nbytes} bytes; per-slot limit is {slot} bytes")
         return batch, time.perf_counter() - started, nbytes

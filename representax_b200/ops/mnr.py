@@ -113,6 +113,47 @@ def tc_scores(rows: torch.Tensor, cand_ptrs: list[int], cand_rows: int, rank: in
     return scores, a, b
 
 
+def hardest_candidates(anchor: torch.Tensor, candidates: torch.Tensor, valid: torch.Tensor | None = None,
+                       *, exclude_offset: int | None = 0) -> torch.Tensor:
+    """Index of each anchor row's most cosine-similar candidate (int64 [M]).
+
+    Candidates with ``valid[n]`` false are skipped, and so is column
+    ``m + exclude_offset`` for row m (the row's own pair; ``None`` keeps every
+    column). Ties go to the smaller index; a row without any candidate gets 0.
+    On CUDA one tcgen05 launch scores the unit vectors in split bf16 (near
+    fp32) and reduces every tile to its rows' best candidate in the epilogue,
+    so the [M, N] score matrix is never written. Parity:
+    src/representax/train/mega_batch.py:27-55 (row-chunked masked argmax).
+    """
+
+    a = torch.nn.functional.normalize(anchor.detach().float(), dim=1, eps=1e-12)
+    c = torch.nn.functional.normalize(candidates.detach().float(), dim=1, eps=1e-12)
+    m, n = a.shape[0], c.shape[0]
+    if not a.is_cuda:
+        out = []
+        cols = torch.arange(n)
+        for s in range(0, m, 1024):
+            scores = a[s:s + 1024] @ c.T
+            if valid is not None:
+                scores[:, ~valid.bool().cpu()] = float("-inf")
+            if exclude_offset is not None:
+                rows = torch.arange(s, min(m, s + 1024)) + exclude_offset
+                scores[cols[None, :] == rows[:, None]] = float("-inf")
+            out.append(scores.argmax(1))
+        return torch.cat(out) if out else torch.zeros(0, dtype=torch.long)
+    k = a.shape[1]
+    if k % 8:  # 16-byte rows for the split operands
+        a = torch.nn.functional.pad(a, (0, 8 - k % 8))
+        c = torch.nn.functional.pad(c, (0, 8 - k % 8))
+    ah, al = split_bf16(a)
+    ch, cl = split_bf16(c)
+    best = torch.empty(m, dtype=torch.long, device=a.device)
+    v = None if valid is None else valid.to(device=a.device, dtype=torch.bool).contiguous()
+    off = (1 << 40) if exclude_offset is None else int(exclude_offset)
+    ext().mnr_tc_argmax(ah, al, ch, cl, best, v, off, _status(a.device))
+    return torch.where(best == 0, torch.zeros_like(best), 0xFFFFFFFF - (best & 0xFFFFFFFF))
+
+
 def tc_gemm(a, a_mn: bool, b, b_mn: bool, m: int, n: int, k: int, *, out: torch.Tensor | None = None,
             route: list[int] | None = None, route_rows: int = 1, route_offset: int = 0, ldc: int | None = None,
             accumulate: bool = False) -> None:

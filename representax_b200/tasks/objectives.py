@@ -274,24 +274,23 @@ def contrastive_tension_in_batch_loss(u, v, scale=20.0):
     return (F.cross_entropy(cos, target) + F.cross_entropy(cos.T, target)) / 2
 
 
-def mega_batch_margin_loss(anchor, positive, negative, positive_margin=0.8, negative_margin=0.3):
+def mega_batch_margin_loss(anchor, positive, negative, positive_margin=0.8, negative_margin=0.3, valid=None):
     cp = F.cosine_similarity(_f32(anchor), _f32(positive), dim=1)
     cn = F.cosine_similarity(_f32(anchor), _f32(negative), dim=1)
-    return (F.relu(positive_margin - cp) + F.relu(cn - negative_margin)).mean()
+    rows = F.relu(positive_margin - cp) + F.relu(cn - negative_margin)
+    return _masked_mean(rows, _valid(rows.shape[0], valid, rows.device))
 
 
-def hardest_negative_indices(anchor, candidates, chunk: int = 1024) -> torch.Tensor:
-    """Row-chunked argmax of cosine over candidates, excluding each row's own index."""
+def hardest_negative_indices(anchor, candidates, valid=None, chunk: int = 1024) -> torch.Tensor:
+    """Each anchor's most similar candidate other than its own pair, among valid candidates.
 
-    a = F.normalize(_f32(anchor).detach(), dim=1)
-    c = F.normalize(_f32(candidates).detach(), dim=1)
-    out = []
-    for s in range(0, a.shape[0], chunk):
-        scores = a[s:s + chunk] @ c.T
-        rows = torch.arange(s, min(a.shape[0], s + chunk), device=a.device)
-        scores[torch.arange(rows.numel(), device=a.device), rows] = float("-inf")
-        out.append(scores.argmax(1))
-    return torch.cat(out)
+    The fused tcgen05 mining kernel on CUDA (``ops.mnr.hardest_candidates``);
+    ``chunk`` bounds the rows scored at once on the CPU path only."""
+
+    from representax_b200.ops.mnr import hardest_candidates
+
+    del chunk
+    return hardest_candidates(anchor, candidates, valid, exclude_offset=0)
 
 
 # =============================================================== batches
@@ -379,6 +378,7 @@ class DenoisingBatch:
 class MegaBatch:
     anchor: Any
     positive: Any
+    valid: torch.Tensor | None = None  # rows that take part (padding rows do not)
 
 
 # =============================================================== tasks
@@ -540,8 +540,10 @@ class MegaBatchMarginTask(_RepresentationTask):
 
     def loss_from_representations(self, reps, batch):
         a, p = reps
-        idx = hardest_negative_indices(a, p)
-        return LossOutput(loss=mega_batch_margin_loss(a, p, p[idx], self.positive_margin, self.negative_margin))
+        valid = getattr(batch, "valid", None)
+        idx = hardest_negative_indices(a, p, valid)
+        return LossOutput(loss=mega_batch_margin_loss(a, p, p[idx.to(p.device)], self.positive_margin,
+                                                      self.negative_margin, valid))
 
 
 @dataclass(frozen=True)

@@ -60,15 +60,20 @@ class MegaBatchMining:
                            for s in range(0, rows, chunk)])
             p = torch.cat([encode(model, slice_rows(batch.positive, s, min(rows, s + chunk)), route=Route.DOCUMENT)
                            for s in range(0, rows, chunk)])
-        negatives = hardest_negative_indices(a, p, chunk=self.loss_row_chunk_size or chunk)
+        valid = getattr(batch, "valid", None)
+        negatives = hardest_negative_indices(a, p, valid, chunk=self.loss_row_chunk_size or chunk)
         negative_payload = _gather_rows(batch.positive, negatives)
         total = torch.zeros((), device=a.device)
+        # every chunk's share of the masked mean over the whole mega batch
+        count = rows if valid is None else max(int(valid.bool().sum()), 1)
         for s in range(0, rows, chunk):
             e = min(rows, s + chunk)
             ea = encode(model, slice_rows(batch.anchor, s, e), route=Route.QUERY)
             ep = encode(model, slice_rows(batch.positive, s, e), route=Route.DOCUMENT)
             en = encode(model, slice_rows(negative_payload, s, e), route=Route.DOCUMENT)
-            part = mega_batch_margin_loss(ea, ep, en, task.positive_margin, task.negative_margin) * ((e - s) / rows)
+            v = None if valid is None else valid[s:e]
+            n_rows = (e - s) if v is None else int(v.bool().sum())
+            part = mega_batch_margin_loss(ea, ep, en, task.positive_margin, task.negative_margin, v) * (n_rows / count)
             part.backward()
             total = total + part.detach()
         return LossOutput(loss=total, metrics={})

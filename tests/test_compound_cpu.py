@@ -48,6 +48,51 @@ def test_mega_batch_mining_gradient_equals_direct_margin_loss():
     assert torch.allclose(mined, model.table.grad, atol=1e-6)
 
 
+def test_mega_batch_mining_honours_valid_rows():
+    """Padding rows are neither mined as negatives nor counted in the margin mean."""
+
+    from representax_b200.train.mega_batch import MegaBatchMining
+
+    model = _Table(16, 6, seed=3)
+    valid = torch.tensor([True, True, False, True, True, True, False, True])
+    batch = O.MegaBatch(anchor=torch.arange(0, 8), positive=torch.arange(8, 16), valid=valid)
+    task = O.MegaBatchMarginTask(positive_margin=0.9, negative_margin=-0.5)
+    with precision_context(FP32_POLICY):
+        out = MegaBatchMining(micro_batch_size=3).run(task, model, batch, streams=None)
+        via_task = task.loss_from_representations((model.table[:8], model.table[8:]), batch).loss
+    mined = model.table.grad.clone()
+    model.table.grad = None
+    a, p = model.table[:8].double(), model.table[8:].double()
+    with torch.no_grad():
+        cos = torch.nn.functional.normalize(a, dim=1) @ torch.nn.functional.normalize(p, dim=1).T
+        cos.fill_diagonal_(float("-inf"))
+        cos[:, ~valid] = float("-inf")
+        hardest = cos.argmax(1)
+    assert not valid[hardest].logical_not().any()
+    cp = torch.nn.functional.cosine_similarity(a, p, dim=1)
+    cn = torch.nn.functional.cosine_similarity(a, p[hardest], dim=1)
+    rows = torch.relu(0.9 - cp) + torch.relu(cn + 0.5)
+    direct = (rows * valid).sum() / valid.sum()
+    direct.backward()
+    assert abs(float(out.loss) - float(direct)) < 1e-6
+    assert abs(float(via_task) - float(direct)) < 1e-6
+    assert torch.allclose(mined.double(), model.table.grad.double(), atol=1e-6)
+
+
+def test_hardest_candidates_masks_and_offsets():
+    from representax_b200.ops.mnr import hardest_candidates
+
+    g = torch.Generator().manual_seed(5)
+    a, c = torch.randn(10, 5, generator=g), torch.randn(14, 5, generator=g)
+    valid = torch.rand(14, generator=g) > 0.3
+    got = hardest_candidates(a, c, valid, exclude_offset=4)
+    cos = torch.nn.functional.normalize(a.double(), dim=1) @ torch.nn.functional.normalize(c.double(), dim=1).T
+    cos[:, ~valid] = float("-inf")
+    cos[torch.arange(10), torch.arange(10) + 4] = float("-inf")
+    assert torch.equal(got, cos.argmax(1))
+    assert torch.equal(hardest_candidates(a, c, exclude_offset=None), (a @ c.T / c.norm(dim=1)).argmax(1))
+
+
 def test_pair_classifier_softmax_task():
     from representax_b200.models.composition import PairClassifier
 

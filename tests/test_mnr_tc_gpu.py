@@ -113,3 +113,34 @@ def test_unaligned_batch_mnr_matches_reference():
     assert abs(loss.item() - ref.item()) < 1e-4
     assert (q.grad.double() - q2.grad).abs().max().item() < 1e-5 + 1e-3 * q2.grad.abs().max().item()
     assert (d.grad.double() - d2.grad).abs().max().item() < 1e-5 + 1e-3 * d2.grad.abs().max().item()
+
+
+@pytest.mark.parametrize("m,n,k,offset,masked", [(1000, 1000, 64, 0, True), (300, 2048, 768, 100, False),
+                                                 (129, 77, 20, None, True)])
+def test_mining_argmax_matches_fp64(m, n, k, offset, masked):
+    """Fused mining kernel: each row's best allowed candidate without storing scores."""
+
+    from representax_b200.ops._ext import check_status
+    from representax_b200.ops.mnr import hardest_candidates
+
+    g = torch.Generator(device="cpu").manual_seed(17)
+    a = (torch.randn(m, k, generator=g) * 3).to(_dev())
+    c = torch.randn(n, k, generator=g).to(_dev())
+    valid = (torch.rand(n, generator=g) > 0.25).to(_dev()) if masked else None
+    got = hardest_candidates(a, c, valid, exclude_offset=offset)
+    torch.cuda.synchronize()
+    check_status(_dev())
+    cos = torch.nn.functional.normalize(a.double(), dim=1) @ torch.nn.functional.normalize(c.double(), dim=1).T
+    if valid is not None:
+        cos[:, ~valid] = float("-inf")
+    if offset is not None:
+        rows = torch.arange(m, device=_dev())
+        keep = rows + offset < n
+        cos[rows[keep], rows[keep] + offset] = float("-inf")
+    want = cos.argmax(1)
+    best = cos.max(1).values
+    picked = cos.gather(1, got[:, None])[:, 0]
+    # the picked candidate is allowed and within split-bf16 rounding of the best
+    assert torch.isfinite(picked).all()
+    assert (best - picked).max().item() < 2e-5
+    assert (got != want).float().mean().item() < 0.01

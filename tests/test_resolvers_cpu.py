@@ -158,3 +158,28 @@ def test_token_balanced_shards_equalise_work():
         assert loader.data_contract["rank_assignment"] == "token_balanced"
     whole = DataLoader([records], weights=[1.0], seed=0, batch_size=32, num_threads=1, prefetch=1)
     assert sorted(seen) == sorted(r["n"] for r in whole.make_batch(0)[0])  # same global batch
+
+
+def test_host_memory_budget_bounds_each_prefetch_slot():
+    """The budget is split over prefetch + 1 model-ready batch slots (ref data/distribution.py:700-720)."""
+
+    import numpy as np
+
+    from representax_b200.data.loader import DataLoader
+
+    rows = [np.zeros(16, dtype=np.float32) for _ in range(64)]  # 64 bytes a row
+
+    def collate(records):
+        return np.stack(records)
+
+    ok = DataLoader([rows], weights=[1.0], batch_size=4, collate=collate, prefetch=3, num_batches=2,
+                    host_memory_budget_bytes=4 * 256)  # 256 bytes a slot: one 4-row batch fits
+    assert [b.shape for b in ok] == [(4, 16), (4, 16)]
+    tight = DataLoader([rows], weights=[1.0], batch_size=8, collate=collate, prefetch=3, num_batches=1,
+                       host_memory_budget_bytes=4 * 256)  # 512-byte batches do not
+    with pytest.raises(MemoryError, match="per-slot limit"):
+        list(tight)
+    with pytest.raises(ValueError, match="cannot hold"):
+        DataLoader([rows], weights=[1.0], batch_size=4, prefetch=3, host_memory_budget_bytes=3)
+    with pytest.raises(ValueError, match="positive"):
+        DataLoader([rows], weights=[1.0], batch_size=4, host_memory_budget_bytes=0)
