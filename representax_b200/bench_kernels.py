@@ -221,6 +221,78 @@ def bench_mnr(timer, hbm, flops_peak, tag, report):
                     "value": (scores.double() - ref).abs().max().item()})
 
 
+def bench_pool(timer, hbm, flops_peak, tag, report):
+    """Mean pooling + L2 normalisation of one GradCache chunk (128 rows, 18432 packed tokens)."""
+
+    from representax_b200.ops._ext import ext
+
+    C = ext()
+    h, rows = 768, 128
+    lens = torch.full((rows,), 18432 // rows, dtype=torch.int32)
+    cu = torch.zeros(rows + 1, dtype=torch.int32)
+    cu[1:] = torch.cumsum(lens, 0)
+    cu = cu.cuda()
+    x = torch.randn(int(cu[-1]), h, device="cuda").to(torch.bfloat16)
+    out = torch.empty(rows, h, device="cuda")
+    norm = torch.empty(rows, device="cuda")
+    t = timer(lambda: C.pool_forward(x, cu, out, norm, 0, True))
+    by = x.numel() * 2
+    report({"kernel": "pool_mean_fwd", "tokens": x.shape[0], "H": h, "ms": t * 1e3, "gbs": by / t / 1e9,
+            f"frac_of_{tag}_hbm": by / t / hbm})
+    g = torch.randn(rows, h, device="cuda")
+    dh = torch.empty_like(x)
+    t = timer(lambda: C.pool_backward(g, out, norm, cu, dh, 0, True))
+    report({"kernel": "pool_mean_bwd", "tokens": x.shape[0], "H": h, "ms": t * 1e3, "gbs": by / t / 1e9,
+            f"frac_of_{tag}_hbm": by / t / hbm})
+
+
+def bench_mxfp8(timer, hbm, flops_peak, tag, report):
+    """Block-scaled MXFP8 GEMM (tcgen05 kind::mxf8f6f4.block_scale) beside the
+    per-tensor fp8 and bf16 tcgen05 GEMMs on the same shapes, plus the quantiser.
+    Fractions are of the measured bf16 peak (nominal dense fp8 is twice bf16)."""
+
+    from representax_b200.ops import gemm as G
+    from representax_b200.ops import mxfp8 as MX
+    from representax_b200.ops._ext import ext, status
+
+    C = ext()
+    for name, m, n, k in [("qkv", 18432, 2304, 768), ("ffn2", 18432, 768, 3072), ("square_8k", 8192, 8192, 8192)]:
+        a = torch.randn(m, k, device="cuda").to(torch.bfloat16)
+        b = (torch.randn(n, k, device="cuda") * 0.05).to(torch.bfloat16)
+        aq, _ = MX.quantize(a, MX.E4M3)
+        bq, _ = MX.quantize(b, MX.E4M3)
+        y = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+        fl = 2.0 * m * n * k
+        t = timer(lambda: MX.gemm(aq, bq, y))
+        t_q = timer(lambda: MX.quantize(a, MX.E4M3))
+        # per-tensor fp8 on the same operands' bits (scales 1)
+        ones = torch.ones(2, device="cuda")
+        t_pt = timer(lambda: C.gemm_fp8(aq.data, bq.data, y, 0, 0, 0, 0, 1.0, ones, None, None, status(y.device)))
+        t_bf = timer(lambda: G.gemm(a, b, y))
+        report({"kernel": "mxfp8_gemm", "case": name, "M": m, "N": n, "K": k, "ms": t * 1e3,
+                "tflops": fl / t / 1e12, f"frac_of_{tag}_bf16": fl / t / flops_peak,
+                "fp8_per_tensor_ms": t_pt * 1e3, "bf16_tcgen05_ms": t_bf * 1e3,
+                "quantize_A_ms": t_q * 1e3, "quantize_A_gbs": (a.numel() * 3 + a.numel() / 16) / t_q / 1e9})
+    # hardest-negative mining: 8192 anchors x 8192 candidates, width 768
+    from representax_b200.ops.mnr import hardest_candidates
+
+    q = torch.randn(8192, 768, device="cuda")
+    d = torch.randn(8192, 768, device="cuda")
+    t = timer(lambda: hardest_candidates(q, d))
+
+    def torch_mining():
+        qn = torch.nn.functional.normalize(q, dim=1)
+        dn = torch.nn.functional.normalize(d, dim=1)
+        for s0 in range(0, 8192, 1024):
+            sc = qn[s0:s0 + 1024] @ dn.T
+            sc[torch.arange(1024, device="cuda"), torch.arange(s0, s0 + 1024, device="cuda")] = float("-inf")
+            sc.argmax(1)
+
+    report({"kernel": "mining_argmax_tcgen05", "M": 8192, "N": 8192, "K": 768, "ms": t * 1e3,
+            "torch_fp32_chunked_ms": timer(torch_mining) * 1e3,
+            "note": "split-bf16 scores (3 MMAs per product) reduced to a row argmax in the epilogue"})
+
+
 def main(argv=None):
     parser = argparse.ArgumentParser()
     parser.add_argument("--only", default="gemm,attention,norm")
@@ -246,6 +318,10 @@ def main(argv=None):
         bench_norm(timer, hbm, flops_peak, tag, report)
     if "mnr" in selected:
         bench_mnr(timer, hbm, flops_peak, tag, report)
+    if "pool" in selected:
+        bench_pool(timer, hbm, flops_peak, tag, report)
+    if "mxfp8" in selected:
+        bench_mxfp8(timer, hbm, flops_peak, tag, report)
     from representax_b200.ops._ext import check_status
 
     torch.cuda.synchronize()

@@ -17,7 +17,8 @@ named shape, with random-init weights and synthetic inputs:
   (12 layers, hidden 768, patch 16 at 512 x 512, pixel shuffle 4 -> 64 image
   tokens). Queries are text of length 128 (ids uniform over the 50368 vocab),
   documents are one N(0, 1) image each; cached MNR (GradCache) with global
-  batch 2048 and mini-batch 64; per-tensor-scaled fp8 linear layers.
+  batch 2048 and mini-batch 64; block-scaled (MXFP8) linear layers
+  (``--fp8 tensor``: the reference's per-tensor scaling).
 * ``qwen3vl`` - Qwen3-VL-2B-style embedder: 28-layer decoder (hidden 2048,
   16 query / 8 KV heads of 128, SwiGLU 6144, M-RoPE, vocab 151936) with packed
   INT4 base weights and LoRA rank 16 on q/k/v/o/gate/up/down, and a 24-layer
@@ -82,7 +83,7 @@ def _mpnet(args, rng_for_rank):
 def _modernvbert(args, rng_for_rank):
     from representax_b200.data.synthetic import token_batch
     from representax_b200.models.modernvbert import ModernVBERTBatch, ModernVBERTConfig, ModernVBERTEncoder
-    from representax_b200.precision import FP8_MIXED_POLICY
+    from representax_b200.precision import FP8_MIXED_POLICY, MXFP8_MIXED_POLICY
     from representax_b200.tasks.retrieval import MNRTask, RetrievalBatch
     from representax_b200.train.execution import GradCache
 
@@ -110,9 +111,13 @@ def _modernvbert(args, rng_for_rank):
                      "patch 16 @ 512x512, pixel shuffle 4)",
             "global_batch": global_batch, "mini_batch": mini, "unit_rows": "pairs", "seq_len": seq,
             "documents": "one 512x512 N(0,1) image (64 image tokens) per document",
-            "loss": "cached MNR (GradCache), scale 20", "precision": "fp8 linear layers (per-tensor scaled E4M3 / "
-            "E5M2 gradients), bf16 elsewhere, fp32 master", "reference_parallelism": "FSDP over 8 GPUs"}
-    return model, task, GradCache(query_chunk_size=mini, retain_bytes="auto"), FP8_MIXED_POLICY, batch, per_rank, info
+            "loss": "cached MNR (GradCache), scale 20",
+            "precision": ("fp8 linear layers (MXFP8: E4M3 / E5M2 gradients with one UE8M0 scale per 32 values, "
+                          "tcgen05 block-scaled MMA)" if args.fp8 == "block" else
+                          "fp8 linear layers (per-tensor scaled E4M3 / E5M2 gradients)")
+            + ", bf16 elsewhere, fp32 master", "reference_parallelism": "FSDP over 8 GPUs"}
+    policy = MXFP8_MIXED_POLICY if args.fp8 == "block" else FP8_MIXED_POLICY
+    return model, task, GradCache(query_chunk_size=mini, retain_bytes="auto"), policy, batch, per_rank, info
 
 
 def _qwen3vl(args, rng_for_rank):
@@ -179,6 +184,8 @@ def main(argv=None) -> None:
     parser.add_argument("--rows", type=int, default=None,
                         help="override the per-rank triplets (mpnet) or global batch (others)")
     parser.add_argument("--dropout", type=float, default=0.1, help="mpnet hidden / attention dropout")
+    parser.add_argument("--fp8", choices=["block", "tensor"], default="block",
+                        help="modernvbert fp8 scaling: MXFP8 blocks (default) or per tensor")
     parser.add_argument("--out", default=None, help="append the JSON line to this file (rank 0)")
     parser.add_argument("--layout", choices=["auto", "dp", "fsdp"], default="auto",
                         help="N > 1: dp = replicated weights + sharded optimizer; fsdp = master weights, moments and "

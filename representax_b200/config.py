@@ -387,6 +387,9 @@ class PrecisionConfig(FrozenConfig):
     matrix_dtype: MatrixDType | None = None
     accumulation_dtype: Literal["float32"] = "float32"
     loss_dtype: Literal["float32"] = "float32"
+    # float8 matrices: one scale per tensor (the reference's recipe) or one
+    # power-of-two scale per 32-value block (MXFP8)
+    fp8_scaling: Literal["tensor", "block"] = "tensor"
 
     @classmethod
     def bfloat16_mixed(cls) -> "PrecisionConfig":

@@ -103,6 +103,11 @@ void mnr_tc_gemm(const at::Tensor& a_hi, const at::Tensor& a_lo, bool a_mn, cons
 void mnr_tc_argmax(const at::Tensor& a_hi, const at::Tensor& a_lo, const at::Tensor& b_hi, const at::Tensor& b_lo,
                    at::Tensor& best, const c10::optional<at::Tensor>& valid, int64_t exclude_off,
                    const at::Tensor& status);
+void mx_quantize(const at::Tensor& x, const c10::optional<at::Tensor>& q, const c10::optional<at::Tensor>& sf,
+                 const c10::optional<at::Tensor>& qt, const c10::optional<at::Tensor>& sft, bool e5m2);
+void mx_gemm(const at::Tensor& a, const at::Tensor& sfa, int64_t a_fmt, const at::Tensor& b, const at::Tensor& sfb,
+             int64_t b_fmt, int64_t K, at::Tensor& out, int64_t out_mode, const c10::optional<at::Tensor>& bias,
+             const c10::optional<at::Tensor>& residual, const at::Tensor& status);
 void sharded_grad_reduce(const at::Tensor& grad_ptrs, int64_t world, int64_t off, int64_t n, at::Tensor& shard,
                          at::Tensor& norm_sq);
 void sharded_adamw(const at::Tensor& shard_grad, int64_t off, int64_t n, const at::Tensor& master_ptrs,
@@ -158,6 +163,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gather_ranges", &rx::gather_ranges, "copy flat [lo, hi) ranges of a sharded bf16 buffer into a full copy");
   m.def("mnr_tc_scores", &rx::mnr_tc_scores, "tcgen05 MNR scores with the candidate all-gather fused in");
   m.def("mnr_tc_gemm", &rx::mnr_tc_gemm, "tcgen05 split-bf16 GEMM, local or row-routed (peer) output");
+  m.def("mx_quantize", &rx::mx_quantize, "MXFP8 quantiser: row-wise and / or transposed 8-bit data + UE8M0 scales");
+  m.def("mx_gemm", &rx::mx_gemm, "tcgen05 block-scaled MXFP8 GEMM (kind::mxf8f6f4.block_scale)");
   m.def("mnr_tc_argmax", &rx::mnr_tc_argmax, "tcgen05 split-bf16 scores reduced to each row's hardest candidate");
   m.def("sharded_grad_reduce", &rx::sharded_grad_reduce);
   m.def("sharded_adamw", &rx::sharded_adamw);

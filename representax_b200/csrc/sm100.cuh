@@ -173,6 +173,37 @@ __device__ __forceinline__ void umma_f8_ss(uint32_t d_tmem, uint64_t a_desc, uin
       : "memory");
 }
 
+// D[tmem] (+)= (A * sfa) . (B * sfb)^T with 8-bit operands and one UE8M0
+// scale per 32 K values (kind::mxf8f6f4, block scaling, K = 32 per
+// instruction). sfa / sfb are TMEM addresses of the scale columns; their bits
+// 30-31 select the scale byte (the K block) inside each 32-bit TMEM word and
+// must match the scale-factor ids in the instruction descriptor.
+__device__ __forceinline__ void umma_mxf8_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+
+// Copy 32 rows x 16 bytes from shared memory (descriptor) into TMEM lanes
+// 0-31 of 4 columns, replicated into all four lane quarters (warpx4).
+__device__ __forceinline__ void tmem_cp_32x128b_warpx4(uint32_t taddr, uint64_t src_desc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(src_desc) : "memory");
+}
+
+// Untiled bulk copy global -> shared (no multicast); 16-byte aligned
+// addresses, size a multiple of 16 bytes, completion counted on `bar`.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // Arrive once on `bar` when every previously issued tcgen05.mma of this
 // thread has completed.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
@@ -250,6 +281,30 @@ __host__ __device__ constexpr uint32_t idesc_f8_f32(int m, int n, int a_fmt, int
          | (static_cast<uint32_t>(b_fmt) << 10)     // B format
          | (static_cast<uint32_t>(n >> 3) << 17)    // N / 8
          | (static_cast<uint32_t>(m >> 4) << 24);   // M / 16
+}
+
+// Shared-memory descriptor without swizzle (K-major core matrices of 8 rows x
+// 16 bytes stored contiguously): `sbo` bytes between 8-row groups.
+__device__ __forceinline__ uint64_t smem_desc_plain(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t desc = 0;
+  desc |= static_cast<uint64_t>((saddr & 0x3FFFF) >> 4);
+  desc |= static_cast<uint64_t>((lbo >> 4) & 0x3FFF) << 16;
+  desc |= static_cast<uint64_t>((sbo >> 4) & 0x3FFF) << 32;
+  desc |= 1ull << 46;  // descriptor version for sm_100; layout type 0 = no swizzle
+  return desc;
+}
+
+// kind::mxf8f6f4 block-scaled descriptor: K-major operands (0 = E4M3,
+// 1 = E5M2), UE8M0 scales, fp32 accumulation, dense K = 32; sf_a / sf_b pick
+// the scale byte inside each TMEM word.
+__host__ __device__ constexpr uint32_t idesc_mxf8(int m, int n, int a_fmt, int b_fmt, int sf_a, int sf_b) {
+  return (static_cast<uint32_t>(sf_b & 3) << 4)      // B scale-factor id
+         | (static_cast<uint32_t>(a_fmt) << 7)       // A format
+         | (static_cast<uint32_t>(b_fmt) << 10)      // B format
+         | (static_cast<uint32_t>(n >> 3) << 17)     // N / 8
+         | (1u << 23)                                // scale format: UE8M0
+         | (static_cast<uint32_t>(m >> 4) << 24)     // M / 16
+         | (static_cast<uint32_t>(sf_a & 3) << 29);  // A scale-factor id
 }
 
 __device__ __forceinline__ int warp_id() { return threadIdx.x >> 5; }

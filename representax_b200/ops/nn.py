@@ -104,7 +104,9 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = No
     """``x W^T (+ b) (+ residual)``; W in the Hugging Face ``[out, in]`` layout.
 
     Under a precision policy whose matrix dtype is ``float8_e4m3fn`` the
-    native path runs the per-tensor-scaled FP8 GEMMs of ``ops.fp8``."""
+    native path runs the per-tensor-scaled FP8 GEMMs of ``ops.fp8``, or the
+    block-scaled MXFP8 GEMMs of ``ops.mxfp8`` when the policy asks for block
+    scaling."""
 
     from representax_b200.models.adapters import QuantizedLoRAWeight
 
@@ -114,10 +116,18 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = No
         y = weight.linear(x, bias)
         return y if residual is None else y + residual
     if native(x) and _fp8_matrices():
-        from .fp8 import fp8_supported, linear_fp8
+        from representax_b200.precision import active_policy
 
-        if fp8_supported(x, weight):
-            return linear_fp8(x, weight, bias, residual)
+        if active_policy().fp8_block_scaled:
+            from .mxfp8 import linear_mxfp8, mxfp8_supported
+
+            if mxfp8_supported(x, weight):
+                return linear_mxfp8(x, weight, bias, residual)
+        else:
+            from .fp8 import fp8_supported, linear_fp8
+
+            if fp8_supported(x, weight):
+                return linear_fp8(x, weight, bias, residual)
     if native(x) and x.shape[1] % 8 == 0 and weight.shape[0] % 8 == 0:
         return _LinearFn.apply(x.contiguous(), weight, bias, residual)
     y = torch.nn.functional.linear(x, weight.to(x.dtype), None if bias is None else bias.to(x.dtype))

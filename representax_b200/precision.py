@@ -7,7 +7,9 @@ meaning: fp32 master parameters live in one flat buffer with a bf16 compute
 copy refreshed by the fused optimizer kernel (instead of a cast per step), and
 a ``float8_e4m3fn`` matrix policy routes packed-row linear layers to
 tcgen05 FP8 GEMMs with the reference's per-tensor dynamic scaling (E4M3
-forward, E5M2 gradients, fp32 accumulation; ``ops.fp8``).
+forward, E5M2 gradients, fp32 accumulation; ``ops.fp8``), or with
+``fp8_scaling="block"`` to the MXFP8 GEMMs of ``ops.mxfp8`` (one UE8M0 scale
+per 32-value block, applied by the tensor core).
 """
 
 from __future__ import annotations
@@ -31,6 +33,7 @@ class PrecisionPolicy:
     matrix_dtype: torch.dtype = torch.float32
     accumulation_dtype: torch.dtype = torch.float32
     loss_dtype: torch.dtype = torch.float32
+    fp8_block_scaled: bool = False  # float8 matrices: MXFP8 (per-32 block) instead of per-tensor scales
 
     @property
     def communication_dtype(self) -> torch.dtype:
@@ -67,6 +70,7 @@ def resolve_precision_policy(config: Any) -> PrecisionPolicy:
         matrix_dtype=_DTYPES[config.resolved_matrix_dtype],
         accumulation_dtype=_DTYPES[config.accumulation_dtype],
         loss_dtype=_DTYPES[config.loss_dtype],
+        fp8_block_scaled=getattr(config, "fp8_scaling", "tensor") == "block",
     )
 
 
@@ -104,10 +108,15 @@ def loss_value(value: torch.Tensor) -> torch.Tensor:
 FP8_MIXED_POLICY = PrecisionPolicy(
     compute_dtype=torch.bfloat16, activation_dtype=torch.bfloat16, matrix_dtype=torch.float8_e4m3fn
 )
+MXFP8_MIXED_POLICY = PrecisionPolicy(
+    compute_dtype=torch.bfloat16, activation_dtype=torch.bfloat16, matrix_dtype=torch.float8_e4m3fn,
+    fp8_block_scaled=True,
+)
 
 __all__ = [
     "BF16_MIXED_POLICY",
     "FP8_MIXED_POLICY",
+    "MXFP8_MIXED_POLICY",
     "FP32_POLICY",
     "PrecisionPolicy",
     "active_compute_dtype",
