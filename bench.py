@@ -175,6 +175,7 @@ def _kernel_table(step, batch, it, path) -> None:
         for key, short in (("gemm_pair_kernel", "gemm_tcgen05_pair"), ("gemm_kernel", "gemm_tcgen05"),
                            ("attn_fwd", "attention_fwd"), ("attn_bwd", "attention_bwd"), ("attn_dvec", "attention_dvec"),
                            ("attn_dq_convert", "attention_dq_convert"), ("norm_fwd", "layernorm_fwd"),
+                           ("norm_param_reduce", "layernorm_param_reduce"),
                            ("norm_bwd", "layernorm_bwd"), ("embed_ln", "embed_layernorm"), ("pool", "pool"),
                            ("colsum", "colsum"), ("mnr", "mnr"), ("sgemm", "mnr_sgemm"), ("adamw", "adamw"),
                            ("grad_norm", "grad_norm"), ("cast_bf16", "cast_bf16")):
@@ -187,10 +188,10 @@ def _kernel_table(step, batch, it, path) -> None:
         rows[name] = (t + e.device_time_total / 1e3, n + 1)
     total = sum(t for t, _ in rows.values())
     with open(path, "w") as f:
-        f.write("| kernel | launches | device ms | share |\n|---|---|---|---|\n")
+        f.write("| kernel | launches | device ms | us per launch | share |\n|---|---|---|---|---|\n")
         for name, (t, n) in sorted(rows.items(), key=lambda kv: -kv[1][0]):
-            f.write(f"| {name} | {n} | {t:.2f} | {t / total:.1%} |\n")
-        f.write(f"| total | {sum(n for _, n in rows.values())} | {total:.2f} | 100% |\n")
+            f.write(f"| {name} | {n} | {t:.2f} | {1e3 * t / n:.1f} | {t / total:.1%} |\n")
+        f.write(f"| total | {sum(n for _, n in rows.values())} | {total:.2f} | | 100% |\n")
 
 
 def main() -> None:

@@ -140,27 +140,33 @@ def bench_attention(timer, hbm, flops_peak, tag, report):
 
 
 def bench_norm(timer, hbm, flops_peak, tag, report):
+    """LayerNorm forward / backward on one GradCache chunk's rows (18432 =
+    128 sequences x 144 tokens, H 768) and on four chunks; the backward also
+    sums the producing linear layer's bias gradient, as in the training step."""
+
     from representax_b200.ops._ext import ext
 
     C = ext()
-    rows, h = 18432 * 4, 768
-    x = torch.randn(rows, h, device="cuda").to(torch.bfloat16)
-    g = torch.ones(h, device="cuda", dtype=torch.bfloat16)
-    b = torch.zeros(h, device="cuda", dtype=torch.bfloat16)
-    y = torch.empty_like(x)
-    mean = torch.empty(rows, device="cuda")
-    rstd = torch.empty(rows, device="cuda")
-    t = timer(lambda: C.norm_forward(x, g, b, y, mean, rstd, 1e-12, False))
-    by = 2 * rows * h * 2
-    report({"kernel": "layernorm_fwd", "rows": rows, "H": h, "ms": t * 1e3, "gbs": by / t / 1e9,
-            f"frac_of_{tag}_hbm": by / t / hbm})
-    dx = torch.empty_like(x)
-    dg = torch.zeros(h, device="cuda")
-    db = torch.zeros(h, device="cuda")
-    t = timer(lambda: C.norm_backward(y, x, mean, rstd, g, dx, dg, db, None, False))
-    by = 3 * rows * h * 2
-    report({"kernel": "layernorm_bwd", "rows": rows, "H": h, "ms": t * 1e3, "gbs": by / t / 1e9,
-            f"frac_of_{tag}_hbm": by / t / hbm})
+    h = 768
+    for rows in (18432, 18432 * 4):
+        x = torch.randn(rows, h, device="cuda").to(torch.bfloat16)
+        g = torch.ones(h, device="cuda", dtype=torch.bfloat16)
+        b = torch.zeros(h, device="cuda", dtype=torch.bfloat16)
+        y = torch.empty_like(x)
+        mean = torch.empty(rows, device="cuda")
+        rstd = torch.empty(rows, device="cuda")
+        t = timer(lambda: C.norm_forward(x, g, b, y, mean, rstd, 1e-12, False))
+        by = 2 * rows * h * 2
+        report({"kernel": "layernorm_fwd", "rows": rows, "H": h, "ms": t * 1e3, "gbs": by / t / 1e9,
+                f"frac_of_{tag}_hbm": by / t / hbm})
+        dx = torch.empty_like(x)
+        dg = torch.zeros(h, device="cuda")
+        db = torch.zeros(h, device="cuda")
+        dbp = torch.zeros(h, device="cuda")
+        t = timer(lambda: C.norm_backward(y, x, mean, rstd, g, dx, dg, db, dbp, False))
+        by = 3 * rows * h * 2
+        report({"kernel": "layernorm_bwd", "rows": rows, "H": h, "ms": t * 1e3, "gbs": by / t / 1e9,
+                f"frac_of_{tag}_hbm": by / t / hbm})
     # bias-gradient column sums of a QKV-shaped gradient (one GradCache chunk)
     g_qkv = torch.randn(18432, 2304, device="cuda").to(torch.bfloat16)
     acc = torch.zeros(2304, device="cuda")
@@ -293,6 +299,47 @@ def bench_mxfp8(timer, hbm, flops_peak, tag, report):
             "note": "split-bf16 scores (3 MMAs per product) reduced to a row argmax in the epilogue"})
 
 
+def bench_int4(timer, hbm, flops_peak, tag, report):
+    """Frozen INT4 base weight (QLoRA): the tcgen05 GEMM that expands packed
+    nibbles in its main loop, beside dequantise-to-HBM + bf16 tcgen05 GEMM, on
+    Qwen3-VL-2B-like projections (hidden 2048, MLP 6144), forward and dgrad."""
+
+    from representax_b200.models.adapters import QuantizedLoRAWeight
+    from representax_b200.ops import gemm as G
+    from representax_b200.ops._ext import ext, status
+
+    C = ext()
+    st = status(torch.device("cuda", 0))
+    cases = [("qkv", t, 4096, 2048) for t in (128, 512, 2048, 4096, 16384)]
+    cases += [("up", 16384, 6144, 2048), ("down", 16384, 2048, 6144), ("down", 1024, 2048, 6144)]
+    for name, t_rows, n, k in cases:
+        if CASE_FILTER and CASE_FILTER not in f"{name}_t{t_rows}":
+            continue
+        q = QuantizedLoRAWeight(torch.randn(n, k) * 0.05, rank=16, alpha=32.0, seed=0).to("cuda")
+        x = torch.randn(t_rows, k, device="cuda").to(torch.bfloat16)
+        dy = torch.randn(t_rows, n, device="cuda").to(torch.bfloat16)
+        y = torch.empty(t_rows, n, dtype=torch.bfloat16, device="cuda")
+        dx = torch.empty(t_rows, k, dtype=torch.bfloat16, device="cuda")
+        w = torch.empty(n, k, dtype=torch.bfloat16, device="cuda")
+        fl = 2.0 * t_rows * n * k
+        t_f = timer(lambda: C.int4_gemm(x, q.packed_weight, q.scale_bits, k, y, None, None, False, st))
+        t_d = timer(lambda: C.int4_gemm(dy, q.packed_weight, q.scale_bits, k, dx, None, None, True, st))
+
+        def unfused_fwd():
+            C.int4_dequantize(q.packed_weight, q.scale_bits, w)
+            G.gemm(x, w, y)
+
+        def unfused_dgrad():
+            C.int4_dequantize(q.packed_weight, q.scale_bits, w)
+            G.linear_dgrad(dy, w, out=dx)
+
+        report({"kernel": "int4_gemm", "case": name, "T": t_rows, "N": n, "K": k, "fwd_ms": t_f * 1e3,
+                "fwd_tflops": fl / t_f / 1e12, f"fwd_frac_of_{tag}_bf16": fl / t_f / flops_peak,
+                "dgrad_ms": t_d * 1e3, "dgrad_tflops": fl / t_d / 1e12,
+                "dequant_then_gemm_fwd_ms": timer(unfused_fwd) * 1e3,
+                "dequant_then_gemm_dgrad_ms": timer(unfused_dgrad) * 1e3})
+
+
 def main(argv=None):
     parser = argparse.ArgumentParser()
     parser.add_argument("--only", default="gemm,attention,norm")
@@ -322,6 +369,8 @@ def main(argv=None):
         bench_pool(timer, hbm, flops_peak, tag, report)
     if "mxfp8" in selected:
         bench_mxfp8(timer, hbm, flops_peak, tag, report)
+    if "int4" in selected:
+        bench_int4(timer, hbm, flops_peak, tag, report)
     from representax_b200.ops._ext import check_status
 
     torch.cuda.synchronize()

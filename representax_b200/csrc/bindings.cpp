@@ -16,6 +16,9 @@ void gemm_fp8(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, int64_t a
               const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& residual,
               const at::Tensor& status);
 void int4_dequantize(const at::Tensor& packed, const at::Tensor& scale_bits, at::Tensor& out);
+void int4_gemm(const at::Tensor& x, const at::Tensor& packed, const at::Tensor& scale_bits, int64_t in_features,
+               at::Tensor& out, const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& residual,
+               bool dgrad, const at::Tensor& status);
 void dropout_apply(const at::Tensor& x, at::Tensor& y, int64_t seed, int64_t stream, double p,
                    const c10::optional<at::Tensor>& colsum);
 void gemm_tcgen05(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_mn, bool b_mn,
@@ -163,6 +166,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gather_ranges", &rx::gather_ranges, "copy flat [lo, hi) ranges of a sharded bf16 buffer into a full copy");
   m.def("mnr_tc_scores", &rx::mnr_tc_scores, "tcgen05 MNR scores with the candidate all-gather fused in");
   m.def("mnr_tc_gemm", &rx::mnr_tc_gemm, "tcgen05 split-bf16 GEMM, local or row-routed (peer) output");
+  m.def("int4_gemm", &rx::int4_gemm, "tcgen05 GEMM with the packed INT4 weight expanded in the main loop");
   m.def("mx_quantize", &rx::mx_quantize, "MXFP8 quantiser: row-wise and / or transposed 8-bit data + UE8M0 scales");
   m.def("mx_gemm", &rx::mx_gemm, "tcgen05 block-scaled MXFP8 GEMM (kind::mxf8f6f4.block_scale)");
   m.def("mnr_tc_argmax", &rx::mnr_tc_argmax, "tcgen05 split-bf16 scores reduced to each row's hardest candidate");

@@ -6,6 +6,8 @@
 // (src/representax/models/components.py:238-258), last-valid-token pooling
 // (src/representax/models/qwen3_vl/model.py:87-93) and CLS pooling
 // (src/representax/models/sentence.py:47-132).
+#include <algorithm>
+
 #include "common.h"
 #include "sm100.cuh"
 
@@ -27,59 +29,37 @@ __device__ __forceinline__ float block_sum(float v, float* scratch) {
   return total;
 }
 
-// The pooled rows are processed in slices of kSliceRows consecutive packed
-// rows (a slice may span sequences), one CTA per slice, 16-byte accesses:
-// the thread for column chunk c (8 columns) of row group g walks rows
-// g, g + G, ... of the slice. Sequence boundaries come from a binary search of
-// cu_seqlens held in shared memory.
-constexpr int kSliceRows = 32;
-constexpr int kMaxBatch = 4096;  // cu_seqlens entries a slice kernel can hold
-
-__device__ __forceinline__ int seq_of(const int* s_cu, int batch, int row) {
-  int lo = 0, hi = batch;  // s_cu[lo] <= row < s_cu[hi]
-  while (hi - lo > 1) {
-    const int mid = (lo + hi) >> 1;
-    if (s_cu[mid] <= row) lo = mid; else hi = mid;
-  }
-  return lo;
+// Every sequence is cut into `splits` contiguous row ranges, one CTA each
+// (grid splits x batch): no searches and no atomics. Thread (g, c) owns the
+// 16-byte column chunk c (8 columns) of rows g, g + G, ... of its range with
+// four loads in flight; the G row groups meet in shared memory.
+__device__ __forceinline__ void row_range(const int* cu, int b, int s, int splits, int& r0, int& r1, int& len) {
+  const int start = cu[b], end = cu[b + 1];
+  len = end - start;
+  r0 = start + static_cast<int>(static_cast<int64_t>(len) * s / splits);
+  r1 = start + static_cast<int>(static_cast<int64_t>(len) * (s + 1) / splits);
 }
 
-__device__ __forceinline__ void load_cu(const int* cu, int batch, int* s_cu) {
-  for (int i = threadIdx.x; i <= batch; i += blockDim.x) s_cu[i] = cu[i];
-  __syncthreads();
-}
-
-// MEAN, phase 1: acc[b] += sum of the slice's rows of sequence b (fp32
-// atomics, one per column per sequence run per thread). Rows are loaded four
-// at a time before they are accumulated, so each thread keeps four 16-byte
-// loads in flight.
-__device__ __forceinline__ void sum_rows(const __nv_bfloat16* __restrict__ h, const int* s_cu, int batch,
-                                         float* __restrict__ acc, int H, int c, int first, int end, int step) {
+// MEAN, phase 1: part[b, s, :] = sum of the rows of range s of sequence b.
+__global__ void __launch_bounds__(1024)
+    pool_partial_kernel(const __nv_bfloat16* __restrict__ h, const int* __restrict__ cu, float* __restrict__ part,
+                        int H, int splits) {
+  extern __shared__ float red[];  // [G][H]
+  const int s = blockIdx.x, b = blockIdx.y;
+  int r0, r1, len;
+  row_range(cu, b, s, splits, r0, r1, len);
+  const int chunks = H >> 3, G = blockDim.x / chunks;
+  const int c = threadIdx.x % chunks, g = threadIdx.x / chunks;  // g == G: padding threads of the last warp
   float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  int run = -1;
-  for (int r = first; r < end; r += 4 * step) {
+  for (int r = g < G ? r0 + g : r1; r < r1; r += 4 * G) {
     uint4 w[4];
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
-      const int rr = r + u * step;
-      w[u] = rr < end ? reinterpret_cast<const uint4*>(h + static_cast<int64_t>(rr) * H)[c] : make_uint4(0u, 0u, 0u, 0u);
+      const int rr = r + u * G;
+      w[u] = rr < r1 ? reinterpret_cast<const uint4*>(h + static_cast<int64_t>(rr) * H)[c] : make_uint4(0u, 0u, 0u, 0u);
     }
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
-      const int rr = r + u * step;
-      if (rr >= end) break;
-      const int b = seq_of(s_cu, batch, rr);
-      if (b != run) {
-        if (run >= 0) {
-          float* dst = acc + static_cast<int64_t>(run) * H + c * 8;
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            atomicAdd(dst + j, a[j]);
-            a[j] = 0.f;
-          }
-        }
-        run = b;
-      }
       const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&w[u]);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -89,36 +69,32 @@ __device__ __forceinline__ void sum_rows(const __nv_bfloat16* __restrict__ h, co
       }
     }
   }
-  if (run >= 0) {
-    float* dst = acc + static_cast<int64_t>(run) * H + c * 8;
+  float* dst = part + (static_cast<int64_t>(b) * splits + s) * H;
+  if (G == 1) {
+    if (g > 0) return;
+    reinterpret_cast<float4*>(dst)[2 * c] = make_float4(a[0], a[1], a[2], a[3]);
+    reinterpret_cast<float4*>(dst)[2 * c + 1] = make_float4(a[4], a[5], a[6], a[7]);
+    return;
+  }
+  if (g < G) {
 #pragma unroll
-    for (int j = 0; j < 8; ++j) atomicAdd(dst + j, a[j]);
+    for (int j = 0; j < 8; ++j) red[g * H + c * 8 + j] = a[j];
+  }
+  __syncthreads();
+  for (int col = threadIdx.x; col < H; col += blockDim.x) {
+    float t = 0.f;
+    for (int q = 0; q < G; ++q) t += red[q * H + col];
+    dst[col] = t;
   }
 }
 
-__global__ void __launch_bounds__(kThreads)
-    pool_sum_kernel(const __nv_bfloat16* __restrict__ h, const int* __restrict__ cu, int batch, int total,
-                    float* __restrict__ acc, int H) {
-  extern __shared__ int s_cu[];
-  load_cu(cu, batch, s_cu);
-  const int chunks = H >> 3;
-  const int r0 = blockIdx.x * kSliceRows, r1 = min(total, r0 + kSliceRows);
-  if (chunks <= kThreads) {  // `groups` row groups of one thread per column chunk
-    const int groups = kThreads / chunks;
-    const int g = threadIdx.x / chunks;
-    if (g < groups) sum_rows(h, s_cu, batch, acc, H, threadIdx.x % chunks, r0 + g, r1, groups);
-  } else {
-    for (int c = threadIdx.x; c < chunks; c += kThreads) sum_rows(h, s_cu, batch, acc, H, c, r0, r1, 1);
-  }
-}
-
-// Phase 2 (every mode): one CTA per sequence. MEAN divides the accumulated
-// sum by the length; FIRST / LAST read their one row from h. Then the L2
-// norm and the optional normalisation; out and norm are written.
+// Phase 2 (every mode): one CTA per sequence. MEAN adds the partial sums in
+// order and divides by the length; FIRST / LAST read their one row from h.
+// Then the L2 norm and the optional normalisation; out and norm are written.
 template <int MODE>
 __global__ void __launch_bounds__(kThreads)
-    pool_finish_kernel(const __nv_bfloat16* __restrict__ h, const int* __restrict__ cu,
-                       float* __restrict__ out, float* __restrict__ norm, int H, bool normalize) {
+    pool_finish_kernel(const __nv_bfloat16* __restrict__ h, const int* __restrict__ cu, const float* __restrict__ part,
+                       int splits, float* __restrict__ out, float* __restrict__ norm, int H, bool normalize) {
   __shared__ float scratch[32];
   const int b = blockIdx.x;
   const int s = cu[b], e = cu[b + 1];
@@ -128,11 +104,13 @@ __global__ void __launch_bounds__(kThreads)
   const float inv_len = 1.f / fmaxf(static_cast<float>(len), 1.f);
   float sq = 0.f;
   for (int c = threadIdx.x; c < H; c += kThreads) {
-    float v;
+    float v = 0.f;
     if (MODE == MEAN) {
-      v = row[c] * inv_len;
-    } else {
-      v = len > 0 ? __bfloat162float(h[static_cast<int64_t>(row_src) * H + c]) : 0.f;
+      const float* pp = part + static_cast<int64_t>(b) * splits * H + c;
+      for (int q = 0; q < splits; ++q) v += pp[static_cast<int64_t>(q) * H];
+      v *= inv_len;
+    } else if (len > 0) {
+      v = __bfloat162float(h[static_cast<int64_t>(row_src) * H + c]);
     }
     row[c] = v;
     sq += v * v;
@@ -145,62 +123,56 @@ __global__ void __launch_bounds__(kThreads)
   if (threadIdx.x == 0) norm[b] = n;
 }
 
-// Backward, phase 1: g[b] = (dout - out <out, dout>) / max(norm, eps) when
-// normalised, times 1 / len for MEAN (the weight of every pooled token).
+// Backward, one launch: CTA (s, b) recomputes its sequence's pooled gradient
+// g = (dout - out <out, dout>) / max(norm, eps) (when normalised) times
+// 1 / len for MEAN, then writes g (MEAN) or g / 0 (FIRST / LAST: only the
+// pooled row is non-zero) as bf16 into every row of its range.
 template <int MODE>
-__global__ void __launch_bounds__(kThreads)
-    pool_grad_kernel(const float* __restrict__ dout, const float* __restrict__ out,
-                     const float* __restrict__ norm, const int* __restrict__ cu, float* __restrict__ g,
-                     int H, bool normalize) {
+__global__ void __launch_bounds__(1024)
+    pool_backward_kernel(const float* __restrict__ dout, const float* __restrict__ out,
+                         const float* __restrict__ norm, const int* __restrict__ cu, __nv_bfloat16* __restrict__ dh,
+                         int H, int splits, bool normalize) {
   __shared__ float scratch[32];
-  const int b = blockIdx.x;
-  const int len = cu[b + 1] - cu[b];
-  const float* d = dout + static_cast<int64_t>(b) * H;
-  const float* o = out + static_cast<int64_t>(b) * H;
+  const int s = blockIdx.x, b = blockIdx.y;
+  int r0, r1, len;
+  row_range(cu, b, s, splits, r0, r1, len);
+  const int chunks = H >> 3, G = blockDim.x / chunks;
+  const int c = threadIdx.x % chunks, g = threadIdx.x / chunks;
+  const float* d = dout + static_cast<int64_t>(b) * H + c * 8;
+  const float* o = out + static_cast<int64_t>(b) * H + c * 8;
+  float dv[8], ov[8];
+  const float4 d0 = reinterpret_cast<const float4*>(d)[0], d1 = reinterpret_cast<const float4*>(d)[1];
+  const float4 o0 = reinterpret_cast<const float4*>(o)[0], o1 = reinterpret_cast<const float4*>(o)[1];
+  dv[0] = d0.x; dv[1] = d0.y; dv[2] = d0.z; dv[3] = d0.w; dv[4] = d1.x; dv[5] = d1.y; dv[6] = d1.z; dv[7] = d1.w;
+  ov[0] = o0.x; ov[1] = o0.y; ov[2] = o0.z; ov[3] = o0.w; ov[4] = o1.x; ov[5] = o1.y; ov[6] = o1.z; ov[7] = o1.w;
   float dot = 0.f;
-  if (normalize)
-    for (int c = threadIdx.x; c < H; c += kThreads) dot += d[c] * o[c];
-  dot = normalize ? block_sum(dot, scratch) : 0.f;
+  if (normalize) {
+    if (g == 0) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) dot += dv[j] * ov[j];
+    }
+    dot = block_sum(dot, scratch);
+  }
   const float inv = normalize ? 1.f / fmaxf(norm[b], 1e-12f) : 1.f;
   const float w = MODE == MEAN ? 1.f / fmaxf(static_cast<float>(len), 1.f) : 1.f;
-  for (int c = threadIdx.x; c < H; c += kThreads) g[static_cast<int64_t>(b) * H + c] = (d[c] - o[c] * dot) * inv * w;
-}
-
-// Backward, phase 2: every row of a slice gets g[its sequence] (MEAN) or
-// g / 0 (FIRST / LAST: only the pooled row is non-zero), as bf16.
-template <int MODE>
-__global__ void __launch_bounds__(kThreads)
-    pool_rows_kernel(const float* __restrict__ g, const int* __restrict__ cu, int batch, int total,
-                     __nv_bfloat16* __restrict__ dh, int H) {
-  extern __shared__ int s_cu[];
-  load_cu(cu, batch, s_cu);
-  const int chunks = H >> 3;
-  const int r0 = blockIdx.x * kSliceRows, r1 = min(total, r0 + kSliceRows);
-  const int items = (r1 - r0) * chunks;
-  for (int i = threadIdx.x; i < items; i += kThreads) {
-    const int r = r0 + i / chunks, c = i % chunks;
-    const int b = seq_of(s_cu, batch, r);
-    bool take = true;
-    if (MODE == FIRST) take = r == s_cu[b];
-    if (MODE == LAST) take = r == s_cu[b + 1] - 1;
-    uint4 w = make_uint4(0u, 0u, 0u, 0u);
-    if (take) {
-      const float4* src = reinterpret_cast<const float4*>(g + static_cast<int64_t>(b) * H + c * 8);
-      const float4 lo = src[0], hi = src[1];
-      __nv_bfloat162 q[4] = {__floats2bfloat162_rn(lo.x, lo.y), __floats2bfloat162_rn(lo.z, lo.w),
-                             __floats2bfloat162_rn(hi.x, hi.y), __floats2bfloat162_rn(hi.z, hi.w)};
-      w = *reinterpret_cast<uint4*>(q);
-    }
-    reinterpret_cast<uint4*>(dh + static_cast<int64_t>(r) * H)[c] = w;
+  uint4 val;
+  __nv_bfloat162* v2 = reinterpret_cast<__nv_bfloat162*>(&val);
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    v2[j] = __floats2bfloat162_rn((dv[2 * j] - ov[2 * j] * dot) * inv * w, (dv[2 * j + 1] - ov[2 * j + 1] * dot) * inv * w);
+  const int pooled = MODE == FIRST ? cu[b] : cu[b + 1] - 1;
+  const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
+  for (int r = g < G ? r0 + g : r1; r < r1; r += G) {
+    const bool take = MODE == MEAN || r == pooled;
+    reinterpret_cast<uint4*>(dh + static_cast<int64_t>(r) * H)[c] = take ? val : zero;
   }
 }
 
 // out[col] += sum_rows x[row, col]  (bf16 input, fp32 accumulator).
 // One CTA per slice of `slice` rows; thread (g, c) owns the 16-byte
-// column chunk c (8 columns) for rows g, g + G, ... of the slice (G row groups
-// when the row has at most 256 chunks, else one group of `chunks` threads),
-// keeping four loads in flight; row groups meet in shared memory and each
-// column gets one atomic per CTA.
+// column chunk c (8 columns) for rows g, g + G, ... of the slice (G row
+// groups of `chunks` threads), keeping four loads in flight; row groups meet
+// in shared memory and each column gets one atomic per CTA.
 __global__ void __launch_bounds__(1024)
     colsum_kernel(const __nv_bfloat16* __restrict__ x, int64_t ld, int rows, int cols, int slice,
                   float* __restrict__ out) {
@@ -267,36 +239,52 @@ __global__ void cast_bf16_kernel(const float* __restrict__ src, __nv_bfloat16* _
 
 }  // namespace pool
 
+// Row groups per CTA of the pooling kernels: up to 512 threads of 8-column chunks.
+static int pool_groups(int64_t H) { return std::max<int64_t>(1, 512 / (H / 8)); }
+// Row ranges per sequence: enough CTAs for about four per SM.
+static int pool_splits(int batch, int device) {
+  return std::max(1, std::min(16, (4 * num_sms(device) + batch - 1) / batch));
+}
+
 void pool_forward(const at::Tensor& h, const at::Tensor& cu_seqlens, at::Tensor& out,
                   at::Tensor& norm, int64_t mode, bool normalize) {
   check_bf16(h, "h");
   check_f32(out, "out");
   const int64_t H = h.size(1);
-  RX_CHECK(H % 8 == 0 && H <= 4096, "pool width must be a multiple of 8 and <= 4096");
+  RX_CHECK(H % 8 == 0 && H <= 8192, "pool width must be a multiple of 8 and <= 8192");
   RX_CHECK(h.is_contiguous() && out.is_contiguous(), "pool tensors must be contiguous");
   RX_CHECK(reinterpret_cast<uintptr_t>(h.data_ptr()) % 16 == 0, "h must be 16-byte aligned");
   const int batch = static_cast<int>(cu_seqlens.numel() - 1);
   if (batch <= 0) return;
-  RX_CHECK(batch <= pool::kMaxBatch, "at most ", pool::kMaxBatch, " sequences per pooling call");
-  c10::cuda::CUDAGuard guard(h.get_device());
+  const int device = h.get_device();
+  c10::cuda::CUDAGuard guard(device);
   auto st = at::cuda::getCurrentCUDAStream().stream();
   auto* hp = reinterpret_cast<const __nv_bfloat16*>(h.data_ptr());
   const int* cu = cu_seqlens.data_ptr<int>();
-  const int total = static_cast<int>(h.size(0));
   float* o = out.data_ptr<float>();
   switch (mode) {
     case pool::MEAN: {
-      RX_CUDA_CHECK(cudaMemsetAsync(o, 0, sizeof(float) * batch * H, st));
-      if (total > 0) {
-        const int slices = (total + pool::kSliceRows - 1) / pool::kSliceRows;
-        pool::pool_sum_kernel<<<slices, pool::kThreads, sizeof(int) * (batch + 1), st>>>(hp, cu, batch, total, o,
-                                                                                         static_cast<int>(H));
-      }
-      pool::pool_finish_kernel<pool::MEAN><<<batch, pool::kThreads, 0, st>>>(hp, cu, o, norm.data_ptr<float>(), H, normalize);
+      const int splits = pool_splits(batch, device), G = pool_groups(H);
+      const int threads = (G * static_cast<int>(H / 8) + 31) / 32 * 32;
+      at::Tensor part = at::empty({batch, splits, H}, out.options());
+      const size_t smem = G > 1 ? sizeof(float) * G * H : 0;
+      if (smem > 48 * 1024)
+        RX_CUDA_CHECK(cudaFuncSetAttribute(pool::pool_partial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(smem)));
+      pool::pool_partial_kernel<<<dim3(splits, batch), threads, smem, st>>>(hp, cu, part.data_ptr<float>(),
+                                                                           static_cast<int>(H), splits);
+      pool::pool_finish_kernel<pool::MEAN><<<batch, pool::kThreads, 0, st>>>(
+          hp, cu, part.data_ptr<float>(), splits, o, norm.data_ptr<float>(), H, normalize);
       break;
     }
-    case pool::FIRST: pool::pool_finish_kernel<pool::FIRST><<<batch, pool::kThreads, 0, st>>>(hp, cu, o, norm.data_ptr<float>(), H, normalize); break;
-    case pool::LAST: pool::pool_finish_kernel<pool::LAST><<<batch, pool::kThreads, 0, st>>>(hp, cu, o, norm.data_ptr<float>(), H, normalize); break;
+    case pool::FIRST:
+      pool::pool_finish_kernel<pool::FIRST><<<batch, pool::kThreads, 0, st>>>(hp, cu, nullptr, 0, o,
+                                                                              norm.data_ptr<float>(), H, normalize);
+      break;
+    case pool::LAST:
+      pool::pool_finish_kernel<pool::LAST><<<batch, pool::kThreads, 0, st>>>(hp, cu, nullptr, 0, o,
+                                                                             norm.data_ptr<float>(), H, normalize);
+      break;
     default: RX_CHECK(false, "unknown pooling mode");
   }
   RX_CUDA_CHECK(cudaGetLastError());
@@ -307,27 +295,26 @@ void pool_backward(const at::Tensor& dout, const at::Tensor& out, const at::Tens
   check_f32(dout, "dout");
   check_bf16(dh, "dh");
   const int64_t H = dh.size(1);
-  RX_CHECK(H % 8 == 0 && H <= 4096, "pool width must be a multiple of 8 and <= 4096");
+  RX_CHECK(H % 8 == 0 && H <= 8192, "pool width must be a multiple of 8 and <= 8192");
   RX_CHECK(dout.is_contiguous() && out.is_contiguous() && dh.is_contiguous(), "pool tensors must be contiguous");
-  RX_CHECK(reinterpret_cast<uintptr_t>(dh.data_ptr()) % 16 == 0, "dh must be 16-byte aligned");
+  RX_CHECK(reinterpret_cast<uintptr_t>(dh.data_ptr()) % 16 == 0 &&
+               reinterpret_cast<uintptr_t>(dout.data_ptr()) % 16 == 0 &&
+               reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0,
+           "pool tensors must be 16-byte aligned");
   const int batch = static_cast<int>(cu_seqlens.numel() - 1);
   if (batch <= 0) return;
-  RX_CHECK(batch <= pool::kMaxBatch, "at most ", pool::kMaxBatch, " sequences per pooling call");
-  c10::cuda::CUDAGuard guard(dh.get_device());
+  const int device = dh.get_device();
+  c10::cuda::CUDAGuard guard(device);
   auto st = at::cuda::getCurrentCUDAStream().stream();
   auto* dhp = reinterpret_cast<__nv_bfloat16*>(dh.data_ptr());
   const int* cu = cu_seqlens.data_ptr<int>();
-  const int total = static_cast<int>(dh.size(0));
-  at::Tensor g = at::empty({batch, H}, dout.options());
-  const int slices = (total + pool::kSliceRows - 1) / pool::kSliceRows;
-  const size_t smem = sizeof(int) * (batch + 1);
-#define RX_POOL_BWD(M)                                                                                           \
-  pool::pool_grad_kernel<M><<<batch, pool::kThreads, 0, st>>>(dout.data_ptr<float>(), out.data_ptr<float>(),   \
-                                                              norm.data_ptr<float>(), cu, g.data_ptr<float>(),  \
-                                                              static_cast<int>(H), normalize);                  \
-  if (total > 0)                                                                                                 \
-    pool::pool_rows_kernel<M><<<slices, pool::kThreads, smem, st>>>(g.data_ptr<float>(), cu, batch, total, dhp,  \
-                                                                    static_cast<int>(H))
+  const int splits = pool_splits(batch, device), G = pool_groups(H);
+  const dim3 grid(splits, batch);
+  const int threads = (G * static_cast<int>(H / 8) + 31) / 32 * 32;  // whole warps for block_sum
+#define RX_POOL_BWD(M)                                                                                            \
+  pool::pool_backward_kernel<M><<<grid, threads, 0, st>>>(dout.data_ptr<float>(), out.data_ptr<float>(),         \
+                                                          norm.data_ptr<float>(), cu, dhp, static_cast<int>(H), \
+                                                          splits, normalize)
   switch (mode) {
     case pool::MEAN: RX_POOL_BWD(pool::MEAN); break;
     case pool::FIRST: RX_POOL_BWD(pool::FIRST); break;
@@ -359,16 +346,14 @@ void colsum_accumulate(const at::Tensor& x, at::Tensor& out) {
   }
   c10::cuda::CUDAGuard guard(x.get_device());
   const int chunks = cols / 8;
-  // up to 256 threads of row groups for narrow rows, else one thread per chunk
-  const int threads = chunks <= 256 ? (256 / chunks) * chunks : (chunks + 31) / 32 * 32;
-  const int groups = threads / chunks;
+  // one CTA per SM of up to 1024 threads (row groups of one thread per chunk,
+  // each keeping four 16-byte loads in flight); the groups meet in shared
+  // memory, so every column takes one atomic per CTA
+  const int groups = std::max(1, 1024 / chunks);
+  const int threads = groups * chunks;
   const size_t smem = groups > 1 ? static_cast<size_t>(groups) * cols * sizeof(float) : 0;
-  // enough CTAs to fill every SM (up to 8 resident each) so that ~64 KB of
-  // loads are in flight per SM; each CTA sums a slice of at least 4 rows per group
-  int sms = 148;
-  RX_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, x.get_device()));
-  const int per_sm = std::max(1, std::min(8, 2048 / threads));
-  const int slice = std::max(4 * groups, (rows + sms * per_sm - 1) / (sms * per_sm));
+  const int sms = num_sms(x.get_device());
+  const int slice = std::max(4 * groups, (rows + sms - 1) / sms);
   const int grid = (rows + slice - 1) / slice;
   auto kern = pool::colsum_kernel;
   if (smem > 48 * 1024)

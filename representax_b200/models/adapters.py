@@ -98,13 +98,32 @@ class QuantizedLoRAWeight(nn.Module):
             return out
         return self.base_weight().to(torch.bfloat16)
 
+    # Expand the packed weight inside the GEMM's main loop instead of
+    # dequantising it to a bf16 temporary first. Off by default: on B200 the
+    # one-pass dequantisation (a few microseconds, one layer's weight at a
+    # time) plus the CTA-pair bf16 GEMM measured faster at every token count
+    # tried (128 to 16384 tokens, Qwen3-VL-2B projections), because every M
+    # tile re-expands its B tiles and that costs as much issue time as the MMAs.
+    mainloop_dequant: bool = False
+
+    def fused_int4(self) -> bool:
+        """Whether the tcgen05 GEMM can expand this packed weight in its main
+        loop: 16-byte packed rows (in_features % 32) and 16-byte output rows."""
+
+        p = self.packed_weight
+        return (p.is_cuda and p.dim() == 2 and self.input_size % 32 == 0 and self.output_size % 8 == 0
+                and p.stride(1) == 1 and p.stride(0) % 16 == 0 and p.data_ptr() % 16 == 0
+                and self.scale_bits.data_ptr() % 16 == 0)
+
     def linear_native(self, x: torch.Tensor, bias: torch.Tensor | None = None,
                       residual: torch.Tensor | None = None) -> torch.Tensor:
         """Packed-row bf16 path: ``x W_q^T + bias + residual + ((x A^T) * alpha / r) B^T``.
 
-        The LoRA product is added by the base GEMM's residual epilogue; the
-        base weight is dequantised by a kernel in the forward and again in the
-        backward (it is frozen, so only dx flows through it).
+        The LoRA product is added by the base GEMM's residual epilogue. The
+        frozen base weight (only dx flows through it) is dequantised by one
+        kernel per use into a bf16 temporary for the tcgen05 GEMM, or, with
+        ``mainloop_dequant``, expanded from its packed nibbles inside the
+        GEMM's main loop so that no bf16 copy reaches HBM.
         """
 
         from representax_b200.ops import nn as N
@@ -131,8 +150,17 @@ class _FrozenLinearFn(torch.autograd.Function):
         from representax_b200.ops import gemm as G
         from representax_b200.ops.functional import compute_view
 
-        w = owner.base_weight_bf16()
-        y = G.linear_forward(x.contiguous(), w, None if bias is None else compute_view(bias), residual=residual)
+        x = x.contiguous()
+        b = None if bias is None else compute_view(bias)
+        if owner.mainloop_dequant and owner.fused_int4():
+            # the packed weight is expanded inside the GEMM's main loop
+            from representax_b200.ops._ext import ext, status
+
+            y = torch.empty(x.shape[0], owner.output_size, dtype=torch.bfloat16, device=x.device)
+            ext().int4_gemm(x, owner.packed_weight, owner.scale_bits, owner.input_size, y, b,
+                            None if residual is None else residual.contiguous(), False, status(x.device))
+        else:
+            y = G.linear_forward(x, owner.base_weight_bf16(), b, residual=residual)
         ctx.owner = owner
         ctx.save_for_backward(bias if bias is not None else torch.empty(0, device=x.device))
         ctx.has_b = bias is not None
@@ -145,7 +173,17 @@ class _FrozenLinearFn(torch.autograd.Function):
 
         (bias,) = ctx.saved_tensors
         dy = dy.contiguous()
-        dx = G.linear_dgrad(dy, ctx.owner.base_weight_bf16()) if ctx.needs_input_grad[0] else None
+        dx = None
+        if ctx.needs_input_grad[0]:
+            owner = ctx.owner
+            if owner.mainloop_dequant and owner.fused_int4():
+                from representax_b200.ops._ext import ext, status
+
+                dx = torch.empty(dy.shape[0], owner.input_size, dtype=torch.bfloat16, device=dy.device)
+                ext().int4_gemm(dy, owner.packed_weight, owner.scale_bits, owner.input_size, dx, None, None, True,
+                                status(dy.device))
+            else:
+                dx = G.linear_dgrad(dy, owner.base_weight_bf16())
         sb = _GradSink(bias) if ctx.has_b else None
         if sb is not None:
             _colsum_into(dy, sb)

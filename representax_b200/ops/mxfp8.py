@@ -59,8 +59,10 @@ def quantize(x: torch.Tensor, fmt: int, *, rowwise: bool = True, transposed: boo
         qt = torch.empty(c, (r + 31) // 32 * 32, dtype=torch.uint8, device=dev)
         sft = torch.zeros(_scale_bytes(c, r), dtype=torch.uint8, device=dev)
     ext().mx_quantize(x, q, sf, qt, sft, fmt == E5M2)
+    # the transposed operand contracts over R rounded up to a whole block: the
+    # quantiser zero-fills the rows past R, so both sides of a product agree
     return (MXOperand(q, sf, fmt, c) if rowwise else None,
-            MXOperand(qt, sft, fmt, r) if transposed else None)
+            MXOperand(qt, sft, fmt, (r + 31) // 32 * 32) if transposed else None)
 
 
 def gemm(a: MXOperand, b: MXOperand, out: torch.Tensor, mode: int = OUT_BF16, bias=None, residual=None) -> None:

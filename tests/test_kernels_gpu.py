@@ -506,3 +506,30 @@ def test_native_mnr_loss_matches_reference(symmetric):
     assert abs(fwd.item() - rf.item()) < 1e-4
     _close(gq, q2.grad, rtol=1e-3, atol=1e-5, what="dq")
     _close(gd, d2.grad, rtol=1e-3, atol=1e-5, what="dd")
+
+
+@pytest.mark.parametrize("t,n,k", [(300, 384, 256), (1000, 2112, 960), (129, 256, 2048)])
+def test_int4_mainloop_gemm_forward_and_dgrad(C, t, n, k):
+    """Packed INT4 weight expanded inside the tcgen05 main loop == dequantised weight product."""
+
+    from representax_b200.models.adapters import QuantizedLoRAWeight
+
+    g = torch.Generator().manual_seed(t + n)
+    q = QuantizedLoRAWeight(torch.randn(n, k, generator=g) * 0.05, rank=4, alpha=8.0, seed=1).to(_dev())
+    assert q.fused_int4()
+    w = torch.empty(n, k, dtype=torch.bfloat16, device=_dev())
+    C.int4_dequantize(q.packed_weight, q.scale_bits, w)
+    x = _rand(t, k)
+    bias = _rand(n)
+    res = _rand(t, n)
+    st = torch.zeros(1, dtype=torch.int32, device=_dev())
+    y = torch.empty(t, n, dtype=torch.bfloat16, device=_dev())
+    C.int4_gemm(x, q.packed_weight, q.scale_bits, k, y, bias, res, False, st)
+    ref = x.double() @ w.double().T + bias.double() + res.double()
+    _close(y, ref, rtol=1e-2, atol=2e-2, what="int4 fwd")
+    dy = _rand(t, n)
+    dx = torch.empty(t, k, dtype=torch.bfloat16, device=_dev())
+    C.int4_gemm(dy, q.packed_weight, q.scale_bits, k, dx, None, None, True, st)
+    _close(dx, dy.double() @ w.double(), rtol=1e-2, atol=2e-2, what="int4 dgrad")
+    torch.cuda.synchronize()
+    assert int(st.item()) == 0

@@ -233,12 +233,15 @@ def test_fp8_policy_routes_modernvbert_linears():
     assert m.text.layers[0].Wqkv.grad is not None
 
 
-def test_int4_lora_linear_native_matches_reference():
+@pytest.mark.parametrize("mainloop", [False, True])
+def test_int4_lora_linear_native_matches_reference(mainloop):
     from representax_b200.models.adapters import QuantizedLoRAWeight, unpack_int4_rows
 
     g = torch.Generator().manual_seed(0)
     w = torch.randn(384, 256, generator=g) * 0.05
     q = QuantizedLoRAWeight(w, rank=16, alpha=32.0, seed=1).to(DEV)
+    q.mainloop_dequant = mainloop  # packed nibbles expanded inside the tcgen05 main loop
+    assert q.fused_int4()
     with torch.no_grad():
         q.lora_b.normal_(0, 0.02, generator=torch.Generator(device=DEV).manual_seed(2))
     base = q.base_weight_bf16()
