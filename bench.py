@@ -167,7 +167,7 @@ def _kernel_table(step, batch, it, path) -> None:
     with profile(activities=[ProfilerActivity.CUDA]) as prof:
         step(batch, it)
         torch.cuda.synchronize()
-    rows = {}
+    rows, examples = {}, {}
     for e in prof.events():
         if e.device_type.name != "CUDA":
             continue
@@ -176,8 +176,8 @@ def _kernel_table(step, batch, it, path) -> None:
                            ("attn_fwd", "attention_fwd"), ("attn_bwd", "attention_bwd"), ("attn_dvec", "attention_dvec"),
                            ("attn_dq_convert", "attention_dq_convert"), ("norm_fwd", "layernorm_fwd"),
                            ("norm_param_reduce", "layernorm_param_reduce"),
-                           ("norm_bwd", "layernorm_bwd"), ("embed_ln", "embed_layernorm"), ("pool", "pool"),
-                           ("colsum", "colsum"), ("mnr", "mnr"), ("sgemm", "mnr_sgemm"), ("adamw", "adamw"),
+                           ("norm_bwd", "layernorm_bwd"), ("embed_ln", "embed_layernorm"), ("pool_", "pool"),
+                           ("dropout_colsum", "dropout_colsum"), ("colsum", "colsum"), ("mnr", "mnr"), ("sgemm", "mnr_sgemm"), ("adamw", "adamw"),
                            ("grad_norm", "grad_norm"), ("cast_bf16", "cast_bf16")):
             if key in name:
                 name = short
@@ -186,12 +186,16 @@ def _kernel_table(step, batch, it, path) -> None:
             name = name[:60]
         t, n = rows.get(name, (0.0, 0))
         rows[name] = (t + e.device_time_total / 1e3, n + 1)
+        examples.setdefault(name, set()).add(e.name[:90])
     total = sum(t for t, _ in rows.values())
     with open(path, "w") as f:
         f.write("| kernel | launches | device ms | us per launch | share |\n|---|---|---|---|---|\n")
         for name, (t, n) in sorted(rows.items(), key=lambda kv: -kv[1][0]):
             f.write(f"| {name} | {n} | {t:.2f} | {1e3 * t / n:.1f} | {t / total:.1%} |\n")
         f.write(f"| total | {sum(n for _, n in rows.values())} | {total:.2f} | | 100% |\n")
+        f.write("\nKernels behind each label:\n\n")
+        for name in sorted(examples):
+            f.write(f"- {name}: " + "; ".join(sorted(examples[name])[:4]) + "\n")
 
 
 def main() -> None:

@@ -21,6 +21,8 @@
 // (src/representax/models/modernvbert/model.py:217-230) and GQA
 // (src/representax/models/qwen3_vl/text.py:188-199).
 #include "attention_kernels.cuh"
+#include <algorithm>
+
 #include "common.h"
 #include "sm100.cuh"
 
@@ -330,6 +332,43 @@ __global__ void attn_dvec_kernel(const __nv_bfloat16* __restrict__ o, int64_t ld
   if (lane == 0) dvec[static_cast<int64_t>(h) * total + tok] = s;
 }
 
+// Backward prep, one pass over the tokens: dvec[h, t] = sum_d dO[t, h, d] *
+// O[t, h, d], and the fp32 dQ accumulator row of (t, h) is zeroed. A group of
+// D / 8 threads owns one (t, h): each thread loads 16 bytes of O and of dO and
+// stores 8 zero floats; the group sums with shuffles.
+template <int D>
+__global__ void __launch_bounds__(256)
+    attn_bwd_prep_kernel(const __nv_bfloat16* __restrict__ o, int64_t ldo, const __nv_bfloat16* __restrict__ dO,
+                         int64_t ld_do, float* __restrict__ dvec, float* __restrict__ dq_acc, int total, int heads) {
+  constexpr int G = D / 8;  // threads per (token, head)
+  const int64_t gid = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x);
+  const int64_t item = gid / G;
+  const int c = static_cast<int>(gid % G);
+  const bool live = item < static_cast<int64_t>(total) * heads;
+  float s = 0.f;
+  int64_t tok = 0;
+  int h = 0;
+  if (live) {
+    tok = item / heads;
+    h = static_cast<int>(item % heads);
+    const uint4 a = reinterpret_cast<const uint4*>(o + tok * ldo + h * D)[c];
+    const uint4 d = reinterpret_cast<const uint4*>(dO + tok * ld_do + h * D)[c];
+    const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a);
+    const __nv_bfloat162* d2 = reinterpret_cast<const __nv_bfloat162*>(&d);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 fa = __bfloat1622float2(a2[j]), fd = __bfloat1622float2(d2[j]);
+      s += fa.x * fd.x + fa.y * fd.y;
+    }
+    float4* z = reinterpret_cast<float4*>(dq_acc + tok * (static_cast<int64_t>(heads) * D) + h * D + c * 8);
+    z[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+    z[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+#pragma unroll
+  for (int off = G / 2; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  if (live && c == 0) dvec[static_cast<int64_t>(h) * total + tok] = s;
+}
+
 // dq[t, h*D + d] = bf16(dq_acc[t, h*D + d])
 __global__ void attn_dq_convert_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ dq,
                                        int64_t ld_dq, int total, int width) {
@@ -341,6 +380,71 @@ __global__ void attn_dq_convert_kernel(const float* __restrict__ acc, __nv_bfloa
   w.x = pack_bf16(v.x, v.y);
   w.y = pack_bf16(v.z, v.w);
   *reinterpret_cast<uint2*>(dq + tok * ld_dq + col) = w;
+}
+
+// dq = bf16(dq_acc) with the column sums of the rounded values added into
+// `colsum` (the query part of a fused QKV bias gradient). One CTA per slice
+// of rows; thread (g, c) owns 4 columns of rows g, g + G, ... with eight
+// 16-byte loads in flight; row groups meet in shared memory, so each column
+// takes one atomic per CTA.
+__global__ void __launch_bounds__(1024)
+    attn_dq_convert_colsum_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ dq, int64_t ld_dq,
+                                  int total, int width, int slice, float* __restrict__ colsum) {
+  extern __shared__ float part[];  // [groups][width]
+  const int chunks = width >> 2;
+  const int groups = blockDim.x / chunks;
+  const int c = threadIdx.x % chunks, g = threadIdx.x / chunks;
+  const int r0 = blockIdx.x * slice, r1 = min(total, r0 + slice);
+  float s[4] = {0.f, 0.f, 0.f, 0.f};
+  if (g < groups) {
+    for (int r = r0 + g; r < r1; r += 8 * groups) {
+      // unconditional loads (rows past the slice re-read its last row; they
+      // are neither stored nor summed) so that all eight are in flight at once
+      uint4 w[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int rr = min(r + u * groups, r1 - 1);
+        w[u] = ldg_v4_issue(reinterpret_cast<const float4*>(acc + static_cast<int64_t>(rr) * width) + c);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) hold_v4(w[u]);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int rr = r + u * groups;
+        if (rr < r1) {
+          const __nv_bfloat162 lo = __floats2bfloat162_rn(__uint_as_float(w[u].x), __uint_as_float(w[u].y));
+          const __nv_bfloat162 hi = __floats2bfloat162_rn(__uint_as_float(w[u].z), __uint_as_float(w[u].w));
+          uint2 o;
+          o.x = *reinterpret_cast<const uint32_t*>(&lo);
+          o.y = *reinterpret_cast<const uint32_t*>(&hi);
+          *reinterpret_cast<uint2*>(dq + static_cast<int64_t>(rr) * ld_dq + c * 4) = o;
+          const float2 a = __bfloat1622float2(lo), b = __bfloat1622float2(hi);
+          s[0] += a.x;
+          s[1] += a.y;
+          s[2] += b.x;
+          s[3] += b.y;
+        }
+      }
+    }
+  }
+  if (colsum == nullptr) return;
+  if (groups == 1) {
+    if (g == 0) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) atomicAdd(colsum + c * 4 + j, s[j]);
+    }
+    return;
+  }
+  if (g < groups) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) part[g * width + c * 4 + j] = s[j];
+  }
+  __syncthreads();
+  for (int col = threadIdx.x; col < width; col += blockDim.x) {
+    float t = 0.f;
+    for (int q = 0; q < groups; ++q) t += part[q * width + col];
+    atomicAdd(colsum + col, t);
+  }
 }
 
 // ==================================================================== backward
@@ -613,6 +717,9 @@ template __global__ void attn_bwd_kernel<128, true>(const Params p);
 bool tc_attention_enabled();
 void tc_forward(Params p, int d, int64_t max_len, cudaStream_t st, int device);
 void tc_backward(Params p, int d, int64_t max_len, cudaStream_t st, int device);
+int* tc_status_word(int device);
+bool ws_backward_enabled();
+void tc_backward_ws(Params p, int64_t max_len, cudaStream_t st, int device, int* status);
 
 }  // namespace attn
 
@@ -713,13 +820,20 @@ void attention_forward(const at::Tensor& q, const at::Tensor& k, const at::Tenso
   RX_CUDA_CHECK(cudaGetLastError());
 }
 
-void attention_backward(const at::Tensor& dO, const at::Tensor& q, const at::Tensor& k,
-                        const at::Tensor& v, const at::Tensor& o, const at::Tensor& lse,
-                        at::Tensor& dq, at::Tensor& dk, at::Tensor& dv, at::Tensor& dq_acc,
-                        at::Tensor& dvec, const at::Tensor& cu_seqlens, int64_t max_len,
-                        int64_t heads, int64_t kv_heads, double scale, bool causal,
-                        int64_t window, int64_t drop_seed, int64_t drop_stream, double drop_p,
-                        const c10::optional<at::Tensor>& rel_lut, const c10::optional<at::Tensor>& drel) {
+void colsum_accumulate(const at::Tensor& x, at::Tensor& out);
+
+// `dbias_qkv` (optional fp32 [heads * D + 2 * kv_heads * D]): the column sums
+// of dq | dk | dv are added into it (a fused QKV projection's bias gradient),
+// inside the dQ conversion and the warp-specialised backward's dK / dV
+// epilogue when that kernel runs, else by column-sum passes over dk and dv.
+void attention_backward_bias(const at::Tensor& dO, const at::Tensor& q, const at::Tensor& k,
+                             const at::Tensor& v, const at::Tensor& o, const at::Tensor& lse,
+                             at::Tensor& dq, at::Tensor& dk, at::Tensor& dv, at::Tensor& dq_acc,
+                             at::Tensor& dvec, const at::Tensor& cu_seqlens, int64_t max_len,
+                             int64_t heads, int64_t kv_heads, double scale, bool causal,
+                             int64_t window, int64_t drop_seed, int64_t drop_stream, double drop_p,
+                             const c10::optional<at::Tensor>& rel_lut, const c10::optional<at::Tensor>& drel,
+                             const c10::optional<at::Tensor>& dbias_qkv) {
   attn::Params p{};
   fill_common(p, q, k, v, cu_seqlens, heads, kv_heads, scale, causal, window);
   p.pdrop = make_dropout_site(drop_seed, drop_stream, drop_p);
@@ -738,24 +852,42 @@ void attention_backward(const at::Tensor& dO, const at::Tensor& q, const at::Ten
   p.dv = reinterpret_cast<__nv_bfloat16*>(dv.data_ptr());
   p.ld_dk = dk.stride(0);
   p.ld_dv = dv.stride(0);
+  if (dbias_qkv.has_value()) {
+    check_f32(*dbias_qkv, "dbias_qkv");
+    RX_CHECK(dbias_qkv->is_contiguous() && dbias_qkv->numel() == (heads + 2 * kv_heads) * d,
+             "dbias_qkv must be a contiguous fp32 [(heads + 2 kv_heads) * head_dim]");
+    p.dbias_qkv = dbias_qkv->data_ptr<float>();
+  }
   const int total = p.total_tokens;
   if (p.batch == 0 || max_len == 0 || total == 0) return;
   c10::cuda::CUDAGuard guard(q.get_device());
   auto st = at::cuda::getCurrentCUDAStream().stream();
-  RX_CUDA_CHECK(cudaMemsetAsync(dq_acc.data_ptr(), 0, dq_acc.numel() * sizeof(float), st));
   {
-    const int64_t warps = static_cast<int64_t>(total) * heads;
+    RX_CHECK(aligned_rows(o) && aligned_rows(dO), "attention backward: O and dO rows must be 16-byte aligned");
+    const int64_t threads_needed = static_cast<int64_t>(total) * heads * (d / 8);
     const int threads = 256;
-    attn::attn_dvec_kernel<<<(warps * 32 + threads - 1) / threads, threads, 0, st>>>(
-        reinterpret_cast<const __nv_bfloat16*>(o.data_ptr()), o.stride(0), p.dO, p.ld_do,
-        dvec.data_ptr<float>(), total, static_cast<int>(heads), d);
+    const int64_t blocks = (threads_needed + threads - 1) / threads;
+    auto* op = reinterpret_cast<const __nv_bfloat16*>(o.data_ptr());
+    if (d == 64)
+      attn::attn_bwd_prep_kernel<64><<<blocks, threads, 0, st>>>(op, o.stride(0), p.dO, p.ld_do, dvec.data_ptr<float>(),
+                                                                 p.dq_acc, total, static_cast<int>(heads));
+    else
+      attn::attn_bwd_prep_kernel<128><<<blocks, threads, 0, st>>>(op, o.stride(0), p.dO, p.ld_do,
+                                                                  dvec.data_ptr<float>(), p.dq_acc, total,
+                                                                  static_cast<int>(heads));
     RX_CUDA_CHECK(cudaGetLastError());
   }
   dim3 grid((max_len + attn::BN - 1) / attn::BN, kv_heads, p.batch);
   const bool gqa = kv_heads != heads;
+  bool bias_kv_done = false;  // dK / dV column sums taken by the kernel's epilogue
   if (attn::tc_attention_enabled() && aligned_rows(dO) &&
       aligned_rows(dk) && aligned_rows(dv)) {
-    attn::tc_backward(p, d, max_len, st, q.get_device());
+    if (d == 64 && p.rel_lut == nullptr && attn::ws_backward_enabled()) {
+      attn::tc_backward_ws(p, max_len, st, q.get_device(), attn::tc_status_word(q.get_device()));
+      bias_kv_done = true;
+    } else {
+      attn::tc_backward(p, d, max_len, st, q.get_device());
+    }
   } else if (d == 64) {
     if (gqa) attn::attn_bwd_kernel<64, true><<<grid, attn::kThreads, attn::bwd_smem_bytes<64>(), st>>>(p);
     else attn::attn_bwd_kernel<64, false><<<grid, attn::kThreads, attn::bwd_smem_bytes<64>(), st>>>(p);
@@ -769,11 +901,39 @@ void attention_backward(const at::Tensor& dO, const at::Tensor& q, const at::Ten
   RX_CUDA_CHECK(cudaGetLastError());
   {
     const int width = static_cast<int>(heads * d);
-    const int64_t n4 = static_cast<int64_t>(total) * width / 4;
-    attn::attn_dq_convert_kernel<<<(n4 + 255) / 256, 256, 0, st>>>(
-        p.dq_acc, reinterpret_cast<__nv_bfloat16*>(dq.data_ptr()), dq.stride(0), total, width);
+    RX_CHECK(aligned_rows(dq), "attention backward: dq rows must be 16-byte aligned");
+    const int chunks = width / 4;
+    RX_CHECK(chunks <= 1024, "attention backward: dq rows wider than 4096 columns");
+    const int groups = std::max(1, 1024 / chunks);
+    const int threads = groups * chunks;
+    const int sms = num_sms(q.get_device());
+    const int slice = std::max(8 * groups, (total + sms - 1) / sms);
+    const int grid = (total + slice - 1) / slice;
+    const size_t smem = groups > 1 ? static_cast<size_t>(groups) * width * sizeof(float) : 0;
+    auto kern = attn::attn_dq_convert_colsum_kernel;
+    if (smem > 48 * 1024)
+      RX_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+    kern<<<grid, threads, smem, st>>>(p.dq_acc, reinterpret_cast<__nv_bfloat16*>(dq.data_ptr()), dq.stride(0), total,
+                                      width, slice, p.dbias_qkv);
     RX_CUDA_CHECK(cudaGetLastError());
   }
+  if (p.dbias_qkv != nullptr && !bias_kv_done) {
+    const int64_t qd = heads * d, kd = kv_heads * d;
+    at::Tensor bk = dbias_qkv->narrow(0, qd, kd), bv = dbias_qkv->narrow(0, qd + kd, kd);
+    colsum_accumulate(dk, bk);
+    colsum_accumulate(dv, bv);
+  }
+}
+
+void attention_backward(const at::Tensor& dO, const at::Tensor& q, const at::Tensor& k,
+                        const at::Tensor& v, const at::Tensor& o, const at::Tensor& lse,
+                        at::Tensor& dq, at::Tensor& dk, at::Tensor& dv, at::Tensor& dq_acc,
+                        at::Tensor& dvec, const at::Tensor& cu_seqlens, int64_t max_len,
+                        int64_t heads, int64_t kv_heads, double scale, bool causal,
+                        int64_t window, int64_t drop_seed, int64_t drop_stream, double drop_p,
+                        const c10::optional<at::Tensor>& rel_lut, const c10::optional<at::Tensor>& drel) {
+  attention_backward_bias(dO, q, k, v, o, lse, dq, dk, dv, dq_acc, dvec, cu_seqlens, max_len, heads, kv_heads, scale,
+                          causal, window, drop_seed, drop_stream, drop_p, rel_lut, drel, c10::nullopt);
 }
 
 }  // namespace rx

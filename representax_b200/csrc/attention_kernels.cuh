@@ -55,6 +55,9 @@ struct Params {
   __nv_bfloat16* dk;
   __nv_bfloat16* dv;
   int64_t ld_dk, ld_dv;
+  // Optional fp32 [heads * D + 2 * kv_heads * D] accumulator of the column
+  // sums of (dQ | dK | dV): the gradient of a fused QKV projection's bias.
+  float* dbias_qkv;
   // Bounded waits of the tcgen05 kernels (attention_tc.cu): error word and budget.
   int* status;
   uint64_t timeout_ns;
@@ -79,6 +82,10 @@ __global__ void attn_dvec_kernel(const __nv_bfloat16* __restrict__ o, int64_t ld
                                  float* __restrict__ dvec, int total, int heads, int head_dim);
 __global__ void attn_dq_convert_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ dq,
                                        int64_t ld_dq, int total, int width);
+// dq = bf16(dq_acc) and, when colsum != nullptr, colsum[c] += sum_t dq[t, c].
+__global__ void attn_dq_convert_colsum_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ dq,
+                                              int64_t ld_dq, int total, int width, int slice,
+                                              float* __restrict__ colsum);
 
 }  // namespace attn
 }  // namespace rx

@@ -58,6 +58,14 @@ void attention_backward(const at::Tensor& dO, const at::Tensor& q, const at::Ten
                         int64_t heads, int64_t kv_heads, double scale, bool causal,
                         int64_t window, int64_t drop_seed, int64_t drop_stream, double drop_p,
                         const c10::optional<at::Tensor>& rel_lut, const c10::optional<at::Tensor>& drel);
+void attention_backward_bias(const at::Tensor& dO, const at::Tensor& q, const at::Tensor& k,
+                             const at::Tensor& v, const at::Tensor& o, const at::Tensor& lse,
+                             at::Tensor& dq, at::Tensor& dk, at::Tensor& dv, at::Tensor& dq_acc,
+                             at::Tensor& dvec, const at::Tensor& cu_seqlens, int64_t max_len,
+                             int64_t heads, int64_t kv_heads, double scale, bool causal,
+                             int64_t window, int64_t drop_seed, int64_t drop_stream, double drop_p,
+                             const c10::optional<at::Tensor>& rel_lut, const c10::optional<at::Tensor>& drel,
+                             const c10::optional<at::Tensor>& dbias_qkv);
 void pool_forward(const at::Tensor& h, const at::Tensor& cu_seqlens, at::Tensor& out,
                   at::Tensor& norm, int64_t mode, bool normalize);
 void pool_backward(const at::Tensor& dout, const at::Tensor& out, const at::Tensor& norm,
@@ -124,6 +132,8 @@ namespace attn {
 bool tc_attention_enabled();
 void set_tc_attention_enabled(bool on);
 void register_tc_status(int device, int* status);
+bool ws_backward_enabled();
+void set_ws_backward_enabled(bool on);
 }  // namespace attn
 }  // namespace rx
 
@@ -136,9 +146,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embed_ln_backward", &rx::embed_ln_backward);
   m.def("attention_forward", &rx::attention_forward);
   m.def("attention_backward", &rx::attention_backward);
+  m.def("attention_backward_bias", &rx::attention_backward_bias,
+        "attention backward that also adds the column sums of dq | dk | dv into a QKV bias gradient");
   m.def("set_attention_tcgen05", &rx::attn::set_tc_attention_enabled,
         "route eligible attention calls (no dropout, no relative bias) to the tcgen05 kernels");
   m.def("attention_tcgen05_enabled", &rx::attn::tc_attention_enabled);
+  m.def("set_attention_backward_ws", &rx::attn::set_ws_backward_enabled,
+        "use the warp-specialised persistent tcgen05 backward for head dim 64 (default on)");
+  m.def("attention_backward_ws_enabled", &rx::attn::ws_backward_enabled);
   m.def("register_status_word", [](const at::Tensor& status) {
     TORCH_CHECK(status.is_cuda() && status.scalar_type() == at::kInt, "status must be CUDA int32");
     rx::attn::register_tc_status(status.get_device(), status.data_ptr<int>());

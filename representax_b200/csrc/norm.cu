@@ -12,6 +12,8 @@
 // Reference parity: LayerNorm / RMSNorm with fp32 statistics
 // (src/representax/models/components.py:97-150) and BERT embeddings with
 // padding-row gradient suppression (src/representax/models/bert/model.py:74-146).
+#include <algorithm>
+
 #include "common.h"
 #include "sm100.cuh"
 
@@ -256,6 +258,127 @@ __global__ void __launch_bounds__(kWarps * 32, (MAXV <= 4 ? 3 : 1))
   }
 }
 
+// Backward of a plain (non-embedding) normalisation with the next row's
+// inputs prefetched: each warp keeps its current row's raw x / dy vectors and
+// the next row's loads in flight while it computes, so two rows per warp are
+// outstanding (the one-row loop above is latency-bound on these shapes).
+// Same arithmetic and the same per-warp shared-memory partial sums as
+// norm_bwd_kernel.
+template <int MAXV, bool RMS>
+__global__ void __launch_bounds__(kWarps * 32, (MAXV <= 2 ? 3 : MAXV <= 4 ? 2 : 1))
+    norm_bwd_prefetch_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
+                             const float* __restrict__ mean_in, const float* __restrict__ rstd_in,
+                             const __nv_bfloat16* __restrict__ gamma, __nv_bfloat16* __restrict__ dx,
+                             float* __restrict__ dgamma, float* __restrict__ dbeta,
+                             float* __restrict__ dbias_prev, int rows, int H) {
+  extern __shared__ float red[];  // [kWarps][3][H] partial sums
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int nv = H >> 3;
+  float* pg = red + static_cast<size_t>(warp) * 3 * H;
+  float* pb = pg + H;
+  float* pd = pb + H;
+  for (int i = lane; i < 3 * H; i += 32) pg[i] = 0.f;
+  __syncwarp();
+
+  const int stride = gridDim.x * kWarps;
+  uint4 xr[MAXV], dr[MAXV];
+  float mean = 0.f, rstd = 0.f;
+  auto load = [&](int row, uint4 (&xa)[MAXV], uint4 (&da)[MAXV], float& m, float& r) {
+    if (row >= rows) return;
+    m = RMS ? 0.f : mean_in[row];
+    r = rstd_in[row];
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const int c = lane + 32 * i;
+      if (c < nv) {
+        xa[i] = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(row) * H)[c];
+        da[i] = reinterpret_cast<const uint4*>(dy + static_cast<int64_t>(row) * H)[c];
+      }
+    }
+  };
+  int row = blockIdx.x * kWarps + warp;
+  load(row, xr, dr, mean, rstd);
+  for (; row < rows; row += stride) {
+    uint4 xn[MAXV], dn[MAXV];
+    float mean_n = 0.f, rstd_n = 0.f;
+    load(row + stride, xn, dn, mean_n, rstd_n);
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const int c = lane + 32 * i;
+      if (c < nv) {
+        float xv[8], d[8], g[8];
+        unpack8(xr[i], xv);
+        unpack8(dr[i], d);
+        unpack8(reinterpret_cast<const uint4*>(gamma)[c], g);
+        float4* gp = reinterpret_cast<float4*>(pg + c * 8);
+        float4* bp = reinterpret_cast<float4*>(pb + c * 8);
+        float4 g0 = gp[0], g1 = gp[1], b0 = bp[0], b1 = bp[1];
+        float xh[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          xh[j] = (xv[j] - mean) * rstd;
+          const float dyg = d[j] * g[j];
+          s1 += dyg;
+          s2 += dyg * xh[j];
+        }
+        g0.x += d[0] * xh[0]; g0.y += d[1] * xh[1]; g0.z += d[2] * xh[2]; g0.w += d[3] * xh[3];
+        g1.x += d[4] * xh[4]; g1.y += d[5] * xh[5]; g1.z += d[6] * xh[6]; g1.w += d[7] * xh[7];
+        b0.x += d[0]; b0.y += d[1]; b0.z += d[2]; b0.w += d[3];
+        b1.x += d[4]; b1.y += d[5]; b1.z += d[6]; b1.w += d[7];
+        gp[0] = g0; gp[1] = g1; bp[0] = b0; bp[1] = b1;
+      }
+    }
+    s1 = warp_sum(s1) / H;
+    s2 = warp_sum(s2) / H;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const int c = lane + 32 * i;
+      if (c < nv) {
+        float xv[8], d[8], g[8], o[8];
+        unpack8(xr[i], xv);
+        unpack8(dr[i], d);
+        unpack8(reinterpret_cast<const uint4*>(gamma)[c], g);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float xh = (xv[j] - mean) * rstd;
+          o[j] = rstd * (d[j] * g[j] - (RMS ? 0.f : s1) - xh * s2);
+        }
+        if (dbias_prev != nullptr) {
+          float4* dp = reinterpret_cast<float4*>(pd + c * 8);
+          float4 a0 = dp[0], a1 = dp[1];
+          a0.x += o[0]; a0.y += o[1]; a0.z += o[2]; a0.w += o[3];
+          a1.x += o[4]; a1.y += o[5]; a1.z += o[6]; a1.w += o[7];
+          dp[0] = a0; dp[1] = a1;
+        }
+        reinterpret_cast<uint4*>(dx + static_cast<int64_t>(row) * H)[c] = pack8(o);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      xr[i] = xn[i];
+      dr[i] = dn[i];
+    }
+    mean = mean_n;
+    rstd = rstd_n;
+  }
+  __syncthreads();
+  for (int col = threadIdx.x; col < H; col += blockDim.x) {
+    float a = 0.f, b = 0.f, d = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const float* base = red + static_cast<size_t>(w) * 3 * H;
+      a += base[col];
+      b += base[H + col];
+      d += base[2 * H + col];
+    }
+    if (dgamma) atomicAdd(dgamma + col, a);
+    if (dbeta && !RMS) atomicAdd(dbeta + col, b);
+    if (dbias_prev) atomicAdd(dbias_prev + col, d);
+  }
+}
+
 template <bool RMS>
 void launch_fwd(int maxv, dim3 grid, cudaStream_t st, const __nv_bfloat16* x, const int* ids,
                 const int* pos_ids, const int* type_ids, const __nv_bfloat16* word,
@@ -277,21 +400,33 @@ void launch_fwd(int maxv, dim3 grid, cudaStream_t st, const __nv_bfloat16* x, co
 }
 
 template <bool RMS>
-void launch_bwd(int maxv, int grid, size_t smem, cudaStream_t st, const __nv_bfloat16* dy,
+void launch_bwd(int maxv, int grid, int sms, size_t smem, cudaStream_t st, const __nv_bfloat16* dy,
                 const __nv_bfloat16* x, const float* mean, const float* rstd,
                 const __nv_bfloat16* gamma, __nv_bfloat16* dx, float* dgamma, float* dbeta,
                 float* dbias_prev, int rows, int H, const int* ids, const int* pos_ids,
                 const int* type_ids, const __nv_bfloat16* word, const __nv_bfloat16* pos,
                 const __nv_bfloat16* type, float* wg, float* pg, float* tg, int pad_id) {
-#define RX_NORM_BWD(V)                                                                          \
-  do {                                                                                          \
-    auto k = norm_bwd_kernel<V, RMS>;                                                           \
-    if (smem > 48 * 1024)                                                                       \
-      RX_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,       \
-                                         static_cast<int>(smem)));                              \
-    k<<<grid, kWarps * 32, smem, st>>>(dy, x, mean, rstd, gamma, dx, dgamma, dbeta, dbias_prev, \
-                                       rows, H, ids, pos_ids, type_ids, word, pos, type, wg, pg, \
-                                       tg, pad_id);                                             \
+#define RX_NORM_BWD(V)                                                                            \
+  do {                                                                                            \
+    if (word == nullptr) {                                                                        \
+      auto k = norm_bwd_prefetch_kernel<V, RMS>;                                                  \
+      if (smem > 48 * 1024)                                                                       \
+        RX_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,       \
+                                           static_cast<int>(smem)));                              \
+      int per_sm = 1; /* one wave of resident CTAs: each warp strides over rows */                \
+      RX_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kWarps * 32, smem));  \
+      const int g = std::max(1, std::min(grid, std::max(1, per_sm) * sms));                       \
+      k<<<g, kWarps * 32, smem, st>>>(dy, x, mean, rstd, gamma, dx, dgamma, dbeta, dbias_prev,    \
+                                      rows, H);                                                   \
+    } else {                                                                                      \
+      auto k = norm_bwd_kernel<V, RMS>;                                                           \
+      if (smem > 48 * 1024)                                                                       \
+        RX_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,       \
+                                           static_cast<int>(smem)));                              \
+      k<<<grid, kWarps * 32, smem, st>>>(dy, x, mean, rstd, gamma, dx, dgamma, dbeta, dbias_prev, \
+                                         rows, H, ids, pos_ids, type_ids, word, pos, type, wg, pg, \
+                                         tg, pad_id);                                             \
+    }                                                                                             \
   } while (0)
   if (maxv <= 1) RX_NORM_BWD(1);
   else if (maxv <= 2) RX_NORM_BWD(2);
@@ -362,7 +497,7 @@ void norm_backward(const at::Tensor& dy, const at::Tensor& x, const c10::optiona
   const size_t smem = 3 * norm::kWarps * H * sizeof(float);
   auto st = at::cuda::getCurrentCUDAStream().stream();
   auto launch = rms ? norm::launch_bwd<true> : norm::launch_bwd<false>;
-  launch(maxv_for(H), grid, smem, st, reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()),
+  launch(maxv_for(H), grid, sms, smem, st, reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()),
          reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), opt_ptr<float>(mean),
          rstd.data_ptr<float>(), reinterpret_cast<const __nv_bfloat16*>(gamma.data_ptr()),
          reinterpret_cast<__nv_bfloat16*>(dx.data_ptr()), opt_mut<float>(dgamma),
@@ -414,7 +549,7 @@ void embed_ln_backward(const at::Tensor& dy, const at::Tensor& ids, const at::Te
   const int grid = static_cast<int>(std::min<int64_t>((rows + norm::kWarps - 1) / norm::kWarps, 3 * sms));
   const size_t smem = 3 * norm::kWarps * H * sizeof(float);
   norm::launch_bwd<false>(
-      maxv_for(H), grid, smem, at::cuda::getCurrentCUDAStream().stream(),
+      maxv_for(H), grid, sms, smem, at::cuda::getCurrentCUDAStream().stream(),
       reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()), nullptr, mean.data_ptr<float>(),
       rstd.data_ptr<float>(), reinterpret_cast<const __nv_bfloat16*>(gamma.data_ptr()), nullptr,
       dgamma.data_ptr<float>(), dbeta.data_ptr<float>(), nullptr, static_cast<int>(rows),

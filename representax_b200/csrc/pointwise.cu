@@ -289,35 +289,70 @@ __global__ void dropout_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
 // Dropout of a [rows, cols] matrix that also adds the column sums of the
 // result into colsum (fp32 [cols]): a block owns 256 columns (4 per thread)
 // and a range of rows, and adds its partial sums with one atomic per column.
-__global__ void dropout_colsum_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, __nv_bfloat16* y,
-                                      int64_t ldy, int64_t rows, int64_t cols, DropoutSite site,
-                                      float* __restrict__ colsum, int64_t rows_per_block) {
-  const int64_t q = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;  // quad of columns
-  if (q * 4 >= cols) return;
-  const int64_t r0 = static_cast<int64_t>(blockIdx.y) * rows_per_block;
+// y = dropout(x) with the column sums of the (rounded) result added into
+// `colsum` (a bias gradient). One CTA per slice of rows: thread (g, q) owns
+// column quad q of rows g, g + G, ... of the slice, with eight rows' loads in
+// flight; the G row groups meet in shared memory, so each column takes one
+// atomic per CTA.
+__global__ void __launch_bounds__(512)
+    dropout_colsum_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, __nv_bfloat16* y, int64_t ldy,
+                          int64_t rows, int64_t cols, DropoutSite site, float* __restrict__ colsum,
+                          int64_t rows_per_block) {
+  extern __shared__ float part[];  // [groups][cols]
+  const int quads = static_cast<int>(cols / 4);
+  const int groups = blockDim.x / quads;
+  const int q = threadIdx.x % quads, g = threadIdx.x / quads;
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rows_per_block;
   const int64_t r1 = r0 + rows_per_block < rows ? r0 + rows_per_block : rows;
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int64_t r = r0; r < r1; ++r) {
-    const Philox4 bits = dropout_block(site, static_cast<uint32_t>(r), static_cast<uint32_t>(q));
-    const uint2 in = *reinterpret_cast<const uint2*>(x + r * ldx + 4 * q);
-    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&in);
-    const float2 a = __bfloat1622float2(h[0]), b = __bfloat1622float2(h[1]);
-    float v[4] = {a.x, a.y, b.x, b.y};
+  if (g < groups) {
+    for (int64_t r = r0 + g; r < r1; r += 8 * groups) {
+      uint2 in[8];
 #pragma unroll
-    for (int w = 0; w < 4; ++w) v[w] = word_of(bits, w) >= site.threshold ? v[w] * site.scale : 0.f;
-    uint2 out;
-    __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(&out);
-    o[0] = __floats2bfloat162_rn(v[0], v[1]);
-    o[1] = __floats2bfloat162_rn(v[2], v[3]);
-    *reinterpret_cast<uint2*>(y + r * ldy + 4 * q) = out;
-    const float2 ra = __bfloat1622float2(o[0]), rb = __bfloat1622float2(o[1]);
-    acc[0] += ra.x;
-    acc[1] += ra.y;
-    acc[2] += rb.x;
-    acc[3] += rb.y;
+      for (int u = 0; u < 8; ++u) {
+        const int64_t rr = r + u * groups < r1 ? r + u * groups : r1 - 1;  // past the slice: re-read, not used
+        in[u] = __ldg(reinterpret_cast<const uint2*>(x + rr * ldx + 4 * q));
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int64_t rr = r + u * groups;
+        if (rr >= r1) break;
+        const Philox4 bits = dropout_block(site, static_cast<uint32_t>(rr), static_cast<uint32_t>(q));
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&in[u]);
+        const float2 a = __bfloat1622float2(h[0]), b = __bfloat1622float2(h[1]);
+        float v[4] = {a.x, a.y, b.x, b.y};
+#pragma unroll
+        for (int w = 0; w < 4; ++w) v[w] = word_of(bits, w) >= site.threshold ? v[w] * site.scale : 0.f;
+        uint2 out;
+        __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(&out);
+        o[0] = __floats2bfloat162_rn(v[0], v[1]);
+        o[1] = __floats2bfloat162_rn(v[2], v[3]);
+        *reinterpret_cast<uint2*>(y + rr * ldy + 4 * q) = out;
+        const float2 ra = __bfloat1622float2(o[0]), rb = __bfloat1622float2(o[1]);
+        acc[0] += ra.x;
+        acc[1] += ra.y;
+        acc[2] += rb.x;
+        acc[3] += rb.y;
+      }
+    }
   }
+  if (groups == 1) {
+    if (g == 0) {
 #pragma unroll
-  for (int w = 0; w < 4; ++w) atomicAdd(colsum + 4 * q + w, acc[w]);
+      for (int w = 0; w < 4; ++w) atomicAdd(colsum + 4 * q + w, acc[w]);
+    }
+    return;
+  }
+  if (g < groups) {
+#pragma unroll
+    for (int w = 0; w < 4; ++w) part[g * cols + 4 * q + w] = acc[w];
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < cols; c += blockDim.x) {
+    float t = 0.f;
+    for (int k = 0; k < groups; ++k) t += part[k * cols + c];
+    atomicAdd(colsum + c, t);
+  }
 }
 
 }  // namespace pw
@@ -494,6 +529,8 @@ void activation_backward(const at::Tensor& dy, const at::Tensor& z, at::Tensor& 
   RX_CUDA_CHECK(cudaGetLastError());
 }
 
+void colsum_accumulate(const at::Tensor& x, at::Tensor& out);
+
 void dropout_apply(const at::Tensor& x, at::Tensor& y, int64_t seed, int64_t stream, double p,
                    const c10::optional<at::Tensor>& colsum) {
   check_bf16(x, "x");
@@ -511,13 +548,27 @@ void dropout_apply(const at::Tensor& x, at::Tensor& y, int64_t seed, int64_t str
     check_f32(*colsum, "colsum");
     RX_CHECK(colsum->numel() == cols && colsum->is_contiguous(), "colsum must be fp32 [cols]");
     const int64_t quads = cols / 4;
-    const int threads = 64;
-    const int64_t col_blocks = (quads + threads - 1) / threads;
-    const int64_t row_blocks = std::max<int64_t>(1, std::min<int64_t>((rows + 63) / 64,
-                                                                        (4ll * num_sms(device)) / col_blocks + 1));
-    const int64_t rows_per_block = (rows + row_blocks - 1) / row_blocks;
-    dim3 grid2(static_cast<unsigned>(col_blocks), static_cast<unsigned>((rows + rows_per_block - 1) / rows_per_block));
-    pw::dropout_colsum_kernel<<<grid2, threads, 0, at::cuda::getCurrentCUDAStream(device).stream()>>>(
+    if (quads > 512) {  // wider rows: the plain dropout kernel, then a column-sum pass
+      const int grid = grid_for(rows * cols / 4, 256, device);
+      pw::dropout_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream(device).stream()>>>(
+          reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0),
+          reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), y.stride(0), rows, cols, make_dropout_site(seed, stream, p));
+      RX_CUDA_CHECK(cudaGetLastError());
+      at::Tensor sums = *colsum;
+      colsum_accumulate(y, sums);
+      return;
+    }
+    const int groups = static_cast<int>(std::max<int64_t>(1, 512 / quads));
+    const int threads = static_cast<int>(groups * quads);
+    const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>(4ll * num_sms(device), (rows + 8 * groups - 1) /
+                                                                                          (8 * groups)));
+    const int64_t rows_per_block = (rows + blocks - 1) / blocks;
+    const dim3 grid2(static_cast<unsigned>((rows + rows_per_block - 1) / rows_per_block));
+    const size_t smem = groups > 1 ? static_cast<size_t>(groups) * cols * sizeof(float) : 0;
+    if (smem > 48 * 1024)
+      RX_CUDA_CHECK(cudaFuncSetAttribute(pw::dropout_colsum_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem)));
+    pw::dropout_colsum_kernel<<<grid2, threads, smem, at::cuda::getCurrentCUDAStream(device).stream()>>>(
         reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0),
         reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), y.stride(0), rows, cols, make_dropout_site(seed, stream, p),
         colsum->data_ptr<float>(), rows_per_block);

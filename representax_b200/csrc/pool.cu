@@ -171,7 +171,7 @@ __global__ void __launch_bounds__(1024)
 // out[col] += sum_rows x[row, col]  (bf16 input, fp32 accumulator).
 // One CTA per slice of `slice` rows; thread (g, c) owns the 16-byte
 // column chunk c (8 columns) for rows g, g + G, ... of the slice (G row
-// groups of `chunks` threads), keeping four loads in flight; row groups meet
+// groups of `chunks` threads), keeping eight loads in flight; row groups meet
 // in shared memory and each column gets one atomic per CTA.
 __global__ void __launch_bounds__(1024)
     colsum_kernel(const __nv_bfloat16* __restrict__ x, int64_t ld, int rows, int cols, int slice,
@@ -183,16 +183,23 @@ __global__ void __launch_bounds__(1024)
   const int r0 = blockIdx.x * slice, r1 = min(rows, r0 + slice);
   float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   if (g < groups) {
-    for (int r = r0 + g; r < r1; r += 4 * groups) {
-      uint4 w[4];
+    for (int r = r0 + g; r < r1; r += 8 * groups) {
+      // unconditional loads (rows past the slice re-read its last row and are
+      // masked below) so that all eight are issued before the first is used
+      uint4 w[8];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int rr = r + u * groups;
-        w[u] = rr < r1 ? reinterpret_cast<const uint4*>(x + static_cast<int64_t>(rr) * ld)[c]
-                       : make_uint4(0u, 0u, 0u, 0u);
+      for (int u = 0; u < 8; ++u) {
+        const int rr = min(r + u * groups, r1 - 1);
+        w[u] = ldg_v4_issue(reinterpret_cast<const uint4*>(x + static_cast<int64_t>(rr) * ld) + c);
       }
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < 8; ++u) hold_v4(w[u]);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (r + u * groups >= r1) w[u] = make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
         const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w[u]);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -347,13 +354,13 @@ void colsum_accumulate(const at::Tensor& x, at::Tensor& out) {
   c10::cuda::CUDAGuard guard(x.get_device());
   const int chunks = cols / 8;
   // one CTA per SM of up to 1024 threads (row groups of one thread per chunk,
-  // each keeping four 16-byte loads in flight); the groups meet in shared
+  // each keeping eight 16-byte loads in flight); the groups meet in shared
   // memory, so every column takes one atomic per CTA
   const int groups = std::max(1, 1024 / chunks);
   const int threads = groups * chunks;
   const size_t smem = groups > 1 ? static_cast<size_t>(groups) * cols * sizeof(float) : 0;
   const int sms = num_sms(x.get_device());
-  const int slice = std::max(4 * groups, (rows + sms - 1) / sms);
+  const int slice = std::max(8 * groups, (rows + sms - 1) / sms);
   const int grid = (rows + slice - 1) / slice;
   auto kern = pool::colsum_kernel;
   if (smem > 48 * 1024)

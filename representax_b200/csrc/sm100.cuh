@@ -55,6 +55,12 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                : "memory");
 }
 
+// Raise the transaction count of the current phase without arriving.
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
@@ -305,6 +311,23 @@ __host__ __device__ constexpr uint32_t idesc_mxf8(int m, int n, int a_fmt, int b
          | (1u << 23)                                // scale format: UE8M0
          | (static_cast<uint32_t>(m >> 4) << 24)     // M / 16
          | (static_cast<uint32_t>(sf_a & 3) << 29);  // A scale-factor id
+}
+
+// 16-byte read-only global load issued as written (volatile asm keeps a run
+// of these ahead of the code that consumes them, so they are all in flight).
+__device__ __forceinline__ uint4 ldg_v4_issue(const void* ptr) {
+  uint4 v;
+  asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(ptr));
+  return v;
+}
+
+// Marks a loaded vector as used here: placed after a run of ldg_v4_issue, it
+// keeps the compiler from consuming (and so waiting on) one load before the
+// next is issued.
+__device__ __forceinline__ void hold_v4(uint4& v) {
+  asm volatile("" : "+r"(v.x), "+r"(v.y), "+r"(v.z), "+r"(v.w));
 }
 
 __device__ __forceinline__ int warp_id() { return threadIdx.x >> 5; }

@@ -30,7 +30,7 @@ class KernelTimeoutError(RuntimeError):
 
 
 # Kernels launched per binding call (used to count our own launches).
-KERNELS_PER_CALL = {"attention_backward": 3, "grad_norm_sq": 1}
+KERNELS_PER_CALL = {"attention_backward": 3, "attention_backward_bias": 3, "grad_norm_sq": 1}
 
 
 class _CountingModule:

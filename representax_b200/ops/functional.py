@@ -166,10 +166,13 @@ class AttentionBlockFn(torch.autograd.Function):
         dvec = torch.empty(heads, T, dtype=torch.float32, device=x.device)
         rel_table, rel_buckets, lut = ctx.rel
         drel = None if lut is None else torch.zeros_like(lut)
-        C.attention_backward(da, q, k, v, a, lse, dqkv[:, :qd], dqkv[:, qd:qd + kd], dqkv[:, qd + kd:],
-                             dq_acc, dvec, cu, max_len, heads, kv_heads, scale, causal, window,
-                             drop.seed if drop is not None else 0, drop.site if drop is not None else 0,
-                             drop.attention if drop is not None else 0.0, lut, drel)
+        # the QKV bias gradient (column sums of dq | dk | dv) is taken inside the
+        # backward's dQ conversion and dK / dV epilogue
+        C.attention_backward_bias(da, q, k, v, a, lse, dqkv[:, :qd], dqkv[:, qd:qd + kd], dqkv[:, qd + kd:],
+                                  dq_acc, dvec, cu, max_len, heads, kv_heads, scale, causal, window,
+                                  drop.seed if drop is not None else 0, drop.site if drop is not None else 0,
+                                  drop.attention if drop is not None else 0.0, lut, drel,
+                                  g_bqkv.buffer() if g_bqkv.wanted else None)
         g_rel = None
         if drel is not None and rel_table.requires_grad:
             sink = _GradSink(rel_table)
@@ -177,7 +180,6 @@ class AttentionBlockFn(torch.autograd.Function):
             g_rel = sink.result()
         if g_wqkv.wanted:
             G.linear_wgrad(dqkv, x, g_wqkv.buffer())
-        _colsum_into(dqkv, g_bqkv)
         dx = G.linear_dgrad(dqkv, compute_view(w_qkv), residual=ds)
         return (dx, g_wqkv.result(), g_bqkv.result(), g_wo.result(), g_bo.result(), None, None, None, None, None,
                 None, None, None, g_rel, None)

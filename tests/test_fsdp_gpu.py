@@ -92,7 +92,7 @@ def _fsdp_worker(rank, world, port, out):
     cfg = BertConfig(vocab_size=3000, hidden_size=256, intermediate_size=1024, num_hidden_layers=2,
                      num_attention_heads=4, max_position_embeddings=128, hidden_dropout_probability=0.0,
                      attention_dropout_probability=0.0)
-    full = retrieval_pairs(np.random.default_rng(3), 32, 48, vocab=3000, low=100, min_len=8)
+    full = retrieval_pairs(np.random.default_rng(3), 16 * world, 48, vocab=3000, low=100, min_len=8)
     local = to_device(slice_rows(full, rank * 16, rank * 16 + 16), dev)
     results = {}
     for mode in ("replicated", "fsdp"):
@@ -124,15 +124,18 @@ def _fsdp_worker(rank, world, port, out):
     dist.destroy_process_group()
 
 
-def test_fsdp_two_ranks_matches_replicated_layout(tmp_path):
-    if torch.cuda.device_count() < 2:
+def test_fsdp_ranks_match_replicated_layout(tmp_path):
+    """FSDP on every GPU of the box (2 to 4 ranks) against the replicated layout."""
+
+    world = min(torch.cuda.device_count(), 4)
+    if world < 2:
         pytest.skip("needs two GPUs")
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     out = str(tmp_path / "fsdp.pt")
-    mp.spawn(_fsdp_worker, args=(2, _port(), out), nprocs=2, join=True)
+    mp.spawn(_fsdp_worker, args=(world, _port(), out), nprocs=world, join=True)
     r = torch.load(out)
     rep, fsdp = r["replicated"], r["fsdp"]
-    assert fsdp["segment"] * 2 == fsdp["numel"]  # master weights: one half per rank
+    assert fsdp["segment"] == -(-fsdp["numel"] // world)  # master weights: one 1/N segment per rank
     assert fsdp["stats"]["fused_gathers"] >= 8 * 2  # 4 GEMM weights per layer, 2 layers, from step 2 on
     assert fsdp["restored"]
     # Same kernels on the same operands; only the order of a few fp32 atomic

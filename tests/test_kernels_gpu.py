@@ -228,11 +228,15 @@ def _attn_ref(q, k, v, lens, heads, kv_heads, scale, causal, window, d=64):
     return torch.cat(outs)
 
 
-@pytest.fixture(params=["tcgen05", "mma_sync"])
+@pytest.fixture(params=["tcgen05", "tcgen05_per_tile", "mma_sync"])
 def attn_impl(request, C):
-    C.set_attention_tcgen05(request.param == "tcgen05")
+    """tcgen05: default (warp-specialised persistent backward at head dim 64);
+    tcgen05_per_tile: the one-CTA-per-key-tile tcgen05 backward; mma_sync: legacy."""
+    C.set_attention_tcgen05(request.param != "mma_sync")
+    C.set_attention_backward_ws(request.param == "tcgen05")
     yield request.param
     C.set_attention_tcgen05(True)
+    C.set_attention_backward_ws(True)
 
 
 @pytest.mark.parametrize(
@@ -278,6 +282,56 @@ def test_attention_fwd_bwd(C, attn_impl, lens, heads, kv_heads, causal, window, 
     _close(dq, qf.grad, rtol=3e-2, atol=3e-2 * gain, what=f"dq ({attn_impl})")
     _close(dk, kf.grad, rtol=3e-2, atol=3e-2 * gain, what=f"dk ({attn_impl})")
     _close(dv, vf.grad, rtol=3e-2, atol=3e-2 * gain, what=f"dv ({attn_impl})")
+
+
+@pytest.mark.parametrize(
+    "lens,heads,kv_heads,causal,window,drop",
+    [
+        ([1, 17, 64, 65, 200, 256, 31, 128, 129], 12, 12, False, -1, 0.0),
+        ([1, 17, 64, 65, 200, 256], 12, 12, False, -1, 0.1),
+        ([100, 257, 640], 4, 2, True, -1, 0.1),
+        ([300, 129, 5], 4, 1, False, 64, 0.0),
+        ([700, 3], 2, 2, True, 40, 0.2),
+    ],
+)
+def test_attention_backward_ws_matches_per_tile_kernel(C, lens, heads, kv_heads, causal, window, drop):
+    """The warp-specialised persistent backward (pipelined S / softmax / gradient
+    MMAs, dQ drained by its own warps) against the per-key-tile tcgen05 backward
+    on the same forward, dropout masks included; both also fuse the QKV bias
+    gradient, checked against the column sums of the gradients they wrote."""
+    torch.manual_seed(5)
+    d = 64
+    total = sum(lens)
+    hd, kvd = heads * d, kv_heads * d
+    qkv = _rand(total, hd + 2 * kvd)
+    q, k, v = qkv[:, :hd], qkv[:, hd:hd + kvd], qkv[:, hd + kvd:]
+    do = _rand(total, hd)
+    cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), dtype=torch.int32, device=_dev())
+    o = torch.empty(total, hd, dtype=torch.bfloat16, device=_dev())
+    lse = torch.empty(heads, total, device=_dev())
+    C.attention_forward(q, k, v, o, lse, cu, max(lens), heads, kv_heads, d ** -0.5, causal, window, 99, 3, drop, None)
+    out, bias = {}, {}
+    for ws in (True, False):
+        C.set_attention_backward_ws(ws)
+        dqkv = torch.full_like(qkv, float("nan"))
+        acc = torch.empty(total, hd, device=_dev())
+        dvec = torch.empty(heads, total, device=_dev())
+        db = torch.full((hd + 2 * kvd,), 0.5, device=_dev())  # accumulates onto what is there
+        C.attention_backward_bias(do, q, k, v, o, lse, dqkv[:, :hd], dqkv[:, hd:hd + kvd], dqkv[:, hd + kvd:], acc,
+                                  dvec, cu, max(lens), heads, kv_heads, d ** -0.5, causal, window, 99, 3, drop, None,
+                                  None, db)
+        out[ws] = dqkv.float()
+        bias[ws] = db
+    C.set_attention_backward_ws(True)
+    torch.cuda.synchronize()
+    from representax_b200.ops._ext import check_status
+
+    check_status(_dev())  # no bounded wait ran out
+    assert torch.isfinite(out[True]).all(), "ws backward left unwritten gradient rows"
+    _close(out[True], out[False], rtol=1e-2, atol=1e-2, what="ws vs per-tile backward")
+    for ws in (True, False):  # fused bias gradient == column sums of the bf16 gradients
+        want = out[ws].double().sum(0) + 0.5
+        _close(bias[ws], want, rtol=1e-4, atol=1e-3 * float(want.abs().max()), what=f"qkv bias grad (ws={ws})")
 
 
 @pytest.mark.parametrize("d", [64, 128])
