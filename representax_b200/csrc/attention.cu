@@ -720,6 +720,8 @@ void tc_backward(Params p, int d, int64_t max_len, cudaStream_t st, int device);
 int* tc_status_word(int device);
 bool ws_backward_enabled();
 void tc_backward_ws(Params p, int64_t max_len, cudaStream_t st, int device, int* status);
+bool ws_forward_enabled();
+void tc_forward_ws(Params p, int64_t max_len, cudaStream_t st, int device, int* status);
 
 }  // namespace attn
 
@@ -807,7 +809,11 @@ void attention_forward(const at::Tensor& q, const at::Tensor& k, const at::Tenso
   c10::cuda::CUDAGuard guard(q.get_device());
   auto st = at::cuda::getCurrentCUDAStream().stream();
   if (attn::tc_attention_enabled() && aligned_rows(o)) {
-    attn::tc_forward(p, static_cast<int>(q.size(1) / heads), max_len, st, q.get_device());
+    const int d = static_cast<int>(q.size(1) / heads);
+    if (d == 64 && p.rel_lut == nullptr && attn::ws_forward_enabled())
+      attn::tc_forward_ws(p, max_len, st, q.get_device(), attn::tc_status_word(q.get_device()));
+    else
+      attn::tc_forward(p, d, max_len, st, q.get_device());
     return;
   }
   dim3 grid((max_len + attn::BM - 1) / attn::BM, heads, p.batch);

@@ -134,6 +134,8 @@ void set_tc_attention_enabled(bool on);
 void register_tc_status(int device, int* status);
 bool ws_backward_enabled();
 void set_ws_backward_enabled(bool on);
+bool ws_forward_enabled();
+void set_ws_forward_enabled(bool on);
 }  // namespace attn
 }  // namespace rx
 
@@ -154,6 +156,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("set_attention_backward_ws", &rx::attn::set_ws_backward_enabled,
         "use the warp-specialised persistent tcgen05 backward for head dim 64 (default on)");
   m.def("attention_backward_ws_enabled", &rx::attn::ws_backward_enabled);
+  m.def("set_attention_forward_ws", &rx::attn::set_ws_forward_enabled,
+        "use the warp-specialised persistent tcgen05 forward for head dim 64");
+  m.def("attention_forward_ws_enabled", &rx::attn::ws_forward_enabled);
   m.def("register_status_word", [](const at::Tensor& status) {
     TORCH_CHECK(status.is_cuda() && status.scalar_type() == at::kInt, "status must be CUDA int32");
     rx::attn::register_tc_status(status.get_device(), status.data_ptr<int>());

@@ -23,7 +23,7 @@ SOURCES = [
     "pool.cu",
     "mnr.cu",
     "optim.cu",
-    "comm.cu", "pointwise.cu", "gemm_fp8.cu", "int4.cu", "mnr_tc.cu", "mxfp8.cu", "int4_gemm.cu", "attention_bwd_ws.cu",
+    "comm.cu", "pointwise.cu", "gemm_fp8.cu", "int4.cu", "mnr_tc.cu", "mxfp8.cu", "int4_gemm.cu", "attention_bwd_ws.cu", "attention_fwd_ws.cu",
 ]
 
 NVCC_FLAGS = [

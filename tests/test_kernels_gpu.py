@@ -230,13 +230,16 @@ def _attn_ref(q, k, v, lens, heads, kv_heads, scale, causal, window, d=64):
 
 @pytest.fixture(params=["tcgen05", "tcgen05_per_tile", "mma_sync"])
 def attn_impl(request, C):
-    """tcgen05: default (warp-specialised persistent backward at head dim 64);
-    tcgen05_per_tile: the one-CTA-per-key-tile tcgen05 backward; mma_sync: legacy."""
+    """tcgen05: the warp-specialised persistent kernels at head dim 64;
+    tcgen05_per_tile: the one-CTA-per-tile tcgen05 kernels; mma_sync: legacy."""
+    fwd_default = C.attention_forward_ws_enabled()
     C.set_attention_tcgen05(request.param != "mma_sync")
     C.set_attention_backward_ws(request.param == "tcgen05")
+    C.set_attention_forward_ws(request.param == "tcgen05")
     yield request.param
     C.set_attention_tcgen05(True)
     C.set_attention_backward_ws(True)
+    C.set_attention_forward_ws(fwd_default)
 
 
 @pytest.mark.parametrize(
@@ -332,6 +335,48 @@ def test_attention_backward_ws_matches_per_tile_kernel(C, lens, heads, kv_heads,
     for ws in (True, False):  # fused bias gradient == column sums of the bf16 gradients
         want = out[ws].double().sum(0) + 0.5
         _close(bias[ws], want, rtol=1e-4, atol=1e-3 * float(want.abs().max()), what=f"qkv bias grad (ws={ws})")
+
+
+@pytest.mark.parametrize(
+    "lens,heads,kv_heads,causal,window,drop,q_gain",
+    [
+        ([1, 17, 64, 65, 200, 256, 31, 128, 129], 12, 12, False, -1, 0.0, 1.0),
+        ([1, 17, 64, 65, 200, 256], 12, 12, False, -1, 0.1, 1.0),
+        ([100, 257, 640], 4, 2, True, -1, 0.1, 1.0),
+        ([300, 129, 5], 4, 1, False, 64, 0.0, 1.0),
+        ([513, 40, 384], 2, 2, False, -1, 0.0, 4.0),  # sharp scores: running-max moves, O rescales
+        ([700, 3], 2, 2, True, 40, 0.2, 1.0),
+    ],
+)
+def test_attention_forward_ws_matches_per_tile_kernel(C, lens, heads, kv_heads, causal, window, drop, q_gain):
+    """The warp-specialised persistent forward (two pipelines per SM, score MMAs
+    of the next block overlapping the softmax) against the per-tile tcgen05
+    forward: outputs and log-sum-exps, dropout masks included."""
+    torch.manual_seed(9)
+    d = 64
+    total = sum(lens)
+    hd, kvd = heads * d, kv_heads * d
+    qkv = _rand(total, hd + 2 * kvd)
+    qkv[:, :hd] = (qkv[:, :hd].float() * q_gain).to(torch.bfloat16)
+    q, k, v = qkv[:, :hd], qkv[:, hd:hd + kvd], qkv[:, hd + kvd:]
+    cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), dtype=torch.int32, device=_dev())
+    default = C.attention_forward_ws_enabled()
+    res = {}
+    for ws in (True, False):
+        C.set_attention_forward_ws(ws)
+        o = torch.full((total, hd), float("nan"), dtype=torch.bfloat16, device=_dev())
+        lse = torch.full((heads, total), float("nan"), device=_dev())
+        C.attention_forward(q, k, v, o, lse, cu, max(lens), heads, kv_heads, d ** -0.5, causal, window, 77, 2, drop,
+                            None)
+        res[ws] = (o.float(), lse)
+    C.set_attention_forward_ws(default)
+    torch.cuda.synchronize()
+    from representax_b200.ops._ext import check_status
+
+    check_status(_dev())
+    assert torch.isfinite(res[True][0]).all() and torch.isfinite(res[True][1]).all()
+    _close(res[True][0], res[False][0], rtol=1e-2, atol=1e-2, what="ws vs per-tile forward O")
+    _close(res[True][1], res[False][1], rtol=1e-4, atol=1e-3, what="ws vs per-tile forward lse")
 
 
 @pytest.mark.parametrize("d", [64, 128])
