@@ -63,6 +63,8 @@ def _args():
                         "ddp = NCCL all-reduce + replicated AdamW")
     p.add_argument("--dropout", type=float, default=0.1,
                    help="hidden and attention dropout (BERT-base default 0.1; native Philox masks)")
+    p.add_argument("--gemm-table", default=None,
+                   help="write per-shape GEMM device times of one extra step to this markdown file (rank 0)")
     p.add_argument("--kernel-table", default=None,
                    help="after the timed steps, run one more step under torch.profiler (CUPTI) and write a "
                         "per-kernel device-time table to this path (rank 0); not part of the timed number")
@@ -156,6 +158,39 @@ class ClockSampler:
         loaded = [x for x in sm if mx and x > 0.3 * mx] or sm
         return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": mx,
                 "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def _gemm_table(step, batch, it, path) -> None:
+    """Device time of every tcgen05 GEMM launch of one training step, grouped by
+    kind / shape / epilogue (CUDA events around each launch)."""
+
+    from representax_b200.ops import gemm as G
+
+    torch.cuda.synchronize()
+    G.profile_gemms(True)
+    step(batch, it)
+    records = G.profile_gemms(False)
+    rows = G.gemm_table(records)
+    peak = _measured_bf16()
+    total = sum(t for _, _, t in rows)
+    with open(path, "w") as f:
+        f.write("| GEMM (kind, M N K, epilogue bits, output mode) | launches | device ms | us per launch "
+                "| TFLOP/s | of measured bf16 | share |\n|---|---|---|---|---|---|---|\n")
+        for key, n, t in rows:
+            m, nn, k = (int(tok[1:]) for tok in key.split()[1:4])  # "M.. N.. K.."
+            flops = 2.0 * m * nn * k * n
+            tf = flops / (t / 1e3) / 1e12
+            f.write(f"| {key} | {n} | {t:.2f} | {1e3 * t / n:.1f} | {tf:.0f} | {tf * 1e12 / peak:.2f} | "
+                    f"{t / total:.1%} |\n")
+        f.write(f"| total | {sum(n for _, n, _ in rows)} | {total:.2f} | | | | 100% |\n")
+
+
+def _measured_bf16() -> float:
+    try:
+        with open(os.path.join(os.path.dirname(os.path.abspath(__file__)), "MEASURED_PEAKS.json")) as handle:
+            return float(json.load(handle)["bf16_tflops"]) * 1e12
+    except (OSError, KeyError, ValueError):
+        return 1.59e15
 
 
 def _kernel_table(step, batch, it, path) -> None:
@@ -306,6 +341,9 @@ def main() -> None:
     elapsed = float(t)
     final_loss = float(metrics.loss)
 
+    if args.gemm_table and ctx.world_size == 1:
+        _gemm_table(step, resident[it % n_host], it, args.gemm_table)
+        it += 1
     if args.kernel_table and ctx.rank == 0:
         _kernel_table(step, resident[it % n_host], it, args.kernel_table)
         it += 1

@@ -15,9 +15,10 @@
 //               and tcgen05.commit.
 //   warps 2-9   epilogue: two warps per 32-lane TMEM quadrant, each taking half
 //               of the tile's columns; tcgen05.ld gives one output row per
-//               thread; fused bias / GELU / GELU-backward /
-//               residual, bf16 or fp32 stores, fp32 accumulate or split-K
-//               atomic reduction.
+//               thread; fused bias / GELU (also writing gelu'(z) for the
+//               backward) / GELU-backward (a product with that saved
+//               derivative) / residual, bf16 or fp32 stores, fp32 accumulate or
+//               split-K atomic reduction.
 // The double-buffered accumulator lets the epilogue of tile i overlap the
 // main loop of tile i+1.
 //
@@ -86,14 +87,33 @@ struct Params {
 constexpr int kKindBf16 = 0;
 constexpr int fp8_kind(int a_fmt, int b_fmt) { return 1 + (a_fmt | (b_fmt << 1)); }
 
-__device__ __forceinline__ float gelu_erf(float x) {
-  return 0.5f * x * (1.0f + erff(x * 0.70710678118654752440f));
+// GELU (erf form) and its derivative from one exponential: the normal CDF
+// Phi(x) = (1 + erf(x / sqrt 2)) / 2 uses the rational approximation of
+// Abramowitz & Stegun, Handbook of Mathematical Functions, eq. 7.1.26
+// (|error of erf| <= 1.5e-7, far below bf16's resolution), whose exp(-u^2)
+// factor at u = |x| / sqrt 2 is exp(-x^2 / 2), the same exponential the normal
+// density phi(x) needs. gelu = x Phi(x); gelu' = Phi(x) + x phi(x).
+__device__ __forceinline__ void gelu_and_grad(float x, float& gelu, float& grad) {
+  const float u = fabsf(x) * 0.70710678118654752440f;
+  float t;  // 1 / (1 + p u) by the approximate reciprocal (a few ulp, far below bf16's resolution)
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t) : "f"(fmaf(0.3275911f, u, 1.0f)));
+  float poly = fmaf(1.061405429f, t, -1.453152027f);
+  poly = fmaf(poly, t, 1.421413741f);
+  poly = fmaf(poly, t, -0.284496736f);
+  poly = fmaf(poly, t, 0.254829592f);
+  poly *= t;
+  float e;  // exp(-x^2 / 2) = 2^(-x^2 / 2 * log2(e))
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(-0.72134752044448170368f * x * x));
+  const float erf_u = 1.0f - poly * e;  // erf(|x| / sqrt 2)
+  const float cdf = 0.5f + 0.5f * copysignf(erf_u, x);
+  gelu = x * cdf;
+  grad = fmaf(x * 0.39894228040143267794f, e, cdf);
 }
 
-__device__ __forceinline__ float gelu_erf_grad(float x) {
-  const float cdf = 0.5f * (1.0f + erff(x * 0.70710678118654752440f));
-  const float pdf = 0.39894228040143267794f * __expf(-0.5f * x * x);
-  return cdf + x * pdf;
+__device__ __forceinline__ float gelu_erf(float x) {
+  float g, d;
+  gelu_and_grad(x, g, d);
+  return g;
 }
 
 __device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* src, float (&v)[32]) {
@@ -160,6 +180,39 @@ __device__ __forceinline__ void warp_load_tile32_sw64(uint8_t* buf, const __nv_b
   }
 }
 
+// The same 32 x 32 tile in two steps, so the loads of the next tile can be
+// in flight while the current one is computed: fetch into registers (lane
+// holds pieces lane, lane + 32, lane + 64, lane + 96) ...
+__device__ __forceinline__ void warp_fetch_tile32(const __nv_bfloat16* src, int64_t ld, int row0, int n_base,
+                                                  int rows_valid, int cols_valid, int lane, uint4 (&w)[4]) {
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {
+    const int c = lane + 32 * it;
+    const int row = c >> 2, piece = c & 3;
+    const int m = row0 + row, n = n_base + piece * 8;
+    w[it] = make_uint4(0u, 0u, 0u, 0u);
+    if (m < rows_valid) {
+      const __nv_bfloat16* g = src + static_cast<int64_t>(m) * ld + n;
+      if (n + 8 <= cols_valid) {
+        w[it] = *reinterpret_cast<const uint4*>(g);
+      } else {
+        __nv_bfloat16* e = reinterpret_cast<__nv_bfloat16*>(&w[it]);
+        for (int k = 0; k < 8; ++k) e[k] = n + k < cols_valid ? g[k] : __float2bfloat16_rn(0.f);
+      }
+    }
+  }
+}
+
+// ... then place it in `buf` with the 64-byte swizzle.
+__device__ __forceinline__ void warp_put_tile32_sw64(uint8_t* buf, int lane, const uint4 (&w)[4]) {
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {
+    const int c = lane + 32 * it;
+    const int row = c >> 2, piece = c & 3;
+    *reinterpret_cast<uint4*>(buf + row * 64 + ((piece ^ ((row >> 1) & 3)) * 16)) = w[it];
+  }
+}
+
 // Row `lane` of a 64-byte-swizzled 32 x 32 bf16 tile as 32 floats.
 __device__ __forceinline__ void read_row32_sw64(const uint8_t* buf, int lane, float (&v)[32]) {
 #pragma unroll
@@ -176,8 +229,8 @@ __device__ __forceinline__ void read_row32_sw64(const uint8_t* buf, int lane, fl
 }
 
 // Epilogue values of one row segment for the staged tile store, with the
-// residual (EPI_RESID) or GELU pre-activation input (EPI_DGELU) already in
-// `side`; with EPI_GELU the pre-activation is returned in `pre`.
+// residual (EPI_RESID) or the saved GELU derivative (EPI_DGELU) already in
+// `side`; with EPI_GELU the derivative gelu'(z) is returned in `pre`.
 template <int EPI>
 __device__ __forceinline__ void epilogue_tile_values32(const Params& p, int m, int n_base, const uint32_t (&r)[32],
                                                        const float (&side)[32], float (&v)[32], float (&pre)[32]) {
@@ -195,15 +248,17 @@ __device__ __forceinline__ void epilogue_tile_values32(const Params& p, int m, i
       for (int i = 0; i < 32; ++i) v[i] += n_base + i < p.N ? __bfloat162float(p.bias[n_base + i]) : 0.f;
     }
   }
-  if constexpr ((EPI & EPI_DGELU) != 0) {
+  if constexpr ((EPI & EPI_DGELU) != 0) {  // side = gelu'(z) saved by the forward
 #pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] *= gelu_erf_grad(side[i]);
+    for (int i = 0; i < 32; ++i) v[i] *= side[i];
   }
-  if constexpr ((EPI & EPI_GELU) != 0) {
+  if constexpr ((EPI & EPI_GELU) != 0) {  // pre receives gelu'(z) for the backward
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
-      pre[i] = v[i];
-      v[i] = gelu_erf(v[i]);
+      float g, d;
+      gelu_and_grad(v[i], g, d);
+      pre[i] = d;
+      v[i] = g;
     }
   }
   if constexpr ((EPI & EPI_DROP) != 0) {
@@ -238,16 +293,17 @@ __device__ __forceinline__ void epilogue_row32(const Params& p, int m, int n_bas
 #pragma unroll
       for (int i = 0; i < 32; ++i) v[i] += b[i];
     }
-    if constexpr ((EPI & EPI_DGELU) != 0) {
-      float z[32];
-      load_bf16x32(p.aux_in + static_cast<int64_t>(m) * p.ld_aux_in + n_base, z);
+    if constexpr ((EPI & EPI_DGELU) != 0) {  // times gelu'(z) saved by the forward
+      float d[32];
+      load_bf16x32(p.aux_in + static_cast<int64_t>(m) * p.ld_aux_in + n_base, d);
 #pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] *= gelu_erf_grad(z[i]);
+      for (int i = 0; i < 32; ++i) v[i] *= d[i];
     }
-    if constexpr ((EPI & EPI_GELU) != 0) {
-      store_bf16x32(p.aux_out + static_cast<int64_t>(m) * p.ld_aux_out + n_base, v);
+    if constexpr ((EPI & EPI_GELU) != 0) {  // aux_out receives gelu'(z)
+      float d[32];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
+      for (int i = 0; i < 32; ++i) gelu_and_grad(v[i], v[i], d[i]);
+      store_bf16x32(p.aux_out + static_cast<int64_t>(m) * p.ld_aux_out + n_base, d);
     }
     if constexpr ((EPI & EPI_DROP) != 0) {
 #pragma unroll
@@ -294,10 +350,11 @@ __device__ __forceinline__ void epilogue_row32(const Params& p, int m, int n_bas
       float x = v[i];
       if constexpr ((EPI & EPI_BIAS) != 0) x += __bfloat162float(p.bias[n]);
       if constexpr ((EPI & EPI_DGELU) != 0)
-        x *= gelu_erf_grad(__bfloat162float(p.aux_in[static_cast<int64_t>(m) * p.ld_aux_in + n]));
+        x *= __bfloat162float(p.aux_in[static_cast<int64_t>(m) * p.ld_aux_in + n]);
       if constexpr ((EPI & EPI_GELU) != 0) {
-        p.aux_out[static_cast<int64_t>(m) * p.ld_aux_out + n] = __float2bfloat16_rn(x);
-        x = gelu_erf(x);
+        float d;
+        gelu_and_grad(x, x, d);
+        p.aux_out[static_cast<int64_t>(m) * p.ld_aux_out + n] = __float2bfloat16_rn(d);
       }
       if constexpr ((EPI & EPI_DROP) != 0) {
         const Philox4 r = dropout_block(p.drop, static_cast<uint32_t>(m), static_cast<uint32_t>(n >> 2));
@@ -887,6 +944,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int m = m0 + static_cast<int>(rank) * BM + row_local;
       const uint32_t t_row =
           tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      constexpr bool kSide = (EPI & (EPI_RESID | EPI_DGELU)) != 0;
+      const __nv_bfloat16* side_src = (EPI & EPI_RESID) != 0 ? p.residual : p.aux_in;
+      const int64_t side_ld = (EPI & EPI_RESID) != 0 ? p.ld_res : p.ld_aux_in;
+      const int side_row0 = m0 + static_cast<int>(rank) * BM + quad * 32;
+      uint4 side_next[4];  // the next chunk's residual / saved-derivative tile, in flight
+      if constexpr (kTileStore && kSide) {
+        if (n0 + chunk0 * 32 < p.N && side_row0 < p.M)
+          warp_fetch_tile32(side_src, side_ld, side_row0, n0 + chunk0 * 32, p.M, p.N, lane, side_next);
+      }
 #pragma unroll 1
       for (int c = chunk0; c < chunk0 + kChunksPerWarp; ++c) {
         uint32_t r[32];
@@ -894,32 +960,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld_wait();
         const int n_base = n0 + c * 32;
         if constexpr (kTileStore) {
-          const int row0 = m0 + static_cast<int>(rank) * BM + quad * 32;
+          const int row0 = side_row0;
+          uint4 side_cur[4];
+          if constexpr (kSide) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) side_cur[q] = side_next[q];
+            if (c + 1 < chunk0 + kChunksPerWarp && n_base + 32 < p.N && row0 < p.M)
+              warp_fetch_tile32(side_src, side_ld, row0, n_base + 32, p.M, p.N, lane, side_next);
+          }
           if (n_base < p.N && row0 < p.M) {  // warp-uniform
             uint8_t* buf = sC + ((warp - 2) * 2 + (store_seq & 1)) * 2048;
             if (lane == 0) tma_store_wait_read<1>();  // the store that last read `buf` is done reading
             __syncwarp();
             float side[32], v[32], pre[32];
-            if constexpr ((EPI & (EPI_RESID | EPI_DGELU)) != 0) {
-              const bool resid = (EPI & EPI_RESID) != 0;
-              warp_load_tile32_sw64(buf, resid ? p.residual : p.aux_in, resid ? p.ld_res : p.ld_aux_in, row0,
-                                    n_base, p.M, p.N, lane);
+            if constexpr (kSide) {
+              warp_put_tile32_sw64(buf, lane, side_cur);
               __syncwarp();
               read_row32_sw64(buf, lane, side);
               __syncwarp();  // every lane has its row before the buffer is overwritten
             }
             epilogue_tile_values32<EPI>(p, m, n_base, r, side, v, pre);
-            if constexpr ((EPI & EPI_GELU) != 0) {
-              stage_row32_sw64(buf, lane, pre);
-              fence_proxy_async_smem();
-              __syncwarp();
-              if (lane == 0) {
-                tma_store_2d(&tmAux, buf, n_base, row0);
-                tma_store_commit();
-                tma_store_wait_read<0>();
-              }
-              __syncwarp();
-            }
             stage_row32_sw64(buf, lane, v);
             fence_proxy_async_smem();
             __syncwarp();
@@ -938,6 +998,21 @@ __global__ void __launch_bounds__(kThreads, 1)
               tma_store_commit();
             }
             ++store_seq;
+            if constexpr ((EPI & EPI_GELU) != 0) {
+              // gelu'(z) through the other staging buffer: only the store issued
+              // two stores ago must have finished reading it
+              uint8_t* buf2 = sC + ((warp - 2) * 2 + (store_seq & 1)) * 2048;
+              if (lane == 0) tma_store_wait_read<1>();
+              __syncwarp();
+              stage_row32_sw64(buf2, lane, pre);
+              fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0) {
+                tma_store_2d(&tmAux, buf2, n_base, row0);
+                tma_store_commit();
+              }
+              ++store_seq;
+            }
           }
         } else {
           if (m < p.M && n_base < p.N) epilogue_row32<EPI, OUT>(p, m, n_base, r);

@@ -379,6 +379,198 @@ __global__ void __launch_bounds__(kWarps * 32, (MAXV <= 2 ? 3 : MAXV <= 4 ? 2 : 
   }
 }
 
+// Backward of a plain normalisation fed by bulk copies: rows are
+// contiguous, so one warp (the producer) moves 8-row chunks of x and dy into a
+// four-stage shared-memory ring with cp.async.bulk (one copy per tensor per
+// chunk, completion counted on the stage's mbarrier) and loads the chunk's
+// mean / rstd; each of the 8 compute warps takes one row of the chunk, frees
+// the stage as soon as its row is in registers, and writes dx with 16-byte
+// stores. 32 rows (96 KB at H = 768) are in flight per SM with no register
+// cost. Parameter-gradient partials accumulate in registers (this lane's
+// columns) and meet in shared memory once per CTA. Waits are bounded
+// (%globaltimer) and report to the status word; an aborting CTA drains its
+// copies before it exits.
+namespace bulk {
+constexpr int kRows = 8, kStages = 4, kComputeWarps = 8;
+constexpr int kThreads = 32 * (kComputeWarps + 1);
+}  // namespace bulk
+
+template <int MAXV, bool RMS>
+__global__ void __launch_bounds__(bulk::kThreads, 1)
+    norm_bwd_bulk_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
+                         const float* __restrict__ mean_in, const float* __restrict__ rstd_in,
+                         const __nv_bfloat16* __restrict__ gamma, __nv_bfloat16* __restrict__ dx,
+                         float* __restrict__ dgamma, float* __restrict__ dbeta, float* __restrict__ dbias_prev,
+                         int rows, int H, int* status, uint64_t timeout_ns) {
+  using namespace bulk;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nv = H >> 3;
+  const size_t tile = static_cast<size_t>(kRows) * H * 2;  // bytes of one tensor's chunk
+  float* red = reinterpret_cast<float*>(smem);              // [kComputeWarps][3][H]
+  uint8_t* ring = smem + static_cast<size_t>(kComputeWarps) * 3 * H * 4;
+  // stage s: x chunk, dy chunk, then -mean / rstd [2][kRows] floats
+  const size_t stage_bytes = 2 * tile + 2 * kRows * 4;
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + kStages * stage_bytes);
+  uint64_t* empty = full + kStages;
+  volatile int* abort = reinterpret_cast<volatile int*>(empty + kStages);
+  const int chunks = (rows + kRows - 1) / kRows;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 32);
+      mbar_init(&empty[s], kComputeWarps * 32);
+    }
+    *abort = 0;
+    fence_mbarrier_init();
+  }
+  if (warp < kComputeWarps) {
+    float* pg = red + static_cast<size_t>(warp) * 3 * H;
+    for (int i = lane; i < 3 * H; i += 32) pg[i] = 0.f;
+  }
+  __syncthreads();
+
+  if (warp == kComputeWarps) {
+    // ---------------------------------------------------------------- producer
+    int k = 0;
+    uint32_t issued[kStages] = {0, 0, 0, 0};
+    for (int c = blockIdx.x; c < chunks; c += gridDim.x, ++k) {
+      const int s = k % kStages;
+      bool ok = true;
+      if (lane == 0) {
+        ok = !*abort && mbar_wait(&empty[s], ((k / kStages) & 1) ^ 1, timeout_ns);
+        if (!ok && !*abort) {
+          report_status(status, kStatusTimeoutProducer);
+          *abort = 1;
+        }
+      }
+      if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+      const int r0 = c * kRows, nr = min(kRows, rows - r0);
+      uint8_t* st = ring + s * stage_bytes;
+      if (lane == 0) {
+        const uint32_t bytes = static_cast<uint32_t>(nr) * H * 2;
+        mbar_expect_tx(&full[s], 2 * bytes);
+        bulk_load(st, x + static_cast<int64_t>(r0) * H, bytes, &full[s]);
+        bulk_load(st + tile, dy + static_cast<int64_t>(r0) * H, bytes, &full[s]);
+        ++issued[s];
+      }
+      float* stats = reinterpret_cast<float*>(st + 2 * tile);
+      if (lane < kRows) {
+        const int r = r0 + lane;
+        stats[lane] = r < rows && !RMS ? mean_in[r] : 0.f;
+        stats[kRows + lane] = r < rows ? rstd_in[r] : 0.f;
+      }
+      mbar_arrive(&full[s]);
+    }
+    if (*abort && lane == 0)
+      for (int s = 0; s < kStages; ++s)
+        if (issued[s] > 0 && !mbar_wait(&full[s], (issued[s] - 1) & 1, timeout_ns))
+          report_status(status, kStatusTimeoutDrain);
+  } else {
+    // ---------------------------------------------------------------- compute
+    // parameter-gradient partials of this lane's columns stay in registers
+    // (one CTA per SM leaves room) and meet in shared memory once at the end
+    float ag[MAXV][8], ab[MAXV][8], ad[MAXV][8];
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ag[i][j] = ab[i][j] = ad[i][j] = 0.f;
+    int k = 0;
+    for (int c = blockIdx.x; c < chunks; c += gridDim.x, ++k) {
+      const int s = k % kStages;
+      bool ok = !*abort && mbar_wait(&full[s], (k / kStages) & 1, timeout_ns);
+      if (!__all_sync(0xffffffffu, ok)) {
+        if (lane == 0 && !*abort) {
+          report_status(status, kStatusTimeoutEpilogue);
+          *abort = 1;
+        }
+        break;
+      }
+      const uint8_t* st = ring + s * stage_bytes;
+      const int row = c * kRows + warp;
+      uint4 xr[MAXV], dr[MAXV];
+#pragma unroll
+      for (int i = 0; i < MAXV; ++i) {
+        const int cc = lane + 32 * i;
+        if (cc < nv) {
+          xr[i] = reinterpret_cast<const uint4*>(st + static_cast<size_t>(warp) * H * 2)[cc];
+          dr[i] = reinterpret_cast<const uint4*>(st + tile + static_cast<size_t>(warp) * H * 2)[cc];
+        }
+      }
+      const float* stats = reinterpret_cast<const float*>(st + 2 * tile);
+      const float mean = stats[warp], rstd = stats[kRows + warp];
+      mbar_arrive(&empty[s]);  // the row is in registers: the stage may refill
+      if (row >= rows) continue;
+      float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+      for (int i = 0; i < MAXV; ++i) {
+        const int cc = lane + 32 * i;
+        if (cc < nv) {
+          float xv[8], d[8], g[8];
+          unpack8(xr[i], xv);
+          unpack8(dr[i], d);
+          unpack8(reinterpret_cast<const uint4*>(gamma)[cc], g);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float xh = (xv[j] - mean) * rstd;
+            const float dyg = d[j] * g[j];
+            s1 += dyg;
+            s2 += dyg * xh;
+            ag[i][j] += d[j] * xh;
+            ab[i][j] += d[j];
+          }
+        }
+      }
+      s1 = warp_sum(s1) / H;
+      s2 = warp_sum(s2) / H;
+#pragma unroll
+      for (int i = 0; i < MAXV; ++i) {
+        const int cc = lane + 32 * i;
+        if (cc < nv) {
+          float xv[8], d[8], g[8], o[8];
+          unpack8(xr[i], xv);
+          unpack8(dr[i], d);
+          unpack8(reinterpret_cast<const uint4*>(gamma)[cc], g);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float xh = (xv[j] - mean) * rstd;
+            o[j] = rstd * (d[j] * g[j] - (RMS ? 0.f : s1) - xh * s2);
+            ad[i][j] += o[j];
+          }
+          reinterpret_cast<uint4*>(dx + static_cast<int64_t>(row) * H)[cc] = pack8(o);
+        }
+      }
+    }
+    float* pg = red + static_cast<size_t>(warp) * 3 * H;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const int cc = lane + 32 * i;
+      if (cc < nv) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          pg[cc * 8 + j] = ag[i][j];
+          pg[H + cc * 8 + j] = ab[i][j];
+          pg[2 * H + cc * 8 + j] = ad[i][j];
+        }
+      }
+    }
+  }
+  __syncthreads();
+  for (int col = threadIdx.x; col < H; col += blockDim.x) {
+    float a = 0.f, b = 0.f, d = 0.f;
+#pragma unroll
+    for (int w = 0; w < kComputeWarps; ++w) {
+      const float* base = red + static_cast<size_t>(w) * 3 * H;
+      a += base[col];
+      b += base[H + col];
+      d += base[2 * H + col];
+    }
+    if (dgamma) atomicAdd(dgamma + col, a);
+    if (dbeta && !RMS) atomicAdd(dbeta + col, b);
+    if (dbias_prev) atomicAdd(dbias_prev + col, d);
+  }
+}
+
 template <bool RMS>
 void launch_fwd(int maxv, dim3 grid, cudaStream_t st, const __nv_bfloat16* x, const int* ids,
                 const int* pos_ids, const int* type_ids, const __nv_bfloat16* word,
@@ -400,7 +592,7 @@ void launch_fwd(int maxv, dim3 grid, cudaStream_t st, const __nv_bfloat16* x, co
 }
 
 template <bool RMS>
-void launch_bwd(int maxv, int grid, int sms, size_t smem, cudaStream_t st, const __nv_bfloat16* dy,
+void launch_bwd(int maxv, int grid, int sms, int* status, size_t smem, cudaStream_t st, const __nv_bfloat16* dy,
                 const __nv_bfloat16* x, const float* mean, const float* rstd,
                 const __nv_bfloat16* gamma, __nv_bfloat16* dx, float* dgamma, float* dbeta,
                 float* dbias_prev, int rows, int H, const int* ids, const int* pos_ids,
@@ -408,7 +600,18 @@ void launch_bwd(int maxv, int grid, int sms, size_t smem, cudaStream_t st, const
                 const __nv_bfloat16* type, float* wg, float* pg, float* tg, int pad_id) {
 #define RX_NORM_BWD(V)                                                                            \
   do {                                                                                            \
-    if (word == nullptr) {                                                                        \
+    const size_t bulk_smem = static_cast<size_t>(bulk::kComputeWarps) * 3 * H * 4 +                \
+                             bulk::kStages * (2 * static_cast<size_t>(bulk::kRows) * H * 2 +      \
+                                              2 * bulk::kRows * 4) + 2 * bulk::kStages * 8 + 16;  \
+    if (word == nullptr && bulk_smem <= 200 * 1024 &&                                             \
+        reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(dy) % 16 == 0) { \
+      auto k = norm_bwd_bulk_kernel<V, RMS>;                                                      \
+      RX_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,         \
+                                         static_cast<int>(bulk_smem)));                           \
+      const int chunks = (rows + bulk::kRows - 1) / bulk::kRows;                                  \
+      k<<<std::max(1, std::min(chunks, sms)), bulk::kThreads, bulk_smem, st>>>(                   \
+          dy, x, mean, rstd, gamma, dx, dgamma, dbeta, dbias_prev, rows, H, status, kWaitBudgetNs); \
+    } else if (word == nullptr) {                                                                 \
       auto k = norm_bwd_prefetch_kernel<V, RMS>;                                                  \
       if (smem > 48 * 1024)                                                                       \
         RX_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,       \
@@ -439,6 +642,10 @@ void launch_bwd(int maxv, int grid, int sms, size_t smem, cudaStream_t st, const
 }
 
 }  // namespace norm
+
+namespace attn {
+int* tc_status_word(int device);  // the device status word (attention_tc.cu)
+}  // namespace attn
 
 namespace {
 template <typename T>
@@ -497,7 +704,8 @@ void norm_backward(const at::Tensor& dy, const at::Tensor& x, const c10::optiona
   const size_t smem = 3 * norm::kWarps * H * sizeof(float);
   auto st = at::cuda::getCurrentCUDAStream().stream();
   auto launch = rms ? norm::launch_bwd<true> : norm::launch_bwd<false>;
-  launch(maxv_for(H), grid, sms, smem, st, reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()),
+  launch(maxv_for(H), grid, sms, attn::tc_status_word(x.get_device()), smem, st,
+         reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()),
          reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), opt_ptr<float>(mean),
          rstd.data_ptr<float>(), reinterpret_cast<const __nv_bfloat16*>(gamma.data_ptr()),
          reinterpret_cast<__nv_bfloat16*>(dx.data_ptr()), opt_mut<float>(dgamma),
@@ -549,7 +757,7 @@ void embed_ln_backward(const at::Tensor& dy, const at::Tensor& ids, const at::Te
   const int grid = static_cast<int>(std::min<int64_t>((rows + norm::kWarps - 1) / norm::kWarps, 3 * sms));
   const size_t smem = 3 * norm::kWarps * H * sizeof(float);
   norm::launch_bwd<false>(
-      maxv_for(H), grid, sms, smem, at::cuda::getCurrentCUDAStream().stream(),
+      maxv_for(H), grid, sms, nullptr, smem, at::cuda::getCurrentCUDAStream().stream(),
       reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()), nullptr, mean.data_ptr<float>(),
       rstd.data_ptr<float>(), reinterpret_cast<const __nv_bfloat16*>(gamma.data_ptr()), nullptr,
       dgamma.data_ptr<float>(), dbeta.data_ptr<float>(), nullptr, static_cast<int>(rows),

@@ -191,7 +191,7 @@ class MlpBlockFn(torch.autograd.Function):
         T = x.shape[0]
         inter = w1.shape[0]
         z = torch.empty(T, inter, dtype=torch.bfloat16, device=x.device)
-        g = G.linear_forward(x, compute_view(w1, fused_gather=True), compute_view(b1), gelu_preact=z)
+        g = G.linear_forward(x, compute_view(w1, fused_gather=True), compute_view(b1), gelu_grad=z)
         s = G.linear_forward(g, compute_view(w2, fused_gather=True), compute_view(b2), residual=x,
                              dropout=None if dropout is None else dropout.hidden_args(2))
         ctx.save_for_backward(x, z, g, w1, b1, w2, b2)
@@ -211,7 +211,7 @@ class MlpBlockFn(torch.autograd.Function):
         if not ctx.out_bias_grad_fused and not dropped:
             _colsum_into(dpre, s_b2)
         # dz = (dpre W2) * gelu'(z); the GEMM epilogue also sums dz's columns (the ffn-in bias gradient)
-        dz = G.linear_dgrad(dpre, compute_view(w2), gelu_preact=z, colsum=s_b1.buffer() if s_b1.wanted else None)
+        dz = G.linear_dgrad(dpre, compute_view(w2), gelu_grad=z, colsum=s_b1.buffer() if s_b1.wanted else None)
         if s_w1.wanted:
             G.linear_wgrad(dz, x, s_w1.buffer())
         dx = G.linear_dgrad(dz, compute_view(w1), residual=ds)

@@ -27,6 +27,32 @@ OUT_F32 = 1
 OUT_F32_ACC = 2
 OUT_F32_ATOMIC = 3
 
+# Opt-in per-call timing (``profile_gemms``): None, or a list that collects
+# (shape / layout / epilogue key, start event, end event) for every launch.
+_PROFILE: list | None = None
+
+
+def profile_gemms(on: bool) -> list | None:
+    """Start (on=True) or stop collecting CUDA-event timings of every GEMM launch;
+    stopping returns the collected (key, start, end) records."""
+
+    global _PROFILE
+    records, _PROFILE = _PROFILE, ([] if on else None)
+    return records
+
+
+def gemm_table(records: list) -> list[tuple[str, int, float]]:
+    """(key, launches, total device ms) per GEMM key, largest first (synchronises)."""
+
+    torch.cuda.synchronize()
+    rows: dict[str, list] = {}
+    for key, start, end in records:
+        r = rows.setdefault(key, [0, 0.0])
+        r[0] += 1
+        r[1] += start.elapsed_time(end)
+    return sorted(((k, n, t) for k, (n, t) in rows.items()), key=lambda x: -x[2])
+
+
 # Default tile variant for every GEMM (0 = automatic).
 GEMM_VARIANT = 0
 
@@ -69,10 +95,20 @@ def gemm(
                               GEMM_VARIANT if variant is None else variant)
             return out
         state._gather_slot(slot)
+    if _PROFILE is not None:
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
     ext().gemm(
         a, b, out, a_mn, b_mn, epi, out_mode, alpha, bias, aux_in, aux_out, residual,
         status(out.device), split_k, GEMM_VARIANT if variant is None else variant, seed, stream, p, colsum,
     )
+    if _PROFILE is not None:
+        end.record()
+        m = a.shape[1] if a_mn else a.shape[0]
+        k = a.shape[0] if a_mn else a.shape[1]
+        n = b.shape[1] if b_mn else b.shape[0]
+        kind = "wgrad" if (a_mn and b_mn) else ("dgrad" if b_mn else "fwd")
+        _PROFILE.append((f"{kind} M{m} N{n} K{k} epi{epi} out{out_mode}", start, end))
     return out
 
 
@@ -81,12 +117,13 @@ def linear_forward(
     weight: torch.Tensor,
     bias: torch.Tensor | None = None,
     *,
-    gelu_preact: torch.Tensor | None = None,
+    gelu_grad: torch.Tensor | None = None,
     residual: torch.Tensor | None = None,
     out: torch.Tensor | None = None,
     dropout: tuple[int, int, float] | None = None,
 ) -> torch.Tensor:
-    """``y = x W^T (+ b) (-> gelu, storing the pre-activation) (-> dropout) (+ residual)``.
+    """``y = x W^T (+ b) (-> gelu, storing gelu'(pre-activation) into ``gelu_grad`` for the
+    backward) (-> dropout) (+ residual)``.
 
     ``dropout = (seed, stream, p)`` drops elements of the biased product
     before the residual add (needs bias and residual)."""
@@ -97,35 +134,35 @@ def linear_forward(
     epi = EPI_NONE
     if bias is not None:
         epi |= EPI_BIAS
-    if gelu_preact is not None:
+    if gelu_grad is not None:
         epi |= EPI_GELU
     if residual is not None:
         epi |= EPI_RESID
-    return gemm(x, weight, out, epi=epi, bias=bias, aux_out=gelu_preact, residual=residual, dropout=dropout)
+    return gemm(x, weight, out, epi=epi, bias=bias, aux_out=gelu_grad, residual=residual, dropout=dropout)
 
 
 def linear_dgrad(
     dy: torch.Tensor,
     weight: torch.Tensor,
     *,
-    gelu_preact: torch.Tensor | None = None,
+    gelu_grad: torch.Tensor | None = None,
     residual: torch.Tensor | None = None,
     out: torch.Tensor | None = None,
     colsum: torch.Tensor | None = None,
 ) -> torch.Tensor:
-    """``dx = dy W`` (times gelu'(preact) of the layer below) (+ residual);
+    """``dx = dy W`` (times the layer below's saved gelu derivative ``gelu_grad``) (+ residual);
     ``colsum``: also add dx's column sums into it (the lower layer's bias gradient)."""
 
     rows, k = dy.shape[0], weight.shape[1]
     if out is None:
         out = torch.empty((rows, k), dtype=torch.bfloat16, device=dy.device)
     epi = EPI_NONE
-    if gelu_preact is not None:
+    if gelu_grad is not None:
         epi |= EPI_DGELU
     if residual is not None:
         epi |= EPI_RESID
     return gemm(
-        dy, weight, out, b_mn=True, epi=epi, aux_in=gelu_preact, residual=residual, colsum=colsum
+        dy, weight, out, b_mn=True, epi=epi, aux_in=gelu_grad, residual=residual, colsum=colsum
     )
 
 

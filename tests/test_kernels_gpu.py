@@ -67,10 +67,12 @@ def test_gemm_forward_epilogues(m, n, k, gemm_variant):
     x = _rand(m, k, scale=0.5)
     w = _rand(n, k, scale=0.05)
     bias = _rand(n, scale=0.1)
-    pre = torch.empty(m, n, dtype=torch.bfloat16, device=_dev())
-    y = G.linear_forward(x, w, bias, gelu_preact=pre)
+    grad = torch.empty(m, n, dtype=torch.bfloat16, device=_dev())
+    y = G.linear_forward(x, w, bias, gelu_grad=grad)
     ref_pre = x.float() @ w.float().T + bias.float()
-    _close(pre, ref_pre, rtol=1e-2, atol=2e-2, what="preact")
+    # the epilogue saves gelu'(z) = Phi(z) + z phi(z) for the backward
+    ref_grad = 0.5 * (1 + torch.erf(ref_pre * 0.7071067811865476)) + ref_pre * torch.exp(-0.5 * ref_pre ** 2) * 0.3989422804014327
+    _close(grad, ref_grad, rtol=1e-2, atol=2e-2, what="gelu derivative")
     _close(y, torch.nn.functional.gelu(ref_pre), rtol=1e-2, atol=2e-2, what="gelu")
     res = _rand(m, n)
     y2 = G.linear_forward(x, w, bias, residual=res)
@@ -91,11 +93,18 @@ def test_gemm_dgrad(m, n, k, gemm_variant):
     dx = G.linear_dgrad(dy, w)
     ref = dy.float() @ w.float()
     _close(dx, ref, rtol=1e-2, atol=2e-2, what="dgrad")
-    pre = _rand(m, k)
-    dz = G.linear_dgrad(dy, w, gelu_preact=pre)
-    z = pre.float().requires_grad_(True)
+    saved = _rand(m, k)  # a saved gelu derivative: the epilogue multiplies by it
+    dz = G.linear_dgrad(dy, w, gelu_grad=saved)
+    _close(dz, ref * saved.float(), rtol=2e-2, atol=3e-2, what="dgrad*gelu'")
+    # round trip: forward GELU epilogue saves gelu'(z), the dgrad epilogue applies it
+    x = _rand(m, n, scale=0.5)
+    w1 = _rand(k, n, scale=0.1)
+    grad = torch.empty(m, k, dtype=torch.bfloat16, device=_dev())
+    G.linear_forward(x, w1, torch.zeros(k, dtype=torch.bfloat16, device=_dev()), gelu_grad=grad)
+    z = (x.float() @ w1.float().T).requires_grad_(True)
     torch.nn.functional.gelu(z).backward(ref)
-    _close(dz, z.grad, rtol=2e-2, atol=3e-2, what="dgrad*gelu'")
+    dz2 = G.linear_dgrad(dy, w, gelu_grad=grad)
+    _close(dz2, z.grad, rtol=3e-2, atol=4e-2, what="gelu forward -> backward")
     res = _rand(m, k)
     dr = G.linear_dgrad(dy, w, residual=res)
     _close(dr, ref + res.float(), rtol=1e-2, atol=3e-2, what="dgrad+res")

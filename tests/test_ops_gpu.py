@@ -392,10 +392,10 @@ def test_fused_column_sums_match():
     w = (torch.randn(768, 3072, device=DEV, generator=g) * 0.05).to(torch.bfloat16)
     z = torch.randn(900, 3072, device=DEV, generator=g).to(torch.bfloat16)
     cs = torch.zeros(3072, device=DEV)
-    dz = G.linear_dgrad(dy, w, gelu_preact=z, colsum=cs)
+    dz = G.linear_dgrad(dy, w, gelu_grad=z, colsum=cs)
     _close(cs, dz.float().sum(0), 2e-3)
     small = torch.zeros(3072, device=DEV)  # < 256 rows: the column sums run after the GEMM
-    dz_s = G.linear_dgrad(dy[:100], w, gelu_preact=z[:100], colsum=small)
+    dz_s = G.linear_dgrad(dy[:100], w, gelu_grad=z[:100], colsum=small)
     _close(small, dz_s.float().sum(0), 2e-3)
     x = torch.randn(1000, 768, device=DEV, generator=g).to(torch.bfloat16)
     out = torch.empty_like(x)
