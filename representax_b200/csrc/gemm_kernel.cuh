@@ -262,14 +262,13 @@ __device__ __forceinline__ void epilogue_tile_values32(const Params& p, int m, i
     }
   }
   if constexpr ((EPI & EPI_DROP) != 0) {
-    if (row_ok) {
+    if (row_ok) {  // 8-bit decisions: two Philox blocks cover the 32 columns
+      const Keep8 k8 = keep8_of(p.drop);
+      const uint32_t keep = keep16(p.drop, k8.t8, static_cast<uint32_t>(m), static_cast<uint32_t>(n_base >> 4)) |
+                            (keep16(p.drop, k8.t8, static_cast<uint32_t>(m), static_cast<uint32_t>((n_base >> 4) + 1))
+                             << 16);
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const Philox4 rb = dropout_block(p.drop, static_cast<uint32_t>(m), static_cast<uint32_t>((n_base >> 2) + q));
-#pragma unroll
-        for (int w = 0; w < 4; ++w)
-          v[4 * q + w] = word_of(rb, w) >= p.drop.threshold ? v[4 * q + w] * p.drop.scale : 0.f;
-      }
+      for (int i = 0; i < 32; ++i) v[i] = ((keep >> i) & 1u) ? v[i] * k8.scale : 0.f;
     }
   }
   if constexpr ((EPI & EPI_RESID) != 0) {
@@ -306,13 +305,12 @@ __device__ __forceinline__ void epilogue_row32(const Params& p, int m, int n_bas
       store_bf16x32(p.aux_out + static_cast<int64_t>(m) * p.ld_aux_out + n_base, d);
     }
     if constexpr ((EPI & EPI_DROP) != 0) {
+      const Keep8 k8 = keep8_of(p.drop);
+      const uint32_t keep = keep16(p.drop, k8.t8, static_cast<uint32_t>(m), static_cast<uint32_t>(n_base >> 4)) |
+                            (keep16(p.drop, k8.t8, static_cast<uint32_t>(m), static_cast<uint32_t>((n_base >> 4) + 1))
+                             << 16);
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const Philox4 r = dropout_block(p.drop, static_cast<uint32_t>(m), static_cast<uint32_t>((n_base >> 2) + q));
-#pragma unroll
-        for (int w = 0; w < 4; ++w)
-          v[4 * q + w] = word_of(r, w) >= p.drop.threshold ? v[4 * q + w] * p.drop.scale : 0.f;
-      }
+      for (int i = 0; i < 32; ++i) v[i] = ((keep >> i) & 1u) ? v[i] * k8.scale : 0.f;
     }
     if constexpr ((EPI & EPI_RESID) != 0) {
       float res[32];
@@ -357,8 +355,9 @@ __device__ __forceinline__ void epilogue_row32(const Params& p, int m, int n_bas
         p.aux_out[static_cast<int64_t>(m) * p.ld_aux_out + n] = __float2bfloat16_rn(d);
       }
       if constexpr ((EPI & EPI_DROP) != 0) {
-        const Philox4 r = dropout_block(p.drop, static_cast<uint32_t>(m), static_cast<uint32_t>(n >> 2));
-        x = word_of(r, n & 3) >= p.drop.threshold ? x * p.drop.scale : 0.f;
+        const Keep8 k8 = keep8_of(p.drop);
+        const uint32_t keep = keep16(p.drop, k8.t8, static_cast<uint32_t>(m), static_cast<uint32_t>(n >> 4));
+        x = ((keep >> (n & 15)) & 1u) ? x * k8.scale : 0.f;
       }
       if constexpr ((EPI & EPI_RESID) != 0)
         x += __bfloat162float(p.residual[static_cast<int64_t>(m) * p.ld_res + n]);

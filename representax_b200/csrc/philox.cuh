@@ -9,8 +9,13 @@
 // forward kernel and any backward kernel regenerate the same mask from the
 // element coordinates alone: nothing is stored.
 //
-// Keep decision: an element is kept when its 32-bit word is >= threshold,
-// threshold = round(p * 2^32); kept values are scaled by 1 / (1 - p).
+// Keep decisions are 8-bit: a block's 16 bytes decide 16 elements; an
+// element is kept when its byte is >= t8 = round(p * 256) (at least 1, at most
+// 255) and kept values are scaled by 256 / (256 - t8), which keeps the
+// expectation exact for the quantised probability t8 / 256. Hidden
+// (activation) dropout maps element (row, col) to byte col & 15 of block
+// (row, col >> 4); attention-probability dropout has its own mapping
+// (attention_tc.cuh).
 #pragma once
 #include <stdint.h>
 
@@ -69,6 +74,36 @@ __device__ __forceinline__ uint32_t word_of(const Philox4& r, int i) {
 __device__ __forceinline__ Philox4 dropout_block(const DropoutSite& s, uint32_t a, uint32_t b) {
   return philox4x32<7>(Philox4{a, b, s.stream, 0u}, static_cast<uint32_t>(s.seed),
                        static_cast<uint32_t>(s.seed >> 32));
+}
+
+// 8-bit keep threshold and scale of a site (t8 = 0: dropout off).
+struct Keep8 {
+  uint32_t t8;
+  float scale;
+};
+
+__host__ __device__ __forceinline__ Keep8 keep8_of(const DropoutSite& s) {
+  Keep8 k{0u, 1.f};
+  if (s.threshold == 0u) return k;
+  k.t8 = (s.threshold + (1u << 23)) >> 24;
+  if (k.t8 > 255u) k.t8 = 255u;
+  if (k.t8 == 0u) k.t8 = 1u;  // a requested dropout never rounds to none
+  k.scale = 256.f / static_cast<float>(256u - k.t8);
+  return k;
+}
+
+// Hidden-dropout keep bits of the 16 columns 16 col16 .. 16 col16 + 15 of
+// `row`: bit j set = column 16 col16 + j kept.
+__device__ __forceinline__ uint32_t keep16(const DropoutSite& s, uint32_t t8, uint32_t row, uint32_t col16) {
+  const Philox4 r = dropout_block(s, row, col16);
+  uint32_t m = 0u;
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    const uint32_t word = word_of(r, w);
+#pragma unroll
+    for (int b = 0; b < 4; ++b) m |= static_cast<uint32_t>(((word >> (8 * b)) & 0xffu) >= t8) << (4 * w + b);
+  }
+  return m;
 }
 
 }  // namespace rx

@@ -271,13 +271,14 @@ __global__ void dropout_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t r = i / quads, q = i % quads;
-    const Philox4 bits = dropout_block(site, static_cast<uint32_t>(r), static_cast<uint32_t>(q));
+    const Keep8 k8 = keep8_of(site);
+    const uint32_t keep = keep16(site, k8.t8, static_cast<uint32_t>(r), static_cast<uint32_t>(q >> 2)) >> (4 * (q & 3));
     const uint2 in = *reinterpret_cast<const uint2*>(x + r * ldx + 4 * q);
     const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&in);
     const float2 a = __bfloat1622float2(h[0]), b = __bfloat1622float2(h[1]);
     float v[4] = {a.x, a.y, b.x, b.y};
 #pragma unroll
-    for (int w = 0; w < 4; ++w) v[w] = word_of(bits, w) >= site.threshold ? v[w] * site.scale : 0.f;
+    for (int w = 0; w < 4; ++w) v[w] = ((keep >> w) & 1u) ? v[w] * k8.scale : 0.f;
     uint2 out;
     __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(&out);
     o[0] = __floats2bfloat162_rn(v[0], v[1]);
@@ -290,62 +291,71 @@ __global__ void dropout_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
 // result into colsum (fp32 [cols]): a block owns 256 columns (4 per thread)
 // and a range of rows, and adds its partial sums with one atomic per column.
 // y = dropout(x) with the column sums of the (rounded) result added into
-// `colsum` (a bias gradient). One CTA per slice of rows: thread (g, q) owns
-// column quad q of rows g, g + G, ... of the slice, with eight rows' loads in
-// flight; the G row groups meet in shared memory, so each column takes one
-// atomic per CTA.
+// `colsum` (a bias gradient). One CTA per slice of rows: thread (g, u) owns
+// the 16-column unit u (one Philox block per row) of rows g, g + G, ... of the
+// slice, with four rows' loads in flight; the G row groups meet in shared
+// memory, so each column takes one atomic per CTA.
 __global__ void __launch_bounds__(512)
     dropout_colsum_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, __nv_bfloat16* y, int64_t ldy,
                           int64_t rows, int64_t cols, DropoutSite site, float* __restrict__ colsum,
                           int64_t rows_per_block) {
   extern __shared__ float part[];  // [groups][cols]
-  const int quads = static_cast<int>(cols / 4);
-  const int groups = blockDim.x / quads;
-  const int q = threadIdx.x % quads, g = threadIdx.x / quads;
+  const int units = static_cast<int>(cols / 16);
+  const int groups = blockDim.x / units;
+  const int u = threadIdx.x % units, g = threadIdx.x / units;
   const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rows_per_block;
   const int64_t r1 = r0 + rows_per_block < rows ? r0 + rows_per_block : rows;
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  if (g < groups) {
-    for (int64_t r = r0 + g; r < r1; r += 8 * groups) {
-      uint2 in[8];
+  const Keep8 k8 = keep8_of(site);
+  float acc[16];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int64_t rr = r + u * groups < r1 ? r + u * groups : r1 - 1;  // past the slice: re-read, not used
-        in[u] = __ldg(reinterpret_cast<const uint2*>(x + rr * ldx + 4 * q));
+  for (int j = 0; j < 16; ++j) acc[j] = 0.f;
+  if (g < groups) {
+    for (int64_t r = r0 + g; r < r1; r += 4 * groups) {
+      uint4 in[4][2];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const int64_t rr = r + t * groups < r1 ? r + t * groups : r1 - 1;  // past the slice: re-read, not used
+        const uint4* src = reinterpret_cast<const uint4*>(x + rr * ldx + 16 * u);
+        in[t][0] = __ldg(src);
+        in[t][1] = __ldg(src + 1);
       }
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int64_t rr = r + u * groups;
+      for (int t = 0; t < 4; ++t) {
+        const int64_t rr = r + t * groups;
         if (rr >= r1) break;
-        const Philox4 bits = dropout_block(site, static_cast<uint32_t>(rr), static_cast<uint32_t>(q));
-        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&in[u]);
-        const float2 a = __bfloat1622float2(h[0]), b = __bfloat1622float2(h[1]);
-        float v[4] = {a.x, a.y, b.x, b.y};
+        const uint32_t keep = keep16(site, k8.t8, static_cast<uint32_t>(rr), static_cast<uint32_t>(u));
+        uint4 out[2];
 #pragma unroll
-        for (int w = 0; w < 4; ++w) v[w] = word_of(bits, w) >= site.threshold ? v[w] * site.scale : 0.f;
-        uint2 out;
-        __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(&out);
-        o[0] = __floats2bfloat162_rn(v[0], v[1]);
-        o[1] = __floats2bfloat162_rn(v[2], v[3]);
-        *reinterpret_cast<uint2*>(y + rr * ldy + 4 * q) = out;
-        const float2 ra = __bfloat1622float2(o[0]), rb = __bfloat1622float2(o[1]);
-        acc[0] += ra.x;
-        acc[1] += ra.y;
-        acc[2] += rb.x;
-        acc[3] += rb.y;
+        for (int h = 0; h < 2; ++h) {
+          const __nv_bfloat162* i2 = reinterpret_cast<const __nv_bfloat162*>(&in[t][h]);
+          __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&out[h]);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int c = 8 * h + 2 * j;
+            const float2 f = __bfloat1622float2(i2[j]);
+            o2[j] = __floats2bfloat162_rn(((keep >> c) & 1u) ? f.x * k8.scale : 0.f,
+                                          ((keep >> (c + 1)) & 1u) ? f.y * k8.scale : 0.f);
+            const float2 back = __bfloat1622float2(o2[j]);
+            acc[c] += back.x;
+            acc[c + 1] += back.y;
+          }
+        }
+        uint4* dst = reinterpret_cast<uint4*>(y + rr * ldy + 16 * u);
+        dst[0] = out[0];
+        dst[1] = out[1];
       }
     }
   }
   if (groups == 1) {
     if (g == 0) {
 #pragma unroll
-      for (int w = 0; w < 4; ++w) atomicAdd(colsum + 4 * q + w, acc[w]);
+      for (int j = 0; j < 16; ++j) atomicAdd(colsum + 16 * u + j, acc[j]);
     }
     return;
   }
   if (g < groups) {
 #pragma unroll
-    for (int w = 0; w < 4; ++w) part[g * cols + 4 * q + w] = acc[w];
+    for (int j = 0; j < 16; ++j) part[g * cols + 16 * u + j] = acc[j];
   }
   __syncthreads();
   for (int c = threadIdx.x; c < cols; c += blockDim.x) {
@@ -547,8 +557,11 @@ void dropout_apply(const at::Tensor& x, at::Tensor& y, int64_t seed, int64_t str
   if (colsum.has_value()) {
     check_f32(*colsum, "colsum");
     RX_CHECK(colsum->numel() == cols && colsum->is_contiguous(), "colsum must be fp32 [cols]");
-    const int64_t quads = cols / 4;
-    if (quads > 512) {  // wider rows: the plain dropout kernel, then a column-sum pass
+    const int64_t units = cols / 16;
+    const bool vec_ok = cols % 16 == 0 && x.stride(0) % 8 == 0 && y.stride(0) % 8 == 0 &&
+                        reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0 &&
+                        reinterpret_cast<uintptr_t>(y.data_ptr()) % 16 == 0;
+    if (units > 512 || !vec_ok) {  // wide or unaligned rows: plain dropout kernel, then a column-sum pass
       const int grid = grid_for(rows * cols / 4, 256, device);
       pw::dropout_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream(device).stream()>>>(
           reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0),
@@ -558,10 +571,10 @@ void dropout_apply(const at::Tensor& x, at::Tensor& y, int64_t seed, int64_t str
       colsum_accumulate(y, sums);
       return;
     }
-    const int groups = static_cast<int>(std::max<int64_t>(1, 512 / quads));
-    const int threads = static_cast<int>(groups * quads);
-    const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>(4ll * num_sms(device), (rows + 8 * groups - 1) /
-                                                                                          (8 * groups)));
+    const int groups = static_cast<int>(std::max<int64_t>(1, 512 / units));
+    const int threads = static_cast<int>(groups * units);
+    const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>(4ll * num_sms(device), (rows + 4 * groups - 1) /
+                                                                                          (4 * groups)));
     const int64_t rows_per_block = (rows + blocks - 1) / blocks;
     const dim3 grid2(static_cast<unsigned>((rows + rows_per_block - 1) / rows_per_block));
     const size_t smem = groups > 1 ? static_cast<size_t>(groups) * cols * sizeof(float) : 0;
