@@ -217,7 +217,10 @@ __global__ void __launch_bounds__(kWarps * 32, (MAXV <= 4 ? 3 : 1))
           const float xh = (xv[i][j] - mean) * rstd;
           o[j] = rstd * (d[j] * g[j] - (RMS ? 0.f : s1) - xh * s2);
         }
-        if (dbias_prev != nullptr) {
+        // the producer-bias partial; in embedding mode without type ids (every
+        // token of type 0) it holds the type-row gradient instead, added to
+        // type_grad once per CTA rather than once per token
+        if (dbias_prev != nullptr || (word_grad != nullptr && type_ids == nullptr)) {
           float4* dp = reinterpret_cast<float4*>(pd + c * 8);
           float4 a0 = dp[0], a1 = dp[1];
           a0.x += o[0]; a0.y += o[1]; a0.z += o[2]; a0.w += o[3];
@@ -228,13 +231,13 @@ __global__ void __launch_bounds__(kWarps * 32, (MAXV <= 4 ? 3 : 1))
           const int id = ids[row];
           float* wg = word_grad + static_cast<int64_t>(id) * H + c * 8;
           float* pgp = pos_grad + static_cast<int64_t>(pos_ids[row]) * H + c * 8;
-          float* tg = type_grad + static_cast<int64_t>(type_ids ? type_ids[row] : 0) * H + c * 8;
+          float* tg = type_ids ? type_grad + static_cast<int64_t>(type_ids[row]) * H + c * 8 : nullptr;
 #pragma unroll
           for (int j = 0; j < 8; j += 4) {
             const float4 w4 = make_float4(o[j], o[j + 1], o[j + 2], o[j + 3]);
             if (id != pad_id) atomicAdd(reinterpret_cast<float4*>(wg + j), w4);
             atomicAdd(reinterpret_cast<float4*>(pgp + j), w4);
-            atomicAdd(reinterpret_cast<float4*>(tg + j), w4);
+            if (tg != nullptr) atomicAdd(reinterpret_cast<float4*>(tg + j), w4);
           }
         } else {
           reinterpret_cast<uint4*>(dx + static_cast<int64_t>(row) * H)[c] = pack8(o);
@@ -255,6 +258,7 @@ __global__ void __launch_bounds__(kWarps * 32, (MAXV <= 4 ? 3 : 1))
     if (dgamma) atomicAdd(dgamma + col, a);
     if (dbeta && !RMS) atomicAdd(dbeta + col, b);
     if (dbias_prev) atomicAdd(dbias_prev + col, d);
+    else if (word_grad != nullptr && type_ids == nullptr) atomicAdd(type_grad + col, d);
   }
 }
 
