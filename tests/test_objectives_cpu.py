@@ -68,3 +68,24 @@ def test_every_loss_config_parses(kind):
     definition = BUILTIN_LOSSES.definition(kind)
     config = definition.config_type()
     assert BUILTIN_LOSSES.parse(config.model_dump()) == config
+
+
+def test_task_family_import_paths():
+    """Each objective family is importable from its own subpackage, as in the reference layout."""
+
+    import importlib
+
+    expected = {
+        "pairwise": ["CoSENTTask", "AnglETask", "ContrastiveTask", "CosineRegressionTask", "PairwiseBatch"],
+        "triplet": ["BatchTripletTask", "ExplicitTripletTask", "LabeledExamplesBatch"],
+        "distillation": ["EmbeddingDistillationTask", "MarginDistillationTask", "DistributionDistillationTask"],
+        "classification": ["SoftmaxClassificationTask", "PairClassificationBatch"],
+        "contrastive_tension": ["ContrastiveTensionTask", "ContrastiveTensionInBatchTask"],
+        "mega_batch": ["MegaBatchMarginTask", "MegaBatch"],
+        "reconstruction": ["DenoisingAutoEncoderTask", "DenoisingBatch"],
+        "regularization": ["GlobalOrthogonalRegularizationTask", "RegularizationBatch"],
+    }
+    for family, names in expected.items():
+        module = importlib.import_module(f"representax_b200.tasks.{family}")
+        for name in names:
+            assert name in module.__all__ and getattr(module, name) is not None, (family, name)
