@@ -515,11 +515,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           float4* d4 = reinterpret_cast<float4*>(p.dq_acc + static_cast<int64_t>(it.start + q) * width_q + hq * D);
 #pragma unroll
           for (int e = 0; e < 8; ++e)
-            atomicAdd(d4 + e, make_float4(__uint_as_float(o0[4 * e]), __uint_as_float(o0[4 * e + 1]),
+            red_add_f4(d4 + e, make_float4(__uint_as_float(o0[4 * e]), __uint_as_float(o0[4 * e + 1]),
                                           __uint_as_float(o0[4 * e + 2]), __uint_as_float(o0[4 * e + 3])));
 #pragma unroll
           for (int e = 0; e < 8; ++e)
-            atomicAdd(d4 + 8 + e, make_float4(__uint_as_float(o1[4 * e]), __uint_as_float(o1[4 * e + 1]),
+            red_add_f4(d4 + 8 + e, make_float4(__uint_as_float(o1[4 * e]), __uint_as_float(o1[4 * e + 1]),
                                               __uint_as_float(o1[4 * e + 2]), __uint_as_float(o1[4 * e + 3])));
         }
       }

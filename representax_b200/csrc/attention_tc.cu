@@ -638,7 +638,7 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
           float4* d4 = reinterpret_cast<float4*>(dq + c * 32);
 #pragma unroll
           for (int e = 0; e < 8; ++e)
-            atomicAdd(d4 + e, make_float4(__uint_as_float(o[4 * e]), __uint_as_float(o[4 * e + 1]),
+            red_add_f4(d4 + e, make_float4(__uint_as_float(o[4 * e]), __uint_as_float(o[4 * e + 1]),
                                           __uint_as_float(o[4 * e + 2]), __uint_as_float(o[4 * e + 3])));
         }
       }

@@ -333,7 +333,7 @@ __device__ __forceinline__ void epilogue_row32(const Params& p, int m, int n_bas
           float4 o = c4[q];
           c4[q] = make_float4(o.x + w.x, o.y + w.y, o.z + w.z, o.w + w.w);
         } else {
-          atomicAdd(c4 + q, w);
+          red_add_f4(c4 + q, w);
         }
       }
     }

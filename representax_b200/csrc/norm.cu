@@ -235,9 +235,9 @@ __global__ void __launch_bounds__(kWarps * 32, (MAXV <= 4 ? 3 : 1))
 #pragma unroll
           for (int j = 0; j < 8; j += 4) {
             const float4 w4 = make_float4(o[j], o[j + 1], o[j + 2], o[j + 3]);
-            if (id != pad_id) atomicAdd(reinterpret_cast<float4*>(wg + j), w4);
-            atomicAdd(reinterpret_cast<float4*>(pgp + j), w4);
-            if (tg != nullptr) atomicAdd(reinterpret_cast<float4*>(tg + j), w4);
+            if (id != pad_id) red_add_f4(reinterpret_cast<float4*>(wg + j), w4);
+            red_add_f4(reinterpret_cast<float4*>(pgp + j), w4);
+            if (tg != nullptr) red_add_f4(reinterpret_cast<float4*>(tg + j), w4);
           }
         } else {
           reinterpret_cast<uint4*>(dx + static_cast<int64_t>(row) * H)[c] = pack8(o);

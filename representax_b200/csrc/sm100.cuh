@@ -330,6 +330,14 @@ __device__ __forceinline__ void hold_v4(uint4& v) {
   asm volatile("" : "+r"(v.x), "+r"(v.y), "+r"(v.z), "+r"(v.w));
 }
 
+// Fire-and-forget fp32 vector reduction into global memory (red: no value
+// comes back, so the issuing thread never waits on it).
+__device__ __forceinline__ void red_add_f4(float4* addr, float4 v) {
+  asm volatile("red.relaxed.gpu.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(v.x), "f"(v.y), "f"(v.z),
+               "f"(v.w)
+               : "memory");
+}
+
 __device__ __forceinline__ int warp_id() { return threadIdx.x >> 5; }
 __device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
 
