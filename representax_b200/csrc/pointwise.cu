@@ -293,7 +293,7 @@ __global__ void dropout_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
 // y = dropout(x) with the column sums of the (rounded) result added into
 // `colsum` (a bias gradient). One CTA per slice of rows: thread (g, u) owns
 // the 16-column unit u (one Philox block per row) of rows g, g + G, ... of the
-// slice, with four rows' loads in flight; the G row groups meet in shared
+// slice, with eight rows' loads in flight; the G row groups meet in shared
 // memory, so each column takes one atomic per CTA.
 __global__ void __launch_bounds__(512)
     dropout_colsum_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, __nv_bfloat16* y, int64_t ldy,
@@ -310,17 +310,17 @@ __global__ void __launch_bounds__(512)
 #pragma unroll
   for (int j = 0; j < 16; ++j) acc[j] = 0.f;
   if (g < groups) {
-    for (int64_t r = r0 + g; r < r1; r += 4 * groups) {
-      uint4 in[4][2];
+    for (int64_t r = r0 + g; r < r1; r += 8 * groups) {
+      uint4 in[8][2];
 #pragma unroll
-      for (int t = 0; t < 4; ++t) {
+      for (int t = 0; t < 8; ++t) {
         const int64_t rr = r + t * groups < r1 ? r + t * groups : r1 - 1;  // past the slice: re-read, not used
         const uint4* src = reinterpret_cast<const uint4*>(x + rr * ldx + 16 * u);
         in[t][0] = __ldg(src);
         in[t][1] = __ldg(src + 1);
       }
 #pragma unroll
-      for (int t = 0; t < 4; ++t) {
+      for (int t = 0; t < 8; ++t) {
         const int64_t rr = r + t * groups;
         if (rr >= r1) break;
         const uint32_t keep = keep16(site, k8.t8, static_cast<uint32_t>(rr), static_cast<uint32_t>(u));
@@ -573,8 +573,8 @@ void dropout_apply(const at::Tensor& x, at::Tensor& y, int64_t seed, int64_t str
     }
     const int groups = static_cast<int>(std::max<int64_t>(1, 512 / units));
     const int threads = static_cast<int>(groups * units);
-    const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>(4ll * num_sms(device), (rows + 4 * groups - 1) /
-                                                                                          (4 * groups)));
+    const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>(4ll * num_sms(device), (rows + 8 * groups - 1) /
+                                                                                          (8 * groups)));
     const int64_t rows_per_block = (rows + blocks - 1) / blocks;
     const dim3 grid2(static_cast<unsigned>((rows + rows_per_block - 1) / rows_per_block));
     const size_t smem = groups > 1 ? static_cast<size_t>(groups) * cols * sizeof(float) : 0;
